@@ -1,0 +1,282 @@
+// extern "C" entry points of the transducer losses (RNN-T, TDT): argument
+// checks, workspace carving and the launch sequence of each op. The CTC entry
+// points live in ctc.cu.
+//
+// Launch sequence (all on the caller's stream, no host synchronisation):
+//   forward : lattice_prep -> joint forward (GEMM + fused log-softmax gather)
+//             -> alpha recursion (loss, log_prob)
+//   backward: lattice_prep -> beta recursion (posteriors, duration-logit grads)
+//             -> zero the gradients -> joint backward (dlogits, dH, dW)
+#include <algorithm>
+#include <cstring>
+
+#include "dp.cuh"
+#include "joint.cuh"
+
+using namespace asr;
+
+namespace {
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int64_t node_capacity(int B, int T, int U) { return (int64_t)B * T * U; }
+
+bool bad_dims(int B, int T, int U, int V, int d) { return B < 0 || T < 1 || U < 1 || V < 1 || d < 1; }
+
+// Layout of a transducer workspace.
+struct TrWorkspace {
+    LatticeMeta meta;
+    float* cb = nullptr;    // backward: (cap,)
+    float* ct = nullptr;    // backward: (cap,)
+    float* gdur = nullptr;  // backward TDT: (cap, n_dur)
+    void* joint = nullptr;  // joint-network scratch
+    size_t joint_bytes = 0;
+};
+
+size_t joint_scratch_bytes(const JointArgs& a, int64_t cap, bool tc, bool backward) {
+    if (tc) return backward ? tc_backward_scratch_bytes(a, (int)cap) : tc_forward_scratch_bytes(a);
+    return backward ? simt_backward_scratch_bytes(a.V + a.n_dur, (int)cap) : 0;
+}
+
+size_t tr_workspace_bytes(const JointArgs& a, int64_t cap, bool tc, bool backward) {
+    size_t n = lattice_meta_bytes(a.B);
+    if (backward) {
+        n += 2 * align256(sizeof(float) * cap);
+        if (a.n_dur > 0) n += align256(sizeof(float) * cap * a.n_dur);
+    }
+    n += align256(joint_scratch_bytes(a, cap, tc, backward));
+    return n + 256;  // slack for aligning the base pointer
+}
+
+TrWorkspace carve(void* ws, const JointArgs& a, int64_t cap, bool tc, bool backward) {
+    TrWorkspace w;
+    char* p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+    p = lattice_meta_carve(p, a.B, &w.meta);
+    if (backward) {
+        w.cb = reinterpret_cast<float*>(p);
+        p += align256(sizeof(float) * cap);
+        w.ct = reinterpret_cast<float*>(p);
+        p += align256(sizeof(float) * cap);
+        if (a.n_dur > 0) {
+            w.gdur = reinterpret_cast<float*>(p);
+            p += align256(sizeof(float) * cap * a.n_dur);
+        }
+    }
+    w.joint = p;
+    w.joint_bytes = joint_scratch_bytes(a, cap, tc, backward);
+    return w;
+}
+
+JointArgs make_args(const float* enc, const float* dec, const float* W, const float* Wd, const int32_t* targets,
+                    int B, int T, int U, int V, int n_dur, int d, int S, int blank, float sigma) {
+    JointArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.enc = enc;
+    a.dec = dec;
+    a.W = W;
+    a.Wd = Wd;
+    a.targets = targets;
+    a.B = B;
+    a.T = T;
+    a.U = U;
+    a.V = V;
+    a.n_dur = n_dur;
+    a.d = d;
+    a.S = S;
+    a.blank = blank;
+    a.sigma = sigma;
+    return a;
+}
+
+bool use_tc(int tf32, const JointArgs& a) { return tf32 != 0 && tc_supported(a); }
+
+}  // namespace
+
+extern "C" const char* asr_status_string(int status) {
+    switch (status) {
+        case ASR_OK: return "ok";
+        case ASR_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case ASR_ERR_WORKSPACE: return "workspace missing or too small";
+        case ASR_ERR_UNSUPPORTED: return "shape outside the supported kernel range";
+        case ASR_ERR_CUDA: return "CUDA launch or runtime error";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int asr_abi_version(void) { return 1; }
+
+// ------------------------------------------------------------------------ RNN-T
+
+extern "C" size_t asr_rnnt_workspace_bytes(int B, int T, int U, int V, int d, int tf32, int backward) {
+    if (bad_dims(B, T, U, V, d)) return 0;
+    JointArgs a = make_args(nullptr, nullptr, nullptr, nullptr, nullptr, B, T, U, V, 0, d, U - 1, 0, 0.f);
+    return tr_workspace_bytes(a, node_capacity(B, T, U), use_tc(tf32, a), backward != 0);
+}
+
+extern "C" int asr_rnnt_forward(const float* encoder, const float* decoder, const float* joint_W,
+                                const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens, int B,
+                                int T, int U, int V, int d, int S, int blank_idx, int tf32, float* loss, double* alpha,
+                                float* log_P_blank, float* log_P_y, float* log_prob, void* workspace,
+                                size_t workspace_bytes, asr_stream_t stream) {
+    if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V) return ASR_ERR_INVALID_ARGUMENT;
+    if (B == 0) return ASR_OK;
+    if (!encoder || !decoder || !joint_W || !in_lens || !tgt_lens || !loss || !alpha || !log_P_blank || !log_P_y ||
+        !log_prob || (S > 0 && !targets))
+        return ASR_ERR_INVALID_ARGUMENT;
+    if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
+    JointArgs a = make_args(encoder, decoder, joint_W, nullptr, targets, B, T, U, V, 0, d, S, blank_idx, 0.f);
+    const int64_t cap = node_capacity(B, T, U);
+    const bool tc = use_tc(tf32, a);
+    if (!workspace || workspace_bytes < tr_workspace_bytes(a, cap, tc, false)) return ASR_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    TrWorkspace w = carve(workspace, a, cap, tc, false);
+    a.m = w.meta;
+    int rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
+    if (rc) return rc;
+    JointFwdOut o{log_P_blank, log_P_blank + cap, log_P_y, nullptr};
+    rc = tc ? tc_joint_forward(a, o, w.joint, w.joint_bytes, st) : simt_joint_forward(a, o, st);
+    if (rc) return rc;
+    return launch_rnnt_alpha(w.meta, B, U, log_P_blank, log_P_y, alpha, log_prob, loss, st);
+}
+
+extern "C" int asr_rnnt_backward(const float* encoder, const float* decoder, const float* joint_W,
+                                 const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens, int B,
+                                 int T, int U, int V, int d, int S, int blank_idx, const double* alpha,
+                                 const float* log_P_blank, const float* log_P_y, const float* log_prob,
+                                 const float* grad_loss, int tf32, float* grad_encoder, float* grad_decoder,
+                                 float* grad_joint_W, void* workspace, size_t workspace_bytes,
+                                 asr_stream_t stream) {
+    if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V) return ASR_ERR_INVALID_ARGUMENT;
+    if (!grad_joint_W) return ASR_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (B == 0) {
+        ASR_CUDA_TRY(cudaMemsetAsync(grad_joint_W, 0, sizeof(float) * (size_t)V * d, st));
+        return ASR_OK;
+    }
+    if (!encoder || !decoder || !joint_W || !in_lens || !tgt_lens || !alpha || !log_P_blank || !log_P_y ||
+        !log_prob || !grad_loss || !grad_encoder || !grad_decoder || (S > 0 && !targets))
+        return ASR_ERR_INVALID_ARGUMENT;
+    if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
+    JointArgs a = make_args(encoder, decoder, joint_W, nullptr, targets, B, T, U, V, 0, d, S, blank_idx, 0.f);
+    const int64_t cap = node_capacity(B, T, U);
+    const bool tc = use_tc(tf32, a);
+    if (!workspace || workspace_bytes < tr_workspace_bytes(a, cap, tc, true)) return ASR_ERR_WORKSPACE;
+    TrWorkspace w = carve(workspace, a, cap, tc, true);
+    a.m = w.meta;
+    int rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
+    if (rc) return rc;
+    rc = launch_rnnt_beta(w.meta, B, U, log_P_blank, log_P_y, alpha, grad_loss, w.cb, w.ct, st);
+    if (rc) return rc;
+    ASR_CUDA_TRY(cudaMemsetAsync(grad_encoder, 0, sizeof(float) * (size_t)B * T * d, st));
+    ASR_CUDA_TRY(cudaMemsetAsync(grad_decoder, 0, sizeof(float) * (size_t)B * U * d, st));
+    ASR_CUDA_TRY(cudaMemsetAsync(grad_joint_W, 0, sizeof(float) * (size_t)V * d, st));
+    JointBwdIn in{log_P_blank + cap, w.cb, w.ct, nullptr};
+    JointBwdOut o{grad_encoder, grad_decoder, grad_joint_W, nullptr};
+    return tc ? tc_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st)
+              : simt_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st);
+}
+
+// -------------------------------------------------------------------------- TDT
+
+namespace {
+bool bad_tdt(int n_dur, int max_duration) {
+    return n_dur < 1 || n_dur > kTdtMaxDurClasses || max_duration < 1 || max_duration > kTdtMaxDuration;
+}
+}  // namespace
+
+extern "C" size_t asr_tdt_workspace_bytes(int B, int T, int U, int V, int n_dur, int d, int tf32, int backward) {
+    if (bad_dims(B, T, U, V, d) || n_dur < 1) return 0;
+    JointArgs a = make_args(nullptr, nullptr, nullptr, nullptr, nullptr, B, T, U, V, n_dur, d, U - 1, 0, 0.f);
+    return tr_workspace_bytes(a, node_capacity(B, T, U), use_tc(tf32, a), backward != 0);
+}
+
+extern "C" int asr_tdt_forward(const float* encoder, const float* decoder, const float* joint_W,
+                               const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                               const int32_t* tgt_lens, const int32_t* durations, int n_dur, int max_duration,
+                               int has_zero, int B, int T, int U, int V, int d, int S, int blank_idx, float sigma,
+                               int tf32, float* loss, double* alpha, float* log_P_blank, float* log_P_y,
+                               float* log_P_dur, float* log_prob, void* workspace, size_t workspace_bytes,
+                               asr_stream_t stream) {
+    if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || bad_tdt(n_dur, max_duration))
+        return ASR_ERR_INVALID_ARGUMENT;
+    if (B == 0) return ASR_OK;
+    if (!encoder || !decoder || !joint_W || !joint_W_dur || !durations || !in_lens || !tgt_lens || !loss ||
+        !alpha || !log_P_blank || !log_P_y || !log_P_dur || !log_prob || (S > 0 && !targets))
+        return ASR_ERR_INVALID_ARGUMENT;
+    if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
+    JointArgs a = make_args(encoder, decoder, joint_W, joint_W_dur, targets, B, T, U, V, n_dur, d, S, blank_idx,
+                            sigma);
+    const int64_t cap = node_capacity(B, T, U);
+    const bool tc = use_tc(tf32, a);
+    if (!workspace || workspace_bytes < tr_workspace_bytes(a, cap, tc, false)) return ASR_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    TrWorkspace w = carve(workspace, a, cap, tc, false);
+    a.m = w.meta;
+    int rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
+    if (rc) return rc;
+    JointFwdOut o{log_P_blank, log_P_blank + cap, log_P_y, log_P_dur};
+    rc = tc ? tc_joint_forward(a, o, w.joint, w.joint_bytes, st) : simt_joint_forward(a, o, st);
+    if (rc) return rc;
+    return launch_tdt_alpha(w.meta, B, U, max_duration, durations, n_dur, has_zero, log_P_blank, log_P_y, log_P_dur,
+                            alpha, log_prob, loss, st);
+}
+
+extern "C" int asr_tdt_backward(const float* encoder, const float* decoder, const float* joint_W,
+                                const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                                const int32_t* tgt_lens, const int32_t* durations, int n_dur, int max_duration,
+                                int has_zero, int B, int T, int U, int V, int d, int S, int blank_idx,
+                                const double* alpha, const float* log_P_blank, const float* log_P_y,
+                                const float* log_P_dur, const float* log_prob, const float* grad_loss, int tf32,
+                                float* grad_encoder, float* grad_decoder, float* grad_joint_W,
+                                float* grad_joint_W_dur, void* workspace, size_t workspace_bytes,
+                                asr_stream_t stream) {
+    if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || bad_tdt(n_dur, max_duration))
+        return ASR_ERR_INVALID_ARGUMENT;
+    if (!grad_joint_W || !grad_joint_W_dur) return ASR_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (B == 0) {
+        ASR_CUDA_TRY(cudaMemsetAsync(grad_joint_W, 0, sizeof(float) * (size_t)V * d, st));
+        ASR_CUDA_TRY(cudaMemsetAsync(grad_joint_W_dur, 0, sizeof(float) * (size_t)n_dur * d, st));
+        return ASR_OK;
+    }
+    if (!encoder || !decoder || !joint_W || !joint_W_dur || !durations || !in_lens || !tgt_lens || !alpha ||
+        !log_P_blank || !log_P_y || !log_P_dur || !log_prob || !grad_loss || !grad_encoder || !grad_decoder ||
+        (S > 0 && !targets))
+        return ASR_ERR_INVALID_ARGUMENT;
+    if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
+    JointArgs a = make_args(encoder, decoder, joint_W, joint_W_dur, targets, B, T, U, V, n_dur, d, S, blank_idx,
+                            0.f);
+    const int64_t cap = node_capacity(B, T, U);
+    const bool tc = use_tc(tf32, a);
+    if (!workspace || workspace_bytes < tr_workspace_bytes(a, cap, tc, true)) return ASR_ERR_WORKSPACE;
+    TrWorkspace w = carve(workspace, a, cap, tc, true);
+    a.m = w.meta;
+    int rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
+    if (rc) return rc;
+    rc = launch_tdt_beta(w.meta, B, U, max_duration, durations, n_dur, has_zero, log_P_blank, log_P_y, log_P_dur,
+                         alpha, grad_loss, w.cb, w.ct, w.gdur, st);
+    if (rc) return rc;
+    ASR_CUDA_TRY(cudaMemsetAsync(grad_encoder, 0, sizeof(float) * (size_t)B * T * d, st));
+    ASR_CUDA_TRY(cudaMemsetAsync(grad_decoder, 0, sizeof(float) * (size_t)B * U * d, st));
+    ASR_CUDA_TRY(cudaMemsetAsync(grad_joint_W, 0, sizeof(float) * (size_t)V * d, st));
+    ASR_CUDA_TRY(cudaMemsetAsync(grad_joint_W_dur, 0, sizeof(float) * (size_t)n_dur * d, st));
+    JointBwdIn in{log_P_blank + cap, w.cb, w.ct, w.gdur};
+    JointBwdOut o{grad_encoder, grad_decoder, grad_joint_W, grad_joint_W_dur};
+    return tc ? tc_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st)
+              : simt_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st);
+}
+
+// ------------------------------------------------------------------ diagnostics
+
+extern "C" int asr_workspace_status(const void* workspace, int B, int* clamped, asr_stream_t stream) {
+    if (!workspace || !clamped || B < 1) return ASR_ERR_INVALID_ARGUMENT;
+    LatticeMeta m;
+    char* p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+    lattice_meta_carve(p, B, &m);
+    int32_t v = 0;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    ASR_CUDA_TRY(cudaMemcpyAsync(&v, m.status, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    ASR_CUDA_TRY(cudaStreamSynchronize(st));
+    *clamped = v;
+    return ASR_OK;
+}

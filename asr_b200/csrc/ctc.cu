@@ -1,0 +1,288 @@
+// CTC forward (alpha) and backward (beta fused with d loss / d logits).
+//
+// One warp per utterance. The 2S+1 extended-label states are split into
+// lane-contiguous blocks of KS states held in registers; the stay / advance /
+// skip moves (ctc.cu:84-98 of the reference) need the two states just left of a
+// block, which come from the neighbouring lane by shuffle. Each time step is
+// therefore a handful of register ops plus two shuffles, with the next step's
+// emission log-probs prefetched while the current step computes.
+// The backward scatters state posteriors into a per-warp shared-memory row of
+// V bins (no global atomics, deterministic) and writes each gradient row once.
+#include "common.cuh"
+
+namespace asr {
+namespace {
+
+constexpr int kCtcWarps = 4;  // utterances per block
+
+// log(exp(a) + exp(b) + exp(c)) with float64 state and an fp32 correction term.
+__device__ __forceinline__ double lse3_d(double a, double b, double c) {
+    const double m = fmax(a, fmax(b, c));
+    if (m == -INFINITY) return -INFINITY;
+    return m + (double)__logf(__expf((float)(a - m)) + __expf((float)(b - m)) + __expf((float)(c - m)));
+}
+
+struct CtcUtt {
+    int Tb, Sb, L;
+};
+
+__device__ __forceinline__ CtcUtt ctc_utt(const int32_t* in_lens, const int32_t* tgt_lens, int b, int T, int S) {
+    CtcUtt u;
+    u.Tb = min(max(in_lens[b], 1), T);
+    u.Sb = min(max(tgt_lens[b], 0), S);
+    u.L = 2 * u.Sb + 1;
+    return u;
+}
+
+// Value held by state s = src_lane*KS + j of array a (register-resident), broadcast.
+template <int KS>
+__device__ __forceinline__ double warp_pick(const double (&a)[KS], int s) {
+    const int src = s / KS, jj = s - src * KS;
+    double v = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < KS; ++j)
+        if (j == jj) v = a[j];
+    return __shfl_sync(0xffffffffu, v, src);
+}
+
+// log Z from the last blank and last label state (ctc.cu:106-113).
+__device__ __forceinline__ double ctc_logz(double last, double prev, int L) {
+    if (L == 1) return last;
+    const double m = fmax(last, prev);
+    if (m == -INFINITY) return -INFINITY;
+    return m + (double)log1pf(__expf((float)(fmin(last, prev) - m)));
+}
+
+// The forward variable is float64: on T ~ 10^2..10^3 frames |alpha| reaches 10^3,
+// where fp32 rounding along the recursion would cost ~1e-3 in the posteriors.
+template <int KS>
+__global__ void __launch_bounds__(32 * kCtcWarps)
+    ctc_alpha_kernel(const float* __restrict__ lp, const int32_t* __restrict__ targets,
+                     const int32_t* __restrict__ in_lens, const int32_t* __restrict__ tgt_lens, int B, int T, int V,
+                     int S, double* __restrict__ alpha, float* __restrict__ log_Z) {
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.x * kCtcWarps + (threadIdx.x >> 5);
+    if (b >= B) return;
+    const CtcUtt ut = ctc_utt(in_lens, tgt_lens, b, T, S);
+    const int Lmax = 2 * S + 1;
+    const int32_t* y = targets + (int64_t)b * S;
+    const float* lpb = lp + (int64_t)b * T * V;
+    double* ab = alpha + (int64_t)b * T * Lmax;
+
+    int lab[KS];
+    bool skip[KS], in[KS];
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+        const int s = lane * KS + j;
+        in[j] = s < ut.L;
+        const bool odd = s & 1;
+        lab[j] = (odd && in[j]) ? y[s >> 1] : 0;
+        skip[j] = in[j] && odd && (s >> 1) > 0 && y[s >> 1] != y[(s >> 1) - 1];
+    }
+    double a[KS];
+    float nxt[KS];
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+        const int s = lane * KS + j;
+        a[j] = (in[j] && s <= 1) ? (double)lpb[lab[j]] : -INFINITY;
+        if (in[j]) ab[s] = a[j];
+        nxt[j] = (in[j] && ut.Tb > 1) ? lpb[V + lab[j]] : 0.f;
+    }
+    for (int t = 1; t < ut.Tb; ++t) {
+        float cur[KS];
+#pragma unroll
+        for (int j = 0; j < KS; ++j) cur[j] = nxt[j];
+        if (t + 1 < ut.Tb) {
+#pragma unroll
+            for (int j = 0; j < KS; ++j) nxt[j] = in[j] ? lpb[(int64_t)(t + 1) * V + lab[j]] : 0.f;
+        }
+        // states s-1, s-2 left of this lane's block (previous time step)
+        double x1 = __shfl_up_sync(0xffffffffu, a[KS - 1], 1);
+        double x2 = (KS >= 2) ? __shfl_up_sync(0xffffffffu, a[KS >= 2 ? KS - 2 : 0], 1)
+                              : __shfl_up_sync(0xffffffffu, a[0], 2);
+        if (lane == 0) x1 = x2 = -INFINITY;
+        if (KS == 1 && lane == 1) x2 = -INFINITY;
+        double na[KS];
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+            const double p1 = (j >= 1) ? a[j >= 1 ? j - 1 : 0] : x1;
+            const double p2 = (j >= 2) ? a[j >= 2 ? j - 2 : 0] : (j == 1 ? x1 : x2);
+            na[j] = in[j] ? lse3_d(a[j], p1, skip[j] ? p2 : -INFINITY) + cur[j] : -INFINITY;
+        }
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+            a[j] = na[j];
+            if (in[j]) ab[(int64_t)t * Lmax + lane * KS + j] = a[j];
+        }
+    }
+    const double zl = warp_pick<KS>(a, ut.L - 1);
+    const double zp = (ut.L >= 2) ? warp_pick<KS>(a, ut.L - 2) : -INFINITY;
+    if (lane == 0) log_Z[b] = (float)ctc_logz(zl, zp, ut.L);
+}
+
+template <int KS>
+__global__ void __launch_bounds__(32 * kCtcWarps)
+    ctc_grad_kernel(const double* __restrict__ alpha, const float* __restrict__ lp,
+                    const int32_t* __restrict__ targets, const int32_t* __restrict__ in_lens,
+                    const int32_t* __restrict__ tgt_lens, const float* __restrict__ grad_loss, int zero_infinity,
+                    int B, int T, int V, int S, float* __restrict__ grad) {
+    extern __shared__ float smem_rows[];
+    const int lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5;
+    const int b = blockIdx.x * kCtcWarps + w;
+    if (b >= B) return;
+    float* row = smem_rows + (int64_t)w * V;
+    const CtcUtt ut = ctc_utt(in_lens, tgt_lens, b, T, S);
+    const int Lmax = 2 * S + 1;
+    const int32_t* y = targets + (int64_t)b * S;
+    const float* lpb = lp + (int64_t)b * T * V;
+    const double* ab = alpha + (int64_t)b * T * Lmax;
+    float* gb = grad + (int64_t)b * T * V;
+    // log Z in float64, from the stored forward variable
+    const double* alast = ab + (int64_t)(ut.Tb - 1) * Lmax;
+    const double logZ = ctc_logz(alast[ut.L - 1], ut.L >= 2 ? alast[ut.L - 2] : -INFINITY, ut.L);
+    const float gl = grad_loss[b];
+
+    const bool dead = zero_infinity && !isfinite(logZ);
+    // rows the recursion never reaches are zero (the reference zero-initialises)
+    for (int64_t i = (int64_t)(dead ? 0 : ut.Tb) * V + lane; i < (int64_t)T * V; i += 32) gb[i] = 0.f;
+    if (dead) return;
+    for (int v = lane; v < V; v += 32) row[v] = 0.f;
+
+    int lab[KS];
+    bool skip[KS], in[KS];
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+        const int s = lane * KS + j;
+        in[j] = s < ut.L;
+        const bool odd = s & 1;
+        lab[j] = (odd && in[j]) ? y[s >> 1] : 0;
+        // skip move s -> s+2 allowed when labels differ (ctc.cu:183-185)
+        skip[j] = in[j] && odd && (s >> 1) < ut.Sb - 1 && y[s >> 1] != y[(s >> 1) + 1];
+    }
+    // beta at t = T_b - 1 excludes the emission at t (ctc.cu:137-146)
+    double be[KS];
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+        const int s = lane * KS + j;
+        be[j] = (in[j] && (s == ut.L - 1 || s == ut.L - 2)) ? 0.0 : -INFINITY;
+    }
+    float lpt[KS];
+#pragma unroll
+    for (int j = 0; j < KS; ++j) lpt[j] = in[j] ? lpb[(int64_t)(ut.Tb - 1) * V + lab[j]] : 0.f;
+    __syncwarp();
+    for (int t = ut.Tb - 1; t >= 0; --t) {
+        // state posteriors scattered to vocabulary bins (ctc.cu:152-165)
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+            if (in[j]) {
+                const float post = __expf((float)(ab[(int64_t)t * Lmax + lane * KS + j] + be[j] - logZ));
+                atomicAdd(row + lab[j], post);
+            }
+        }
+        __syncwarp();
+        for (int v = lane; v < V; v += 32) {
+            const int64_t idx = (int64_t)t * V + v;
+            gb[idx] = gl * (__expf(lpb[idx]) - row[v]);
+            row[v] = 0.f;
+        }
+        __syncwarp();
+        if (t == 0) break;
+        // beta recursion (ctc.cu:180-204): c[s] = beta[s] + lp[t][lab(s)]
+        double c[KS];
+#pragma unroll
+        for (int j = 0; j < KS; ++j) c[j] = in[j] ? be[j] + lpt[j] : -INFINITY;
+        double r1 = __shfl_down_sync(0xffffffffu, c[0], 1);
+        double r2 = (KS >= 2) ? __shfl_down_sync(0xffffffffu, c[KS >= 2 ? 1 : 0], 1)
+                              : __shfl_down_sync(0xffffffffu, c[0], 2);
+        if (lane == 31) r1 = r2 = -INFINITY;
+        if (KS == 1 && lane == 30) r2 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+            const double n1 = (j + 1 < KS) ? c[j + 1 < KS ? j + 1 : 0] : r1;
+            const double n2 = (j + 2 < KS) ? c[j + 2 < KS ? j + 2 : 0] : (j + 1 < KS ? r1 : r2);
+            be[j] = in[j] ? lse3_d(c[j], n1, skip[j] ? n2 : -INFINITY) : -INFINITY;
+        }
+#pragma unroll
+        for (int j = 0; j < KS; ++j) lpt[j] = in[j] ? lpb[(int64_t)(t - 1) * V + lab[j]] : 0.f;
+    }
+}
+
+template <int KS>
+int launch_ctc_alpha(const float* lp, const int32_t* tg, const int32_t* il, const int32_t* tl, int B, int T, int V,
+                     int S, double* alpha, float* logz, cudaStream_t st) {
+    const int blocks = (B + kCtcWarps - 1) / kCtcWarps;
+    ctc_alpha_kernel<KS><<<blocks, 32 * kCtcWarps, 0, st>>>(lp, tg, il, tl, B, T, V, S, alpha, logz);
+    ASR_LAUNCH_CHECK();
+    return ASR_OK;
+}
+
+template <int KS>
+int launch_ctc_grad(const double* alpha, const float* lp, const int32_t* tg, const int32_t* il, const int32_t* tl,
+                    const float* gl, int zinf, int B, int T, int V, int S, float* grad, cudaStream_t st) {
+    const int blocks = (B + kCtcWarps - 1) / kCtcWarps;
+    const size_t smem = sizeof(float) * (size_t)V * kCtcWarps;
+    if (smem > 48 * 1024) {
+        if (cudaFuncSetAttribute(ctc_grad_kernel<KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return ASR_ERR_UNSUPPORTED;
+    }
+    ctc_grad_kernel<KS><<<blocks, 32 * kCtcWarps, smem, st>>>(alpha, lp, tg, il, tl, gl, zinf, B, T, V, S, grad);
+    ASR_LAUNCH_CHECK();
+    return ASR_OK;
+}
+
+int ctc_ks(int S) {
+    const int L = 2 * S + 1;
+    if (L <= 32) return 1;
+    if (L <= 64) return 2;
+    if (L <= 128) return 4;
+    if (L <= 256) return 8;
+    if (L <= 512) return 16;
+    if (L <= 1024) return 32;
+    return 0;
+}
+
+}  // namespace
+}  // namespace asr
+
+using namespace asr;
+
+extern "C" int asr_ctc_alpha(const float* log_probs, const int32_t* targets, const int32_t* in_lens,
+                             const int32_t* tgt_lens, int B, int T, int V, int S, double* alpha, float* log_Z,
+                             asr_stream_t stream) {
+    if (B < 0 || T < 1 || V < 1 || S < 0) return ASR_ERR_INVALID_ARGUMENT;
+    if (B == 0) return ASR_OK;
+    if (!log_probs || !in_lens || !tgt_lens || !alpha || !log_Z || (S > 0 && !targets)) return ASR_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    switch (ctc_ks(S)) {
+        case 1: return launch_ctc_alpha<1>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 2: return launch_ctc_alpha<2>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 4: return launch_ctc_alpha<4>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 8: return launch_ctc_alpha<8>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 16: return launch_ctc_alpha<16>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 32: return launch_ctc_alpha<32>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        default: return ASR_ERR_UNSUPPORTED;
+    }
+}
+
+extern "C" int asr_ctc_grad(const double* alpha, const float* log_Z, const float* log_probs, const int32_t* targets,
+                            const int32_t* in_lens, const int32_t* tgt_lens, const float* grad_loss,
+                            int zero_infinity, int B, int T, int V, int S, float* grad_logits, asr_stream_t stream) {
+    if (B < 0 || T < 1 || V < 1 || S < 0) return ASR_ERR_INVALID_ARGUMENT;
+    if (B == 0) return ASR_OK;
+    if (!alpha || !log_Z || !log_probs || !in_lens || !tgt_lens || !grad_loss || !grad_logits ||
+        (S > 0 && !targets))
+        return ASR_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int z = zero_infinity ? 1 : 0;
+    switch (ctc_ks(S)) {
+        case 1: return launch_ctc_grad<1>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
+        case 2: return launch_ctc_grad<2>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
+        case 4: return launch_ctc_grad<4>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
+        case 8: return launch_ctc_grad<8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
+        case 16: return launch_ctc_grad<16>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
+        case 32: return launch_ctc_grad<32>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
+        default: return ASR_ERR_UNSUPPORTED;
+    }
+}

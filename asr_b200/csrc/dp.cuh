@@ -1,0 +1,37 @@
+// Launchers of the lattice recursions (dp_rnnt.cu, dp_tdt.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace asr {
+
+// Label positions per lane for a warp that covers U positions (U <= 512).
+inline int dp_lanes_k(int U) {
+    if (U <= 32) return 1;
+    if (U <= 64) return 2;
+    if (U <= 128) return 4;
+    if (U <= 256) return 8;
+    if (U <= 512) return 16;
+    return 0;
+}
+
+// Largest supported max_duration of the TDT recursions.
+constexpr int kTdtMaxDuration = 16;
+// Largest supported number of duration classes.
+constexpr int kTdtMaxDurClasses = 32;
+
+// The forward variable is stored in float64 (see lae_d); log P(y|x) for the
+// backward posteriors is recomputed from it rather than read from the fp32 output.
+int launch_rnnt_alpha(const LatticeMeta& m, int B, int U, const float* lpb, const float* lpy, double* alpha,
+                      float* log_prob, float* loss, cudaStream_t st);
+int launch_rnnt_beta(const LatticeMeta& m, int B, int U, const float* lpb, const float* lpy, const double* alpha,
+                     const float* grad_loss, float* cb, float* ct, cudaStream_t st);
+
+int launch_tdt_alpha(const LatticeMeta& m, int B, int U, int max_duration, const int32_t* durations, int n_dur,
+                     int has_zero, const float* lpb, const float* lpy, const float* lpd, double* alpha,
+                     float* log_prob, float* loss, cudaStream_t st);
+int launch_tdt_beta(const LatticeMeta& m, int B, int U, int max_duration, const int32_t* durations, int n_dur,
+                    int has_zero, const float* lpb, const float* lpy, const float* lpd, const double* alpha,
+                    const float* grad_loss, float* cb, float* ct, float* gdur, cudaStream_t st);
+
+}  // namespace asr

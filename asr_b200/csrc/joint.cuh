@@ -1,0 +1,64 @@
+// Joint network + fused epilogues: shared argument block and launchers for the
+// fp32 SIMT path (joint_simt.cu) and the bf16 tcgen05 path (joint_tc.cu).
+//
+// The joint output is  logits[n, c] = sum_k tanh(enc[b,t,k] + dec[b,u,k]) * Wf[c, k]
+// over the compact valid nodes n = (b, t, u) and the "full" column set
+// c in [0, Vf), Vf = V + n_dur: token columns first (joint_W), then the duration
+// head (joint_W_dur). No launcher ever writes the (nodes x Vf) logits to HBM.
+#pragma once
+
+#include "common.cuh"
+
+namespace asr {
+
+struct JointArgs {
+    const float* enc;      // (B, T, d)
+    const float* dec;      // (B, U, d)
+    const float* W;        // (V, d)
+    const float* Wd;       // (n_dur, d) or nullptr
+    const int32_t* targets;  // (B, S)
+    LatticeMeta m;
+    int B, T, U, V, n_dur, d, S, blank;
+    float sigma;
+};
+
+// Forward epilogue outputs (compact per-node arrays).
+struct JointFwdOut {
+    float* lpb;  // blank log-prob (minus sigma)
+    float* lse;  // token log-partition
+    float* lpy;  // label log-prob (minus sigma), kNeg without a label edge
+    float* lpd;  // (nodes, n_dur) duration log-probs, or nullptr
+};
+
+// Backward: per-node coefficients from the beta pass and the gradient outputs.
+struct JointBwdIn {
+    const float* lse;   // token log-partition (forward)
+    const float* cb;    // grad_loss * blank posterior
+    const float* ct;    // grad_loss * label posterior
+    const float* gdur;  // (nodes, n_dur) d loss / d duration logit, or nullptr
+};
+
+struct JointBwdOut {
+    float* d_enc;  // (B, T, d), accumulated
+    float* d_dec;  // (B, U, d), accumulated
+    float* dW;     // (V, d), accumulated
+    float* dWd;    // (n_dur, d), accumulated, or nullptr
+};
+
+// ---- fp32 SIMT path -----------------------------------------------------------
+int simt_joint_forward(const JointArgs& a, const JointFwdOut& o, cudaStream_t st);
+// Backward over node chunks [c0, c0 + chunk); G is a (chunk, Vf) fp32 scratch.
+size_t simt_backward_scratch_bytes(int Vf, int chunk);
+int simt_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOut& o, int node_capacity,
+                        void* scratch, size_t scratch_bytes, cudaStream_t st);
+
+// ---- bf16 tcgen05 path --------------------------------------------------------
+bool tc_supported(const JointArgs& a);
+size_t tc_forward_scratch_bytes(const JointArgs& a);
+int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, void* scratch, size_t scratch_bytes,
+                     cudaStream_t st);
+size_t tc_backward_scratch_bytes(const JointArgs& a, int node_capacity);
+int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOut& o, int node_capacity,
+                      void* scratch, size_t scratch_bytes, cudaStream_t st);
+
+}  // namespace asr

@@ -1,0 +1,281 @@
+// PyTorch stable-ABI operator shim: registers the six `asr::*` ops with the
+// exact schemas of the reference (src/asr/loss/csrc/ctc_bindings.cpp:16-22,
+// rnnt_bindings.cpp:22-30, tdt_bindings.cpp:26-36), so the reference's Python
+// loss modules run on this library unchanged. Each op validates its tensors
+// like the reference (CUDA, contiguous, float32 / int32), allocates outputs and
+// workspace through the torch caching allocator, and calls the C ABI of
+// include/asr_b200.h on the current stream of the input's device.
+#include <torch/csrc/inductor/aoti_torch/c/shim.h>
+#include <torch/csrc/stable/accelerator.h>
+#include <torch/csrc/stable/library.h>
+#include <torch/csrc/stable/ops.h>
+#include <torch/csrc/stable/tensor.h>
+
+#include <tuple>
+
+#include "asr_b200.h"
+
+using torch::stable::Tensor;
+using torch::headeronly::ScalarType;
+
+namespace {
+
+#define ASR_CHECK_F32(x)                                                                                   \
+    STD_TORCH_CHECK(x.is_cuda(), #x " must be a CUDA tensor");                                             \
+    STD_TORCH_CHECK(x.is_contiguous(), #x " must be contiguous");                                          \
+    STD_TORCH_CHECK(x.scalar_type() == ScalarType::Float, #x " must be float32")
+
+#define ASR_CHECK_F64(x)                                                                                   \
+    STD_TORCH_CHECK(x.is_cuda(), #x " must be a CUDA tensor");                                             \
+    STD_TORCH_CHECK(x.is_contiguous(), #x " must be contiguous");                                          \
+    STD_TORCH_CHECK(x.scalar_type() == ScalarType::Double, #x " must be the float64 forward variable of the forward op")
+
+#define ASR_CHECK_I32(x)                                                                                   \
+    STD_TORCH_CHECK(x.is_cuda(), #x " must be a CUDA tensor");                                             \
+    STD_TORCH_CHECK(x.is_contiguous(), #x " must be contiguous");                                          \
+    STD_TORCH_CHECK(x.scalar_type() == ScalarType::Int, #x " must be int")
+
+asr_stream_t current_stream(const Tensor& t) {
+    void* s = nullptr;
+    TORCH_ERROR_CODE_CHECK(aoti_torch_get_current_cuda_stream(t.get_device_index(), &s));
+    return reinterpret_cast<asr_stream_t>(s);
+}
+
+void check_rc(int rc, const char* op) { STD_TORCH_CHECK(rc == ASR_OK, op, ": ", asr_status_string(rc)); }
+
+Tensor workspace(const Tensor& like, size_t bytes) {
+    return torch::stable::new_empty(like, {(int64_t)(bytes > 0 ? bytes : 1)}, ScalarType::Byte);
+}
+
+int dim(const Tensor& t, int i) { return (int)t.sizes()[i]; }
+
+int target_cols(const Tensor& targets) { return targets.dim() >= 2 ? dim(targets, 1) : 0; }
+
+// --------------------------------------------------------------------- CTC
+
+std::tuple<Tensor, Tensor> ctc_alpha(const Tensor& log_probs, const Tensor& targets, const Tensor& in_lens,
+                                     const Tensor& tgt_lens) {
+    ASR_CHECK_F32(log_probs);
+    ASR_CHECK_I32(targets);
+    ASR_CHECK_I32(in_lens);
+    ASR_CHECK_I32(tgt_lens);
+    torch::stable::accelerator::DeviceGuard guard(log_probs.get_device_index());
+    const int B = dim(log_probs, 0), T = dim(log_probs, 1), V = dim(log_probs, 2), S = target_cols(targets);
+    Tensor alpha = torch::stable::new_empty(log_probs, {B, T, 2 * S + 1}, ScalarType::Double);
+    Tensor log_Z = torch::stable::new_empty(log_probs, {B});
+    check_rc(asr_ctc_alpha(log_probs.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
+                           in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, V, S,
+                           alpha.mutable_data_ptr<double>(), log_Z.mutable_data_ptr<float>(),
+                           current_stream(log_probs)),
+             "asr::ctc_alpha");
+    return {alpha, log_Z};
+}
+
+Tensor ctc_grad(const Tensor& alpha, const Tensor& log_Z, const Tensor& log_probs, const Tensor& targets,
+                const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& grad_loss, bool zero_infinity) {
+    ASR_CHECK_F64(alpha);
+    ASR_CHECK_F32(log_Z);
+    ASR_CHECK_F32(log_probs);
+    ASR_CHECK_I32(targets);
+    ASR_CHECK_I32(in_lens);
+    ASR_CHECK_I32(tgt_lens);
+    ASR_CHECK_F32(grad_loss);
+    torch::stable::accelerator::DeviceGuard guard(log_probs.get_device_index());
+    const int B = dim(log_probs, 0), T = dim(log_probs, 1), V = dim(log_probs, 2), S = target_cols(targets);
+    Tensor grad = torch::stable::new_empty(log_probs, {B, T, V});
+    check_rc(asr_ctc_grad(alpha.const_data_ptr<double>(), log_Z.const_data_ptr<float>(),
+                          log_probs.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
+                          in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(),
+                          grad_loss.const_data_ptr<float>(), zero_infinity ? 1 : 0, B, T, V, S,
+                          grad.mutable_data_ptr<float>(), current_stream(log_probs)),
+             "asr::ctc_grad");
+    return grad;
+}
+
+// -------------------------------------------------------------------- RNN-T
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> rnnt_forward(const Tensor& encoder, const Tensor& decoder,
+                                                                const Tensor& joint_W, const Tensor& targets,
+                                                                const Tensor& in_lens, const Tensor& tgt_lens,
+                                                                int64_t blank_idx, int64_t tf32) {
+    ASR_CHECK_F32(encoder);
+    ASR_CHECK_F32(decoder);
+    ASR_CHECK_F32(joint_W);
+    ASR_CHECK_I32(targets);
+    ASR_CHECK_I32(in_lens);
+    ASR_CHECK_I32(tgt_lens);
+    torch::stable::accelerator::DeviceGuard guard(encoder.get_device_index());
+    const int B = dim(encoder, 0), T = dim(encoder, 1), d = dim(encoder, 2), U = dim(decoder, 1);
+    const int V = dim(joint_W, 0), S = target_cols(targets);
+    STD_TORCH_CHECK(dim(decoder, 0) == B && dim(decoder, 2) == d && dim(joint_W, 1) == d, "rnnt_forward: shape mismatch");
+    Tensor loss = torch::stable::new_empty(encoder, {B});
+    Tensor log_prob = torch::stable::new_empty(encoder, {B});
+    Tensor alpha = torch::stable::new_empty(encoder, {B, T, U}, ScalarType::Double);
+    Tensor log_P_blank = torch::stable::new_empty(encoder, {2, B, T, U});
+    Tensor log_P_y = torch::stable::new_empty(encoder, {B, T, U});
+    const size_t wsb = asr_rnnt_workspace_bytes(B, T, U, V, d, (int)tf32, 0);
+    Tensor ws = workspace(encoder, wsb);
+    check_rc(asr_rnnt_forward(encoder.const_data_ptr<float>(), decoder.const_data_ptr<float>(),
+                              joint_W.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
+                              in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, U, V, d, S,
+                              (int)blank_idx, (int)tf32, loss.mutable_data_ptr<float>(),
+                              alpha.mutable_data_ptr<double>(), log_P_blank.mutable_data_ptr<float>(),
+                              log_P_y.mutable_data_ptr<float>(), log_prob.mutable_data_ptr<float>(),
+                              ws.mutable_data_ptr(), wsb, current_stream(encoder)),
+             "asr::rnnt_forward");
+    return {loss, alpha, log_P_blank, log_P_y, log_prob};
+}
+
+std::tuple<Tensor, Tensor, Tensor> rnnt_backward(const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W,
+                                                 const Tensor& targets, const Tensor& in_lens,
+                                                 const Tensor& tgt_lens, int64_t blank_idx, const Tensor& alpha,
+                                                 const Tensor& log_P_blank, const Tensor& log_P_y,
+                                                 const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32) {
+    ASR_CHECK_F32(encoder);
+    ASR_CHECK_F32(decoder);
+    ASR_CHECK_F32(joint_W);
+    ASR_CHECK_I32(targets);
+    ASR_CHECK_I32(in_lens);
+    ASR_CHECK_I32(tgt_lens);
+    ASR_CHECK_F64(alpha);
+    ASR_CHECK_F32(log_P_blank);
+    ASR_CHECK_F32(log_P_y);
+    ASR_CHECK_F32(log_prob);
+    ASR_CHECK_F32(grad_loss);
+    torch::stable::accelerator::DeviceGuard guard(encoder.get_device_index());
+    const int B = dim(encoder, 0), T = dim(encoder, 1), d = dim(encoder, 2), U = dim(decoder, 1);
+    const int V = dim(joint_W, 0), S = target_cols(targets);
+    STD_TORCH_CHECK(log_P_blank.numel() == 2LL * B * T * U, "rnnt_backward: log_P_blank is not a forward output");
+    Tensor g_enc = torch::stable::new_empty(encoder, {B, T, d});
+    Tensor g_dec = torch::stable::new_empty(encoder, {B, U, d});
+    Tensor g_W = torch::stable::new_empty(joint_W, {V, d});
+    const size_t wsb = asr_rnnt_workspace_bytes(B, T, U, V, d, (int)tf32, 1);
+    Tensor ws = workspace(encoder, wsb);
+    check_rc(asr_rnnt_backward(encoder.const_data_ptr<float>(), decoder.const_data_ptr<float>(),
+                               joint_W.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
+                               in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, U, V, d,
+                               S, (int)blank_idx, alpha.const_data_ptr<double>(), log_P_blank.const_data_ptr<float>(),
+                               log_P_y.const_data_ptr<float>(), log_prob.const_data_ptr<float>(),
+                               grad_loss.const_data_ptr<float>(), (int)tf32, g_enc.mutable_data_ptr<float>(),
+                               g_dec.mutable_data_ptr<float>(), g_W.mutable_data_ptr<float>(), ws.mutable_data_ptr(),
+                               wsb, current_stream(encoder)),
+             "asr::rnnt_backward");
+    return {g_enc, g_dec, g_W};
+}
+
+// ---------------------------------------------------------------------- TDT
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> tdt_forward(
+    const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
+    const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
+    int64_t max_duration, int64_t has_zero, int64_t blank_idx, double sigma, int64_t tf32) {
+    ASR_CHECK_F32(encoder);
+    ASR_CHECK_F32(decoder);
+    ASR_CHECK_F32(joint_W);
+    ASR_CHECK_F32(joint_W_dur);
+    ASR_CHECK_I32(targets);
+    ASR_CHECK_I32(in_lens);
+    ASR_CHECK_I32(tgt_lens);
+    ASR_CHECK_I32(durations);
+    torch::stable::accelerator::DeviceGuard guard(encoder.get_device_index());
+    const int B = dim(encoder, 0), T = dim(encoder, 1), d = dim(encoder, 2), U = dim(decoder, 1);
+    const int V = dim(joint_W, 0), Dn = dim(joint_W_dur, 0), S = target_cols(targets);
+    STD_TORCH_CHECK(durations.numel() == Dn, "tdt_forward: durations must have one entry per joint_W_dur row");
+    Tensor loss = torch::stable::new_empty(encoder, {B});
+    Tensor log_prob = torch::stable::new_empty(encoder, {B});
+    Tensor alpha = torch::stable::new_empty(encoder, {B, T + 1, U}, ScalarType::Double);
+    Tensor log_P_blank = torch::stable::new_empty(encoder, {2, B, T, U});
+    Tensor log_P_y = torch::stable::new_empty(encoder, {B, T, U});
+    Tensor log_P_dur = torch::stable::new_empty(encoder, {B, T, U, Dn});
+    const size_t wsb = asr_tdt_workspace_bytes(B, T, U, V, Dn, d, (int)tf32, 0);
+    Tensor ws = workspace(encoder, wsb);
+    check_rc(asr_tdt_forward(encoder.const_data_ptr<float>(), decoder.const_data_ptr<float>(),
+                             joint_W.const_data_ptr<float>(), joint_W_dur.const_data_ptr<float>(),
+                             targets.const_data_ptr<int32_t>(), in_lens.const_data_ptr<int32_t>(),
+                             tgt_lens.const_data_ptr<int32_t>(), durations.const_data_ptr<int32_t>(), Dn,
+                             (int)max_duration, (int)has_zero, B, T, U, V, d, S, (int)blank_idx, (float)sigma,
+                             (int)tf32, loss.mutable_data_ptr<float>(), alpha.mutable_data_ptr<double>(),
+                             log_P_blank.mutable_data_ptr<float>(), log_P_y.mutable_data_ptr<float>(),
+                             log_P_dur.mutable_data_ptr<float>(), log_prob.mutable_data_ptr<float>(),
+                             ws.mutable_data_ptr(), wsb, current_stream(encoder)),
+             "asr::tdt_forward");
+    return {loss, alpha, log_P_blank, log_P_y, log_P_dur, log_prob};
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward(
+    const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
+    const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
+    int64_t max_duration, int64_t has_zero, int64_t blank_idx, const Tensor& alpha, const Tensor& log_P_blank,
+    const Tensor& log_P_y, const Tensor& log_P_dur, const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32) {
+    ASR_CHECK_F32(encoder);
+    ASR_CHECK_F32(decoder);
+    ASR_CHECK_F32(joint_W);
+    ASR_CHECK_F32(joint_W_dur);
+    ASR_CHECK_I32(targets);
+    ASR_CHECK_I32(in_lens);
+    ASR_CHECK_I32(tgt_lens);
+    ASR_CHECK_I32(durations);
+    ASR_CHECK_F64(alpha);
+    ASR_CHECK_F32(log_P_blank);
+    ASR_CHECK_F32(log_P_y);
+    ASR_CHECK_F32(log_P_dur);
+    ASR_CHECK_F32(log_prob);
+    ASR_CHECK_F32(grad_loss);
+    torch::stable::accelerator::DeviceGuard guard(encoder.get_device_index());
+    const int B = dim(encoder, 0), T = dim(encoder, 1), d = dim(encoder, 2), U = dim(decoder, 1);
+    const int V = dim(joint_W, 0), Dn = dim(joint_W_dur, 0), S = target_cols(targets);
+    STD_TORCH_CHECK(log_P_blank.numel() == 2LL * B * T * U, "tdt_backward: log_P_blank is not a forward output");
+    Tensor g_enc = torch::stable::new_empty(encoder, {B, T, d});
+    Tensor g_dec = torch::stable::new_empty(encoder, {B, U, d});
+    Tensor g_W = torch::stable::new_empty(joint_W, {V, d});
+    Tensor g_Wd = torch::stable::new_empty(joint_W_dur, {Dn, d});
+    const size_t wsb = asr_tdt_workspace_bytes(B, T, U, V, Dn, d, (int)tf32, 1);
+    Tensor ws = workspace(encoder, wsb);
+    check_rc(asr_tdt_backward(encoder.const_data_ptr<float>(), decoder.const_data_ptr<float>(),
+                              joint_W.const_data_ptr<float>(), joint_W_dur.const_data_ptr<float>(),
+                              targets.const_data_ptr<int32_t>(), in_lens.const_data_ptr<int32_t>(),
+                              tgt_lens.const_data_ptr<int32_t>(), durations.const_data_ptr<int32_t>(), Dn,
+                              (int)max_duration, (int)has_zero, B, T, U, V, d, S, (int)blank_idx,
+                              alpha.const_data_ptr<double>(), log_P_blank.const_data_ptr<float>(),
+                              log_P_y.const_data_ptr<float>(), log_P_dur.const_data_ptr<float>(),
+                              log_prob.const_data_ptr<float>(), grad_loss.const_data_ptr<float>(), (int)tf32,
+                              g_enc.mutable_data_ptr<float>(), g_dec.mutable_data_ptr<float>(),
+                              g_W.mutable_data_ptr<float>(), g_Wd.mutable_data_ptr<float>(), ws.mutable_data_ptr(),
+                              wsb, current_stream(encoder)),
+             "asr::tdt_backward");
+    return {g_enc, g_dec, g_W, g_Wd};
+}
+
+}  // namespace
+
+STABLE_TORCH_LIBRARY(asr, m) {
+    m.def("ctc_alpha(Tensor log_probs, Tensor targets, Tensor in_lens, Tensor tgt_lens) -> (Tensor, Tensor)");
+    m.def(
+        "ctc_grad(Tensor alpha, Tensor log_Z, Tensor log_probs, Tensor targets, Tensor in_lens, Tensor tgt_lens, "
+        "Tensor grad_loss, bool zero_infinity) -> Tensor");
+    m.def(
+        "rnnt_forward(Tensor encoder, Tensor decoder, Tensor joint_W, Tensor targets, Tensor in_lens, "
+        "Tensor tgt_lens, int blank_idx, int tf32) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+    m.def(
+        "rnnt_backward(Tensor encoder, Tensor decoder, Tensor joint_W, Tensor targets, Tensor in_lens, "
+        "Tensor tgt_lens, int blank_idx, Tensor alpha, Tensor log_P_blank, Tensor log_P_y, Tensor log_prob, "
+        "Tensor grad_loss, int tf32) -> (Tensor, Tensor, Tensor)");
+    m.def(
+        "tdt_forward(Tensor encoder, Tensor decoder, Tensor joint_W, Tensor joint_W_dur, Tensor targets, "
+        "Tensor in_lens, Tensor tgt_lens, Tensor durations, int max_duration, int has_zero, int blank_idx, "
+        "float sigma, int tf32) -> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)");
+    m.def(
+        "tdt_backward(Tensor encoder, Tensor decoder, Tensor joint_W, Tensor joint_W_dur, Tensor targets, "
+        "Tensor in_lens, Tensor tgt_lens, Tensor durations, int max_duration, int has_zero, int blank_idx, "
+        "Tensor alpha, Tensor log_P_blank, Tensor log_P_y, Tensor log_P_dur, Tensor log_prob, Tensor grad_loss, "
+        "int tf32) -> (Tensor, Tensor, Tensor, Tensor)");
+}
+
+STABLE_TORCH_LIBRARY_IMPL(asr, CUDA, m) {
+    m.impl("ctc_alpha", TORCH_BOX(&ctc_alpha));
+    m.impl("ctc_grad", TORCH_BOX(&ctc_grad));
+    m.impl("rnnt_forward", TORCH_BOX(&rnnt_forward));
+    m.impl("rnnt_backward", TORCH_BOX(&rnnt_backward));
+    m.impl("tdt_forward", TORCH_BOX(&tdt_forward));
+    m.impl("tdt_backward", TORCH_BOX(&tdt_backward));
+}

@@ -1,0 +1,139 @@
+/*
+ * asr_b200 — C ABI of the B200 (sm_100a) fused sequence-loss library:
+ * CTC, RNN-T and TDT losses with their joint network, forward and backward.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream, is
+ * asynchronous on that stream, performs no host<->device synchronisation and
+ * allocates no memory: scratch space is passed in as `workspace` (size from the
+ * matching *_workspace_bytes query). Inputs are row-major and contiguous, as in
+ * the reference ops (src/asr/loss/csrc/rnnt.cu:13-26). A non-zero return is an
+ * asr_status_t; kernels are not launched in that case.
+ *
+ * Lengths follow the reference contract: in_lens[b] in [1, T], tgt_lens[b] in
+ * [0, U-1] (and <= S). Out-of-range lengths are clamped into range on the
+ * device so no access leaves the buffers (the reference leaves this undefined).
+ *
+ * Lattice buffers exchanged between forward and backward ("opaque" outputs of
+ * the reference ops) hold only the valid nodes of each utterance, packed
+ * utterance after utterance with node (t, u) of utterance b at
+ * off[b] + t * U_b + u, U_b = tgt_lens[b] + 1; their capacities are the
+ * reference tensor sizes, so callers allocate exactly what the reference did,
+ * except log_P_blank which carries a second plane (the per-node token
+ * log-partition, reused by the backward softmax).
+ */
+#ifndef ASR_B200_H_
+#define ASR_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; NULL selects the legacy default stream. */
+typedef struct CUstream_st* asr_stream_t;
+
+typedef enum {
+    ASR_OK = 0,
+    ASR_ERR_INVALID_ARGUMENT = 1, /* a size/flag/pointer check failed on the host */
+    ASR_ERR_WORKSPACE = 2,        /* workspace missing or smaller than *_workspace_bytes */
+    ASR_ERR_UNSUPPORTED = 3,      /* shape outside the compiled kernel range (e.g. U > 512) */
+    ASR_ERR_CUDA = 4              /* a CUDA launch or runtime call failed */
+} asr_status_t;
+
+/* Human-readable name of a status code. */
+const char* asr_status_string(int status);
+
+/* ABI revision of this header (bumped on any signature change). */
+int asr_abi_version(void);
+
+/* ------------------------------------------------------------------ CTC */
+
+/* Replaces ctc_alpha_cuda (reference src/asr/loss/csrc/ctc.cu:214-238; op schema
+ * asr::ctc_alpha, ctc_bindings.cpp:17).
+ * log_probs (B,T,V) log-softmax over V, blank = 0; targets (B,S).
+ * Writes alpha (B,T,2S+1), float64, for t < in_lens[b] and log_Z (B,) (-inf when infeasible). */
+int asr_ctc_alpha(const float* log_probs, const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens,
+                  int B, int T, int V, int S, double* alpha, float* log_Z, asr_stream_t stream);
+
+/* Replaces ctc_grad_cuda (ctc.cu:241-269; asr::ctc_grad, ctc_bindings.cpp:19-21).
+ * Writes all of grad_logits (B,T,V): d loss_b / d logits for log_probs =
+ * log_softmax(logits), scaled by grad_loss[b]; zero rows past in_lens[b] and,
+ * with zero_infinity, for utterances whose log Z is not finite. log Z is recomputed in
+ * float64 from alpha; the log_Z argument is accepted for interface parity only. */
+int asr_ctc_grad(const double* alpha, const float* log_Z, const float* log_probs, const int32_t* targets,
+                 const int32_t* in_lens, const int32_t* tgt_lens, const float* grad_loss, int zero_infinity, int B,
+                 int T, int V, int S, float* grad_logits, asr_stream_t stream);
+
+/* ---------------------------------------------------------------- RNN-T */
+
+/* Workspace for asr_rnnt_forward (backward = 0) or asr_rnnt_backward (backward = 1). */
+size_t asr_rnnt_workspace_bytes(int B, int T, int U, int V, int d, int tf32, int backward);
+
+/* Replaces rnnt_forward_cuda (rnnt.cu:320-380; asr::rnnt_forward, rnnt_bindings.cpp:24-26).
+ * encoder (B,T,d), decoder (B,U,d), joint_W (V,d), targets (B,S) with S >= U-1.
+ * tf32 = 0: fp32-accurate joint GEMMs (SIMT FMA). tf32 != 0: bf16 tcgen05 tensor-core
+ * joint with fp32 accumulation (the reference's opt-in fast mode).
+ * Outputs: loss (B,) = -log P(y|x); log_prob (B,) = log P(y|x);
+ *   alpha        capacity B*T*U      float64 forward variable per valid node;
+ *   log_P_blank  capacity 2*B*T*U    plane 0: blank log-prob, plane 1: token log-partition;
+ *   log_P_y      capacity B*T*U      label log-prob (-1e30 where no label edge). */
+int asr_rnnt_forward(const float* encoder, const float* decoder, const float* joint_W, const int32_t* targets,
+                     const int32_t* in_lens, const int32_t* tgt_lens, int B, int T, int U, int V, int d, int S,
+                     int blank_idx, int tf32, float* loss, double* alpha, float* log_P_blank, float* log_P_y,
+                     float* log_prob, void* workspace, size_t workspace_bytes, asr_stream_t stream);
+
+/* Replaces rnnt_backward_cuda (rnnt.cu:382-458; asr::rnnt_backward, rnnt_bindings.cpp:27-29).
+ * Consumes the forward's lattice buffers; writes (overwrites) grad_encoder (B,T,d),
+ * grad_decoder (B,U,d), grad_joint_W (V,d), scaled per utterance by grad_loss (B,).
+ * log P(y|x) is recomputed in float64 from alpha; log_prob is accepted for
+ * interface parity only. */
+int asr_rnnt_backward(const float* encoder, const float* decoder, const float* joint_W, const int32_t* targets,
+                      const int32_t* in_lens, const int32_t* tgt_lens, int B, int T, int U, int V, int d, int S,
+                      int blank_idx, const double* alpha, const float* log_P_blank, const float* log_P_y,
+                      const float* log_prob, const float* grad_loss, int tf32, float* grad_encoder,
+                      float* grad_decoder, float* grad_joint_W, void* workspace, size_t workspace_bytes,
+                      asr_stream_t stream);
+
+/* ------------------------------------------------------------------ TDT */
+
+/* Workspace for asr_tdt_forward (backward = 0) or asr_tdt_backward (backward = 1). */
+size_t asr_tdt_workspace_bytes(int B, int T, int U, int V, int n_dur, int d, int tf32, int backward);
+
+/* Replaces tdt_forward_cuda (tdt.cu:523-600; asr::tdt_forward, tdt_bindings.cpp:28-31).
+ * joint_W_dur (n_dur,d); durations (n_dur,) device int32, non-negative, containing 1;
+ * max_duration = max(durations) (<= 16 supported); has_zero = (0 in durations);
+ * sigma >= 0 is subtracted from the blank and label log-probs (tdt.cu:164-165).
+ * loss = -alpha[in_lens, tgt_lens] (exact landing).
+ * Outputs: alpha capacity B*(T+1)*U (float64); log_P_blank capacity 2*B*T*U (as RNN-T);
+ *   log_P_y capacity B*T*U; log_P_dur capacity B*T*U*n_dur. */
+int asr_tdt_forward(const float* encoder, const float* decoder, const float* joint_W, const float* joint_W_dur,
+                    const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens,
+                    const int32_t* durations, int n_dur, int max_duration, int has_zero, int B, int T, int U, int V,
+                    int d, int S, int blank_idx, float sigma, int tf32, float* loss, double* alpha,
+                    float* log_P_blank, float* log_P_y, float* log_P_dur, float* log_prob, void* workspace,
+                    size_t workspace_bytes, asr_stream_t stream);
+
+/* Replaces tdt_backward_cuda (tdt.cu:602-704; asr::tdt_backward, tdt_bindings.cpp:32-35).
+ * Writes (overwrites) grad_encoder, grad_decoder, grad_joint_W (V,d), grad_joint_W_dur (n_dur,d). */
+int asr_tdt_backward(const float* encoder, const float* decoder, const float* joint_W, const float* joint_W_dur,
+                     const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens,
+                     const int32_t* durations, int n_dur, int max_duration, int has_zero, int B, int T, int U,
+                     int V, int d, int S, int blank_idx, const double* alpha, const float* log_P_blank,
+                     const float* log_P_y, const float* log_P_dur, const float* log_prob, const float* grad_loss,
+                     int tf32, float* grad_encoder, float* grad_decoder, float* grad_joint_W,
+                     float* grad_joint_W_dur, void* workspace, size_t workspace_bytes, asr_stream_t stream);
+
+/* ----------------------------------------------------------- diagnostics */
+
+/* Copies the device status word of a workspace used by the last call on it
+ * into *clamped (1 = some length was out of range and was clamped). Synchronises
+ * `stream`. Intended for debugging; the hot path never calls it. */
+int asr_workspace_status(const void* workspace, int B, int* clamped, asr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASR_B200_H_ */

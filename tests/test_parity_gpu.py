@@ -1,0 +1,366 @@
+"""Parity of the CUDA path with the reference on identical inputs.
+
+Checked against (a) the committed golden vectors produced by the reference's
+own float64 oracles / torch CTC, and (b) the C oracle (oracle/) on seeded
+inputs larger than the fixtures. Tolerances (fp32 mode, tf32 = 0):
+loss relative error <= 1e-5 and gradient max-abs error <= 1e-4, the bar the
+reference's float32 kernels are held to; bf16 tensor-core mode (tf32 = 1) is
+held to the reference's own tf32 test bar (loss 5e-2, gradient rel-norm 5e-2).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests.golden_io import load_cases
+from tests.gpu_cases import ctc_case, transducer_case
+
+pytestmark = pytest.mark.gpu
+
+LOSS_RTOL = 1e-5
+LOSS_ATOL = 1e-5
+GRAD_ATOL = 1e-4
+GRAD_RTOL = 1e-4
+
+CTC = load_cases("ctc")
+RNNT = load_cases("rnnt")
+TDT = load_cases("tdt")
+
+
+def cuda(x, dtype=None):
+    t = torch.as_tensor(np.ascontiguousarray(x), device="cuda")
+    return t if dtype is None else t.to(dtype)
+
+
+def leaf(x):
+    return cuda(x).float().requires_grad_(True)
+
+
+def assert_loss(got, want):
+    got = got.detach().double().cpu().numpy()
+    want = np.asarray(want, np.float64)
+    np.testing.assert_allclose(got, want, rtol=LOSS_RTOL, atol=LOSS_ATOL)
+
+
+def assert_grad(got, want, name, atol=GRAD_ATOL, rtol=GRAD_RTOL):
+    """|got - want| <= atol + rtol * |want| elementwise: the criterion of the
+    reference's own tests (torch.testing.assert_close, atol = rtol = 1e-4).
+    Cases drawn from the benchmark distributions pass rtol=0, i.e. a strict
+    max-abs bound."""
+    g = got.detach().double().cpu().numpy()
+    w = np.asarray(want, np.float64)
+    if not g.size:
+        return
+    excess = (np.abs(g - w) - (atol + rtol * np.abs(w))).max()
+    err = np.abs(g - w).max()
+    assert excess <= 0, f"{name}: max-abs error {err:.3e} exceeds {atol:.0e} + {rtol:.0e}*|ref|"
+
+
+def assert_bf16_close(got_loss, want_loss, grads):
+    """The reference's tf32 tolerance (tests/loss/test_tdt_loss.py:166-169)."""
+    np.testing.assert_allclose(got_loss.detach().double().cpu().numpy(), want_loss, rtol=5e-2, atol=5e-2)
+    for name, g, w in grads:
+        g = g.detach().double().cpu().numpy()
+        rel = np.linalg.norm(g - w) / max(np.linalg.norm(w), 1e-30)
+        assert np.isfinite(g).all() and rel < 5e-2, f"{name}: bf16 grad rel-err {rel:.3e}"
+
+
+# ---------------------------------------------------------------- CTC
+
+
+@pytest.mark.parametrize("name", sorted(CTC))
+def test_ctc_matches_golden(name):
+    from asr_b200.loss.ctc import CTCLossFn
+
+    c = CTC[name]
+    x = leaf(c["logits"])
+    loss = CTCLossFn.apply(x, cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"]),
+                           bool(c["zero_infinity"]))
+    (loss * cuda(c["grad_loss"])).sum().backward()
+    np.testing.assert_allclose(loss.detach().double().cpu().numpy(), c["loss"], rtol=1e-5, atol=2e-5)
+    assert_grad(x.grad, c["grad_logits"], "grad_logits")
+
+
+def test_ctc_module_normalises_by_target_length():
+    from asr_b200.loss.ctc import CTCLoss, CTCLossFn
+
+    c = CTC["varlen_padded"]
+    x = cuda(c["logits"])
+    raw = CTCLossFn.apply(x, cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"]), False)
+    out = CTCLoss()(x, cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"]))
+    torch.testing.assert_close(out, raw / cuda(c["tgt_lens"]).clamp_min(1))
+
+
+def test_ctc_config1_matches_oracle():
+    from asr_b200.loss.ctc import CTCLossFn
+
+    c = ctc_case(11, 8, (150, 200), 29, (20, 60))
+    x = leaf(c["logits"])
+    loss = CTCLossFn.apply(x, cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"]), False)
+    loss.sum().backward()
+    lp = torch.log_softmax(torch.tensor(c["logits"]), -1).numpy()
+    want, grad = oracle.ctc(lp, c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    assert_loss(loss, want)
+    assert_grad(x.grad, grad, "grad_logits", rtol=0)
+
+
+def test_ctc_long_targets():
+    """2S+1 = 601 states: the widest register block (16 states per lane)."""
+    from asr_b200.loss.ctc import CTCLossFn
+
+    c = ctc_case(12, 3, (650, 700), 40, (280, 300))
+    x = leaf(c["logits"])
+    loss = CTCLossFn.apply(x, cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"]), False)
+    loss.sum().backward()
+    lp = torch.log_softmax(torch.tensor(c["logits"]), -1).numpy()
+    want, grad = oracle.ctc(lp, c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    assert_loss(loss, want)
+    assert_grad(x.grad, grad, "grad_logits")
+
+
+# -------------------------------------------------------------- RNN-T
+
+
+def run_rnnt(c, tf32=False):
+    from asr_b200.loss.rnnt import rnnt_loss
+
+    e, d, w = leaf(c["enc"]), leaf(c["dec"]), leaf(c["W"])
+    loss = rnnt_loss(e, d, w, cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"]), 0, tf32)
+    (loss * cuda(c["grad_loss"])).sum().backward()
+    return loss, e.grad, d.grad, w.grad
+
+
+@pytest.mark.parametrize("name", sorted(RNNT))
+def test_rnnt_fp32_matches_golden(name):
+    c = RNNT[name]
+    loss, ge, gd, gw = run_rnnt(c)
+    assert_loss(loss, c["loss"])
+    assert_grad(ge, c["d_enc"], "d_enc")
+    assert_grad(gd, c["d_dec"], "d_dec")
+    assert_grad(gw, c["dW"], "dW")
+
+
+def test_rnnt_char_config_matches_oracle():
+    """Config-2 shape family (V=30, d=640), 4 utterances so the oracle stays fast."""
+    c = transducer_case(21, 4, (100, 160), (30, 60), 30, 640)
+    loss, ge, gd, gw = run_rnnt(c)
+    o = oracle.rnnt(c["enc"], c["dec"], c["W"], c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    assert_loss(loss, o["loss"])
+    assert_grad(ge, o["d_enc"], "d_enc", rtol=0)
+    assert_grad(gd, o["d_dec"], "d_dec", rtol=0)
+    assert_grad(gw, o["dW"], "dW", rtol=0)
+
+
+def test_rnnt_wide_labels():
+    """U = 300 label positions: 16 positions per lane in the recursions."""
+    c = transducer_case(22, 2, (40, 60), (280, 299), 12, 16, act_std=0.5)
+    loss, ge, gd, gw = run_rnnt(c)
+    o = oracle.rnnt(c["enc"], c["dec"], c["W"], c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    assert_loss(loss, o["loss"])
+    assert_grad(ge, o["d_enc"], "d_enc")
+    assert_grad(gd, o["d_dec"], "d_dec")
+    assert_grad(gw, o["dW"], "dW")
+
+
+def test_rnnt_padding_gets_zero_grad_and_module_normalises():
+    from asr_b200.loss.rnnt import RNNTLoss, rnnt_loss
+
+    c = RNNT["padding"]
+    loss, ge, gd, gw = run_rnnt(c)
+    assert torch.count_nonzero(ge[1, 4:]) == 0
+    assert torch.count_nonzero(gd[1, 2:]) == 0
+    args = [cuda(c[k]) for k in ("enc", "dec", "W", "targets", "in_lens", "tgt_lens")]
+    raw = rnnt_loss(*args)
+    torch.testing.assert_close(RNNTLoss()(*args), raw / args[5].clamp_min(1))
+
+
+def test_rnnt_empty_target_closed_form():
+    c = RNNT["empty_target_in_batch"]
+    loss, *_ = run_rnnt(c)
+    h = np.tanh(c["enc"][1][:, None, :].astype(np.float64) + c["dec"][1][None, :, :].astype(np.float64))
+    logits = h @ c["W"].astype(np.float64).T
+    logp = logits - np.log(np.exp(logits).sum(-1, keepdims=True))
+    expected = -logp[: int(c["in_lens"][1]), 0, 0].sum()
+    np.testing.assert_allclose(float(loss[1]), expected, rtol=1e-5)
+
+
+def test_rnnt_bf16_mode_within_reference_tf32_bar():
+    c = transducer_case(23, 4, (20, 30), (6, 10), 32, 64, act_std=1.0)
+    loss, ge, gd, gw = run_rnnt(c, tf32=True)
+    o = oracle.rnnt(c["enc"], c["dec"], c["W"], c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    assert_bf16_close(loss, o["loss"], [("d_enc", ge, o["d_enc"]), ("d_dec", gd, o["d_dec"]), ("dW", gw, o["dW"])])
+
+
+# ---------------------------------------------------------------- TDT
+
+
+def run_tdt(c, tf32=False, sigma=None):
+    from asr_b200.loss.tdt import tdt_loss
+
+    e, d, w, wd = leaf(c["enc"]), leaf(c["dec"]), leaf(c["W"]), leaf(c["W_dur"])
+    s = float(c["sigma"]) if sigma is None else sigma
+    loss = tdt_loss(e, d, w, wd, cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"]),
+                    [int(x) for x in c["durations"]], 0, s, tf32)
+    (loss * cuda(c["grad_loss"])).sum().backward()
+    return loss, e.grad, d.grad, w.grad, wd.grad
+
+
+@pytest.mark.parametrize("name", sorted(TDT))
+def test_tdt_fp32_matches_golden(name):
+    c = TDT[name]
+    loss, ge, gd, gw, gwd = run_tdt(c)
+    assert_loss(loss, c["loss"])
+    assert_grad(ge, c["d_enc"], "d_enc")
+    assert_grad(gd, c["d_dec"], "d_dec")
+    assert_grad(gw, c["dW"], "dW")
+    assert_grad(gwd, c["dW_dur"], "dW_dur")
+
+
+def _tdt_oracle(c, sigma):
+    return oracle.tdt(c["enc"], c["dec"], c["W"], c["W_dur"], c["targets"], c["in_lens"], c["tgt_lens"],
+                      c["durations"], sigma=sigma, grad_loss=c["grad_loss"])
+
+
+@pytest.mark.parametrize("sigma", [0.0, 0.05])
+def test_tdt_bpe_config_matches_oracle(sigma):
+    """Config-3 shape family (V=1024 + 5 durations, d=640), 3 utterances."""
+    c = transducer_case(31, 3, (60, 90), (10, 25), 1024, 640, n_dur=5)
+    loss, ge, gd, gw, gwd = run_tdt(c, sigma=sigma)
+    o = _tdt_oracle(c, sigma)
+    assert_loss(loss, o["loss"])
+    assert_grad(ge, o["d_enc"], "d_enc", rtol=0)
+    assert_grad(gd, o["d_dec"], "d_dec", rtol=0)
+    assert_grad(gw, o["dW"], "dW", rtol=0)
+    assert_grad(gwd, o["dW_dur"], "dW_dur", rtol=0)
+
+
+def test_tdt_irregular_durations():
+    """Durations [0, 1, 3, 3, 7]: a gap, a duplicate and max_duration 7 (the 8-slot ring)."""
+    c = transducer_case(32, 3, (20, 30), (4, 9), 20, 24, n_dur=5, act_std=0.7)
+    c["durations"] = np.array([0, 1, 3, 3, 7], np.int32)
+    loss, ge, gd, gw, gwd = run_tdt(c, sigma=0.1)
+    o = _tdt_oracle(c, 0.1)
+    assert_loss(loss, o["loss"])
+    for name, g in (("d_enc", ge), ("d_dec", gd), ("dW", gw), ("dW_dur", gwd)):
+        assert_grad(g, o[name], name)
+
+
+def test_tdt_no_zero_duration():
+    c = transducer_case(33, 2, (15, 25), (3, 6), 16, 12, n_dur=3, act_std=0.7)
+    c["durations"] = np.array([1, 2, 4], np.int32)
+    loss, ge, gd, gw, gwd = run_tdt(c, sigma=0.0)
+    o = _tdt_oracle(c, 0.0)
+    assert_loss(loss, o["loss"])
+    for name, g in (("d_enc", ge), ("d_dec", gd), ("dW", gw), ("dW_dur", gwd)):
+        assert_grad(g, o[name], name)
+
+
+def test_tdt_padding_gets_zero_grad_and_module_normalises():
+    from asr_b200.loss.tdt import TDTLoss, tdt_loss
+
+    c = TDT["padding"]
+    loss, ge, gd, gw, gwd = run_tdt(c)
+    assert torch.count_nonzero(ge[1, 4:]) == 0
+    assert torch.count_nonzero(gd[1, 2:]) == 0
+    args = [cuda(c[k]) for k in ("enc", "dec", "W", "W_dur", "targets", "in_lens", "tgt_lens")]
+    md = int(c["durations"].max())
+    raw = tdt_loss(*args, list(range(md + 1)))
+    torch.testing.assert_close(TDTLoss(md)(*args), raw / args[6].clamp_min(1))
+
+
+def test_tdt_bf16_mode_within_reference_tf32_bar():
+    c = transducer_case(34, 4, (20, 30), (6, 10), 32, 64, n_dur=5, act_std=1.0)
+    loss, ge, gd, gw, gwd = run_tdt(c, tf32=True, sigma=0.0)
+    o = _tdt_oracle(c, 0.0)
+    assert_bf16_close(loss, o["loss"], [("d_enc", ge, o["d_enc"]), ("d_dec", gd, o["d_dec"]), ("dW", gw, o["dW"]),
+                                        ("dW_dur", gwd, o["dW_dur"])])
+
+
+def test_tdt_bf16_bpe_config_matches_oracle():
+    c = transducer_case(35, 3, (60, 90), (10, 25), 1024, 640, n_dur=5)
+    loss, ge, gd, gw, gwd = run_tdt(c, tf32=True, sigma=0.05)
+    o = _tdt_oracle(c, 0.05)
+    assert_bf16_close(loss, o["loss"], [("d_enc", ge, o["d_enc"]), ("d_dec", gd, o["d_dec"]), ("dW", gw, o["dW"]),
+                                        ("dW_dur", gwd, o["dW_dur"])])
+
+
+# ------------------------------------------------------- direct C ABI
+
+
+def test_capi_tdt_matches_op_path():
+    """Calls libasr_b200.so through ctypes with raw device pointers (what any FFI binds)."""
+    import ctypes
+
+    from asr_b200 import _lib
+
+    lib = _lib.capi()
+    c = TDT["variable_lens_s02"]
+    B, T, d = c["enc"].shape
+    U = c["dec"].shape[1]
+    V = c["W"].shape[0]
+    Dn = c["W_dur"].shape[0]
+    S = c["targets"].shape[1]
+    t = {k: cuda(c[k]) for k in ("enc", "dec", "W", "W_dur", "targets", "in_lens", "tgt_lens", "durations")}
+    f32 = dict(device="cuda", dtype=torch.float32)
+    loss = torch.empty(B, **f32)
+    log_prob = torch.empty(B, **f32)
+    alpha = torch.empty(B, T + 1, U, device="cuda", dtype=torch.float64)
+    lpb = torch.empty(2, B, T, U, **f32)
+    lpy = torch.empty(B, T, U, **f32)
+    lpd = torch.empty(B, T, U, Dn, **f32)
+    lib.asr_tdt_workspace_bytes.restype = ctypes.c_size_t
+    wsb = lib.asr_tdt_workspace_bytes(B, T, U, V, Dn, d, 0, 0)
+    ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    P = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    md = int(c["durations"].max())
+    rc = lib.asr_tdt_forward(P(t["enc"]), P(t["dec"]), P(t["W"]), P(t["W_dur"]), P(t["targets"]), P(t["in_lens"]),
+                             P(t["tgt_lens"]), P(t["durations"]), Dn, md, 1, B, T, U, V, d, S, 0,
+                             ctypes.c_float(float(c["sigma"])), 0, P(loss), P(alpha), P(lpb), P(lpy), P(lpd),
+                             P(log_prob), P(ws), ctypes.c_size_t(wsb), stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert_loss(loss, c["loss"])
+    gl = torch.ones(B, **f32)
+    ge, gd = torch.empty(B, T, d, **f32), torch.empty(B, U, d, **f32)
+    gw, gwd = torch.empty(V, d, **f32), torch.empty(Dn, d, **f32)
+    wsb2 = lib.asr_tdt_workspace_bytes(B, T, U, V, Dn, d, 0, 1)
+    ws2 = torch.empty(wsb2, dtype=torch.uint8, device="cuda")
+    rc = lib.asr_tdt_backward(P(t["enc"]), P(t["dec"]), P(t["W"]), P(t["W_dur"]), P(t["targets"]), P(t["in_lens"]),
+                              P(t["tgt_lens"]), P(t["durations"]), Dn, md, 1, B, T, U, V, d, S, 0, P(alpha), P(lpb),
+                              P(lpy), P(lpd), P(log_prob), P(gl), 0, P(ge), P(gd), P(gw), P(gwd), P(ws2),
+                              ctypes.c_size_t(wsb2), stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert_grad(ge, c["d_enc"], "d_enc")
+    assert_grad(gd, c["d_dec"], "d_dec")
+    assert_grad(gw, c["dW"], "dW")
+    assert_grad(gwd, c["dW_dur"], "dW_dur")
+    clamped = ctypes.c_int(-1)
+    assert lib.asr_workspace_status(P(ws2), B, ctypes.byref(clamped), stream) == 0
+    assert clamped.value == 0
+
+
+def test_capi_ctc_direct():
+    import ctypes
+
+    from asr_b200 import _lib
+
+    lib = _lib.capi()
+    c = CTC["small_fixed"]
+    B, T, V = c["log_probs"].shape
+    S = c["targets"].shape[1]
+    lp = cuda(c["log_probs"])
+    tg, il, tl = cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"])
+    alpha = torch.empty(B, T, 2 * S + 1, device="cuda", dtype=torch.float64)
+    logz = torch.empty(B, device="cuda")
+    P = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.asr_ctc_alpha(P(lp), P(tg), P(il), P(tl), B, T, V, S, P(alpha), P(logz), stream) == 0
+    grad = torch.full((B, T, V), float("nan"), device="cuda")
+    gl = cuda(c["grad_loss"])
+    assert lib.asr_ctc_grad(P(alpha), P(logz), P(lp), P(tg), P(il), P(tl), P(gl), 0, B, T, V, S, P(grad), stream) == 0
+    torch.cuda.synchronize()
+    np.testing.assert_allclose((-logz).double().cpu().numpy(), c["loss"], rtol=1e-5, atol=2e-5)
+    assert_grad(grad, c["grad_logits"], "grad_logits")
