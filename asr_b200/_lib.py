@@ -30,6 +30,18 @@ def load_ops() -> None:
     _ops_loaded = True
 
 
+def capi_ops() -> ctypes.CDLL:
+    """ctypes view of the op library itself (the kernels torch.ops.asr.* run), for
+    the diagnostics entry points (asr_profiler_*, asr_joint_path)."""
+    load_ops()
+    return ctypes.CDLL(str(OPS_SO))
+
+
+def joint_uses_tensor_cores(V: int, n_dur: int, d: int) -> bool:
+    """True when tf32=True selects the bf16 tcgen05 joint for this shape."""
+    return bool(capi_ops().asr_joint_path(1, V, n_dur, d))
+
+
 def capi() -> ctypes.CDLL:
     """The C-ABI library (include/asr_b200.h) for FFI callers and tests."""
     global _capi

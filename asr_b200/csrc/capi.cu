@@ -105,6 +105,12 @@ extern "C" const char* asr_status_string(int status) {
 
 extern "C" int asr_abi_version(void) { return 1; }
 
+extern "C" int asr_joint_path(int tf32, int V, int n_dur, int d) {
+    if (V < 1 || d < 1 || n_dur < 0) return 0;
+    JointArgs a = make_args(nullptr, nullptr, nullptr, nullptr, nullptr, 1, 1, 1, V, n_dur, d, 0, 0, 0.f);
+    return use_tc(tf32, a) ? 1 : 0;
+}
+
 // ------------------------------------------------------------------------ RNN-T
 
 extern "C" size_t asr_rnnt_workspace_bytes(int B, int T, int U, int V, int d, int tf32, int backward) {

@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include "asr_b200.h"
+#include "profiler.cuh"
 
 namespace asr {
 

@@ -212,6 +212,7 @@ template <int KS>
 int launch_ctc_alpha(const float* lp, const int32_t* tg, const int32_t* il, const int32_t* tl, int B, int T, int V,
                      int S, double* alpha, float* logz, cudaStream_t st) {
     const int blocks = (B + kCtcWarps - 1) / kCtcWarps;
+    KernelTimer kt("ctc_alpha", st);
     ctc_alpha_kernel<KS><<<blocks, 32 * kCtcWarps, 0, st>>>(lp, tg, il, tl, B, T, V, S, alpha, logz);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
@@ -227,6 +228,7 @@ int launch_ctc_grad(const double* alpha, const float* lp, const int32_t* tg, con
             cudaSuccess)
             return ASR_ERR_UNSUPPORTED;
     }
+    KernelTimer kt("ctc_beta_grad", st);
     ctc_grad_kernel<KS><<<blocks, 32 * kCtcWarps, smem, st>>>(alpha, lp, tg, il, tl, gl, zinf, B, T, V, S, grad);
     ASR_LAUNCH_CHECK();
     return ASR_OK;

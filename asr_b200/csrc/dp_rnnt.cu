@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(32 * kDpWarps)
 template <int K>
 int launch_rnnt_alpha_k(const LatticeMeta& m, int B, const float* lpb, const float* lpy, double* alpha, float* lp,
                         float* loss, cudaStream_t st) {
+    KernelTimer kt("rnnt_alpha", st);
     rnnt_alpha_kernel<K><<<(B + kDpWarps - 1) / kDpWarps, 32 * kDpWarps, 0, st>>>(m, B, lpb, lpy, alpha, lp, loss);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
@@ -118,6 +119,7 @@ int launch_rnnt_alpha_k(const LatticeMeta& m, int B, const float* lpb, const flo
 template <int K>
 int launch_rnnt_beta_k(const LatticeMeta& m, int B, const float* lpb, const float* lpy, const double* alpha,
                        const float* gl, float* cb, float* ct, cudaStream_t st) {
+    KernelTimer kt("rnnt_beta_posteriors", st);
     rnnt_beta_kernel<K><<<(B + kDpWarps - 1) / kDpWarps, 32 * kDpWarps, 0, st>>>(m, B, lpb, lpy, alpha, gl, cb, ct);
     ASR_LAUNCH_CHECK();
     return ASR_OK;

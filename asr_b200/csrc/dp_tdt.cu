@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(32 * kDpWarps)
 template <int K, int MAXD>
 int tdt_alpha_launch(const LatticeMeta& m, int B, const int32_t* dur, int nd, int hz, const float* lpb,
                      const float* lpy, const float* lpd, double* alpha, float* lp, float* loss, cudaStream_t st) {
+    KernelTimer kt("tdt_alpha", st);
     tdt_alpha_kernel<K, MAXD><<<(B + kDpWarps - 1) / kDpWarps, 32 * kDpWarps, 0, st>>>(m, B, dur, nd, hz, lpb, lpy,
                                                                                      lpd, alpha, lp, loss);
     ASR_LAUNCH_CHECK();
@@ -240,6 +241,7 @@ template <int K, int MAXD>
 int tdt_beta_launch(const LatticeMeta& m, int B, const int32_t* dur, int nd, int hz, const float* lpb,
                     const float* lpy, const float* lpd, const double* alpha, const float* gl, float* cb, float* ct,
                     float* gdur, cudaStream_t st) {
+    KernelTimer kt("tdt_beta_posteriors", st);
     tdt_beta_kernel<K, MAXD><<<(B + kDpWarps - 1) / kDpWarps, 32 * kDpWarps, 0, st>>>(
         m, B, dur, nd, hz, lpb, lpy, lpd, alpha, gl, cb, ct, gdur);
     ASR_LAUNCH_CHECK();

@@ -11,6 +11,7 @@
 // (G, fp32 scratch); (2) dH = G * Wf with tanh' applied in the epilogue and
 // scattered to d_enc / d_dec; (3) dW = G^T * hidden as a split-K GEMM whose B
 // operand (hidden) is recomputed on the fly.
+#include <algorithm>
 #include <cfloat>
 
 #include "joint.cuh"
@@ -346,7 +347,10 @@ int simt_joint_forward(const JointArgs& a, const JointFwdOut& o, cudaStream_t st
     if (a.n_dur > kMaxDur) return ASR_ERR_UNSUPPORTED;
     const int cap_tiles = (int)(((int64_t)a.B * a.T * a.U + BM - 1) / BM);
     const int grid = std::max(1, std::min(cap_tiles, sm_count() * 6));
-    simt_fwd_kernel<<<grid, NT, 0, st>>>(a, o);
+    {
+        KernelTimer kt("joint_fwd_simt", st);
+        simt_fwd_kernel<<<grid, NT, 0, st>>>(a, o);
+    }
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
@@ -364,15 +368,24 @@ int simt_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwd
         const int cn = std::min(chunk, node_capacity - c0);
         const int ntiles = (cn + BM - 1) / BM;
         const int vt = (Vf + BN - 1) / BN, dt = (a.d + BN - 1) / BN;
-        simt_bwd_g_kernel<<<std::max(1, std::min(ntiles * vt, sms * 6)), NT, 0, st>>>(a, in, G, c0, cn);
+        {
+            KernelTimer kt("joint_dlogits_simt", st);
+            simt_bwd_g_kernel<<<std::max(1, std::min(ntiles * vt, sms * 6)), NT, 0, st>>>(a, in, G, c0, cn);
+        }
         ASR_LAUNCH_CHECK();
-        simt_dh_kernel<<<std::max(1, std::min(ntiles * dt, sms * 6)), NT, 0, st>>>(a, G, o, c0, cn);
+        {
+            KernelTimer kt("joint_dhidden_simt", st);
+            simt_dh_kernel<<<std::max(1, std::min(ntiles * dt, sms * 6)), NT, 0, st>>>(a, G, o, c0, cn);
+        }
         ASR_LAUNCH_CHECK();
         const int out_tiles = ((Vf + BM - 1) / BM) * dt;
         const int splits = std::max(1, std::min((sms * 4 + out_tiles - 1) / out_tiles, (cn + 255) / 256));
         const int per = (((cn + splits - 1) / splits) + BK - 1) / BK * BK;
         dim3 g((Vf + BM - 1) / BM, dt, splits);
-        simt_dw_kernel<<<g, NT, 0, st>>>(a, G, o, c0, cn, per);
+        {
+            KernelTimer kt("joint_dweight_simt", st);
+            simt_dw_kernel<<<g, NT, 0, st>>>(a, G, o, c0, cn, per);
+        }
         ASR_LAUNCH_CHECK();
     }
     return ASR_OK;

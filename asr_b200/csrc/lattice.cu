@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(kPrepThreads)
 
 int launch_lattice_prep(const int32_t* in_lens, const int32_t* tgt_lens, int B, int T, int U, int S,
                         const LatticeMeta& m, cudaStream_t stream) {
+    KernelTimer kt("lattice_prep", stream);
     lattice_prep_kernel<<<1, kPrepThreads, 0, stream>>>(in_lens, tgt_lens, B, T, U, S, m);
     ASR_LAUNCH_CHECK();
     return ASR_OK;

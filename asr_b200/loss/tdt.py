@@ -9,6 +9,18 @@ from asr_b200 import _lib
 
 _lib.load_ops()
 
+# Device copies of duration lists, so repeated calls do not re-upload them.
+_durations_cache: dict[tuple, torch.Tensor] = {}
+
+
+def _durations_tensor(durations: list[int], device) -> torch.Tensor:
+    key = (tuple(durations), str(device))
+    t = _durations_cache.get(key)
+    if t is None:
+        t = torch.as_tensor(durations, dtype=torch.int32, device=device)
+        _durations_cache[key] = t
+    return t
+
 
 class TDTLossFn(torch.autograd.Function):
     """Fused two-head joint network + Token-and-Duration Transducer loss."""
@@ -62,7 +74,7 @@ def tdt_loss(encoder, decoder, joint_W, joint_W_dur, targets, in_lens, tgt_lens,
         raise ValueError(f"durations must contain 1 so every frame count is reachable, got {durations}")
     if sigma < 0:
         raise ValueError(f"sigma must be non-negative, got {sigma}")
-    durations_t = torch.as_tensor(durations, dtype=torch.int32, device=encoder.device)
+    durations_t = _durations_tensor(durations, encoder.device)
     return TDTLossFn.apply(encoder, decoder, joint_W, joint_W_dur, in_lens, tgt_lens, targets, durations_t,
                            int(max(durations)), int(0 in durations), blank_idx, float(sigma), int(tf32))
 

@@ -1,0 +1,447 @@
+"""Throughput of the fused joint + sequence-loss path, forward + backward.
+
+Default workload (the TDT BPE-1024 configuration batch-sharded
+over 1/2/4/8 B200s): a global batch of 512 synthetic utterances, T ~ U[200, 500]
+frames, U ~ U[20, 120] labels, joint dim 640, V = 1024 tokens + 5 durations
+{0..4}, sigma = 0.05, activations ~N(0, 1/640), Xavier-uniform joint weights
+(seeded; no dataset is available offline). Utterances are balanced over the
+ranks by lattice size; every step each rank runs the fused TDT forward +
+backward on its shard (public API: asr_b200.loss.tdt.tdt_loss) and the ranks
+all-reduce the joint-weight gradients and the loss sum in one NCCL call.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Rank 0 prints one JSON line. `value` is device-timed (CUDA events, max over
+ranks) with inputs resident in HBM; `e2e` adds, every step, the host->device
+copy of the step's inputs from pinned memory and the device->host read of the
+loss. The reference arm (--impl reference) times the CPU restatement of the
+reference's algorithm (oracle/, the only implementation of the path that runs
+on a host) on all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+D_MODEL = 640
+VOCAB = 1024
+DURATIONS = [0, 1, 2, 3, 4]
+SIGMA = 0.05
+GLOBAL_B = 512
+T_RANGE = (200, 500)
+U_RANGE = (20, 120)
+SEED = 0
+
+
+# ------------------------------------------------------------------ workload
+
+
+def workload_lengths(seed=SEED):
+    rng = np.random.default_rng(seed + 1)
+    in_lens = rng.integers(T_RANGE[0], T_RANGE[1] + 1, size=GLOBAL_B).astype(np.int32)
+    tgt_lens = rng.integers(U_RANGE[0], U_RANGE[1] + 1, size=GLOBAL_B).astype(np.int32)
+    return in_lens, tgt_lens
+
+
+def joint_weights(seed=SEED):
+    rng = np.random.default_rng(seed + 2)
+
+    def xavier(r, c):
+        b = np.sqrt(6.0 / (r + c))
+        return rng.uniform(-b, b, size=(r, c)).astype(np.float32)
+
+    return xavier(VOCAB, D_MODEL), xavier(len(DURATIONS), D_MODEL)
+
+
+def utterance(i, T, U, seed=SEED):
+    """Activations and labels of utterance i (its own seeded stream)."""
+    rng = np.random.default_rng([seed, 1000 + i])
+    std = 1.0 / np.sqrt(D_MODEL)
+    enc = (rng.standard_normal((T, D_MODEL)) * std).astype(np.float32)
+    dec = (rng.standard_normal((U + 1, D_MODEL)) * std).astype(np.float32)
+    y = rng.integers(1, VOCAB, size=U).astype(np.int32)
+    return enc, dec, y
+
+
+def make_batch(idx, in_lens, tgt_lens, seed=SEED):
+    """Padded numpy batch of the utterances in idx (the shard of one rank)."""
+    Bl = len(idx)
+    T = int(in_lens[idx].max())
+    U = int(tgt_lens[idx].max())
+    enc = np.zeros((Bl, T, D_MODEL), np.float32)
+    dec = np.zeros((Bl, U + 1, D_MODEL), np.float32)
+    tg = np.ones((Bl, max(U, 1)), np.int32)
+    for j, i in enumerate(idx):
+        e, d, y = utterance(int(i), int(in_lens[i]), int(tgt_lens[i]), seed)
+        enc[j, : len(e)] = e
+        dec[j, : len(d)] = d
+        tg[j, : len(y)] = y
+    return {"enc": enc, "dec": dec, "targets": tg, "in_lens": in_lens[idx].copy(), "tgt_lens": tgt_lens[idx].copy()}
+
+
+# ------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, out_path=None):
+        self.proc = None
+        self.out_path = out_path
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self, gpu_indices=None):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        if self.out_path:
+            Path(self.out_path).write_text(out)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            if gpu_indices is not None and int(f[0]) not in gpu_indices:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() in ("active", "1"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------- roofline
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def kernel_work(name, N, d, Vf, n_dur):
+    """Algorithmic work of one step of kernel `name`: ('tensor', flops) or ('hbm', bytes).
+    GEMM kernels: 2 * N * d * Vf each (the backward recompute is one of them).
+    Recursions: the lattice bytes of the per-node figures (4-byte values)."""
+    if name.startswith("joint_"):
+        return "tensor", 2.0 * N * d * Vf
+    if name.startswith("tdt_alpha") or name.startswith("rnnt_alpha"):
+        return "hbm", N * 4.0 * ((2 + n_dur) + 1)
+    if name.startswith("tdt_beta") or name.startswith("rnnt_beta"):
+        return "hbm", N * 4.0 * (2 * (2 + n_dur) + 1)
+    return None, 0.0
+
+
+def parse_profile(text):
+    rows = {}
+    for line in text.strip().splitlines():
+        name, n, ms = line.split()
+        rows[name] = (int(n), float(ms))
+    return rows
+
+
+def profiler_report(clear=True):
+    import ctypes
+
+    from asr_b200 import _lib
+
+    lib = _lib.capi_ops()
+    n = lib.asr_profiler_report(None, 0, 0)
+    buf = ctypes.create_string_buffer(max(n, 0) + 1)
+    lib.asr_profiler_report(buf, len(buf), int(clear))
+    return parse_profile(buf.value.decode())
+
+
+# ------------------------------------------------------------ reference arm
+
+
+def run_reference(args, rank):
+    """CPU restatement of the reference path (oracle/) on all host threads."""
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    oracle.build()
+    in_lens, tgt_lens = workload_lengths()
+    W, Wd = joint_weights()
+    threads = os.cpu_count() or 1
+    order = np.argsort(in_lens * (tgt_lens + 1))[GLOBAL_B // 2:]  # median-and-up lattices, cycled
+
+    def one(i):
+        b = make_batch(np.array([i]), in_lens, tgt_lens)
+        oracle.tdt(b["enc"], b["dec"], W, Wd, b["targets"], b["in_lens"], b["tgt_lens"], np.array(DURATIONS, np.int32),
+                   sigma=SIGMA, grad_loss=np.ones(1, np.float32), nthreads=threads)
+
+    k = 0
+    for _ in range(args.warmup):
+        one(int(order[k % len(order)]))
+        k += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one(int(order[k % len(order)]))
+        k += 1
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    line = {
+        "impl": "reference", "metric": "fused joint+loss fwd+bwd utterances/s", "value": round(value, 4),
+        "unit": "utterances/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * dt / args.steps, 3), "higher_is_better": True, "dtype": "f64",
+        "data": "synthetic", "scaling": "strong",
+        "config": {"workload": "tdt_bpe1024_sharded", "global_batch": GLOBAL_B, "vocab": VOCAB,
+                   "durations": DURATIONS, "d_model": D_MODEL, "sample": "1 utterance per step"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "utterances/s", "cores": threads, "kind": "port",
+                         "sample": "1 utterance per step (median-or-longer lattice of the workload), fwd+bwd, "
+                                   "float64 C restatement of the reference algorithm"},
+        "e2e": {"value": round(value, 4), "unit": "utterances/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- our arm
+
+
+def cpu_baseline_leg(in_lens, tgt_lens, W, Wd, sample=2):
+    from oracle import oracle
+
+    oracle.build()
+    threads = os.cpu_count() or 1
+    idx = np.arange(sample)
+    b = make_batch(idx, in_lens, tgt_lens)
+    t0 = time.perf_counter()
+    oracle.tdt(b["enc"], b["dec"], W, Wd, b["targets"], b["in_lens"], b["tgt_lens"], np.array(DURATIONS, np.int32),
+               sigma=SIGMA, grad_loss=np.ones(sample, np.float32), nthreads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": round(sample / dt, 4), "unit": "utterances/s", "cores": threads, "kind": "port",
+            "sample": f"utterances 0..{sample - 1} of the workload (T={list(map(int, in_lens[:sample]))}, "
+                      f"U={list(map(int, tgt_lens[:sample]))}), fwd+bwd, float64 C oracle, {threads} threads"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tf32", type=int, default=1, help="1: bf16 tensor-core joint (the systems' setting)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--clocks-log", default=None)
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    import ctypes  # noqa: F401
+
+    from asr_b200 import _lib
+    from asr_b200.loss.tdt import tdt_loss
+    from asr_b200.shard import allreduce_joint, balance_shards, shard_imbalance
+
+    in_lens, tgt_lens = workload_lengths()
+    shards = balance_shards(in_lens, tgt_lens, world)
+    mine = shards[rank]
+    host = make_batch(mine, in_lens, tgt_lens)
+    W_np, Wd_np = joint_weights()
+    N_local = int((host["in_lens"].astype(np.int64) * (host["tgt_lens"] + 1)).sum())
+    N_global = int((in_lens.astype(np.int64) * (tgt_lens + 1)).sum())
+
+    enc = torch.tensor(host["enc"], device=dev, requires_grad=True)
+    dec = torch.tensor(host["dec"], device=dev, requires_grad=True)
+    W = torch.tensor(W_np, device=dev, requires_grad=True)
+    Wd = torch.tensor(Wd_np, device=dev, requires_grad=True)
+    targets = torch.tensor(host["targets"], device=dev)
+    il = torch.tensor(host["in_lens"], device=dev)
+    tl = torch.tensor(host["tgt_lens"], device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(e, d, tg, ilen, tlen):
+        for p in (e, d, W, Wd):
+            p.grad = None
+        loss = tdt_loss(e, d, W, Wd, tg, ilen, tlen, DURATIONS, 0, SIGMA, bool(args.tf32))
+        per = loss / tlen.clamp_min(1)
+        total = per.sum() / GLOBAL_B  # global mean, as the systems' loss_per.mean()
+        total.backward()
+        return allreduce_joint([W.grad, Wd.grad, total.detach().reshape(1)])
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
+
+    def timed_loop(run, k):
+        times = []
+        for _ in range(k):
+            flush.fill_(1)  # evict L2 between timed iterations (not timed)
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            run()
+            e.record(stream)
+            times.append((s, e))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in times)
+
+    # ---- device-resident inputs
+    for _ in range(args.warmup):
+        step(enc, dec, targets, il, tl)
+    torch.cuda.synchronize()
+    lib = _lib.capi_ops()
+    lib.asr_profiler_report(None, 0, 1)
+    clocks = ClockSampler(args.clocks_log) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    lib.asr_profiler_enable(1)
+    ms_total = timed_loop(lambda: step(enc, dec, targets, il, tl), args.steps)
+    lib.asr_profiler_enable(0)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop() if clocks else None
+    prof = profiler_report(clear=True)
+
+    # ---- end to end: pinned host inputs copied in, loss read back, every step
+    pinned = {k: torch.from_numpy(v).pin_memory() for k, v in host.items()}
+    res_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pinned.values())
+
+    def e2e_step():
+        e = pinned["enc"].to(dev, non_blocking=True).requires_grad_(True)
+        d = pinned["dec"].to(dev, non_blocking=True).requires_grad_(True)
+        tg = pinned["targets"].to(dev, non_blocking=True)
+        ilen = pinned["in_lens"].to(dev, non_blocking=True)
+        tlen = pinned["tgt_lens"].to(dev, non_blocking=True)
+        flat = step(e, d, tg, ilen, tlen)
+        res_host.copy_(flat[-1:], non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_total = timed_loop(e2e_step, args.steps)
+
+    # ---- max over ranks
+    t = torch.tensor([ms_total, e2e_total], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t[0]) / args.steps
+    e2e_ms = float(t[1]) / args.steps
+    value = GLOBAL_B / (ms_step / 1000.0)
+    e2e_value = GLOBAL_B / (e2e_ms / 1000.0)
+
+    # ---- roofline of the dominant kernel (rank 0's live event timings)
+    peaks = measured_peaks()
+    Vf = VOCAB + len(DURATIONS)
+    roof = None
+    if prof:
+        name, (launches, kms) = max(prof.items(), key=lambda kv: kv[1][1])
+        bound, work = kernel_work(name, N_local, D_MODEL, Vf, len(DURATIONS))
+        per_launch_ms = kms / max(launches, 1)
+        steps_launches = launches / args.steps
+        work_per_launch = work / max(steps_launches, 1)
+        if bound == "tensor":
+            achieved = work_per_launch / (per_launch_ms / 1000.0) / 1e12
+            peak = peaks["bf16_tflops_sustained"]
+            unit = "TFLOP/s"
+        else:
+            achieved = work_per_launch / (per_launch_ms / 1000.0) / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        traffic = None
+        tfile = ROOT / "profiles" / "traffic.json"
+        if tfile.exists():
+            tj = json.loads(tfile.read_text()).get(name)
+            if tj:  # bytes per node measured by ncu on a smaller case, scaled to this launch
+                traffic = int(tj["bytes_per_node"] * N_local / max(steps_launches, 1))
+        roof = {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": f"{peaks['source']} ({'bf16 sustained' if bound == 'tensor' else 'hbm copy'})",
+                "launch_ms": round(per_launch_ms, 4),
+                "share": round(kms / max(sum(v[1] for v in prof.values()), 1e-9), 4)}
+    launches_total = int(sum(v[0] for v in prof.values()))
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline_leg(in_lens, tgt_lens, W_np, Wd_np)
+        tc = bool(args.tf32) and _lib.joint_uses_tensor_cores(VOCAB, len(DURATIONS), D_MODEL)
+        line = {
+            "metric": "fused joint+loss fwd+bwd utterances/s", "value": round(value, 3), "unit": "utterances/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if tc else "f32", "data": "synthetic",
+            "config": {"workload": "tdt_bpe1024_sharded", "global_batch": GLOBAL_B, "per_gpu_batch": len(mine),
+                       "T": list(T_RANGE), "U": list(U_RANGE), "d_model": D_MODEL, "vocab": VOCAB,
+                       "durations": DURATIONS, "sigma": SIGMA, "lattice_nodes_global": N_global,
+                       "lattice_nodes_rank0": N_local, "shard_imbalance": round(shard_imbalance(
+                           in_lens, tgt_lens, shards), 4), "parallelism": f"dp{world}",
+                       "l2": "flushed between timed steps (256 MB write)",
+                       "joint_path": "tcgen05 bf16" if tc else "SIMT fp32"},
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": launches_total, "kernel_ms": {k: round(v[1] / args.steps, 4) for k, v in prof.items()},
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

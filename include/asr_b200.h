@@ -132,6 +132,20 @@ int asr_tdt_backward(const float* encoder, const float* decoder, const float* jo
  * `stream`. Intended for debugging; the hot path never calls it. */
 int asr_workspace_status(const void* workspace, int B, int* clamped, asr_stream_t stream);
 
+/* Joint-network path a call takes: 1 = bf16 tcgen05 tensor cores, 0 = fp32 SIMT.
+ * tf32 = 0 always selects the fp32 path. */
+int asr_joint_path(int tf32, int V, int n_dur, int d);
+
+/* Per-kernel device timing of this library's own launches: while enabled, every
+ * kernel launch is bracketed by CUDA events on its stream. Off by default; the
+ * overhead when off is one flag test per launch. No counterpart in the reference. */
+int asr_profiler_enable(int on);
+
+/* Waits for the recorded events and writes "<kernel> <launches> <total_ms>" lines
+ * into buf (NUL-terminated, truncated to len). Returns the full report length, or a
+ * negative asr_status_t. clear != 0 drops the records afterwards. */
+int asr_profiler_report(char* buf, size_t len, int clear);
+
 #ifdef __cplusplus
 }
 #endif

@@ -232,49 +232,50 @@ static void joint_node(const tr_ctx* c, int b, int t, int u, double* h, double* 
     }
 }
 
-static void transducer_utt(void* vctx, int b, int worker) {
-    tr_ctx* c = (tr_ctx*)vctx;
-    const int d = c->d, V = c->V, Dn = c->n_dur, S = c->S;
-    const int Tb = c->in_lens[b];
-    const int Ub = c->tgt_lens[b] + 1;
-    const int tdt = Dn > 0;
-    const int32_t* y = c->targets + (size_t)b * S;
-    const size_t nn = (size_t)Tb * Ub;
+/* Per-utterance scratch shared by the row-parallel phases. */
+typedef struct {
+    tr_ctx* c;
+    int b, Tb, Ub, zk;
+    const int32_t* y;
+    double *lpb, *lpy, *lpd, *alpha, *beta, logZ;
+    double* dW_w;   /* (workers, V, d) */
+    double* dWd_w;  /* (workers, n_dur, d) */
+    double* ddec_w; /* (workers, Ub, d) */
+} utt_t;
 
-    /* per-node edge log-probs (rnnt.cu:148-152, tdt.cu:162-187) */
-    double* lpb = (double*)malloc(sizeof(double) * nn);
-    double* lpy = (double*)malloc(sizeof(double) * nn);
-    double* lpd = tdt ? (double*)malloc(sizeof(double) * nn * Dn) : NULL;
-    double* h = (double*)malloc(sizeof(double) * d);
-    double* lt = (double*)malloc(sizeof(double) * V);
-    double* ld = (double*)malloc(sizeof(double) * (Dn > 0 ? Dn : 1));
-    for (int t = 0; t < Tb; ++t)
-        for (int u = 0; u < Ub; ++u) {
-            double lse_t, lse_d = 0.0;
-            joint_node(c, b, t, u, h, lt, ld, &lse_t, &lse_d);
-            const size_t n = (size_t)t * Ub + u;
-            const int yy = (u < Ub - 1) ? y[u] : -1;
-            lpb[n] = lt[c->blank] - lse_t - c->sigma;
-            lpy[n] = (yy >= 0) ? lt[yy] - lse_t - c->sigma : NEG;
-            for (int j = 0; j < Dn; ++j) lpd[n * Dn + j] = ld[j] - lse_d;
-        }
-
-    /* first zero duration (tdt_reference.py:134-135) */
-    int zk = -1;
-    for (int j = 0; j < Dn; ++j)
-        if (c->durations[j] == 0) {
-            zk = j;
-            break;
-        }
-
-    const int TR = tdt ? Tb + 1 : Tb; /* TDT uses the (T_b+1)-frame grid */
-    double* alpha = (double*)malloc(sizeof(double) * (size_t)TR * Ub);
-    double* beta = (double*)malloc(sizeof(double) * (size_t)TR * Ub);
 #define A(t, u) alpha[(size_t)(t) * Ub + (u)]
 #define Bt(t, u) beta[(size_t)(t) * Ub + (u)]
 #define NI(t, u) ((size_t)(t) * Ub + (u))
-    double logZ;
-    if (!tdt) {
+
+/* Phase 1 (parallel over frames): edge log-probs of row t (rnnt.cu:148-152, tdt.cu:162-187). */
+static void edge_row(void* vu, int t, int worker) {
+    (void)worker;
+    utt_t* s = (utt_t*)vu;
+    tr_ctx* c = s->c;
+    const int Ub = s->Ub, Dn = c->n_dur, V = c->V;
+    double* h = (double*)malloc(sizeof(double) * c->d);
+    double* lt = (double*)malloc(sizeof(double) * V);
+    double* ld = (double*)malloc(sizeof(double) * (Dn > 0 ? Dn : 1));
+    for (int u = 0; u < Ub; ++u) {
+        double lse_t, lse_d = 0.0;
+        joint_node(c, s->b, t, u, h, lt, ld, &lse_t, &lse_d);
+        const size_t n = NI(t, u);
+        const int yy = (u < Ub - 1) ? s->y[u] : -1;
+        s->lpb[n] = lt[c->blank] - lse_t - c->sigma;
+        s->lpy[n] = (yy >= 0) ? lt[yy] - lse_t - c->sigma : NEG;
+        for (int j = 0; j < Dn; ++j) s->lpd[n * Dn + j] = ld[j] - lse_d;
+    }
+    free(h);
+    free(lt);
+    free(ld);
+}
+
+/* Phase 2 (serial): alpha, beta, log Z. */
+static void recursions(utt_t* s) {
+    tr_ctx* c = s->c;
+    const int Tb = s->Tb, Ub = s->Ub, Dn = c->n_dur, zk = s->zk;
+    double *alpha = s->alpha, *beta = s->beta, *lpb = s->lpb, *lpy = s->lpy, *lpd = s->lpd;
+    if (Dn == 0) {
         /* rnnt_reference.py:94-129 */
         for (int t = 0; t < Tb; ++t)
             for (int u = 0; u < Ub; ++u) {
@@ -286,7 +287,7 @@ static void transducer_utt(void* vctx, int b, int worker) {
                 double tv = (u > 0) ? A(t, u - 1) + lpy[NI(t, u - 1)] : NEG;
                 A(t, u) = lae(th, tv);
             }
-        logZ = A(Tb - 1, Ub - 1) + lpb[NI(Tb - 1, Ub - 1)];
+        s->logZ = A(Tb - 1, Ub - 1) + lpb[NI(Tb - 1, Ub - 1)];
         /* rnnt_reference.py:132-178 */
         for (int t = Tb - 1; t >= 0; --t)
             for (int u = Ub - 1; u >= 0; --u) {
@@ -295,172 +296,218 @@ static void transducer_utt(void* vctx, int b, int worker) {
                 double lb = (u < Ub - 1) ? lpy[NI(t, u)] + Bt(t, u + 1) : NEG;
                 Bt(t, u) = lae(bl, lb);
             }
-    } else {
-        /* tdt_reference.py:109-177 (alpha), tdt.cu:212-289 */
-        for (int t = 0; t <= Tb; ++t)
-            for (int u = 0; u < Ub; ++u) {
-                double acc = (t == 0 && u == 0) ? 0.0 : NEG;
-                for (int j = 0; j < Dn; ++j) {
-                    const int dd = c->durations[j];
-                    if (dd < 1) continue;
-                    const int s = t - dd;
-                    if (s < 0 || s >= Tb) continue;
-                    acc = lae(acc, A(s, u) + lpb[NI(s, u)] + lpd[NI(s, u) * Dn + j]);
-                    if (u >= 1) acc = lae(acc, A(s, u - 1) + lpy[NI(s, u - 1)] + lpd[NI(s, u - 1) * Dn + j]);
-                }
-                if (zk >= 0 && t < Tb && u >= 1) acc = lae(acc, A(t, u - 1) + lpy[NI(t, u - 1)] + lpd[NI(t, u - 1) * Dn + zk]);
-                A(t, u) = acc;
+        return;
+    }
+    /* tdt_reference.py:109-177 (alpha), tdt.cu:212-289 */
+    for (int t = 0; t <= Tb; ++t)
+        for (int u = 0; u < Ub; ++u) {
+            double acc = (t == 0 && u == 0) ? 0.0 : NEG;
+            for (int j = 0; j < Dn; ++j) {
+                const int dd = c->durations[j];
+                if (dd < 1) continue;
+                const int src = t - dd;
+                if (src < 0 || src >= Tb) continue;
+                acc = lae(acc, A(src, u) + lpb[NI(src, u)] + lpd[NI(src, u) * Dn + j]);
+                if (u >= 1) acc = lae(acc, A(src, u - 1) + lpy[NI(src, u - 1)] + lpd[NI(src, u - 1) * Dn + j]);
             }
-        logZ = A(Tb, Ub - 1);
-        /* tdt_reference.py:180-248 (beta), tdt.cu:326-398 */
-        for (int u = 0; u < Ub; ++u) Bt(Tb, u) = (u == Ub - 1) ? 0.0 : NEG;
-        for (int t = Tb - 1; t >= 0; --t) {
-            for (int u = Ub - 1; u >= 0; --u) {
-                double acc = NEG;
-                for (int j = 0; j < Dn; ++j) {
-                    const int dd = c->durations[j];
-                    if (dd < 1) continue;
-                    const int nt = t + dd;
-                    if (nt > Tb) continue;
-                    acc = lae(acc, lpb[NI(t, u)] + lpd[NI(t, u) * Dn + j] + Bt(nt, u));
-                    if (u < Ub - 1) acc = lae(acc, lpy[NI(t, u)] + lpd[NI(t, u) * Dn + j] + Bt(nt, u + 1));
+            if (zk >= 0 && t < Tb && u >= 1) acc = lae(acc, A(t, u - 1) + lpy[NI(t, u - 1)] + lpd[NI(t, u - 1) * Dn + zk]);
+            A(t, u) = acc;
+        }
+    s->logZ = A(Tb, Ub - 1);
+    /* tdt_reference.py:180-248 (beta), tdt.cu:326-398 */
+    for (int u = 0; u < Ub; ++u) Bt(Tb, u) = (u == Ub - 1) ? 0.0 : NEG;
+    for (int t = Tb - 1; t >= 0; --t)
+        for (int u = Ub - 1; u >= 0; --u) {
+            double acc = NEG;
+            for (int j = 0; j < Dn; ++j) {
+                const int dd = c->durations[j];
+                if (dd < 1) continue;
+                const int nt = t + dd;
+                if (nt > Tb) continue;
+                acc = lae(acc, lpb[NI(t, u)] + lpd[NI(t, u) * Dn + j] + Bt(nt, u));
+                if (u < Ub - 1) acc = lae(acc, lpy[NI(t, u)] + lpd[NI(t, u) * Dn + j] + Bt(nt, u + 1));
+            }
+            if (zk >= 0 && u < Ub - 1) acc = lae(acc, lpy[NI(t, u)] + lpd[NI(t, u) * Dn + zk] + Bt(t, u + 1));
+            Bt(t, u) = acc;
+        }
+}
+
+/* Phase 3 (parallel over frames): posteriors and gradients of row t. d_enc row t
+ * belongs to this call alone; d_dec and the weight gradients go to per-worker partials. */
+static void grad_row(void* vu, int t, int worker) {
+    utt_t* s = (utt_t*)vu;
+    tr_ctx* c = s->c;
+    const int d = c->d, V = c->V, Dn = c->n_dur, Tb = s->Tb, Ub = s->Ub;
+    const int tdt = Dn > 0;
+    const double logZ = s->logZ;
+    const double gl = (double)c->grad_loss[s->b];
+    double *alpha = s->alpha, *beta = s->beta, *lpb = s->lpb, *lpy = s->lpy, *lpd = s->lpd;
+    double* h = (double*)malloc(sizeof(double) * d);
+    double* lt = (double*)malloc(sizeof(double) * V);
+    double* ld = (double*)malloc(sizeof(double) * (Dn > 0 ? Dn : 1));
+    double* gt = (double*)malloc(sizeof(double) * V);
+    double* gh = (double*)malloc(sizeof(double) * d);
+    double* gb = (double*)malloc(sizeof(double) * (Dn > 0 ? Dn : 1));
+    double* gk = (double*)malloc(sizeof(double) * (Dn > 0 ? Dn : 1));
+    double* dW = s->dW_w + (size_t)worker * V * d;
+    double* dWd = tdt ? s->dWd_w + (size_t)worker * Dn * d : NULL;
+    double* ddec = s->ddec_w + (size_t)worker * Ub * d;
+    double* de = c->d_enc + ((size_t)s->b * c->T + t) * d;
+    for (int u = 0; u < Ub; ++u) {
+        const size_t n = NI(t, u);
+        const double a = A(t, u);
+        double bp = 0.0, tp = 0.0;
+        if (!tdt) {
+            /* rnnt.cu:286-303, rnnt_reference.py:223-235 */
+            const int is_term = (t == Tb - 1) && (u == Ub - 1);
+            if (is_term)
+                bp = exp(a + lpb[n] - logZ);
+            else if (t < Tb - 1)
+                bp = exp(a + lpb[n] + Bt(t + 1, u) - logZ);
+            if (u < Ub - 1) tp = exp(a + lpy[n] + Bt(t, u + 1) - logZ);
+        } else {
+            /* tdt.cu:400-426, tdt_reference.py:302-325 */
+            for (int j = 0; j < Dn; ++j) {
+                const int dd = c->durations[j];
+                const int nt = t + dd;
+                double g_b = 0.0, g_t = 0.0;
+                if (nt <= Tb) {
+                    if (dd >= 1) g_b = exp(a + lpb[n] + lpd[n * Dn + j] + Bt(nt, u) - logZ);
+                    if (u < Ub - 1) g_t = exp(a + lpy[n] + lpd[n * Dn + j] + Bt(nt, u + 1) - logZ);
                 }
-                if (zk >= 0 && u < Ub - 1) acc = lae(acc, lpy[NI(t, u)] + lpd[NI(t, u) * Dn + zk] + Bt(t, u + 1));
-                Bt(t, u) = acc;
+                bp += g_b;
+                tp += g_t;
+                gb[j] = -(g_b + g_t); /* d loss / d log_P_dur[j] */
             }
         }
-    }
-    c->log_prob[b] = logZ;
-    c->loss[b] = -logZ;
-
-    if (c->d_enc) {
-        const double gl = (double)c->grad_loss[b];
-        double* gt = (double*)malloc(sizeof(double) * V);
-        double* gd = (double*)malloc(sizeof(double) * (Dn > 0 ? Dn : 1));
-        double* gh = (double*)malloc(sizeof(double) * d);
-        double* gb = (double*)malloc(sizeof(double) * (Dn > 0 ? Dn : 1));
-        double* gk = (double*)malloc(sizeof(double) * (Dn > 0 ? Dn : 1));
-        double* dW = c->dW_w + (size_t)worker * V * d;
-        double* dWd = tdt ? c->dWd_w + (size_t)worker * Dn * d : NULL;
-        for (int t = 0; t < Tb; ++t)
-            for (int u = 0; u < Ub; ++u) {
-                const size_t n = NI(t, u);
-                const double a = A(t, u);
-                double bp = 0.0, tp = 0.0;
-                if (!tdt) {
-                    /* rnnt.cu:286-303, rnnt_reference.py:223-235 */
-                    const int is_term = (t == Tb - 1) && (u == Ub - 1);
-                    if (is_term)
-                        bp = exp(a + lpb[n] - logZ);
-                    else if (t < Tb - 1)
-                        bp = exp(a + lpb[n] + Bt(t + 1, u) - logZ);
-                    if (u < Ub - 1) tp = exp(a + lpy[n] + Bt(t, u + 1) - logZ);
-                } else {
-                    /* tdt.cu:400-426, tdt_reference.py:302-325 */
-                    for (int j = 0; j < Dn; ++j) {
-                        const int dd = c->durations[j];
-                        const int nt = t + dd;
-                        double g_b = 0.0, g_t = 0.0;
-                        if (nt <= Tb) {
-                            if (dd >= 1) g_b = exp(a + lpb[n] + lpd[n * Dn + j] + Bt(nt, u) - logZ);
-                            if (u < Ub - 1) g_t = exp(a + lpy[n] + lpd[n * Dn + j] + Bt(nt, u + 1) - logZ);
-                        }
-                        bp += g_b;
-                        tp += g_t;
-                        gb[j] = -(g_b + g_t); /* d loss / d log_P_dur[j] */
-                    }
-                }
-                if (bp == 0.0 && tp == 0.0 && !tdt) continue;
-                double lse_t, lse_d = 0.0;
-                joint_node(c, b, t, u, h, lt, ld, &lse_t, &lse_d);
-                const int yy = (u < Ub - 1) ? y[u] : -1;
-                /* token head: g = gl*(softmax*(bp+tp) - bp[v=blank] - tp[v=y]) (rnnt.cu:189-194) */
-                for (int v = 0; v < V; ++v) {
-                    double g = gl * exp(lt[v] - lse_t) * (bp + tp);
-                    if (v == c->blank) g -= gl * bp;
-                    if (v == yy) g -= gl * tp;
-                    gt[v] = g;
-                }
-                /* duration head: g = gl*(g_in - softmax*sum(g_in)) (tdt.cu:499) */
-                if (tdt) {
-                    double gsum = 0.0;
-                    for (int j = 0; j < Dn; ++j) gsum += gb[j];
-                    for (int j = 0; j < Dn; ++j) gk[j] = gl * (gb[j] - exp(ld[j] - lse_d) * gsum);
-                }
-                for (int k = 0; k < d; ++k) gh[k] = 0.0;
-                for (int v = 0; v < V; ++v) {
-                    const double g = gt[v];
-                    if (g == 0.0) continue;
-                    const float* w = c->W + (size_t)v * d;
-                    double* dw = dW + (size_t)v * d;
-                    for (int k = 0; k < d; ++k) {
-                        gh[k] += g * (double)w[k];
-                        dw[k] += g * h[k];
-                    }
-                }
-                for (int j = 0; j < Dn; ++j) {
-                    const double g = gk[j];
-                    const float* w = c->W_dur + (size_t)j * d;
-                    double* dw = dWd + (size_t)j * d;
-                    for (int k = 0; k < d; ++k) {
-                        gh[k] += g * (double)w[k];
-                        dw[k] += g * h[k];
-                    }
-                }
-                double* de = c->d_enc + ((size_t)b * c->T + t) * d;
-                double* dd2 = c->d_dec + ((size_t)b * c->U + u) * d;
-                for (int k = 0; k < d; ++k) {
-                    const double gp = gh[k] * (1.0 - h[k] * h[k]);
-                    de[k] += gp;
-                    dd2[k] += gp;
-                }
+        if (bp == 0.0 && tp == 0.0) continue; /* every gradient of this node is zero */
+        double lse_t, lse_d = 0.0;
+        joint_node(c, s->b, t, u, h, lt, ld, &lse_t, &lse_d);
+        const int yy = (u < Ub - 1) ? s->y[u] : -1;
+        /* token head: g = gl*(softmax*(bp+tp) - bp[v=blank] - tp[v=y]) (rnnt.cu:189-194) */
+        for (int v = 0; v < V; ++v) {
+            double g = gl * exp(lt[v] - lse_t) * (bp + tp);
+            if (v == c->blank) g -= gl * bp;
+            if (v == yy) g -= gl * tp;
+            gt[v] = g;
+        }
+        /* duration head: g = gl*(g_in - softmax*sum(g_in)) (tdt.cu:499) */
+        if (tdt) {
+            double gsum = 0.0;
+            for (int j = 0; j < Dn; ++j) gsum += gb[j];
+            for (int j = 0; j < Dn; ++j) gk[j] = gl * (gb[j] - exp(ld[j] - lse_d) * gsum);
+        }
+        for (int k = 0; k < d; ++k) gh[k] = 0.0;
+        for (int v = 0; v < V; ++v) {
+            const double g = gt[v];
+            if (g == 0.0) continue;
+            const float* w = c->W + (size_t)v * d;
+            double* dw = dW + (size_t)v * d;
+            for (int k = 0; k < d; ++k) {
+                gh[k] += g * (double)w[k];
+                dw[k] += g * h[k];
             }
-        free(gt);
-        free(gd);
-        free(gh);
-        free(gb);
-        free(gk);
+        }
+        for (int j = 0; j < Dn; ++j) {
+            const double g = gk[j];
+            const float* w = c->W_dur + (size_t)j * d;
+            double* dw = dWd + (size_t)j * d;
+            for (int k = 0; k < d; ++k) {
+                gh[k] += g * (double)w[k];
+                dw[k] += g * h[k];
+            }
+        }
+        double* dd2 = ddec + (size_t)u * d;
+        for (int k = 0; k < d; ++k) {
+            const double gp = gh[k] * (1.0 - h[k] * h[k]);
+            de[k] += gp;
+            dd2[k] += gp;
+        }
     }
-#undef A
-#undef Bt
-#undef NI
-    free(lpb);
-    free(lpy);
-    free(lpd);
     free(h);
     free(lt);
     free(ld);
-    free(alpha);
-    free(beta);
+    free(gt);
+    free(gh);
+    free(gb);
+    free(gk);
 }
 
+#undef A
+#undef Bt
+#undef NI
+
+/* Utterances run one after another; inside an utterance the joint network and
+ * the gradients are spread over `workers` threads by frame. */
 static void run_transducer(tr_ctx* c, double* dW, double* dW_dur, int nthreads) {
-    int workers = nthreads < 1 ? 1 : nthreads;
-    if (workers > c->B) workers = c->B > 0 ? c->B : 1;
-    if (c->d_enc) {
+    const int workers = nthreads < 1 ? 1 : nthreads;
+    const int grads = c->d_enc != NULL;
+    double* dW_w = NULL;
+    double* dWd_w = NULL;
+    if (grads) {
         memset(c->d_enc, 0, sizeof(double) * (size_t)c->B * c->T * c->d);
         memset(c->d_dec, 0, sizeof(double) * (size_t)c->B * c->U * c->d);
-        c->dW_w = (double*)calloc((size_t)workers * c->V * c->d, sizeof(double));
-        c->dWd_w = c->n_dur > 0 ? (double*)calloc((size_t)workers * c->n_dur * c->d, sizeof(double)) : NULL;
+        dW_w = (double*)calloc((size_t)workers * c->V * c->d, sizeof(double));
+        dWd_w = c->n_dur > 0 ? (double*)calloc((size_t)workers * c->n_dur * c->d, sizeof(double)) : NULL;
     }
-    run_pool(transducer_utt, c, c->B, workers);
-    if (c->d_enc) {
+    for (int b = 0; b < c->B; ++b) {
+        utt_t s;
+        memset(&s, 0, sizeof(s));
+        s.c = c;
+        s.b = b;
+        s.Tb = c->in_lens[b];
+        s.Ub = c->tgt_lens[b] + 1;
+        s.y = c->targets + (size_t)b * c->S;
+        s.zk = -1;
+        for (int j = 0; j < c->n_dur; ++j)
+            if (c->durations[j] == 0) {
+                s.zk = j; /* first zero duration (tdt_reference.py:134-135) */
+                break;
+            }
+        const size_t nn = (size_t)s.Tb * s.Ub;
+        const int TR = c->n_dur > 0 ? s.Tb + 1 : s.Tb; /* TDT uses the (T_b+1)-frame grid */
+        s.lpb = (double*)malloc(sizeof(double) * nn);
+        s.lpy = (double*)malloc(sizeof(double) * nn);
+        s.lpd = c->n_dur > 0 ? (double*)malloc(sizeof(double) * nn * c->n_dur) : NULL;
+        s.alpha = (double*)malloc(sizeof(double) * (size_t)TR * s.Ub);
+        s.beta = (double*)malloc(sizeof(double) * (size_t)TR * s.Ub);
+        run_pool(edge_row, &s, s.Tb, workers);
+        recursions(&s);
+        c->log_prob[b] = s.logZ;
+        c->loss[b] = -s.logZ;
+        if (grads) {
+            s.dW_w = dW_w;
+            s.dWd_w = dWd_w;
+            s.ddec_w = (double*)calloc((size_t)workers * s.Ub * c->d, sizeof(double));
+            run_pool(grad_row, &s, s.Tb, workers);
+            double* dd = c->d_dec + (size_t)b * c->U * c->d;
+            for (int w = 0; w < workers; ++w)
+                for (size_t i = 0; i < (size_t)s.Ub * c->d; ++i) dd[i] += s.ddec_w[(size_t)w * s.Ub * c->d + i];
+            free(s.ddec_w);
+        }
+        free(s.lpb);
+        free(s.lpy);
+        free(s.lpd);
+        free(s.alpha);
+        free(s.beta);
+    }
+    if (grads) {
         const size_t nw = (size_t)c->V * c->d;
         for (size_t i = 0; i < nw; ++i) {
-            double s = 0.0;
-            for (int w = 0; w < workers; ++w) s += c->dW_w[(size_t)w * nw + i];
-            dW[i] = s;
+            double acc = 0.0;
+            for (int w = 0; w < workers; ++w) acc += dW_w[(size_t)w * nw + i];
+            dW[i] = acc;
         }
         if (c->n_dur > 0) {
             const size_t nd = (size_t)c->n_dur * c->d;
             for (size_t i = 0; i < nd; ++i) {
-                double s = 0.0;
-                for (int w = 0; w < workers; ++w) s += c->dWd_w[(size_t)w * nd + i];
-                dW_dur[i] = s;
+                double acc = 0.0;
+                for (int w = 0; w < workers; ++w) acc += dWd_w[(size_t)w * nd + i];
+                dW_dur[i] = acc;
             }
         }
-        free(c->dW_w);
-        free(c->dWd_w);
+        free(dW_w);
+        free(dWd_w);
     }
 }
 
