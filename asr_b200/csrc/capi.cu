@@ -99,6 +99,7 @@ extern "C" const char* asr_status_string(int status) {
         case ASR_ERR_WORKSPACE: return "workspace missing or too small";
         case ASR_ERR_UNSUPPORTED: return "shape outside the supported kernel range";
         case ASR_ERR_CUDA: return "CUDA launch or runtime error";
+        case ASR_ERR_SCRATCH_LIMIT: return "problem exceeds the fixed scratch of the allocation-free entry point";
         default: return "unknown status";
     }
 }

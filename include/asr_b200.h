@@ -39,7 +39,8 @@ typedef enum {
     ASR_ERR_INVALID_ARGUMENT = 1, /* a size/flag/pointer check failed on the host */
     ASR_ERR_WORKSPACE = 2,        /* workspace missing or smaller than *_workspace_bytes */
     ASR_ERR_UNSUPPORTED = 3,      /* shape outside the compiled kernel range (e.g. U > 512) */
-    ASR_ERR_CUDA = 4              /* a CUDA launch or runtime call failed */
+    ASR_ERR_CUDA = 4,             /* a CUDA launch or runtime call failed */
+    ASR_ERR_SCRATCH_LIMIT = 5     /* problem needs more than the fixed scratch of a *_noalloc entry point */
 } asr_status_t;
 
 /* Human-readable name of a status code. */
@@ -124,6 +125,26 @@ int asr_tdt_backward(const float* encoder, const float* decoder, const float* jo
                      const float* log_P_y, const float* log_P_dur, const float* log_prob, const float* grad_loss,
                      int tf32, float* grad_encoder, float* grad_decoder, float* grad_joint_W,
                      float* grad_joint_W_dur, void* workspace, size_t workspace_bytes, asr_stream_t stream);
+
+/* Bytes of the scratch array compiled into the library for asr_tdt_forward_noalloc. */
+#define ASR_TDT_FORWARD_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* asr_tdt_forward without a workspace argument, for callers that cannot allocate
+ * device memory (a bare FFI host with no device allocator, a service that reserves
+ * all GPU memory at start-up, code where a cudaMalloc would synchronise the device).
+ * No counterpart in the reference. Its scratch is a fixed array of
+ * ASR_TDT_FORWARD_NOALLOC_SCRATCH_BYTES in device memory, held by every GPU that
+ * loads the library; problems whose asr_tdt_workspace_bytes(..., backward = 0)
+ * exceed it return ASR_ERR_SCRATCH_LIMIT without launching anything. The first
+ * call on a device looks up the array's device address (make it before any stream
+ * capture). All calls share the array, so calls that overlap on the GPU race;
+ * serialise them. Allocates nothing. */
+int asr_tdt_forward_noalloc(const float* encoder, const float* decoder, const float* joint_W,
+                            const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                            const int32_t* tgt_lens, const int32_t* durations, int n_dur, int max_duration,
+                            int has_zero, int B, int T, int U, int V, int d, int S, int blank_idx, float sigma,
+                            int tf32, float* loss, double* alpha, float* log_P_blank, float* log_P_y,
+                            float* log_P_dur, float* log_prob, asr_stream_t stream);
 
 /* ----------------------------------------------------------- diagnostics */
 
