@@ -89,6 +89,7 @@ JointArgs make_args(const float* enc, const float* dec, const float* W, const fl
 }
 
 bool use_tc(int tf32, const JointArgs& a) { return tf32 != 0 && tc_supported(a); }
+bool use_tc_bwd(int tf32, const JointArgs& a) { return use_tc(tf32, a) && tc_backward_supported(a); }
 
 }  // namespace
 
@@ -117,7 +118,8 @@ extern "C" int asr_joint_path(int tf32, int V, int n_dur, int d) {
 extern "C" size_t asr_rnnt_workspace_bytes(int B, int T, int U, int V, int d, int tf32, int backward) {
     if (bad_dims(B, T, U, V, d)) return 0;
     JointArgs a = make_args(nullptr, nullptr, nullptr, nullptr, nullptr, B, T, U, V, 0, d, U - 1, 0, 0.f);
-    return tr_workspace_bytes(a, node_capacity(B, T, U), use_tc(tf32, a), backward != 0);
+    return tr_workspace_bytes(a, node_capacity(B, T, U), backward ? use_tc_bwd(tf32, a) : use_tc(tf32, a),
+                              backward != 0);
 }
 
 extern "C" int asr_rnnt_forward(const float* encoder, const float* decoder, const float* joint_W,
@@ -166,7 +168,7 @@ extern "C" int asr_rnnt_backward(const float* encoder, const float* decoder, con
     if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
     JointArgs a = make_args(encoder, decoder, joint_W, nullptr, targets, B, T, U, V, 0, d, S, blank_idx, 0.f);
     const int64_t cap = node_capacity(B, T, U);
-    const bool tc = use_tc(tf32, a);
+    const bool tc = use_tc_bwd(tf32, a);
     if (!workspace || workspace_bytes < tr_workspace_bytes(a, cap, tc, true)) return ASR_ERR_WORKSPACE;
     TrWorkspace w = carve(workspace, a, cap, tc, true);
     a.m = w.meta;
@@ -194,7 +196,8 @@ bool bad_tdt(int n_dur, int max_duration) {
 extern "C" size_t asr_tdt_workspace_bytes(int B, int T, int U, int V, int n_dur, int d, int tf32, int backward) {
     if (bad_dims(B, T, U, V, d) || n_dur < 1) return 0;
     JointArgs a = make_args(nullptr, nullptr, nullptr, nullptr, nullptr, B, T, U, V, n_dur, d, U - 1, 0, 0.f);
-    return tr_workspace_bytes(a, node_capacity(B, T, U), use_tc(tf32, a), backward != 0);
+    return tr_workspace_bytes(a, node_capacity(B, T, U), backward ? use_tc_bwd(tf32, a) : use_tc(tf32, a),
+                              backward != 0);
 }
 
 extern "C" int asr_tdt_forward(const float* encoder, const float* decoder, const float* joint_W,
@@ -254,7 +257,7 @@ extern "C" int asr_tdt_backward(const float* encoder, const float* decoder, cons
     JointArgs a = make_args(encoder, decoder, joint_W, joint_W_dur, targets, B, T, U, V, n_dur, d, S, blank_idx,
                             0.f);
     const int64_t cap = node_capacity(B, T, U);
-    const bool tc = use_tc(tf32, a);
+    const bool tc = use_tc_bwd(tf32, a);
     if (!workspace || workspace_bytes < tr_workspace_bytes(a, cap, tc, true)) return ASR_ERR_WORKSPACE;
     TrWorkspace w = carve(workspace, a, cap, tc, true);
     a.m = w.meta;

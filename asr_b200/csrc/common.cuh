@@ -38,7 +38,21 @@ __device__ __forceinline__ double lae_d(double a, double b) {
     const double m = fmax(a, b);
     if (m == -INFINITY) return -INFINITY;
     const float d = (float)(fmin(a, b) - m);
-    return m + (double)log1pf(__expf(d));
+    return m + (double)__logf(1.f + __expf(d));
+}
+
+// Running log-sum-exp of float64 terms: max first, then one exp per term and a
+// single log (the terms of one lattice node are all known before the sum).
+template <int N>
+__device__ __forceinline__ double lse_d(const double (&x)[N]) {
+    double m = x[0];
+#pragma unroll
+    for (int i = 1; i < N; ++i) m = fmax(m, x[i]);
+    if (m <= -1e29) return m;  // every term is the finite log-zero sentinel
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) s += __expf((float)(x[i] - m));
+    return m + (double)__logf(s);
 }
 
 // Per-batch lattice bookkeeping produced by lattice_prep_kernel.

@@ -15,6 +15,25 @@ inline int dp_lanes_k(int U) {
     return 0;
 }
 
+// ---- asynchronous shared-memory prefetch of the next diagonal's lattice weights
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Waits until at most one committed group (the newest prefetch) is still in flight.
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 // Largest supported max_duration of the TDT recursions.
 constexpr int kTdtMaxDuration = 16;
 // Largest supported number of duration classes.

@@ -7,21 +7,51 @@
 // one step earlier and (t, u-1) is the left register, or the left lane's last
 // register for the block head (one shuffle per diagonal). The warp never
 // synchronises with other warps, so T_b + U_b - 1 short steps bound the latency
-// and many utterances run concurrently on every SM.
+// and many utterances run concurrently on every SM. The next diagonal's edge
+// log-probs (and alpha, backward) are prefetched into shared memory with
+// cp.async while the current one computes.
 #include "dp.cuh"
 
 namespace asr {
 namespace {
 
-constexpr int kDpWarps = 4;
+// Utterances (warps) per block: fewer for wide label blocks so the static
+// prefetch buffers stay under 48 KB.
+template <int K>
+constexpr int warps_per_block() {
+    return K >= 16 ? 1 : (K >= 8 ? 2 : 4);
+}
+
+// Next-diagonal prefetch: [slot][j][{blank, label}][lane] floats, plus alpha
+// (backward) as [slot][j][lane] doubles.
+template <int K>
+__device__ __forceinline__ void rnnt_prefetch(float* wb, double* ab, int g, int lane, int Tb, int Ub, int off,
+                                              const float* lpb, const float* lpy, const double* alpha) {
+    const int slot = g & 1;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        const int u = lane * K + j, t = g - u;
+        if (u < Ub && t >= 0 && t < Tb) {
+            const int n = off + t * Ub + u;
+            float* dst = wb + ((slot * K + j) * 2) * 32 + lane;
+            cp_async4(dst, lpb + n);
+            cp_async4(dst + 32, lpy + n);
+            if (ab) cp_async8(ab + (slot * K + j) * 32 + lane, alpha + n);
+        }
+    }
+    cp_async_commit();
+}
 
 template <int K>
-__global__ void __launch_bounds__(32 * kDpWarps)
+__global__ void __launch_bounds__(32 * warps_per_block<K>())
     rnnt_alpha_kernel(LatticeMeta m, int B, const float* __restrict__ lpb, const float* __restrict__ lpy,
                       double* __restrict__ alpha, float* __restrict__ log_prob, float* __restrict__ loss) {
+    __shared__ float wbuf_all[warps_per_block<K>()][2 * K * 2 * 32];
     const int lane = threadIdx.x & 31;
-    const int b = blockIdx.x * kDpWarps + (threadIdx.x >> 5);
+    const int warp = threadIdx.x >> 5;
+    const int b = blockIdx.x * warps_per_block<K>() + warp;
     if (b >= B) return;
+    float* wb = wbuf_all[warp];
     const int Tb = m.Tb[b], Ub = m.Ub[b], off = m.off[b];
     // hb / hy: alpha + edge log-prob of the node this register held on the previous
     // diagonal (outgoing blank / label value), kNeg when that node was not in the lattice.
@@ -29,7 +59,14 @@ __global__ void __launch_bounds__(32 * kDpWarps)
 #pragma unroll
     for (int j = 0; j < K; ++j) hb[j] = hy[j] = kNeg;
     const int last = Tb + Ub - 2;
+    rnnt_prefetch<K>(wb, nullptr, 0, lane, Tb, Ub, off, lpb, lpy, nullptr);
     for (int g = 0; g <= last; ++g) {
+        if (g < last)
+            rnnt_prefetch<K>(wb, nullptr, g + 1, lane, Tb, Ub, off, lpb, lpy, nullptr);
+        else
+            cp_async_commit();
+        cp_async_wait_prev();
+        __syncwarp();
         double left = __shfl_up_sync(0xffffffffu, hy[K - 1], 1);
         if (lane == 0) left = kNeg;
         double nb[K], ny[K];
@@ -41,7 +78,8 @@ __global__ void __launch_bounds__(32 * kDpWarps)
                 const double from_label = (j > 0) ? hy[j > 0 ? j - 1 : 0] : left;
                 const double a = (t == 0 && u == 0) ? 0.0 : lae_d(hb[j], from_label);
                 const int n = off + t * Ub + u;
-                const float lb = lpb[n], ly = lpy[n];
+                const float* w = wb + (((g & 1) * K + j) * 2) * 32 + lane;
+                const float lb = w[0], ly = w[32];
                 alpha[n] = a;
                 nb[j] = a + lb;
                 ny[j] = a + ly;
@@ -51,6 +89,7 @@ __global__ void __launch_bounds__(32 * kDpWarps)
                 }
             }
         }
+        __syncwarp();
 #pragma unroll
         for (int j = 0; j < K; ++j) {
             hb[j] = nb[j];
@@ -62,13 +101,18 @@ __global__ void __launch_bounds__(32 * kDpWarps)
 // Writes cb = grad_loss * blank posterior and ct = grad_loss * label posterior per
 // node. log P(y|x) is recomputed from the float64 forward variable.
 template <int K>
-__global__ void __launch_bounds__(32 * kDpWarps)
+__global__ void __launch_bounds__(32 * warps_per_block<K>())
     rnnt_beta_kernel(LatticeMeta m, int B, const float* __restrict__ lpb, const float* __restrict__ lpy,
                      const double* __restrict__ alpha, const float* __restrict__ grad_loss, float* __restrict__ cb,
                      float* __restrict__ ct) {
+    __shared__ float wbuf_all[warps_per_block<K>()][2 * K * 2 * 32];
+    __shared__ double abuf_all[warps_per_block<K>()][2 * K * 32];
     const int lane = threadIdx.x & 31;
-    const int b = blockIdx.x * kDpWarps + (threadIdx.x >> 5);
+    const int warp = threadIdx.x >> 5;
+    const int b = blockIdx.x * warps_per_block<K>() + warp;
     if (b >= B) return;
+    float* wb = wbuf_all[warp];
+    double* ab = abuf_all[warp];
     const int Tb = m.Tb[b], Ub = m.Ub[b], off = m.off[b];
     const int nterm = off + (Tb - 1) * Ub + Ub - 1;
     const double logZ = alpha[nterm] + lpb[nterm];
@@ -76,7 +120,15 @@ __global__ void __launch_bounds__(32 * kDpWarps)
     double bn[K];  // beta of the node this register held on diagonal g+1, i.e. (t+1, u)
 #pragma unroll
     for (int j = 0; j < K; ++j) bn[j] = kNeg;
-    for (int g = Tb + Ub - 2; g >= 0; --g) {
+    const int first = Tb + Ub - 2;
+    rnnt_prefetch<K>(wb, ab, first, lane, Tb, Ub, off, lpb, lpy, alpha);
+    for (int g = first; g >= 0; --g) {
+        if (g > 0)
+            rnnt_prefetch<K>(wb, ab, g - 1, lane, Tb, Ub, off, lpb, lpy, alpha);
+        else
+            cp_async_commit();
+        cp_async_wait_prev();
+        __syncwarp();
         double right = __shfl_down_sync(0xffffffffu, bn[0], 1);  // (t, u+1) for the block tail
         if (lane == 31) right = kNeg;
         double nbeta[K];
@@ -86,8 +138,9 @@ __global__ void __launch_bounds__(32 * kDpWarps)
             nbeta[j] = kNeg;
             if (u < Ub && t >= 0 && t < Tb) {
                 const int n = off + t * Ub + u;
-                const float lb = lpb[n], ly = lpy[n];
-                const double a = alpha[n];
+                const float* w = wb + (((g & 1) * K + j) * 2) * 32 + lane;
+                const float lb = w[0], ly = w[32];
+                const double a = ab[((g & 1) * K + j) * 32 + lane];
                 const double b_t1 = bn[j];
                 const double b_u1 = (j + 1 < K) ? bn[j + 1 < K ? j + 1 : 0] : right;
                 const bool term = (t == Tb - 1) && (u == Ub - 1);
@@ -102,6 +155,7 @@ __global__ void __launch_bounds__(32 * kDpWarps)
                 ct[n] = gl * tp;
             }
         }
+        __syncwarp();
 #pragma unroll
         for (int j = 0; j < K; ++j) bn[j] = nbeta[j];
     }
@@ -111,7 +165,7 @@ template <int K>
 int launch_rnnt_alpha_k(const LatticeMeta& m, int B, const float* lpb, const float* lpy, double* alpha, float* lp,
                         float* loss, cudaStream_t st) {
     KernelTimer kt("rnnt_alpha", st);
-    rnnt_alpha_kernel<K><<<(B + kDpWarps - 1) / kDpWarps, 32 * kDpWarps, 0, st>>>(m, B, lpb, lpy, alpha, lp, loss);
+    rnnt_alpha_kernel<K><<<(B + warps_per_block<K>() - 1) / warps_per_block<K>(), 32 * warps_per_block<K>(), 0, st>>>(m, B, lpb, lpy, alpha, lp, loss);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
@@ -120,7 +174,7 @@ template <int K>
 int launch_rnnt_beta_k(const LatticeMeta& m, int B, const float* lpb, const float* lpy, const double* alpha,
                        const float* gl, float* cb, float* ct, cudaStream_t st) {
     KernelTimer kt("rnnt_beta_posteriors", st);
-    rnnt_beta_kernel<K><<<(B + kDpWarps - 1) / kDpWarps, 32 * kDpWarps, 0, st>>>(m, B, lpb, lpy, alpha, gl, cb, ct);
+    rnnt_beta_kernel<K><<<(B + warps_per_block<K>() - 1) / warps_per_block<K>(), 32 * warps_per_block<K>(), 0, st>>>(m, B, lpb, lpy, alpha, gl, cb, ct);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
