@@ -132,7 +132,7 @@ extern "C" int asr_rnnt_forward(const float* encoder, const float* decoder, cons
     if (!encoder || !decoder || !joint_W || !in_lens || !tgt_lens || !loss || !alpha || !log_P_blank || !log_P_y ||
         !log_prob || (S > 0 && !targets))
         return ASR_ERR_INVALID_ARGUMENT;
-    if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
+    if (U > kMaxLabelPositions) return ASR_ERR_UNSUPPORTED;
     JointArgs a = make_args(encoder, decoder, joint_W, nullptr, targets, B, T, U, V, 0, d, S, blank_idx, 0.f);
     const int64_t cap = node_capacity(B, T, U);
     const bool tc = use_tc(tf32, a);
@@ -165,7 +165,7 @@ extern "C" int asr_rnnt_backward(const float* encoder, const float* decoder, con
     if (!encoder || !decoder || !joint_W || !in_lens || !tgt_lens || !alpha || !log_P_blank || !log_P_y ||
         !log_prob || !grad_loss || !grad_encoder || !grad_decoder || (S > 0 && !targets))
         return ASR_ERR_INVALID_ARGUMENT;
-    if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
+    if (U > kMaxLabelPositions) return ASR_ERR_UNSUPPORTED;
     JointArgs a = make_args(encoder, decoder, joint_W, nullptr, targets, B, T, U, V, 0, d, S, blank_idx, 0.f);
     const int64_t cap = node_capacity(B, T, U);
     const bool tc = use_tc_bwd(tf32, a);
@@ -213,7 +213,7 @@ extern "C" int asr_tdt_forward(const float* encoder, const float* decoder, const
     if (!encoder || !decoder || !joint_W || !joint_W_dur || !durations || !in_lens || !tgt_lens || !loss ||
         !alpha || !log_P_blank || !log_P_y || !log_P_dur || !log_prob || (S > 0 && !targets))
         return ASR_ERR_INVALID_ARGUMENT;
-    if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
+    if (U > kMaxLabelPositions) return ASR_ERR_UNSUPPORTED;
     JointArgs a = make_args(encoder, decoder, joint_W, joint_W_dur, targets, B, T, U, V, n_dur, d, S, blank_idx,
                             sigma);
     const int64_t cap = node_capacity(B, T, U);
@@ -253,7 +253,7 @@ extern "C" int asr_tdt_backward(const float* encoder, const float* decoder, cons
         !log_P_blank || !log_P_y || !log_P_dur || !log_prob || !grad_loss || !grad_encoder || !grad_decoder ||
         (S > 0 && !targets))
         return ASR_ERR_INVALID_ARGUMENT;
-    if (dp_lanes_k(U) == 0) return ASR_ERR_UNSUPPORTED;
+    if (U > kMaxLabelPositions) return ASR_ERR_UNSUPPORTED;
     JointArgs a = make_args(encoder, decoder, joint_W, joint_W_dur, targets, B, T, U, V, n_dur, d, S, blank_idx,
                             0.f);
     const int64_t cap = node_capacity(B, T, U);

@@ -5,15 +5,9 @@
 
 namespace asr {
 
-// Label positions per lane for a warp that covers U positions (U <= 512).
-inline int dp_lanes_k(int U) {
-    if (U <= 32) return 1;
-    if (U <= 64) return 2;
-    if (U <= 128) return 4;
-    if (U <= 256) return 8;
-    if (U <= 512) return 16;
-    return 0;
-}
+// Largest label axis (U = max target length + 1) the recursions support: one
+// thread per label position in a CTA.
+constexpr int kMaxLabelPositions = 1024;
 
 // ---- asynchronous shared-memory prefetch of the next diagonal's lattice weights
 

@@ -304,7 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* er = P.a.enc + eo;
             const float* dr = P.a.dec + dofs;
             for (int kc = 0; kc < g.kchunks; ++kc) {
-                if (it > 0 && !mbar_wait(&sm.a_empty[kc], (it - 1) & 1, err, 7)) {
+                // warp-uniform outcome: lanes must not leave the loop separately
+                const bool got = __all_sync(0xffffffffu, it == 0 || mbar_wait(&sm.a_empty[kc], (it - 1) & 1, err, 7));
+                if (!got) {
                     ok = false;
                     break;
                 }
@@ -341,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     w.z = pack_bf16(h[8 * q + 4], h[8 * q + 5]);
                     w.w = pack_bf16(h[8 * q + 6], h[8 * q + 7]);
                     *reinterpret_cast<uint4*>(arow + ((u ^ (r & 7)) << 4)) = w;
-                    if (kBwd && valid) *reinterpret_cast<uint4*>(P.H + (int64_t)(n - begin) * g.kpad + kbase + 8 * q) = w;
+                    if (kBwd) *reinterpret_cast<uint4*>(P.H + (int64_t)(n - begin) * g.kpad + kbase + 8 * q) = w;
                 }
                 fence_async_smem();
                 __syncwarp();
@@ -380,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int col, width;
                 chunk_of(g, j, col, width);
                 const uint32_t buf = q & 1;
-                if (!mbar_wait(&sm.t_full[buf], (q >> 1) & 1, err, 8)) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&sm.t_full[buf], (q >> 1) & 1, err, 8))) {
                     ok = false;
                     break;
                 }
@@ -425,14 +427,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 }
                             }
                         }
-                    } else if (valid) {
+                    } else {
+                        // rows past the pass end are written as zeros: dW contracts over rows
                         const float Pn = cb + ct;
                         float gv[16];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             const int c = c0 + i;
                             float x = 0.f;
-                            if (c < a.V) {
+                            if (!valid) {
+                            } else if (c < a.V) {
                                 x = __expf(v[i] - lse) * Pn;
                                 if (c == a.blank) x -= cb;
                                 if (c == y) x -= ct;
@@ -597,10 +601,650 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, void* scratch, si
     return ASR_OK;
 }
 
-bool tc_backward_supported(const JointArgs&) { return false; }
-size_t tc_backward_scratch_bytes(const JointArgs&, int) { return 0; }
-int tc_joint_backward(const JointArgs&, const JointBwdIn&, const JointBwdOut&, int, void*, size_t, cudaStream_t) {
-    return ASR_ERR_UNSUPPORTED;
+// =================================================================== backward
+//
+// Per pass of nodes [s, e) (pass bounds fall on band boundaries, computed on the
+// device): the dlogits kernel above writes G = d loss / d logits (bf16, rows of
+// the pass) and H = hidden (bf16); then
+//   dH  kernel: per band (kBandT frames x all labels of one utterance) and
+//               128-wide slice of the hidden dimension, D = G * Wf^T (M = 128
+//               nodes, N = 128, K = vocabulary) in TMEM; the epilogue applies
+//               tanh' = 1 - h^2 and reduces the band: d_enc rows (one per frame)
+//               with warp segmented scans into shared memory and one exclusive
+//               store per element, d_dec rows with shared-memory atomics and one
+//               global atomic per element per band;
+//   dW  kernel: split-K over the pass rows, D = G^T H (M = 128 vocabulary rows,
+//               N = 320 hidden columns, both operands MN-major straight from G
+//               and H), added to dW / dW_dur once per CTA.
+
+namespace {
+
+constexpr int kBandT = 64;        // frames per band of the dH reduction
+constexpr int kDhN = 128;         // hidden columns per dH work item (UMMA N)
+constexpr int kDwM = 128;         // vocabulary rows per dW work item (UMMA M)
+constexpr int kDwN = 320;         // hidden columns per dW work item (UMMA N = 256 + 64)
+constexpr int kBwdThreads = 192;  // TMA, MMA, 4 epilogue warps
+constexpr int kDhStageBytes = 2 * kBM * kAK * 2;            // A (128 x 64) + B (128 x 64), 32 KB
+constexpr int kDwStageBytes = (2 + kDwN / 64) * 64 * 64 * 2;  // 2 + 5 boxes of 64 x 64, 56 KB
+constexpr int64_t kMaxPassNodes = 4 << 20;
+
+__device__ __forceinline__ void named_sync_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Bands: utterance b has ceil(T_b / kBandT); boff is their exclusive prefix sum.
+__global__ void band_prep_kernel(LatticeMeta m, int B, int32_t* __restrict__ boff) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    int acc = 0;
+    for (int b = 0; b < B; ++b) {
+        boff[b] = acc;
+        acc += (m.Tb[b] + kBandT - 1) / kBandT;
+    }
+    boff[B] = acc;
+}
+
+// bounds[p] = start of pass p, rounded down to a band boundary; pbands[p] = its band index.
+__global__ void plan_passes_kernel(LatticeMeta m, int B, const int32_t* __restrict__ boff, int P, int64_t step,
+                                   int32_t* __restrict__ bounds, int32_t* __restrict__ pbands) {
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p > P) return;
+    const int N = total_nodes(m, B);
+    const int64_t x = (p == P) ? N : std::min<int64_t>((int64_t)p * step, N);
+    if (x >= N) {
+        bounds[p] = N;
+        pbands[p] = boff[B];
+        return;
+    }
+    const int b = find_utt(m.off, B, (int)x);
+    const int bs = kBandT * m.Ub[b];
+    const int j = ((int)x - m.off[b]) / bs;
+    bounds[p] = m.off[b] + j * bs;
+    pbands[p] = boff[b] + j;
+}
+
+struct BandInfo {
+    int b, t0, nt, Ub, r0, r1;  // utterance, first frame, frames, label positions, pass rows [r0, r1)
+};
+
+__device__ __forceinline__ BandInfo band_info(const LatticeMeta& m, int B, const int32_t* boff, int band, int s) {
+    BandInfo bi;
+    int lo = 0, hi = B - 1;  // utterance owning `band`
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (boff[mid] <= band)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    bi.b = lo;
+    const int j = band - boff[lo];
+    const int Tb = m.Tb[lo];
+    bi.Ub = m.Ub[lo];
+    bi.t0 = j * kBandT;
+    bi.nt = min(kBandT, Tb - bi.t0);
+    const int n0 = m.off[lo] + bi.t0 * bi.Ub;
+    bi.r0 = n0 - s;
+    bi.r1 = n0 + bi.nt * bi.Ub - s;
+    return bi;
+}
+
+struct DhParams {
+    JointArgs a;
+    Geom g;
+    const __nv_bfloat16* H;
+    const int32_t* bounds;
+    const int32_t* pbands;
+    const int32_t* boff;
+    int pass;
+    int stages;
+    int sdec_rows;  // label rows of the shared d_dec partial (0: global atomics)
+    float* d_enc;
+    float* d_dec;
+    int* err;
+};
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    tc_dh_kernel(const __grid_constant__ CUtensorMap map_g, const __grid_constant__ CUtensorMap map_wt, DhParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const JointArgs& a = P.a;
+    const int S = P.stages;
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stages = base;
+    float* senc = reinterpret_cast<float*>(stages + (size_t)S * kDhStageBytes);   // [kBandT][kDhN + 1]
+    float* sdec = senc + kBandT * (kDhN + 1);                                    // [sdec_rows][kDhN + 1]
+    // the partials are (rows x 129) floats: realign for the 8-byte mbarriers
+    uint64_t* bars = reinterpret_cast<uint64_t*>(
+        (reinterpret_cast<uintptr_t>(sdec + (size_t)P.sdec_rows * (kDhN + 1)) + 15) & ~uintptr_t(15));
+    uint64_t* b_full = bars;
+    uint64_t* b_empty = bars + S;
+    uint64_t* t_full = bars + 2 * S;
+    uint64_t* t_empty = t_full + 2;
+    uint64_t* done = t_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    int* err = P.err;
+
+    const int s = P.bounds[P.pass], e = P.bounds[P.pass + 1];
+    const int band0 = P.pbands[P.pass], nbands = P.pbands[P.pass + 1] - band0;
+    const int ndt = (P.g.kpad + kDhN - 1) / kDhN;  // the last slice may extend past kpad (zero weights)
+    const int items = e > s ? nbands * ndt : 0;
+    const int kchunks = (P.g.vpad + kAK - 1) / kAK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&t_full[i], 1);
+            mbar_init(&t_empty[i], 4);
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&map_g);
+        prefetch_tensormap(&map_wt);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool issued[8] = {};
+            uint32_t ipar[8] = {};
+            bool ok = true;
+            for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+                const BandInfo bi = band_info(a.m, a.B, P.boff, band0 + w / ndt, s);
+                const int dt = w % ndt;
+                for (int r = bi.r0; ok && r < bi.r1; r += kBM) {
+                    for (int kc = 0; kc < kchunks; ++kc) {
+                        if (!mbar_wait(&b_empty[stage], phase ^ 1, err, 11)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* st = stages + (size_t)stage * kDhStageBytes;
+                        mbar_arrive_expect_tx(&b_full[stage], kDhStageBytes);
+                        tma_load_2d(st, &map_g, kc * kAK, r, &b_full[stage]);
+                        tma_load_2d(st + kBM * kAK * 2, &map_wt, kc * kAK, dt * kDhN, &b_full[stage]);
+                        issued[stage] = true;
+                        ipar[stage] = phase;
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+            }
+            for (int i = 0; i < S; ++i)
+                if (issued[i]) mbar_wait(&b_full[i], ipar[i], err, 12);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16(kBM, kDhN, false, false);
+            const uint32_t sbase = smem_u32(stages);
+            int stage = 0;
+            uint32_t phase = 0, q = 0;
+            bool ok = true;
+            for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+                const BandInfo bi = band_info(a.m, a.B, P.boff, band0 + w / ndt, s);
+                for (int r = bi.r0; ok && r < bi.r1; r += kBM, ++q) {
+                    const uint32_t buf = q & 1;
+                    if (!mbar_wait(&t_empty[buf], ((q >> 1) & 1) ^ 1, err, 13)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int kc = 0; kc < kchunks; ++kc) {
+                        if (!mbar_wait(&b_full[stage], phase, err, 14)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t st = sbase + stage * kDhStageBytes;
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_bf16(tmem_base + buf * kDhN, desc_k128(st + kk * 32),
+                                     desc_k128(st + kBM * kAK * 2 + kk * 32), idesc, (kc | kk) != 0 ? 1u : 0u);
+                        mma_commit(&b_empty[stage]);
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (ok) mma_commit(&t_full[buf]);
+                }
+            }
+            mma_commit(done);
+            mbar_wait(done, 0, err, 15);
+        }
+    } else {
+        // ------------------------------------------------------------------- epilogue
+        const int et = threadIdx.x - 64;  // 0..127
+        const int lane_base = 32 * (warp & 3);
+        const int row_in_tile = lane_base + lane;
+        const int SD = kDhN + 1;
+        uint32_t q = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; w < items; w += gridDim.x) {
+            const BandInfo bi = band_info(a.m, a.B, P.boff, band0 + w / ndt, s);
+            const int dt = w % ndt;
+            const bool use_sdec = bi.Ub <= P.sdec_rows;
+            for (int i = et; i < bi.nt * SD; i += 128) senc[i] = 0.f;
+            if (use_sdec)
+                for (int i = et; i < bi.Ub * SD; i += 128) sdec[i] = 0.f;
+            named_sync_epilogue();
+            for (int r = bi.r0; r < bi.r1; r += kBM, ++q) {
+                const uint32_t buf = q & 1;
+                if (ok && !__all_sync(0xffffffffu, mbar_wait(&t_full[buf], (q >> 1) & 1, err, 16))) ok = false;
+                tc_fence_after();
+                const int row = r + row_in_tile;
+                const bool valid = ok && row < bi.r1;
+                int tr = -1, u = 0;
+                if (valid) {
+                    const int rel = row - bi.r0;
+                    tr = rel / bi.Ub;
+                    u = rel - tr * bi.Ub;
+                }
+                // segmented-scan neighbours over equal frame index (rows of one frame are contiguous)
+                bool same[5];
+#pragma unroll
+                for (int sft = 0; sft < 5; ++sft) {
+                    const int ko = __shfl_up_sync(0xffffffffu, tr, 1 << sft);
+                    same[sft] = lane >= (1 << sft) && ko == tr;
+                }
+                const int kn = __shfl_down_sync(0xffffffffu, tr, 1);
+                const bool tail = valid && (lane == 31 || kn != tr);
+                const __nv_bfloat16* hrow = P.H + (int64_t)(valid ? row : 0) * P.g.kpad + dt * kDhN;
+                const int64_t dec_row = ((int64_t)bi.b * a.U + u) * a.d + dt * kDhN;
+                const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + buf * kDhN;
+                for (int gi = 0; gi < kDhN / 16; ++gi) {
+                    float acc[16];
+                    if (ok) tmem_ld16(taddr + gi * 16, acc);
+                    float gp[16];
+                    if (valid && dt * kDhN + gi * 16 < P.g.kpad) {
+                        const uint4 h0 = *reinterpret_cast<const uint4*>(hrow + gi * 16);
+                        const uint4 h1 = *reinterpret_cast<const uint4*>(hrow + gi * 16 + 8);
+                        const __nv_bfloat162* hv0 = reinterpret_cast<const __nv_bfloat162*>(&h0);
+                        const __nv_bfloat162* hv1 = reinterpret_cast<const __nv_bfloat162*>(&h1);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float2 x0 = __bfloat1622float2(hv0[i]);
+                            const float2 x1 = __bfloat1622float2(hv1[i]);
+                            gp[2 * i] = acc[2 * i] * (1.f - x0.x * x0.x);
+                            gp[2 * i + 1] = acc[2 * i + 1] * (1.f - x0.y * x0.y);
+                            gp[8 + 2 * i] = acc[8 + 2 * i] * (1.f - x1.x * x1.x);
+                            gp[8 + 2 * i + 1] = acc[8 + 2 * i + 1] * (1.f - x1.y * x1.y);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) gp[i] = 0.f;
+                    }
+                    // d_dec: rows of one label position are U_b apart; shared (or global) atomics
+                    if (valid) {
+                        if (use_sdec) {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) atomicAdd(&sdec[u * SD + gi * 16 + i], gp[i]);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                if (dt * kDhN + gi * 16 + i < a.d) atomicAdd(P.d_dec + dec_row + gi * 16 + i, gp[i]);
+                        }
+                    }
+                    // d_enc: segmented sums over the rows of one frame, one shared atomic per segment
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float v = gp[i];
+#pragma unroll
+                        for (int sft = 0; sft < 5; ++sft) {
+                            const float o = __shfl_up_sync(0xffffffffu, v, 1 << sft);
+                            if (same[sft]) v += o;
+                        }
+                        if (tail) atomicAdd(&senc[tr * SD + gi * 16 + i], v);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&t_empty[buf]);
+            }
+            named_sync_epilogue();
+            // flush the band: d_enc rows are exclusive to this work item, d_dec rows are shared
+            const int kb = dt * kDhN;
+            for (int i = et; i < bi.nt * kDhN; i += 128) {
+                const int tr = i / kDhN, c = i - tr * kDhN;
+                if (kb + c < a.d) P.d_enc[((int64_t)bi.b * a.T + bi.t0 + tr) * a.d + kb + c] = senc[tr * SD + c];
+            }
+            if (use_sdec)
+                for (int i = et; i < bi.Ub * kDhN; i += 128) {
+                    const int uu = i / kDhN, c = i - uu * kDhN;
+                    if (kb + c < a.d) atomicAdd(P.d_dec + ((int64_t)bi.b * a.U + uu) * a.d + kb + c, sdec[uu * SD + c]);
+                }
+            named_sync_epilogue();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, 256);
+}
+
+struct DwParams {
+    JointArgs a;
+    Geom g;
+    const int32_t* bounds;
+    int pass;
+    int splits;
+    float* dW;
+    float* dWd;
+    int* err;
+};
+
+constexpr int kDwStages = 3;
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    tc_dw_kernel(const __grid_constant__ CUtensorMap map_g, const __grid_constant__ CUtensorMap map_h, DwParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stages + (size_t)kDwStages * kDwStageBytes);
+    uint64_t* b_full = bars;
+    uint64_t* b_empty = bars + kDwStages;
+    uint64_t* t_full = bars + 2 * kDwStages;
+    uint64_t* done = t_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    int* err = P.err;
+
+    const int nvt = (P.g.vpad + kDwM - 1) / kDwM;
+    const int nkt = (P.g.kpad + kDwN - 1) / kDwN;
+    const int item = blockIdx.x;
+    const int split = item % P.splits;
+    const int kt = (item / P.splits) % nkt;
+    const int vt = item / (P.splits * nkt);
+    const int s = P.bounds[P.pass], e = P.bounds[P.pass + 1];
+    const int rows = e > s ? (e - s + 63) / 64 * 64 : 0;  // zero rows pad the pass to 64
+    const int per = ((rows / 64 + P.splits - 1) / P.splits) * 64;
+    const int r0 = split * per, r1 = min(rows, r0 + per);
+    const int nsteps = (vt < nvt && r1 > r0) ? (r1 - r0) / 64 : 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDwStages; ++i) {
+            mbar_init(&b_full[i], 1);
+            mbar_init(&b_empty[i], 1);
+        }
+        mbar_init(t_full, 1);
+        mbar_init(done, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&map_g);
+        prefetch_tensormap(&map_h);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    constexpr int kBox = 64 * 64 * 2;  // one 64 x 64 bf16 TMA box
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool issued[kDwStages] = {};
+            uint32_t ipar[kDwStages] = {};
+            for (int i = 0; i < nsteps; ++i) {
+                if (!mbar_wait(&b_empty[stage], phase ^ 1, err, 21)) break;
+                uint8_t* st = stages + (size_t)stage * kDwStageBytes;
+                const int r = r0 + i * 64;
+                mbar_arrive_expect_tx(&b_full[stage], kDwStageBytes);
+                tma_load_2d(st, &map_g, vt * kDwM, r, &b_full[stage]);
+                tma_load_2d(st + kBox, &map_g, vt * kDwM + 64, r, &b_full[stage]);
+#pragma unroll
+                for (int j = 0; j < kDwN / 64; ++j)
+                    tma_load_2d(st + (2 + j) * kBox, &map_h, kt * kDwN + j * 64, r, &b_full[stage]);
+                issued[stage] = true;
+                ipar[stage] = phase;
+                if (++stage == kDwStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            for (int i = 0; i < kDwStages; ++i)
+                if (issued[i]) mbar_wait(&b_full[i], ipar[i], err, 22);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t id256 = idesc_bf16(kDwM, 256, true, true);
+            const uint32_t id64 = idesc_bf16(kDwM, 64, true, true);
+            const uint32_t sbase = smem_u32(stages);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int i = 0; i < nsteps; ++i) {
+                if (!mbar_wait(&b_full[stage], phase, err, 23)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = sbase + stage * kDwStageBytes;
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {  // 16 rows (K) per MMA
+                    const uint64_t ad = desc_mn128(st + ks * 2048, kBox);
+                    const uint64_t b0 = desc_mn128(st + 2 * kBox + ks * 2048, kBox);
+                    const uint64_t b1 = desc_mn128(st + 6 * kBox + ks * 2048, kBox);
+                    const uint32_t acc = (i | ks) != 0 ? 1u : 0u;
+                    mma_bf16(tmem_base, ad, b0, id256, acc);
+                    mma_bf16(tmem_base + 256, ad, b1, id64, acc);
+                }
+                mma_commit(&b_empty[stage]);
+                if (++stage == kDwStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            if (ok) mma_commit(t_full);
+            mma_commit(done);
+            mbar_wait(done, 0, err, 24);
+        }
+    } else if (nsteps > 0) {
+        // --------------------------------------------------------------- epilogue
+        const int lane_base = 32 * (warp & 3);
+        const int v = vt * kDwM + lane_base + lane;
+        const JointArgs& a = P.a;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(t_full, 0, err, 25));
+        tc_fence_after();
+        if (ok) {
+            float* dst = nullptr;
+            if (v < a.V)
+                dst = P.dW + (int64_t)v * a.d;
+            else if (v < a.V + a.n_dur)
+                dst = P.dWd + (int64_t)(v - a.V) * a.d;
+            const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16);
+            for (int gi = 0; gi < kDwN / 16; ++gi) {
+                float acc[16];
+                tmem_ld16(taddr + gi * 16, acc);
+                if (dst) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int k = kt * kDwN + gi * 16 + i;
+                        if (k < a.d) atomicAdd(dst + k, acc[i]);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, 512);
+}
+
+// ---------------------------------------------------------- backward host side
+
+struct BwdLayout {
+    int64_t pass_rows;  // rows of the G / H buffers (multiple of 128)
+    int64_t step;       // nominal pass stride in nodes (bounds are rounded down to bands)
+    int passes;
+    size_t wf, wt, g, h, bounds, pbands, boff, err, total;
+};
+
+BwdLayout bwd_layout(const JointArgs& a, int64_t cap) {
+    const Geom g = make_geom(a);
+    BwdLayout L;
+    const int64_t band_max = (int64_t)kBandT * a.U;
+    const int64_t want = std::min<int64_t>(cap, kMaxPassNodes);
+    L.pass_rows = (want + band_max + 2 * kBM + kBM - 1) / kBM * kBM;
+    L.step = L.pass_rows - band_max - 2 * kBM;
+    L.passes = (int)std::max<int64_t>(1, (cap + L.step - 1) / L.step);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += al256(bytes);
+        return o;
+    };
+    L.wf = take(sizeof(__nv_bfloat16) * (size_t)g.vpad * g.kpad);
+    L.wt = take(sizeof(__nv_bfloat16) * (size_t)g.kpad * g.vpad);
+    L.g = take(sizeof(__nv_bfloat16) * (size_t)L.pass_rows * g.vpad);
+    L.h = take(sizeof(__nv_bfloat16) * (size_t)L.pass_rows * g.kpad);
+    L.bounds = take(sizeof(int32_t) * (L.passes + 1));
+    L.pbands = take(sizeof(int32_t) * (L.passes + 1));
+    L.boff = take(sizeof(int32_t) * (a.B + 1));
+    L.err = take(sizeof(int));
+    L.total = off;
+    return L;
+}
+
+size_t dh_smem_bytes(int stages, int sdec_rows) {
+    return 1024 + (size_t)stages * kDhStageBytes + sizeof(float) * (size_t)(kBandT + sdec_rows) * (kDhN + 1) +
+           8 * (2 * stages + 5) + 16;
+}
+
+size_t dw_smem_bytes() { return 1024 + (size_t)kDwStages * kDwStageBytes + 8 * (2 * kDwStages + 2) + 16; }
+
+}  // namespace
+
+bool tc_backward_supported(const JointArgs& a) {
+    if (!tc_supported(a)) return false;
+    const Geom g = make_geom(a);
+    return (int)dh_smem_bytes(2, 0) <= dyn_smem_limit() &&
+           (int)dw_smem_bytes() <= dyn_smem_limit();
+}
+
+size_t tc_backward_scratch_bytes(const JointArgs& a, int node_capacity) {
+    return bwd_layout(a, node_capacity).total + 256;
+}
+
+int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOut& o, int node_capacity, void* scratch,
+                      size_t scratch_bytes, cudaStream_t st) {
+    const Geom g = make_geom(a);
+    const BwdLayout L = bwd_layout(a, node_capacity);
+    if (scratch_bytes < L.total) return ASR_ERR_WORKSPACE;
+    char* base = reinterpret_cast<char*>(scratch);
+    auto* Wf = reinterpret_cast<__nv_bfloat16*>(base + L.wf);
+    auto* Wt = reinterpret_cast<__nv_bfloat16*>(base + L.wt);
+    auto* G = reinterpret_cast<__nv_bfloat16*>(base + L.g);
+    auto* H = reinterpret_cast<__nv_bfloat16*>(base + L.h);
+    auto* bounds = reinterpret_cast<int32_t*>(base + L.bounds);
+    auto* pbands = reinterpret_cast<int32_t*>(base + L.pbands);
+    auto* boff = reinterpret_cast<int32_t*>(base + L.boff);
+    int* err = reinterpret_cast<int*>(base + L.err);
+    const int sms = sm_count();
+    ASR_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
+    {
+        KernelTimer kt("joint_prep_weights", st);
+        prep_weights_kernel<<<sms * 4, 256, 0, st>>>(a.W, a.Wd, a.V, a.n_dur, a.d, g.vpad, g.kpad, Wf, Wt);
+        ASR_LAUNCH_CHECK();
+    }
+    {
+        KernelTimer kt("joint_plan_passes", st);
+        band_prep_kernel<<<1, 32, 0, st>>>(a.m, a.B, boff);
+        ASR_LAUNCH_CHECK();
+        plan_passes_kernel<<<(L.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, boff, L.passes, L.step, bounds,
+                                                                        pbands);
+        ASR_LAUNCH_CHECK();
+    }
+    // tensor maps
+    CUtensorMap mfull, mtail, m_gk, m_wt, m_gmn, m_hmn;
+    if (!make_map(&mtail, Wf, g.vpad, g.kpad, kBK, g.tail > 0 ? g.tail : 16, CU_TENSOR_MAP_SWIZZLE_64B))
+        return ASR_ERR_CUDA;
+    if (g.nfull == 0)
+        mfull = mtail;
+    else if (!make_map(&mfull, Wf, g.vpad, g.kpad, kBK, kNC, CU_TENSOR_MAP_SWIZZLE_64B))
+        return ASR_ERR_CUDA;
+    if (!make_map(&m_gk, G, (int)L.pass_rows, g.vpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_wt, Wt, g.kpad, g.vpad, kAK, kDhN, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_gmn, G, (int)L.pass_rows, g.vpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_hmn, H, (int)L.pass_rows, g.kpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
+
+    // dlogits kernel parameters
+    TcParams TP;
+    std::memset(&TP, 0, sizeof(TP));
+    TP.a = a;
+    TP.g = g;
+    TP.bwd = in;
+    TP.G = G;
+    TP.H = H;
+    TP.range.bounds = bounds;
+    TP.err = err;
+    const size_t smem_fw = smem_bytes_for(g.kchunks);
+    ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fw));
+    const int grid_fw = (int)std::max<int64_t>(1, std::min<int64_t>(L.pass_rows / kBM, sms));
+
+    // dH parameters: deepest pipeline that leaves room for the band partials
+    DhParams DP;
+    std::memset(&DP, 0, sizeof(DP));
+    DP.a = a;
+    DP.g = g;
+    DP.H = H;
+    DP.bounds = bounds;
+    DP.pbands = pbands;
+    DP.boff = boff;
+    DP.d_enc = o.d_enc;
+    DP.d_dec = o.d_dec;
+    DP.err = err;
+    const int limit = dyn_smem_limit();
+    DP.stages = 4;
+    DP.sdec_rows = a.U;
+    while (DP.stages > 2 && (int)dh_smem_bytes(DP.stages, DP.sdec_rows) > limit) --DP.stages;
+    if ((int)dh_smem_bytes(DP.stages, DP.sdec_rows) > limit) DP.sdec_rows = 0;  // global atomics for d_dec
+    const size_t smem_dh = dh_smem_bytes(DP.stages, DP.sdec_rows);
+    ASR_CUDA_TRY(cudaFuncSetAttribute(tc_dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dh));
+
+    DwParams WP;
+    std::memset(&WP, 0, sizeof(WP));
+    WP.a = a;
+    WP.g = g;
+    WP.bounds = bounds;
+    WP.dW = o.dW;
+    WP.dWd = o.dWd;
+    WP.err = err;
+    const int nvt = (g.vpad + kDwM - 1) / kDwM, nkt = (g.kpad + kDwN - 1) / kDwN;
+    WP.splits = std::max(1, (sms + nvt * nkt - 1) / (nvt * nkt));
+    const size_t smem_dw = dw_smem_bytes();
+    ASR_CUDA_TRY(cudaFuncSetAttribute(tc_dw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dw));
+
+    for (int p = 0; p < L.passes; ++p) {
+        TP.range.pass = p;
+        DP.pass = p;
+        WP.pass = p;
+        {
+            KernelTimer kt("joint_dlogits_tc", st);
+            tc_joint_kernel<true><<<grid_fw, kThreads, smem_fw, st>>>(mfull, mtail, TP);
+            ASR_LAUNCH_CHECK();
+        }
+        {
+            KernelTimer kt("joint_dhidden_tc", st);
+            tc_dh_kernel<<<sms, kBwdThreads, smem_dh, st>>>(m_gk, m_wt, DP);
+            ASR_LAUNCH_CHECK();
+        }
+        {
+            KernelTimer kt("joint_dweight_tc", st);
+            tc_dw_kernel<<<nvt * nkt * WP.splits, kBwdThreads, smem_dw, st>>>(m_gmn, m_hmn, WP);
+            ASR_LAUNCH_CHECK();
+        }
+    }
+    return ASR_OK;
 }
 
 }  // namespace asr
