@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -123,7 +124,7 @@ __device__ __forceinline__ Smem carve_smem(uint8_t* raw, int kchunks) {
     return s;
 }
 
-// Per-pass node range of the backward (pass p covers [bounds[2p], bounds[2p+1])).
+// Per-pass node range of the backward (pass p covers [bounds[p], bounds[p+1])).
 struct PassRange {
     const int32_t* bounds;
     int pass;
@@ -146,8 +147,8 @@ __device__ __forceinline__ void node_range(const TcParams& P, bool bwd, int& beg
         begin = 0;
         end = N;
     } else {
-        begin = min(P.range.bounds[2 * P.range.pass], N);
-        end = min(P.range.bounds[2 * P.range.pass + 1], N);
+        begin = min(P.range.bounds[P.range.pass], N);
+        end = min(P.range.bounds[P.range.pass + 1], N);
     }
 }
 
@@ -603,117 +604,196 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, void* scratch, si
 
 // =================================================================== backward
 //
-// Per pass of nodes [s, e) (pass bounds fall on band boundaries, computed on the
-// device): the dlogits kernel above writes G = d loss / d logits (bf16, rows of
-// the pass) and H = hidden (bf16); then
-//   dH  kernel: per band (kBandT frames x all labels of one utterance) and
-//               128-wide slice of the hidden dimension, D = G * Wf^T (M = 128
-//               nodes, N = 128, K = vocabulary) in TMEM; the epilogue applies
-//               tanh' = 1 - h^2 and reduces the band: d_enc rows (one per frame)
-//               with warp segmented scans into shared memory and one exclusive
-//               store per element, d_dec rows with shared-memory atomics and one
-//               global atomic per element per band;
+// Per pass of nodes [s, e) (bounds computed on the device): the dlogits kernel
+// above writes G = d loss / d logits (bf16 rows of the pass) and H = hidden
+// (bf16); then
+//   dH  kernel: the transposed product D^T = Wf^T G^T per (128-wide hidden
+//               slice, 256-node tile): M = 128 hidden columns on the TMEM
+//               lanes, N = 256 consecutive nodes on the TMEM columns, K = the
+//               vocabulary. Each epilogue thread owns one hidden column, so both
+//               reductions of d_hidden = D ⊙ (1 - h^2) are thread-private:
+//               d_enc[b, t] is a running sum over the contiguous label positions
+//               of frame t (one global add per frame), d_dec[b, u] accumulates in
+//               the thread's own column of a shared-memory row block of the
+//               current utterance (flushed with one global add per element
+//               when the utterance ends). h = tanh(enc + dec) is recomputed from
+//               the fp32 activations (a register copy of the frame's enc value
+//               and a shared copy of the utterance's dec rows).
 //   dW  kernel: split-K over the pass rows, D = G^T H (M = 128 vocabulary rows,
 //               N = 320 hidden columns, both operands MN-major straight from G
 //               and H), added to dW / dW_dur once per CTA.
 
 namespace {
 
-constexpr int kBandT = 64;        // frames per band of the dH reduction
-constexpr int kDhN = 128;         // hidden columns per dH work item (UMMA N)
+constexpr int kDhM = 128;                          // hidden columns per work item (UMMA M)
+constexpr int kDhNodes = 256;                      // nodes per tile (UMMA N)
+constexpr int kDhK = 32;                           // vocabulary per stage (64 B rows)
+constexpr int kDhABytes = kDhM * kDhK * 2;         // 8 KB
+constexpr int kDhStageBytes = kDhABytes + kDhNodes * kDhK * 2;  // 24 KB
 constexpr int kDwM = 128;         // vocabulary rows per dW work item (UMMA M)
 constexpr int kDwN = 320;         // hidden columns per dW work item (UMMA N = 256 + 64)
 constexpr int kBwdThreads = 192;  // TMA, MMA, 4 epilogue warps
-constexpr int kDhStageBytes = 2 * kBM * kAK * 2;            // A (128 x 64) + B (128 x 64), 32 KB
 constexpr int kDwStageBytes = (2 + kDwN / 64) * 64 * 64 * 2;  // 2 + 5 boxes of 64 x 64, 56 KB
 constexpr int64_t kMaxPassNodes = 4 << 20;
 
-__device__ __forceinline__ void named_sync_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// Bands: utterance b has ceil(T_b / kBandT); boff is their exclusive prefix sum.
-__global__ void band_prep_kernel(LatticeMeta m, int B, int32_t* __restrict__ boff) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    int acc = 0;
-    for (int b = 0; b < B; ++b) {
-        boff[b] = acc;
-        acc += (m.Tb[b] + kBandT - 1) / kBandT;
-    }
-    boff[B] = acc;
-}
-
-// bounds[p] = start of pass p, rounded down to a band boundary; pbands[p] = its band index.
-__global__ void plan_passes_kernel(LatticeMeta m, int B, const int32_t* __restrict__ boff, int P, int64_t step,
-                                   int32_t* __restrict__ bounds, int32_t* __restrict__ pbands) {
+// bounds[p] = first node of pass p (p = 0..P), clamped to the node count.
+__global__ void plan_passes_kernel(LatticeMeta m, int B, int P, int64_t step, int32_t* __restrict__ bounds) {
     const int p = blockIdx.x * blockDim.x + threadIdx.x;
     if (p > P) return;
     const int N = total_nodes(m, B);
-    const int64_t x = (p == P) ? N : std::min<int64_t>((int64_t)p * step, N);
-    if (x >= N) {
-        bounds[p] = N;
-        pbands[p] = boff[B];
-        return;
-    }
-    const int b = find_utt(m.off, B, (int)x);
-    const int bs = kBandT * m.Ub[b];
-    const int j = ((int)x - m.off[b]) / bs;
-    bounds[p] = m.off[b] + j * bs;
-    pbands[p] = boff[b] + j;
-}
-
-struct BandInfo {
-    int b, t0, nt, Ub, r0, r1;  // utterance, first frame, frames, label positions, pass rows [r0, r1)
-};
-
-__device__ __forceinline__ BandInfo band_info(const LatticeMeta& m, int B, const int32_t* boff, int band, int s) {
-    BandInfo bi;
-    int lo = 0, hi = B - 1;  // utterance owning `band`
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (boff[mid] <= band)
-            lo = mid;
-        else
-            hi = mid - 1;
-    }
-    bi.b = lo;
-    const int j = band - boff[lo];
-    const int Tb = m.Tb[lo];
-    bi.Ub = m.Ub[lo];
-    bi.t0 = j * kBandT;
-    bi.nt = min(kBandT, Tb - bi.t0);
-    const int n0 = m.off[lo] + bi.t0 * bi.Ub;
-    bi.r0 = n0 - s;
-    bi.r1 = n0 + bi.nt * bi.Ub - s;
-    return bi;
+    bounds[p] = (p == P) ? N : (int)std::min<int64_t>((int64_t)p * step, N);
 }
 
 struct DhParams {
     JointArgs a;
     Geom g;
-    const __nv_bfloat16* H;
     const int32_t* bounds;
-    const int32_t* pbands;
-    const int32_t* boff;
     int pass;
     int stages;
-    int sdec_rows;  // label rows of the shared d_dec partial (0: global atomics)
+    int ndt;       // hidden slices of kDhM columns
+    int groups;    // node-range groups; CTA i works on slice i % ndt of range i / ndt
+    int dec_rows;  // label rows of the shared dec copy / d_dec accumulator (0: global path)
     float* d_enc;
     float* d_dec;
     int* err;
 };
 
+// Walk state of one epilogue thread over consecutive nodes (warp-uniform except
+// the per-column values).
+struct DhWalk {
+    int b, t, u, Tb, Ub;
+    float e_cur, e_nxt;  // enc[b, t, col], enc[b, t + 1, col]
+    float acc_e;         // running d_enc sum of frame t
+    bool dirty;          // d_dec rows of utterance b hold unflushed sums
+};
+
+template <bool kSmemDec>
+struct DhEpilogue {
+    const DhParams& P;
+    const int col;     // hidden column
+    const bool col_ok;
+    const int cl;      // column within the slice (shared-memory column)
+    float* sdin;       // [dec_rows][kDhM] dec copy
+    float* sacc;       // [dec_rows][kDhM] d_dec sums
+
+    __device__ float enc_at(int b, int t) const {
+        return col_ok ? __ldg(P.a.enc + ((int64_t)b * P.a.T + t) * P.a.d + col) : 0.f;
+    }
+    __device__ float dec_at(const DhWalk& w, int u) const {
+        if (kSmemDec) return sdin[u * kDhM + cl];
+        return col_ok ? __ldg(P.a.dec + ((int64_t)w.b * P.a.U + u) * P.a.d + col) : 0.f;
+    }
+    __device__ void add_dec(const DhWalk& w, int u, float x) const {
+        if (kSmemDec)
+            sacc[u * kDhM + cl] += x;
+        else if (col_ok)
+            atomicAdd(P.d_dec + ((int64_t)w.b * P.a.U + u) * P.a.d + col, x);
+    }
+    // Enter utterance b at frame t (label position 0 follows from the caller).
+    __device__ void enter(DhWalk& w, int b, int t) const {
+        w.b = b;
+        w.t = t;
+        w.Tb = __ldg(P.a.m.Tb + b);
+        w.Ub = __ldg(P.a.m.Ub + b);
+        w.e_cur = enc_at(b, t);
+        w.e_nxt = t + 1 < w.Tb ? enc_at(b, t + 1) : 0.f;
+        if (kSmemDec) {
+            for (int u = 0; u < w.Ub; ++u) {
+                sdin[u * kDhM + cl] = col_ok ? __ldg(P.a.dec + ((int64_t)b * P.a.U + u) * P.a.d + col) : 0.f;
+                sacc[u * kDhM + cl] = 0.f;
+            }
+        }
+        w.dirty = false;
+    }
+    __device__ void flush_dec(DhWalk& w) const {
+        if (kSmemDec && w.dirty && col_ok)
+            for (int u = 0; u < w.Ub; ++u)
+                atomicAdd(P.d_dec + ((int64_t)w.b * P.a.U + u) * P.a.d + col, sacc[u * kDhM + cl]);
+        w.dirty = false;
+    }
+    __device__ void flush_enc(DhWalk& w) const {
+        if (col_ok) atomicAdd(P.d_enc + ((int64_t)w.b * P.a.T + w.t) * P.a.d + col, w.acc_e);
+        w.acc_e = 0.f;
+    }
+    // Frame t of the walk is complete: move to the next frame (or utterance).
+    __device__ void end_frame(DhWalk& w) const {
+        flush_enc(w);
+        w.u = 0;
+        if (++w.t < w.Tb) {
+            w.e_cur = w.e_nxt;
+            w.e_nxt = w.t + 1 < w.Tb ? enc_at(w.b, w.t + 1) : 0.f;
+            return;
+        }
+        flush_dec(w);
+        int b = w.b + 1;
+        while (b < P.a.B && __ldg(P.a.m.Tb + b) == 0) ++b;
+        if (b < P.a.B) enter(w, b, 0);
+        else w.b = P.a.B;  // past the last node
+    }
+    // One node at a time (any U_b, utterance changes inside the group).
+    __device__ void node(DhWalk& w, float g) const {
+        const float h = tanh_fast(w.e_cur + dec_at(w, w.u));
+        const float x = g * (1.f - h * h);
+        w.acc_e += x;
+        add_dec(w, w.u, x);
+        w.dirty = true;
+        if (++w.u == w.Ub) end_frame(w);
+    }
+    // 16 consecutive nodes with U_b >= 16 that stay inside utterance b: the 16
+    // label positions are distinct, so their d_dec rows load and store together.
+    __device__ void group16(DhWalk& w, const float (&v)[16]) const {
+        const int k = w.Ub - w.u;  // nodes left in frame t (at most one frame boundary here)
+        int idx[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            int ui = w.u + i;
+            if (ui >= w.Ub) ui -= w.Ub;
+            idx[i] = ui * kDhM + cl;
+        }
+        float dv[16], sa[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dv[i] = sdin[idx[i]];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sa[i] = sacc[idx[i]];
+        float lo = 0.f, hi = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float h = tanh_fast((i < k ? w.e_cur : w.e_nxt) + dv[i]);
+            const float x = v[i] * (1.f - h * h);
+            sacc[idx[i]] = sa[i] + x;
+            if (i < k)
+                lo += x;
+            else
+                hi += x;
+        }
+        w.dirty = true;
+        if (k < 16) {  // frame t ends inside the group; frame t + 1 is in the same utterance
+            w.acc_e += lo;
+            flush_enc(w);
+            ++w.t;
+            w.e_cur = w.e_nxt;
+            w.e_nxt = w.t + 1 < w.Tb ? enc_at(w.b, w.t + 1) : 0.f;
+            w.acc_e = hi;
+            w.u = 16 - k;
+        } else {
+            w.acc_e += lo;
+            w.u += 16;
+            if (w.u == w.Ub) end_frame(w);
+        }
+    }
+};
+
+template <bool kSmemDec>
 __global__ void __launch_bounds__(kBwdThreads, 1)
-    tc_dh_kernel(const __grid_constant__ CUtensorMap map_g, const __grid_constant__ CUtensorMap map_wt, DhParams P) {
+    tc_dh_kernel(const __grid_constant__ CUtensorMap map_wt, const __grid_constant__ CUtensorMap map_g, DhParams P) {
     extern __shared__ uint8_t smem_raw[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const JointArgs& a = P.a;
     const int S = P.stages;
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stages = base;
-    float* senc = reinterpret_cast<float*>(stages + (size_t)S * kDhStageBytes);   // [kBandT][kDhN + 1]
-    float* sdec = senc + kBandT * (kDhN + 1);                                    // [sdec_rows][kDhN + 1]
-    // the partials are (rows x 129) floats: realign for the 8-byte mbarriers
-    uint64_t* bars = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(sdec + (size_t)P.sdec_rows * (kDhN + 1)) + 15) & ~uintptr_t(15));
+    uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* sdin = reinterpret_cast<float*>(stages + (size_t)S * kDhStageBytes);  // [dec_rows][kDhM]
+    float* sacc = sdin + (size_t)P.dec_rows * kDhM;                               // [dec_rows][kDhM]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sacc + (size_t)P.dec_rows * kDhM);  // 512 B multiples: aligned
     uint64_t* b_full = bars;
     uint64_t* b_empty = bars + S;
     uint64_t* t_full = bars + 2 * S;
@@ -723,10 +803,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int* err = P.err;
 
     const int s = P.bounds[P.pass], e = P.bounds[P.pass + 1];
-    const int band0 = P.pbands[P.pass], nbands = P.pbands[P.pass + 1] - band0;
-    const int ndt = (P.g.kpad + kDhN - 1) / kDhN;  // the last slice may extend past kpad (zero weights)
-    const int items = e > s ? nbands * ndt : 0;
-    const int kchunks = (P.g.vpad + kAK - 1) / kAK;
+    const int dt = blockIdx.x % P.ndt, grp = blockIdx.x / P.ndt;
+    const int ntiles = e > s ? (e - s + kDhNodes - 1) / kDhNodes : 0;
+    const int tile0 = (int)((int64_t)grp * ntiles / P.groups);
+    const int tile1 = (int)((int64_t)(grp + 1) * ntiles / P.groups);
+    const int ksteps = (P.g.vpad + kDhK - 1) / kDhK;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -739,41 +820,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         mbar_init(done, 1);
         fence_barrier_init();
-        prefetch_tensormap(&map_g);
         prefetch_tensormap(&map_wt);
+        prefetch_tensormap(&map_g);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, 256);
+    if (warp == 1) tmem_alloc(tmem_slot, 2 * kDhNodes);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
             bool issued[8] = {};
             uint32_t ipar[8] = {};
             bool ok = true;
-            for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
-                const BandInfo bi = band_info(a.m, a.B, P.boff, band0 + w / ndt, s);
-                const int dt = w % ndt;
-                for (int r = bi.r0; ok && r < bi.r1; r += kBM) {
-                    for (int kc = 0; kc < kchunks; ++kc) {
-                        if (!mbar_wait(&b_empty[stage], phase ^ 1, err, 11)) {
-                            ok = false;
-                            break;
-                        }
-                        uint8_t* st = stages + (size_t)stage * kDhStageBytes;
-                        mbar_arrive_expect_tx(&b_full[stage], kDhStageBytes);
-                        tma_load_2d(st, &map_g, kc * kAK, r, &b_full[stage]);
-                        tma_load_2d(st + kBM * kAK * 2, &map_wt, kc * kAK, dt * kDhN, &b_full[stage]);
-                        issued[stage] = true;
-                        ipar[stage] = phase;
-                        if (++stage == S) {
-                            stage = 0;
-                            phase ^= 1;
-                        }
+            for (int tile = tile0; ok && tile < tile1; ++tile) {
+                for (int k = 0; k < ksteps; ++k) {
+                    if (!mbar_wait(&b_empty[stage], phase ^ 1, err, 11)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = stages + (size_t)stage * kDhStageBytes;
+                    mbar_arrive_expect_tx(&b_full[stage], kDhStageBytes);
+                    tma_load_2d(st, &map_wt, k * kDhK, dt * kDhM, &b_full[stage]);
+                    tma_load_2d(st + kDhABytes, &map_g, k * kDhK, tile * kDhNodes, &b_full[stage]);
+                    issued[stage] = true;
+                    ipar[stage] = phase;
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
                     }
                 }
             }
@@ -781,153 +859,96 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 if (issued[i]) mbar_wait(&b_full[i], ipar[i], err, 12);
         }
     } else if (warp == 1) {
+        // ------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = idesc_bf16(kBM, kDhN, false, false);
+            const uint32_t idesc = idesc_bf16(kDhM, kDhNodes, false, false);
             const uint32_t sbase = smem_u32(stages);
             int stage = 0;
             uint32_t phase = 0, q = 0;
             bool ok = true;
-            for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
-                const BandInfo bi = band_info(a.m, a.B, P.boff, band0 + w / ndt, s);
-                for (int r = bi.r0; ok && r < bi.r1; r += kBM, ++q) {
-                    const uint32_t buf = q & 1;
-                    if (!mbar_wait(&t_empty[buf], ((q >> 1) & 1) ^ 1, err, 13)) {
+            for (int tile = tile0; ok && tile < tile1; ++tile, ++q) {
+                const uint32_t buf = q & 1;
+                if (!mbar_wait(&t_empty[buf], ((q >> 1) & 1) ^ 1, err, 13)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int k = 0; k < ksteps; ++k) {
+                    if (!mbar_wait(&b_full[stage], phase, err, 14)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    for (int kc = 0; kc < kchunks; ++kc) {
-                        if (!mbar_wait(&b_full[stage], phase, err, 14)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t st = sbase + stage * kDhStageBytes;
+                    const uint32_t st = sbase + stage * kDhStageBytes;
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            mma_bf16(tmem_base + buf * kDhN, desc_k128(st + kk * 32),
-                                     desc_k128(st + kBM * kAK * 2 + kk * 32), idesc, (kc | kk) != 0 ? 1u : 0u);
-                        mma_commit(&b_empty[stage]);
-                        if (++stage == S) {
-                            stage = 0;
-                            phase ^= 1;
-                        }
+                    for (int kk = 0; kk < 2; ++kk)
+                        mma_bf16(tmem_base + buf * kDhNodes, desc_k64(st + kk * 32),
+                                 desc_k64(st + kDhABytes + kk * 32), idesc, (k | kk) != 0 ? 1u : 0u);
+                    mma_commit(&b_empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
                     }
-                    if (ok) mma_commit(&t_full[buf]);
                 }
+                if (ok) mma_commit(&t_full[buf]);
             }
             mma_commit(done);
             mbar_wait(done, 0, err, 15);
         }
-    } else {
+    } else if (tile1 > tile0) {
         // ------------------------------------------------------------------- epilogue
-        const int et = threadIdx.x - 64;  // 0..127
         const int lane_base = 32 * (warp & 3);
-        const int row_in_tile = lane_base + lane;
-        const int SD = kDhN + 1;
+        const int cl = lane_base + lane;
+        const int col = dt * kDhM + cl;
+        const DhEpilogue<kSmemDec> ep{P, col, col < a.d, cl, sdin, sacc};
+        DhWalk w;
+        {
+            const int n0 = s + tile0 * kDhNodes;
+            const NodeCoord c = node_coord(a.m, a.B, n0);
+            w.acc_e = 0.f;
+            ep.enter(w, c.b, c.t);
+            w.u = c.u;
+        }
         uint32_t q = 0;
         bool ok = true;
-        for (int w = blockIdx.x; w < items; w += gridDim.x) {
-            const BandInfo bi = band_info(a.m, a.B, P.boff, band0 + w / ndt, s);
-            const int dt = w % ndt;
-            const bool use_sdec = bi.Ub <= P.sdec_rows;
-            for (int i = et; i < bi.nt * SD; i += 128) senc[i] = 0.f;
-            if (use_sdec)
-                for (int i = et; i < bi.Ub * SD; i += 128) sdec[i] = 0.f;
-            named_sync_epilogue();
-            for (int r = bi.r0; r < bi.r1; r += kBM, ++q) {
-                const uint32_t buf = q & 1;
-                if (ok && !__all_sync(0xffffffffu, mbar_wait(&t_full[buf], (q >> 1) & 1, err, 16))) ok = false;
-                tc_fence_after();
-                const int row = r + row_in_tile;
-                const bool valid = ok && row < bi.r1;
-                int tr = -1, u = 0;
-                if (valid) {
-                    const int rel = row - bi.r0;
-                    tr = rel / bi.Ub;
-                    u = rel - tr * bi.Ub;
-                }
-                // segmented-scan neighbours over equal frame index (rows of one frame are contiguous)
-                bool same[5];
-#pragma unroll
-                for (int sft = 0; sft < 5; ++sft) {
-                    const int ko = __shfl_up_sync(0xffffffffu, tr, 1 << sft);
-                    same[sft] = lane >= (1 << sft) && ko == tr;
-                }
-                const int kn = __shfl_down_sync(0xffffffffu, tr, 1);
-                const bool tail = valid && (lane == 31 || kn != tr);
-                const __nv_bfloat16* hrow = P.H + (int64_t)(valid ? row : 0) * P.g.kpad + dt * kDhN;
-                const int64_t dec_row = ((int64_t)bi.b * a.U + u) * a.d + dt * kDhN;
-                const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + buf * kDhN;
-                for (int gi = 0; gi < kDhN / 16; ++gi) {
-                    float acc[16];
-                    if (ok) tmem_ld16(taddr + gi * 16, acc);
-                    float gp[16];
-                    if (valid && dt * kDhN + gi * 16 < P.g.kpad) {
-                        const uint4 h0 = *reinterpret_cast<const uint4*>(hrow + gi * 16);
-                        const uint4 h1 = *reinterpret_cast<const uint4*>(hrow + gi * 16 + 8);
-                        const __nv_bfloat162* hv0 = reinterpret_cast<const __nv_bfloat162*>(&h0);
-                        const __nv_bfloat162* hv1 = reinterpret_cast<const __nv_bfloat162*>(&h1);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float2 x0 = __bfloat1622float2(hv0[i]);
-                            const float2 x1 = __bfloat1622float2(hv1[i]);
-                            gp[2 * i] = acc[2 * i] * (1.f - x0.x * x0.x);
-                            gp[2 * i + 1] = acc[2 * i + 1] * (1.f - x0.y * x0.y);
-                            gp[8 + 2 * i] = acc[8 + 2 * i] * (1.f - x1.x * x1.x);
-                            gp[8 + 2 * i + 1] = acc[8 + 2 * i + 1] * (1.f - x1.y * x1.y);
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) gp[i] = 0.f;
-                    }
-                    // d_dec: rows of one label position are U_b apart; shared (or global) atomics
-                    if (valid) {
-                        if (use_sdec) {
-#pragma unroll
-                            for (int i = 0; i < 16; ++i) atomicAdd(&sdec[u * SD + gi * 16 + i], gp[i]);
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < 16; ++i)
-                                if (dt * kDhN + gi * 16 + i < a.d) atomicAdd(P.d_dec + dec_row + gi * 16 + i, gp[i]);
-                        }
-                    }
-                    // d_enc: segmented sums over the rows of one frame, one shared atomic per segment
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float v = gp[i];
-#pragma unroll
-                        for (int sft = 0; sft < 5; ++sft) {
-                            const float o = __shfl_up_sync(0xffffffffu, v, 1 << sft);
-                            if (same[sft]) v += o;
-                        }
-                        if (tail) atomicAdd(&senc[tr * SD + gi * 16 + i], v);
-                    }
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&t_empty[buf]);
+        for (int tile = tile0; tile < tile1; ++tile, ++q) {
+            const uint32_t buf = q & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&t_full[buf], (q >> 1) & 1, err, 16))) {
+                ok = false;
+                break;
             }
-            named_sync_epilogue();
-            // flush the band: d_enc rows are exclusive to this work item, d_dec rows are shared
-            const int kb = dt * kDhN;
-            for (int i = et; i < bi.nt * kDhN; i += 128) {
-                const int tr = i / kDhN, c = i - tr * kDhN;
-                if (kb + c < a.d) P.d_enc[((int64_t)bi.b * a.T + bi.t0 + tr) * a.d + kb + c] = senc[tr * SD + c];
-            }
-            if (use_sdec)
-                for (int i = et; i < bi.Ub * kDhN; i += 128) {
-                    const int uu = i / kDhN, c = i - uu * kDhN;
-                    if (kb + c < a.d) atomicAdd(P.d_dec + ((int64_t)bi.b * a.U + uu) * a.d + kb + c, sdec[uu * SD + c]);
+            tc_fence_after();
+            const int cnt = min(kDhNodes, e - (s + tile * kDhNodes));
+            const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + buf * kDhNodes;
+            for (int g16 = 0; g16 * 16 < cnt; ++g16) {
+                float v[16];
+                tmem_ld16(taddr + g16 * 16, v);
+                const int left = cnt - g16 * 16;
+                const bool fast = kSmemDec && left >= 16 && w.Ub >= 16 &&
+                                  (w.t < w.Tb - 1 || w.Ub - w.u >= 16);
+                if (fast) {
+                    ep.group16(w, v);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        if (i < left) ep.node(w, v[i]);
                 }
-            named_sync_epilogue();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&t_empty[buf]);
+        }
+        // the range may end inside a frame / an utterance: add the partial sums
+        if (ok && w.b < a.B) {
+            if (w.u > 0) ep.flush_enc(w);
+            ep.flush_dec(w);
         }
     }
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, 256);
+    if (warp == 1) tmem_dealloc(tmem_base, 2 * kDhNodes);
 }
 
 struct DwParams {
@@ -1083,19 +1104,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // ---------------------------------------------------------- backward host side
 
 struct BwdLayout {
-    int64_t pass_rows;  // rows of the G / H buffers (multiple of 128)
-    int64_t step;       // nominal pass stride in nodes (bounds are rounded down to bands)
+    int64_t step;  // nodes per pass (multiple of kDhNodes) = rows of the G / H buffers
     int passes;
-    size_t wf, wt, g, h, bounds, pbands, boff, err, total;
+    size_t wf, wt, g, h, bounds, err, total;
 };
+
+// Nodes per backward pass: at most kMaxPassNodes, or the ASR_B200_BWD_PASS_NODES
+// environment override (a tuning knob; small values exercise multi-pass runs).
+int64_t pass_nodes_limit() {
+    const char* env = std::getenv("ASR_B200_BWD_PASS_NODES");
+    if (env) {
+        const long long v = std::atoll(env);
+        if (v > 0) return v;
+    }
+    return kMaxPassNodes;
+}
 
 BwdLayout bwd_layout(const JointArgs& a, int64_t cap) {
     const Geom g = make_geom(a);
     BwdLayout L;
-    const int64_t band_max = (int64_t)kBandT * a.U;
-    const int64_t want = std::min<int64_t>(cap, kMaxPassNodes);
-    L.pass_rows = (want + band_max + 2 * kBM + kBM - 1) / kBM * kBM;
-    L.step = L.pass_rows - band_max - 2 * kBM;
+    const int64_t want = std::max<int64_t>(1, std::min<int64_t>(cap, pass_nodes_limit()));
+    L.step = (want + kDhNodes - 1) / kDhNodes * kDhNodes;
     L.passes = (int)std::max<int64_t>(1, (cap + L.step - 1) / L.step);
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -1105,19 +1134,17 @@ BwdLayout bwd_layout(const JointArgs& a, int64_t cap) {
     };
     L.wf = take(sizeof(__nv_bfloat16) * (size_t)g.vpad * g.kpad);
     L.wt = take(sizeof(__nv_bfloat16) * (size_t)g.kpad * g.vpad);
-    L.g = take(sizeof(__nv_bfloat16) * (size_t)L.pass_rows * g.vpad);
-    L.h = take(sizeof(__nv_bfloat16) * (size_t)L.pass_rows * g.kpad);
+    L.g = take(sizeof(__nv_bfloat16) * (size_t)L.step * g.vpad);
+    L.h = take(sizeof(__nv_bfloat16) * (size_t)L.step * g.kpad);
     L.bounds = take(sizeof(int32_t) * (L.passes + 1));
-    L.pbands = take(sizeof(int32_t) * (L.passes + 1));
-    L.boff = take(sizeof(int32_t) * (a.B + 1));
     L.err = take(sizeof(int));
     L.total = off;
     return L;
 }
 
-size_t dh_smem_bytes(int stages, int sdec_rows) {
-    return 1024 + (size_t)stages * kDhStageBytes + sizeof(float) * (size_t)(kBandT + sdec_rows) * (kDhN + 1) +
-           8 * (2 * stages + 5) + 16;
+size_t dh_smem_bytes(int stages, int dec_rows) {
+    return 1024 + (size_t)stages * kDhStageBytes + 2 * sizeof(float) * (size_t)dec_rows * kDhM + 8 * (2 * stages + 5) +
+           16;
 }
 
 size_t dw_smem_bytes() { return 1024 + (size_t)kDwStages * kDwStageBytes + 8 * (2 * kDwStages + 2) + 16; }
@@ -1126,9 +1153,7 @@ size_t dw_smem_bytes() { return 1024 + (size_t)kDwStages * kDwStageBytes + 8 * (
 
 bool tc_backward_supported(const JointArgs& a) {
     if (!tc_supported(a)) return false;
-    const Geom g = make_geom(a);
-    return (int)dh_smem_bytes(2, 0) <= dyn_smem_limit() &&
-           (int)dw_smem_bytes() <= dyn_smem_limit();
+    return (int)dh_smem_bytes(2, 0) <= dyn_smem_limit() && (int)dw_smem_bytes() <= dyn_smem_limit();
 }
 
 size_t tc_backward_scratch_bytes(const JointArgs& a, int node_capacity) {
@@ -1146,8 +1171,6 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     auto* G = reinterpret_cast<__nv_bfloat16*>(base + L.g);
     auto* H = reinterpret_cast<__nv_bfloat16*>(base + L.h);
     auto* bounds = reinterpret_cast<int32_t*>(base + L.bounds);
-    auto* pbands = reinterpret_cast<int32_t*>(base + L.pbands);
-    auto* boff = reinterpret_cast<int32_t*>(base + L.boff);
     int* err = reinterpret_cast<int*>(base + L.err);
     const int sms = sm_count();
     ASR_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
@@ -1158,24 +1181,22 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     }
     {
         KernelTimer kt("joint_plan_passes", st);
-        band_prep_kernel<<<1, 32, 0, st>>>(a.m, a.B, boff);
-        ASR_LAUNCH_CHECK();
-        plan_passes_kernel<<<(L.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, boff, L.passes, L.step, bounds,
-                                                                        pbands);
+        plan_passes_kernel<<<(L.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, L.passes, L.step, bounds);
         ASR_LAUNCH_CHECK();
     }
     // tensor maps
-    CUtensorMap mfull, mtail, m_gk, m_wt, m_gmn, m_hmn;
+    const int rows = (int)L.step;
+    CUtensorMap mfull, mtail, m_wt, m_g, m_gmn, m_hmn;
     if (!make_map(&mtail, Wf, g.vpad, g.kpad, kBK, g.tail > 0 ? g.tail : 16, CU_TENSOR_MAP_SWIZZLE_64B))
         return ASR_ERR_CUDA;
     if (g.nfull == 0)
         mfull = mtail;
     else if (!make_map(&mfull, Wf, g.vpad, g.kpad, kBK, kNC, CU_TENSOR_MAP_SWIZZLE_64B))
         return ASR_ERR_CUDA;
-    if (!make_map(&m_gk, G, (int)L.pass_rows, g.vpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
-    if (!make_map(&m_wt, Wt, g.kpad, g.vpad, kAK, kDhN, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
-    if (!make_map(&m_gmn, G, (int)L.pass_rows, g.vpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
-    if (!make_map(&m_hmn, H, (int)L.pass_rows, g.kpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_wt, Wt, g.kpad, g.vpad, kDhK, kDhM, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_g, G, rows, g.vpad, kDhK, kDhNodes, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_gmn, G, rows, g.vpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_hmn, H, rows, g.kpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
 
     // dlogits kernel parameters
     TcParams TP;
@@ -1189,27 +1210,27 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     TP.err = err;
     const size_t smem_fw = smem_bytes_for(g.kchunks);
     ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fw));
-    const int grid_fw = (int)std::max<int64_t>(1, std::min<int64_t>(L.pass_rows / kBM, sms));
+    const int grid_fw = (int)std::max<int64_t>(1, std::min<int64_t>(L.step / kBM, sms));
 
-    // dH parameters: deepest pipeline that leaves room for the band partials
+    // dH parameters: shared dec rows for the whole label range when they fit,
+    // then the deepest pipeline that still fits
     DhParams DP;
     std::memset(&DP, 0, sizeof(DP));
     DP.a = a;
     DP.g = g;
-    DP.H = H;
     DP.bounds = bounds;
-    DP.pbands = pbands;
-    DP.boff = boff;
     DP.d_enc = o.d_enc;
     DP.d_dec = o.d_dec;
     DP.err = err;
+    DP.ndt = (g.kpad + kDhM - 1) / kDhM;
+    DP.groups = std::max(1, sms / DP.ndt);
     const int limit = dyn_smem_limit();
-    DP.stages = 4;
-    DP.sdec_rows = a.U;
-    while (DP.stages > 2 && (int)dh_smem_bytes(DP.stages, DP.sdec_rows) > limit) --DP.stages;
-    if ((int)dh_smem_bytes(DP.stages, DP.sdec_rows) > limit) DP.sdec_rows = 0;  // global atomics for d_dec
-    const size_t smem_dh = dh_smem_bytes(DP.stages, DP.sdec_rows);
-    ASR_CUDA_TRY(cudaFuncSetAttribute(tc_dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dh));
+    DP.dec_rows = (int)dh_smem_bytes(2, a.U) <= limit ? a.U : 0;
+    DP.stages = 2;
+    while (DP.stages < 8 && (int)dh_smem_bytes(DP.stages + 1, DP.dec_rows) <= limit) ++DP.stages;
+    const size_t smem_dh = dh_smem_bytes(DP.stages, DP.dec_rows);
+    auto dh_kernel = DP.dec_rows > 0 ? tc_dh_kernel<true> : tc_dh_kernel<false>;
+    ASR_CUDA_TRY(cudaFuncSetAttribute(dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dh));
 
     DwParams WP;
     std::memset(&WP, 0, sizeof(WP));
@@ -1235,7 +1256,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
         }
         {
             KernelTimer kt("joint_dhidden_tc", st);
-            tc_dh_kernel<<<sms, kBwdThreads, smem_dh, st>>>(m_gk, m_wt, DP);
+            dh_kernel<<<DP.groups * DP.ndt, kBwdThreads, smem_dh, st>>>(m_wt, m_g, DP);
             ASR_LAUNCH_CHECK();
         }
         {

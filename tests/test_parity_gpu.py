@@ -285,6 +285,46 @@ def test_tdt_bf16_bpe_config_matches_oracle():
                                         ("dW_dur", gwd, o["dW_dur"])])
 
 
+def _rel(got, want):
+    return ((got.double() - want.double()).norm() / want.double().norm().clamp_min(1e-30)).item()
+
+
+def test_tdt_bf16_backward_tracks_fp32_path():
+    """The tensor-core path's gradients stay within 1e-2 (relative norm) of the
+    fp32 path on benchmark-distribution inputs: bf16 operand rounding only.
+    Label lengths 14..60 exercise both the 16-node groups of the d_hidden
+    epilogue (U_b >= 16) and its node-by-node path (U_b < 16)."""
+    c = transducer_case(36, 6, (60, 140), (10, 60), 1024, 640, n_dur=5)
+    l16, *g16 = run_tdt(c, tf32=True, sigma=0.05)
+    l32, *g32 = run_tdt(c, tf32=False, sigma=0.05)
+    np.testing.assert_allclose(l16.detach().cpu().numpy(), l32.detach().cpu().numpy(), rtol=2e-3)
+    for name, a, b in zip(("d_enc", "d_dec", "dW", "dW_dur"), g16, g32):
+        assert _rel(a, b) < 1e-2, f"{name}: {_rel(a, b):.3e}"
+
+
+def test_tdt_bf16_backward_multi_pass(monkeypatch):
+    """Backward split into 700-node passes (boundaries inside frames and
+    utterances) gives the single-pass gradients up to fp32 summation order."""
+    c = transducer_case(37, 5, (30, 70), (14, 40), 256, 192, n_dur=5)
+    l1, *g1 = run_tdt(c, tf32=True, sigma=0.05)
+    monkeypatch.setenv("ASR_B200_BWD_PASS_NODES", "700")
+    l2, *g2 = run_tdt(c, tf32=True, sigma=0.05)
+    torch.testing.assert_close(l2, l1, rtol=0, atol=0)
+    for name, a, b in zip(("d_enc", "d_dec", "dW", "dW_dur"), g2, g1):
+        assert _rel(a, b) < 1e-5, f"{name}: {_rel(a, b):.3e}"
+
+
+def test_rnnt_bf16_long_labels():
+    """U = 181..200 label positions: the d_hidden kernel's global d_dec path
+    (the per-utterance shared rows no longer fit)."""
+    c = transducer_case(38, 2, (8, 14), (180, 199), 64, 128)
+    l16, *g16 = run_rnnt(c, tf32=True)
+    l32, *g32 = run_rnnt(c, tf32=False)
+    np.testing.assert_allclose(l16.detach().cpu().numpy(), l32.detach().cpu().numpy(), rtol=2e-3)
+    for name, a, b in zip(("d_enc", "d_dec", "dW"), g16, g32):
+        assert _rel(a, b) < 1e-2, f"{name}: {_rel(a, b):.3e}"
+
+
 # ------------------------------------------------------- direct C ABI
 
 
