@@ -157,16 +157,25 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
+GEMM_KERNELS = ("joint_fwd_tc", "joint_dlogits_tc", "joint_dhidden_tc", "joint_dweight_tc",
+                "joint_fwd_simt", "joint_dlogits_simt", "joint_dhidden_simt", "joint_dweight_simt")
+
+
 def kernel_work(name, N, d, Vf, n_dur):
     """Algorithmic work of one step of kernel `name`: ('tensor', flops) or ('hbm', bytes).
-    GEMM kernels: 2 * N * d * Vf each (the backward recompute is one of them).
-    Recursions: the lattice bytes of the per-node figures (4-byte values)."""
-    if name.startswith("joint_"):
+    Joint GEMMs: 2 * N * d * Vf each (forward, backward recompute, d_hidden, dW).
+    Recursions: per node, the 4-byte lattice weights read plus the float64 alpha
+    written (alpha) or read (beta) plus the 4-byte posteriors written (beta)."""
+    if name in GEMM_KERNELS:
         return "tensor", 2.0 * N * d * Vf
-    if name.startswith("tdt_alpha") or name.startswith("rnnt_alpha"):
-        return "hbm", N * 4.0 * ((2 + n_dur) + 1)
-    if name.startswith("tdt_beta") or name.startswith("rnnt_beta"):
-        return "hbm", N * 4.0 * (2 * (2 + n_dur) + 1)
+    if name == "tdt_alpha":
+        return "hbm", N * (4.0 * (2 + n_dur) + 8.0)
+    if name == "tdt_beta_posteriors":
+        return "hbm", N * (4.0 * (2 + n_dur) + 8.0 + 4.0 * (2 + n_dur))
+    if name == "rnnt_alpha":
+        return "hbm", N * (8.0 + 8.0)
+    if name == "rnnt_beta_posteriors":
+        return "hbm", N * (8.0 + 8.0 + 8.0)
     return None, 0.0
 
 
@@ -263,6 +272,8 @@ def main():
     ap.add_argument("--tf32", type=int, default=1, help="1: bf16 tensor-core joint (the systems' setting)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clocks-log", default=None)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="profiling aid: run only the first BATCH utterances of the workload")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -289,6 +300,10 @@ def main():
     from asr_b200.shard import allreduce_joint, balance_shards, shard_imbalance
 
     in_lens, tgt_lens = workload_lengths()
+    global GLOBAL_B
+    if args.batch:
+        GLOBAL_B = min(args.batch, GLOBAL_B)
+        in_lens, tgt_lens = in_lens[:GLOBAL_B], tgt_lens[:GLOBAL_B]
     shards = balance_shards(in_lens, tgt_lens, world)
     mine = shards[rank]
     host = make_batch(mine, in_lens, tgt_lens)
@@ -385,31 +400,41 @@ def main():
     peaks = measured_peaks()
     Vf = VOCAB + len(DURATIONS)
     roof = None
-    if prof:
-        name, (launches, kms) = max(prof.items(), key=lambda kv: kv[1][1])
+    per_kernel = {}
+    total_ms = max(sum(v[1] for v in prof.values()), 1e-9)
+    for name, (launches, kms) in prof.items():
         bound, work = kernel_work(name, N_local, D_MODEL, Vf, len(DURATIONS))
         per_launch_ms = kms / max(launches, 1)
         steps_launches = launches / args.steps
         work_per_launch = work / max(steps_launches, 1)
+        entry = {"launches_per_step": steps_launches, "ms_per_step": round(kms / args.steps, 4),
+                 "share": round(kms / total_ms, 4)}
         if bound == "tensor":
             achieved = work_per_launch / (per_launch_ms / 1000.0) / 1e12
-            peak = peaks["bf16_tflops_sustained"]
-            unit = "TFLOP/s"
-        else:
+            peak, unit = peaks["bf16_tflops_sustained"], "TFLOP/s"
+        elif bound == "hbm":
             achieved = work_per_launch / (per_launch_ms / 1000.0) / 1e9
-            peak = peaks["hbm_gbs"]
-            unit = "GB/s"
+            peak, unit = peaks["hbm_gbs"], "GB/s"
+        if bound:
+            entry.update({"bound": bound, "achieved": round(achieved, 2), "unit": unit,
+                          "frac": round(achieved / peak, 4)})
+        per_kernel[name] = entry
+    if prof:
+        name, (launches, kms) = max(prof.items(), key=lambda kv: kv[1][1])
+        k = per_kernel[name]
+        steps_launches = launches / args.steps
+        bound = k.get("bound")
+        peak = peaks["bf16_tflops_sustained"] if bound == "tensor" else peaks["hbm_gbs"]
         traffic = None
         tfile = ROOT / "profiles" / "traffic.json"
         if tfile.exists():
             tj = json.loads(tfile.read_text()).get(name)
             if tj:  # bytes per node measured by ncu on a smaller case, scaled to this launch
                 traffic = int(tj["bytes_per_node"] * N_local / max(steps_launches, 1))
-        roof = {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
-                "frac": round(achieved / peak, 4), "traffic": traffic,
+        roof = {"kernel": name, "bound": bound, "achieved": k.get("achieved"), "peak": peak, "unit": k.get("unit"),
+                "frac": k.get("frac"), "traffic": traffic,
                 "peak_source": f"{peaks['source']} ({'bf16 sustained' if bound == 'tensor' else 'hbm copy'})",
-                "launch_ms": round(per_launch_ms, 4),
-                "share": round(kms / max(sum(v[1] for v in prof.values()), 1e-9), 4)}
+                "launch_ms": round(kms / max(launches, 1), 4), "share": k["share"]}
     launches_total = int(sum(v[0] for v in prof.values()))
 
     if world > 1:
@@ -434,7 +459,7 @@ def main():
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": launches_total, "kernel_ms": {k: round(v[1] / args.steps, 4) for k, v in prof.items()},
+            "gpu_launches": launches_total, "kernels": per_kernel,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
