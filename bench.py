@@ -351,12 +351,12 @@ def main():
     lib = _lib.capi_ops()
     lib.asr_profiler_report(None, 0, 1)
     clocks = ClockSampler(args.clocks_log) if rank == 0 else None
+    if clocks:  # before the barrier: no rank may start timing while rank 0 waits for the sampler
+        clocks.start()
+        time.sleep(0.3)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    if clocks:
-        clocks.start()
-        time.sleep(0.3)
     lib.asr_profiler_enable(1)
     ms_total = timed_loop(lambda: step(enc, dec, targets, il, tl), args.steps)
     lib.asr_profiler_enable(0)
