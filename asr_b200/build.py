@@ -34,7 +34,7 @@ NVCC_FLAGS = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-
               "-Xptxas", "-warn-spills", f"-I{INCLUDE}", f"-I{CSRC}"]
 CU_SOURCES = ["lattice.cu", "ctc.cu", "dp_rnnt.cu", "dp_tdt.cu", "joint_simt.cu", "joint_tc.cu", "capi.cu",
               "profiler.cu", "noalloc.cu"]
-HEADERS = ["common.cuh", "dp.cuh", "joint.cuh", "profiler.cuh"]
+HEADERS = ["common.cuh", "dp.cuh", "joint.cuh", "profiler.cuh", "tc_common.cuh"]
 
 
 def _torch_paths():

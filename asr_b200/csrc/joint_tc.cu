@@ -372,12 +372,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             float dur[kMaxDurCols];
 #pragma unroll
             for (int k = 0; k < kMaxDurCols; ++k) dur[k] = 0.f;
-            // backward per-node coefficients
-            float lse = 0.f, cb = 0.f, ct = 0.f;
+            // backward per-node coefficients; rows past the pass end keep zeros, so
+            // their G row is exp(0 - 0) * 0 = 0 (their A row, hence logits, is zero)
+            float lse2 = 0.f, cb = 0.f, ct = 0.f, Pn = 0.f;  // lse2 = lse * log2(e)
             if (kBwd && valid) {
-                lse = P.bwd.lse[n];
+                lse2 = P.bwd.lse[n] * kLog2e;
                 cb = P.bwd.cb[n];
                 ct = P.bwd.ct[n];
+                Pn = cb + ct;
+#pragma unroll
+                for (int k = 0; k < kMaxDurCols; ++k)  // duration-logit grads, used by the tail chunk
+                    if (k < a.n_dur) dur[k] = P.bwd.gdur[(int64_t)n * a.n_dur + k];
             }
             for (int j = 0; j < g.nchunks; ++j, ++q) {
                 int col, width;
@@ -429,22 +434,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         }
                     } else {
-                        // rows past the pass end are written as zeros: dW contracts over rows
-                        const float Pn = cb + ct;
+                        // G = softmax * (cb + ct) - cb [blank] - ct [label]; duration grads
                         float gv[16];
+                        if (c0 + 16 <= a.V) {  // token columns only: branch-free
+                            const int db = a.blank - c0, dy = y - c0;
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const int c = c0 + i;
-                            float x = 0.f;
-                            if (!valid) {
-                            } else if (c < a.V) {
-                                x = __expf(v[i] - lse) * Pn;
-                                if (c == a.blank) x -= cb;
-                                if (c == y) x -= ct;
-                            } else if (c < Vf) {
-                                x = P.bwd.gdur[(int64_t)n * a.n_dur + (c - a.V)];
+                            for (int i = 0; i < 16; ++i) {
+                                float x = ex2_fast(fmaf(v[i], kLog2e, -lse2)) * Pn;
+                                x = (i == db) ? x - cb : x;
+                                gv[i] = (i == dy) ? x - ct : x;
                             }
-                            gv[i] = x;
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const int c = c0 + i;
+                                float x = 0.f;
+                                if (c < a.V) {
+                                    x = ex2_fast(fmaf(v[i], kLog2e, -lse2)) * Pn;
+                                    if (c == a.blank) x -= cb;
+                                    if (c == y) x -= ct;
+                                } else {
+#pragma unroll
+                                    for (int k = 0; k < kMaxDurCols; ++k)
+                                        if (c - a.V == k && k < a.n_dur) x = dur[k];
+                                }
+                                gv[i] = x;
+                            }
                         }
                         uint4 w0, w1;
                         w0.x = pack_bf16(gv[0], gv[1]);

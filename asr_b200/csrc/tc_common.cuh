@@ -177,6 +177,15 @@ __device__ __forceinline__ float tanh_fast(float x) {
     return y;
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x (PTX ex2.approx, flush-to-zero).
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
