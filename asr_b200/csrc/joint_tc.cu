@@ -2,11 +2,15 @@
 //
 // Forward kernel (and the recompute pass of the backward), one persistent CTA
 // per SM over 128-node tiles of the compact lattice:
-//   warp 0      TMA producer: [joint_W; joint_W_dur] bf16 slices (32 K x 256 N,
-//               64 B swizzle) into a 4-stage ring;
+//   warp 0      TMA producer: [joint_W; joint_W_dur] bf16 slices (64 K x one
+//               vocabulary chunk, 128 B swizzle: one large box per stage, the
+//               box count rather than the bytes bounds TMA throughput) into a
+//               2-stage ring;
 //   warp 1      MMA issuer (one thread): tcgen05.mma kind::f16, M = 128 nodes,
-//               N = 256 vocabulary columns per chunk, fp32 accumulation in a
-//               double-buffered TMEM accumulator (2 x 256 columns);
+//               N = one vocabulary chunk (<= 256 columns, e.g. 5 x 208 for
+//               1029 columns), fp32 accumulation in a double-buffered TMEM
+//               accumulator (2 x 256 columns). Optionally a CTA pair runs one
+//               M = 256 MMA (cta_group::2), each CTA streaming half the weights;
 //   warps 2-9   A producers: hidden = tanh(enc + dec) for the tile, converted
 //               to bf16 straight into the 128 B swizzled K-major smem layout the
 //               MMA reads (all of K stays resident while the tile's vocabulary
@@ -38,14 +42,14 @@ using namespace tc;
 
 constexpr int kBM = 128;                      // nodes per tile (UMMA M)
 constexpr int kAK = 64;                       // K width of one A chunk (128 B rows)
-constexpr int kBK = 32;                       // K width of one B stage (64 B rows)
+constexpr int kBK = 64;                       // K width of one B stage (128 B rows, = one A chunk)
 constexpr int kNC = 256;                      // vocabulary columns per chunk (UMMA N)
 constexpr int kMaxKChunks = 10;               // d rounded up to 64 must be <= 640
-constexpr int kStages = 4;
+constexpr int kStages = 2;
 constexpr int kProducerWarps = 8;
 constexpr int kThreads = 32 * (2 + kProducerWarps + 4);  // TMA, MMA, producers, epilogue
 constexpr int kAChunkBytes = kBM * kAK * 2;   // 16 KB
-constexpr int kBStageBytes = kNC * kBK * 2;   // 16 KB
+constexpr int kBStageBytes = kNC * kBK * 2;   // 32 KB
 constexpr int kMaxDurCols = 16;
 constexpr int kTmemCols = 512;
 
@@ -53,45 +57,36 @@ struct Geom {
     int kchunks;  // ceil(d / 64)
     int kpad;     // kchunks * 64
     int vpad;     // ceil((V + n_dur) / 16) * 16
-    int nfull;    // full 256-column chunks
-    int tail;     // width of the remaining chunk (multiple of 16), 0 if none
-    int nchunks;  // nfull + (tail > 0)
+    int cw;       // vocabulary columns of a chunk (multiple of 16, <= 256)
+    int lw;       // columns of the last chunk (multiple of 16, <= cw)
+    int nchunks;  // chunks per tile
 };
 
+// The vocabulary is cut into equal chunks (e.g. 1040 = 5 x 208): every chunk
+// runs the same number of full-width MMAs per weight stage, instead of a narrow
+// remainder chunk paying a full ring of weight stages for a few columns.
 Geom make_geom(const JointArgs& a) {
     Geom g;
     g.kchunks = (a.d + kAK - 1) / kAK;
     g.kpad = g.kchunks * kAK;
     g.vpad = (a.V + a.n_dur + 15) / 16 * 16;
-    g.nfull = g.vpad / kNC;
-    g.tail = g.vpad - g.nfull * kNC;
-    g.nchunks = g.nfull + (g.tail > 0 ? 1 : 0);
+    g.nchunks = (g.vpad + kNC - 1) / kNC;
+    g.cw = ((g.vpad + g.nchunks - 1) / g.nchunks + 15) / 16 * 16;
+    g.nchunks = (g.vpad + g.cw - 1) / g.cw;
+    g.lw = g.vpad - (g.nchunks - 1) * g.cw;
     return g;
 }
 
-// Chunk j of a tile: the narrow tail chunk (if any) runs first, so that the
-// last chunk of every tile is a full 256-wide one that overlaps the next tile's
-// A production.
 __device__ __forceinline__ void chunk_of(const Geom& g, int j, int& col, int& width) {
-    if (g.tail > 0) {
-        if (j == 0) {
-            col = g.nfull * kNC;
-            width = g.tail;
-        } else {
-            col = (j - 1) * kNC;
-            width = kNC;
-        }
-    } else {
-        col = j * kNC;
-        width = kNC;
-    }
+    col = j * g.cw;
+    width = j == g.nchunks - 1 ? g.lw : g.cw;
 }
 
 struct Smem {
     uint8_t* a;         // kchunks x 16 KB
-    uint8_t* b;         // kStages x 16 KB
-    uint64_t* b_full;   // [kStages]
-    uint64_t* b_empty;  // [kStages]
+    uint8_t* b;         // 64 KB weight ring (kStages x 16 KB, or 2 kStages x 8 KB for a pair)
+    uint64_t* b_full;   // [2 kStages]
+    uint64_t* b_empty;  // [2 kStages]
     uint64_t* a_full;   // [kMaxKChunks]
     uint64_t* a_empty;  // [kMaxKChunks]
     uint64_t* t_full;   // [2]
@@ -102,7 +97,7 @@ struct Smem {
 
 __host__ __device__ constexpr size_t smem_bytes_for(int kchunks) {
     return 1024 /* alignment slack */ + (size_t)kchunks * kAChunkBytes + (size_t)kStages * kBStageBytes +
-           8 * (2 * kStages + 2 * kMaxKChunks + 5) + 16;
+           8 * (4 * kStages + 2 * kMaxKChunks + 5) + 16;
 }
 
 __device__ __forceinline__ Smem carve_smem(uint8_t* raw, int kchunks) {
@@ -114,10 +109,10 @@ __device__ __forceinline__ Smem carve_smem(uint8_t* raw, int kchunks) {
     p += (size_t)kStages * kBStageBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(p);
     s.b_full = bars;
-    s.b_empty = bars + kStages;
-    s.a_full = bars + 2 * kStages;
-    s.a_empty = bars + 2 * kStages + kMaxKChunks;
-    s.t_full = bars + 2 * kStages + 2 * kMaxKChunks;
+    s.b_empty = bars + 2 * kStages;
+    s.a_full = bars + 4 * kStages;
+    s.a_empty = bars + 4 * kStages + kMaxKChunks;
+    s.t_full = bars + 4 * kStages + 2 * kMaxKChunks;
     s.t_empty = s.t_full + 2;
     s.done = s.t_empty + 2;
     s.tmem_slot = reinterpret_cast<uint32_t*>(s.done + 1);
@@ -152,134 +147,178 @@ __device__ __forceinline__ void node_range(const TcParams& P, bool bwd, int& beg
     }
 }
 
-template <bool kBwd>
+// B ring geometry per CTA: a pair splits each 256-column chunk, so every CTA
+// streams half the weight bytes and keeps twice as many stages in flight.
+template <int kCta>
+__host__ __device__ constexpr int b_stage_bytes() { return kNC / kCta * kBK * 2; }
+template <int kCta>
+__host__ __device__ constexpr int b_stages() { return kStages * kCta; }
+
+template <bool kBwd, int kCta>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_joint_kernel(const __grid_constant__ CUtensorMap map_full, const __grid_constant__ CUtensorMap map_tail,
                     TcParams P) {
     extern __shared__ uint8_t smem_raw[];
+    constexpr int SB = b_stage_bytes<kCta>();
+    constexpr int NS = b_stages<kCta>();
     const Geom g = P.g;
     Smem sm = carve_smem(smem_raw, g.kchunks);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* err = P.err;
+    const uint32_t rank = kCta == 2 ? cluster_ctarank() : 0;
+    const bool leader = rank == 0;
+    // work units: one 128-node tile (kCta = 1) or a pair of consecutive tiles,
+    // tile 2p + rank in CTA `rank` (kCta = 2)
+    const int unit0 = blockIdx.x / kCta, units_stride = gridDim.x / kCta;
 
     int begin, end;
     node_range(P, kBwd, begin, end);
     const int ntiles = end > begin ? (end - begin + kBM - 1) / kBM : 0;
+    const int nunits = (ntiles + kCta - 1) / kCta;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(&sm.b_full[s], 1);
             mbar_init(&sm.b_empty[s], 1);
         }
         for (int k = 0; k < kMaxKChunks; ++k) {
-            mbar_init(&sm.a_full[k], kProducerWarps);
+            mbar_init(&sm.a_full[k], kProducerWarps * kCta);
             mbar_init(&sm.a_empty[k], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.t_full[i], 1);
-            mbar_init(&sm.t_empty[i], 4);
+            mbar_init(&sm.t_empty[i], 4 * kCta);
         }
         mbar_init(sm.done, 1);
         fence_barrier_init();
         prefetch_tensormap(&map_full);
         prefetch_tensormap(&map_tail);
     }
-    if (warp == 1) tmem_alloc(sm.tmem_slot, kTmemCols);
+    if (kCta == 2) {
+        cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
+        if (warp == 1) tmem_alloc_pair(sm.tmem_slot, kTmemCols);
+    } else if (warp == 1) {
+        tmem_alloc(sm.tmem_slot, kTmemCols);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *sm.tmem_slot;
+    // shared::cluster addresses of the pair's barriers
+    auto in_leader = [&](uint64_t* bar) { return kCta == 2 ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar); };
+    auto in_peer = [&](uint64_t* bar) { return mapa_shared(smem_u32(bar), 1); };
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            uint32_t issued_parity[kStages];
-            bool issued[kStages];
+            uint32_t issued_parity[NS];
+            bool issued[NS];
 #pragma unroll
-            for (int s = 0; s < kStages; ++s) issued[s] = false, issued_parity[s] = 0;
+            for (int s = 0; s < NS; ++s) issued[s] = false, issued_parity[s] = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+            for (int unit = unit0; ok && unit < nunits; unit += units_stride) {
                 for (int j = 0; ok && j < g.nchunks; ++j) {
                     int col, width;
                     chunk_of(g, j, col, width);
-                    for (int ks = 0; ks < 2 * g.kchunks; ++ks) {
-                        if (!mbar_wait(&sm.b_empty[stage], phase ^ 1, err, 1)) {
+                    const int rows = width / kCta;  // weight rows this CTA supplies
+                    for (int ks = 0; ks < g.kchunks; ++ks) {
+                        if (!mbar_wait_cluster(&sm.b_empty[stage], phase ^ 1, err, 1)) {
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(&sm.b_full[stage], (uint32_t)width * kBK * 2);
-                        tma_load_2d(sm.b + (size_t)stage * kBStageBytes, width == kNC ? &map_full : &map_tail,
-                                    ks * kBK, col, &sm.b_full[stage]);
+                        uint8_t* dst = sm.b + (size_t)stage * SB;
+                        const CUtensorMap* map = width == g.cw ? &map_full : &map_tail;
+                        if (kCta == 2) {
+                            if (leader) mbar_arrive_expect_tx(&sm.b_full[stage], (uint32_t)width * kBK * 2);
+                            tma_load_2d_pair(dst, map, ks * kBK, col + (int)rank * rows, in_leader(&sm.b_full[stage]));
+                        } else {
+                            mbar_arrive_expect_tx(&sm.b_full[stage], (uint32_t)width * kBK * 2);
+                            tma_load_2d(dst, map, ks * kBK, col, &sm.b_full[stage]);
+                        }
                         issued[stage] = true;
                         issued_parity[stage] = phase;
-                        if (++stage == kStages) {
+                        if (++stage == NS) {
                             stage = 0;
                             phase ^= 1;
                         }
                     }
                 }
             }
-            // drain: every issued copy has landed before the CTA may exit
+            // drain: every issued copy has landed before the CTA may exit (for a
+            // pair the even CTA's full barrier counts both halves)
+            if (leader) {
 #pragma unroll
-            for (int s = 0; s < kStages; ++s)
-                if (issued[s]) mbar_wait(&sm.b_full[s], issued_parity[s], err, 2);
+                for (int s = 0; s < NS; ++s)
+                    if (issued[s]) mbar_wait_cluster(&sm.b_full[s], issued_parity[s], err, 2);
+            }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc_full = idesc_bf16(kBM, kNC, false, false);
-            const uint32_t idesc_tail = idesc_bf16(kBM, g.tail > 0 ? g.tail : 16, false, false);
+        if (lane == 0 && leader) {
+            const uint32_t idesc_full = idesc_bf16(kBM * kCta, g.cw, false, false);
+            const uint32_t idesc_tail = idesc_bf16(kBM * kCta, g.lw, false, false);
             const uint32_t a_base = smem_u32(sm.a), b_base = smem_u32(sm.b);
+            auto commit_both = [&](uint64_t* bar) {
+                if (kCta == 2) {
+                    mma_commit_pair(smem_u32(bar));
+                    mma_commit_pair(in_peer(bar));
+                } else {
+                    mma_commit(bar);
+                }
+            };
             int stage = 0;
             uint32_t phase = 0;
             uint32_t q = 0;
             uint32_t it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
+            for (int unit = unit0; ok && unit < nunits; unit += units_stride, ++it) {
                 for (int j = 0; ok && j < g.nchunks; ++j, ++q) {
                     int col, width;
                     chunk_of(g, j, col, width);
                     const uint32_t buf = q & 1;
-                    if (!mbar_wait(&sm.t_empty[buf], ((q >> 1) & 1) ^ 1, err, 3)) {
+                    if (!mbar_wait_cluster(&sm.t_empty[buf], ((q >> 1) & 1) ^ 1, err, 3)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + buf * kNC;
-                    const uint32_t idesc = width == kNC ? idesc_full : idesc_tail;
-                    for (int ks = 0; ks < 2 * g.kchunks; ++ks) {
-                        const int kc = ks >> 1;
-                        if (j == 0 && (ks & 1) == 0 && !mbar_wait(&sm.a_full[kc], it & 1, err, 4)) {
+                    const uint32_t idesc = width == g.cw ? idesc_full : idesc_tail;
+                    for (int kc = 0; kc < g.kchunks; ++kc) {
+                        if (j == 0 && !mbar_wait_cluster(&sm.a_full[kc], it & 1, err, 4)) {
                             ok = false;
                             break;
                         }
-                        if (!mbar_wait(&sm.b_full[stage], phase, err, 5)) {
+                        if (!mbar_wait_cluster(&sm.b_full[stage], phase, err, 5)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
 #pragma unroll
-                        for (int kk = 0; kk < 2; ++kk) {
-                            const uint64_t ad =
-                                desc_k128(a_base + kc * kAChunkBytes + (uint32_t)(((ks & 1) * 2 + kk) * 32));
-                            const uint64_t bd = desc_k64(b_base + stage * kBStageBytes + kk * 32);
-                            mma_bf16(d_tmem, ad, bd, idesc, (ks | kk) != 0 ? 1u : 0u);
+                        for (int kk = 0; kk < kBK / 16; ++kk) {
+                            const uint64_t ad = desc_k128(a_base + kc * kAChunkBytes + kk * 32);
+                            const uint64_t bd = desc_k128(b_base + stage * SB + kk * 32);
+                            if (kCta == 2)
+                                mma_bf16_pair(d_tmem, ad, bd, idesc, (kc | kk) != 0 ? 1u : 0u);
+                            else
+                                mma_bf16(d_tmem, ad, bd, idesc, (kc | kk) != 0 ? 1u : 0u);
                         }
-                        mma_commit(&sm.b_empty[stage]);
-                        if (j == g.nchunks - 1 && (ks & 1)) mma_commit(&sm.a_empty[kc]);
-                        if (++stage == kStages) {
+                        commit_both(&sm.b_empty[stage]);
+                        if (j == g.nchunks - 1) commit_both(&sm.a_empty[kc]);
+                        if (++stage == NS) {
                             stage = 0;
                             phase ^= 1;
                         }
                     }
-                    if (ok) mma_commit(&sm.t_full[buf]);
+                    if (ok) commit_both(&sm.t_full[buf]);
                 }
             }
-            // drain: all issued MMAs complete before TMEM is released
-            mma_commit(sm.done);
+            // drain: all issued MMAs complete before either CTA releases its TMEM
+            commit_both(sm.done);
             mbar_wait(sm.done, 0, err, 6);
+        } else if (lane == 0) {
+            mbar_wait_cluster(sm.done, 0, err, 6);  // odd CTA: the even CTA's MMAs write this TMEM
         }
     } else if (warp < 2 + kProducerWarps) {
         // ---------------------------------------------------------- A producers
@@ -293,8 +332,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool vec4 = (P.a.d & 3) == 0;
         uint32_t it = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++it) {
-            const int n = begin + tile * kBM + r;
+        for (int unit = unit0; ok && unit < nunits; unit += units_stride, ++it) {
+            const int n = begin + (unit * kCta + (int)rank) * kBM + r;
             const bool valid = n < end;
             int64_t eo = 0, dofs = 0;
             if (valid) {
@@ -306,7 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* dr = P.a.dec + dofs;
             for (int kc = 0; kc < g.kchunks; ++kc) {
                 // warp-uniform outcome: lanes must not leave the loop separately
-                const bool got = __all_sync(0xffffffffu, it == 0 || mbar_wait(&sm.a_empty[kc], (it - 1) & 1, err, 7));
+                const bool got =
+                    __all_sync(0xffffffffu, it == 0 || mbar_wait_cluster(&sm.a_empty[kc], (it - 1) & 1, err, 7));
                 if (!got) {
                     ok = false;
                     break;
@@ -348,7 +388,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fence_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.a_full[kc]);
+                if (lane == 0) {
+                    if (kCta == 2)
+                        mbar_arrive_cluster(in_leader(&sm.a_full[kc]));
+                    else
+                        mbar_arrive(&sm.a_full[kc]);
+                }
             }
         }
     } else {
@@ -359,8 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int Vf = a.V + a.n_dur;
         uint32_t q = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-            const int n = begin + tile * kBM + row;
+        for (int unit = unit0; ok && unit < nunits; unit += units_stride) {
+            const int n = begin + (unit * kCta + (int)rank) * kBM + row;
             const bool valid = n < end;
             int y = -1;
             if (valid) {
@@ -381,14 +426,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ct = P.bwd.ct[n];
                 Pn = cb + ct;
 #pragma unroll
-                for (int k = 0; k < kMaxDurCols; ++k)  // duration-logit grads, used by the tail chunk
+                for (int k = 0; k < kMaxDurCols; ++k)  // duration-logit grads, used by the last chunk
                     if (k < a.n_dur) dur[k] = P.bwd.gdur[(int64_t)n * a.n_dur + k];
             }
             for (int j = 0; j < g.nchunks; ++j, ++q) {
                 int col, width;
                 chunk_of(g, j, col, width);
                 const uint32_t buf = q & 1;
-                if (!__all_sync(0xffffffffu, mbar_wait(&sm.t_full[buf], (q >> 1) & 1, err, 8))) {
+                if (!__all_sync(0xffffffffu, mbar_wait_cluster(&sm.t_full[buf], (q >> 1) & 1, err, 8))) {
                     ok = false;
                     break;
                 }
@@ -477,7 +522,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.t_empty[buf]);
+                if (lane == 0) {
+                    if (kCta == 2)
+                        mbar_arrive_cluster(in_leader(&sm.t_empty[buf]));
+                    else
+                        mbar_arrive(&sm.t_empty[buf]);
+                }
             }
             if (!kBwd && ok && valid) {
                 const float l = m + __logf(s);
@@ -504,8 +554,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
-    tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+    if (kCta == 2) {
+        cluster_sync();  // no CTA leaves while its pair may still read its smem or signal it
+        tc_fence_after();
+        if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
+    } else {
+        tc_fence_after();
+        if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+    }
 }
 
 // [joint_W; joint_W_dur] -> bf16 (vpad, kpad), zero padded; optionally also the
@@ -567,6 +623,59 @@ int dyn_smem_limit() {
     return v;
 }
 
+// CTA pairs (cta_group::2) for the joint kernel when ASR_B200_JOINT_PAIRS=1. Off
+// by default: on B200 the single-CTA kernel measured faster (5.9 vs 7.1 ms for
+// the config-5-like B = 128 forward), the pair paying cross-CTA barrier traffic
+// for a weight stream that the 128-byte stages already keep up with.
+bool joint_pairs() {
+    static const bool pairs = [] {
+        const char* e = std::getenv("ASR_B200_JOINT_PAIRS");
+        return e && e[0] == '1';
+    }();
+    return pairs;
+}
+
+// Weight tensor maps of the joint kernel: a regular chunk and the last chunk,
+// each split across the pair when pairs are used.
+bool joint_weight_maps(const Geom& g, const __nv_bfloat16* Wf, bool pairs, CUtensorMap* mfull, CUtensorMap* mtail) {
+    const int split = pairs ? 2 : 1;
+    return make_map(mfull, Wf, g.vpad, g.kpad, kBK, g.cw / split, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           make_map(mtail, Wf, g.vpad, g.kpad, kBK, g.lw / split, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Persistent launch over `tiles` 128-node tiles (at most one CTA per SM).
+template <bool kBwd>
+int launch_joint(bool pairs, int64_t tiles, size_t smem, const CUtensorMap& mfull, const CUtensorMap& mtail,
+                 const TcParams& P, cudaStream_t st) {
+    const int sms = sm_count();
+    if (!pairs) {
+        ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sms));
+        tc_joint_kernel<kBwd, 1><<<grid, kThreads, smem, st>>>(mfull, mtail, P);
+        ASR_LAUNCH_CHECK();
+        return ASR_OK;
+    }
+    ASR_CUDA_TRY(
+        cudaFuncSetAttribute(tc_joint_kernel<kBwd, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int64_t units = (tiles + 1) / 2;
+    const int clusters = (int)std::max<int64_t>(1, std::min<int64_t>(units, sms / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ASR_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc_joint_kernel<kBwd, 2>, mfull, mtail, P));
+    return ASR_OK;
+}
+
 }  // namespace
 
 bool tc_supported(const JointArgs& a) {
@@ -594,27 +703,18 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, void* scratch, si
                                                              nullptr);
         ASR_LAUNCH_CHECK();
     }
+    const bool pairs = joint_pairs();
     CUtensorMap mfull, mtail;
-    if (!make_map(&mtail, Wf, g.vpad, g.kpad, kBK, g.tail > 0 ? g.tail : 16, CU_TENSOR_MAP_SWIZZLE_64B))
-        return ASR_ERR_CUDA;
-    if (g.nfull == 0)
-        mfull = mtail;
-    else if (!make_map(&mfull, Wf, g.vpad, g.kpad, kBK, kNC, CU_TENSOR_MAP_SWIZZLE_64B))
-        return ASR_ERR_CUDA;
+    if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
     TcParams P;
     std::memset(&P, 0, sizeof(P));
     P.a = a;
     P.g = g;
     P.fwd = o;
     P.err = err;
-    const size_t smem = smem_bytes_for(g.kchunks);
-    ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t cap_tiles = ((int64_t)a.B * a.T * a.U + kBM - 1) / kBM;
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(cap_tiles, sm_count()));
     KernelTimer kt("joint_fwd_tc", st);
-    tc_joint_kernel<false><<<grid, kThreads, smem, st>>>(mfull, mtail, P);
-    ASR_LAUNCH_CHECK();
-    return ASR_OK;
+    return launch_joint<false>(pairs, cap_tiles, smem_bytes_for(g.kchunks), mfull, mtail, P, st);
 }
 
 // =================================================================== backward
@@ -1201,13 +1301,9 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     }
     // tensor maps
     const int rows = (int)L.step;
+    const bool pairs = joint_pairs();
     CUtensorMap mfull, mtail, m_wt, m_g, m_gmn, m_hmn;
-    if (!make_map(&mtail, Wf, g.vpad, g.kpad, kBK, g.tail > 0 ? g.tail : 16, CU_TENSOR_MAP_SWIZZLE_64B))
-        return ASR_ERR_CUDA;
-    if (g.nfull == 0)
-        mfull = mtail;
-    else if (!make_map(&mfull, Wf, g.vpad, g.kpad, kBK, kNC, CU_TENSOR_MAP_SWIZZLE_64B))
-        return ASR_ERR_CUDA;
+    if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
     if (!make_map(&m_wt, Wt, g.kpad, g.vpad, kDhK, kDhM, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
     if (!make_map(&m_g, G, rows, g.vpad, kDhK, kDhNodes, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
     if (!make_map(&m_gmn, G, rows, g.vpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
@@ -1224,8 +1320,6 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     TP.range.bounds = bounds;
     TP.err = err;
     const size_t smem_fw = smem_bytes_for(g.kchunks);
-    ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fw));
-    const int grid_fw = (int)std::max<int64_t>(1, std::min<int64_t>(L.step / kBM, sms));
 
     // dH parameters: shared dec rows for the whole label range when they fit,
     // then the deepest pipeline that still fits
@@ -1266,8 +1360,8 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
         WP.pass = p;
         {
             KernelTimer kt("joint_dlogits_tc", st);
-            tc_joint_kernel<true><<<grid_fw, kThreads, smem_fw, st>>>(mfull, mtail, TP);
-            ASR_LAUNCH_CHECK();
+            const int rc = launch_joint<true>(pairs, L.step / kBM, smem_fw, mfull, mtail, TP, st);
+            if (rc != ASR_OK) return rc;
         }
         {
             KernelTimer kt("joint_dhidden_tc", st);
