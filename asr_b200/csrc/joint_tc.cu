@@ -614,6 +614,22 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int box_co
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D view of a row-major (rows, cols) bf16 matrix whose columns split into
+// blocks of 64 (cols % 64 == 0): dims (64, rows, cols / 64). A box of
+// (64, box_rows, nblk) lands in shared memory as nblk consecutive 128-byte
+// swizzled (box_rows x 64) tiles, i.e. nblk 2-D boxes in one copy.
+bool make_map_blocks(CUtensorMap* map, const void* base, int rows, int cols, int box_rows, int nblk) {
+    auto enc = tensor_map_encoder();
+    if (!enc || cols % 64 != 0) return false;
+    cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+    cuuint64_t strides[2] = {(cuuint64_t)cols * 2, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)nblk};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 int dyn_smem_limit() {
@@ -744,7 +760,7 @@ constexpr int kDhM = 128;                          // hidden columns per work it
 constexpr int kDhNodes = 256;                      // nodes per tile (UMMA N)
 constexpr int kDhK = 32;                           // vocabulary per stage (64 B rows)
 constexpr int kDhABytes = kDhM * kDhK * 2;         // 8 KB
-constexpr int kDhStageBytes = kDhABytes + kDhNodes * kDhK * 2;  // 24 KB
+constexpr int kDhStageBytes = kDhABytes + kDhNodes * kDhK * 2;  // 24 KB (4 stages beat 2 of 48 KB here)
 constexpr int kDwM = 128;         // vocabulary rows per dW work item (UMMA M)
 constexpr int kDwN = 320;         // hidden columns per dW work item (UMMA N = 256 + 64)
 constexpr int kBwdThreads = 192;  // TMA, MMA, 4 epilogue warps
@@ -996,7 +1012,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     tc_fence_after();
                     const uint32_t st = sbase + stage * kDhStageBytes;
 #pragma unroll
-                    for (int kk = 0; kk < 2; ++kk)
+                    for (int kk = 0; kk < kDhK / 16; ++kk)
                         mma_bf16(tmem_base + buf * kDhNodes, desc_k64(st + kk * 32),
                                  desc_k64(st + kDhABytes + kk * 32), idesc, (k | kk) != 0 ? 1u : 0u);
                     mma_commit(&b_empty[stage]);
@@ -1135,9 +1151,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 mbar_arrive_expect_tx(&b_full[stage], kDwStageBytes);
                 tma_load_2d(st, &map_g, vt * kDwM, r, &b_full[stage]);
                 tma_load_2d(st + kBox, &map_g, vt * kDwM + 64, r, &b_full[stage]);
-#pragma unroll
-                for (int j = 0; j < kDwN / 64; ++j)
-                    tma_load_2d(st + (2 + j) * kBox, &map_h, kt * kDwN + j * 64, r, &b_full[stage]);
+                // H: kDwN / 64 column blocks of 64 in one box of the 3-D view
+                tma_load_3d(st + 2 * kBox, &map_h, 0, r, kt * (kDwN / 64), &b_full[stage]);
                 issued[stage] = true;
                 ipar[stage] = phase;
                 if (++stage == kDwStages) {
@@ -1307,7 +1322,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     if (!make_map(&m_wt, Wt, g.kpad, g.vpad, kDhK, kDhM, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
     if (!make_map(&m_g, G, rows, g.vpad, kDhK, kDhNodes, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
     if (!make_map(&m_gmn, G, rows, g.vpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
-    if (!make_map(&m_hmn, H, rows, g.kpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
+    if (!make_map_blocks(&m_hmn, H, rows, g.kpad, 64, kDwN / 64)) return ASR_ERR_CUDA;
 
     // dlogits kernel parameters
     TcParams TP;
