@@ -34,7 +34,7 @@ struct TrWorkspace {
 };
 
 size_t joint_scratch_bytes(const JointArgs& a, int64_t cap, bool tc, bool backward) {
-    if (tc) return backward ? tc_backward_scratch_bytes(a, (int)cap) : tc_forward_scratch_bytes(a);
+    if (tc) return backward ? tc_backward_scratch_bytes(a, (int)cap) : tc_forward_scratch_bytes(a, (int)cap);
     return backward ? simt_backward_scratch_bytes(a.V + a.n_dur, (int)cap) : 0;
 }
 
@@ -143,7 +143,7 @@ extern "C" int asr_rnnt_forward(const float* encoder, const float* decoder, cons
     int rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
     if (rc) return rc;
     JointFwdOut o{log_P_blank, log_P_blank + cap, log_P_y, nullptr};
-    rc = tc ? tc_joint_forward(a, o, w.joint, w.joint_bytes, st) : simt_joint_forward(a, o, st);
+    rc = tc ? tc_joint_forward(a, o, (int)cap, w.joint, w.joint_bytes, st) : simt_joint_forward(a, o, st);
     if (rc) return rc;
     return launch_rnnt_alpha(w.meta, B, U, log_P_blank, log_P_y, alpha, log_prob, loss, st);
 }
@@ -225,7 +225,7 @@ extern "C" int asr_tdt_forward(const float* encoder, const float* decoder, const
     int rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
     if (rc) return rc;
     JointFwdOut o{log_P_blank, log_P_blank + cap, log_P_y, log_P_dur};
-    rc = tc ? tc_joint_forward(a, o, w.joint, w.joint_bytes, st) : simt_joint_forward(a, o, st);
+    rc = tc ? tc_joint_forward(a, o, (int)cap, w.joint, w.joint_bytes, st) : simt_joint_forward(a, o, st);
     if (rc) return rc;
     return launch_tdt_alpha(w.meta, B, U, max_duration, durations, n_dur, has_zero, log_P_blank, log_P_y, log_P_dur,
                             alpha, log_prob, loss, st);

@@ -54,8 +54,8 @@ int simt_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwd
 
 // ---- bf16 tcgen05 path --------------------------------------------------------
 bool tc_supported(const JointArgs& a);
-size_t tc_forward_scratch_bytes(const JointArgs& a);
-int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, void* scratch, size_t scratch_bytes,
+size_t tc_forward_scratch_bytes(const JointArgs& a, int node_capacity);
+int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity, void* scratch, size_t scratch_bytes,
                      cudaStream_t st);
 bool tc_backward_supported(const JointArgs& a);
 size_t tc_backward_scratch_bytes(const JointArgs& a, int node_capacity);

@@ -46,8 +46,8 @@ constexpr int kBK = 64;                       // K width of one B stage (128 B r
 constexpr int kNC = 256;                      // vocabulary columns per chunk (UMMA N)
 constexpr int kMaxKChunks = 10;               // d rounded up to 64 must be <= 640
 constexpr int kStages = 2;
-constexpr int kProducerWarps = 8;
-constexpr int kThreads = 32 * (2 + kProducerWarps + 4);  // TMA, MMA, producers, epilogue
+constexpr int kEpilogueWarp0 = 4;                    // warps 4-7: epilogue (one TMEM lane quarter each)
+constexpr int kThreads = 32 * (kEpilogueWarp0 + 4);  // weight TMA, MMA, hidden TMA, idle, epilogue
 constexpr int kAChunkBytes = kBM * kAK * 2;   // 16 KB
 constexpr int kBStageBytes = kNC * kBK * 2;   // 32 KB
 constexpr int kMaxDurCols = 16;
@@ -131,20 +131,14 @@ struct TcParams {
     JointFwdOut fwd;  // forward outputs
     JointBwdIn bwd;   // backward inputs
     __nv_bfloat16* G;  // backward: (pass nodes, vpad) d loss / d logits
-    __nv_bfloat16* H;  // backward: (pass nodes, kpad) hidden
-    PassRange range;   // backward pass
+    PassRange range;   // node pass
     int* err;
 };
 
-__device__ __forceinline__ void node_range(const TcParams& P, bool bwd, int& begin, int& end) {
+__device__ __forceinline__ void node_range(const TcParams& P, bool, int& begin, int& end) {
     const int N = total_nodes(P.a.m, P.a.B);
-    if (!bwd) {
-        begin = 0;
-        end = N;
-    } else {
-        begin = min(P.range.bounds[P.range.pass], N);
-        end = min(P.range.bounds[P.range.pass + 1], N);
-    }
+    begin = min(P.range.bounds[P.range.pass], N);
+    end = min(P.range.bounds[P.range.pass + 1], N);
 }
 
 // B ring geometry per CTA: a pair splits each 256-column chunk, so every CTA
@@ -157,7 +151,7 @@ __host__ __device__ constexpr int b_stages() { return kStages * kCta; }
 template <bool kBwd, int kCta>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_joint_kernel(const __grid_constant__ CUtensorMap map_full, const __grid_constant__ CUtensorMap map_tail,
-                    TcParams P) {
+                    const __grid_constant__ CUtensorMap map_h, TcParams P) {
     extern __shared__ uint8_t smem_raw[];
     constexpr int SB = b_stage_bytes<kCta>();
     constexpr int NS = b_stages<kCta>();
@@ -182,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm.b_empty[s], 1);
         }
         for (int k = 0; k < kMaxKChunks; ++k) {
-            mbar_init(&sm.a_full[k], kProducerWarps * kCta);
+            mbar_init(&sm.a_full[k], 1);  // the hidden-tile loader's expect_tx arrival
             mbar_init(&sm.a_empty[k], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -193,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         prefetch_tensormap(&map_full);
         prefetch_tensormap(&map_tail);
+        prefetch_tensormap(&map_h);
     }
     if (kCta == 2) {
         cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
@@ -320,83 +315,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (lane == 0) {
             mbar_wait_cluster(sm.done, 0, err, 6);  // odd CTA: the even CTA's MMAs write this TMEM
         }
-    } else if (warp < 2 + kProducerWarps) {
-        // ---------------------------------------------------------- A producers
-        // Two threads per tile row, each building 32 of the 64 K columns of every
-        // chunk: all 16 float4 loads of a half-chunk are issued before any tanh so
-        // each thread keeps 256 bytes in flight.
-        const int p = threadIdx.x - 64;  // 0..255
-        const int r = p & (kBM - 1);     // tile row
-        const int half = p >> 7;         // which 32 columns of each 64-wide chunk
-        const int row_off = (r >> 3) * 1024 + (r & 7) * 128;
-        const bool vec4 = (P.a.d & 3) == 0;
-        uint32_t it = 0;
-        bool ok = true;
-        for (int unit = unit0; ok && unit < nunits; unit += units_stride, ++it) {
-            const int n = begin + (unit * kCta + (int)rank) * kBM + r;
-            const bool valid = n < end;
-            int64_t eo = 0, dofs = 0;
-            if (valid) {
-                const NodeCoord c = node_coord(P.a.m, P.a.B, n);
-                eo = ((int64_t)c.b * P.a.T + c.t) * P.a.d;
-                dofs = ((int64_t)c.b * P.a.U + c.u) * P.a.d;
+    } else if (warp == 2) {
+        // ------------------------------------------------------- hidden-tile TMA
+        // The tile's rows of H = bf16(tanh(enc + dec)) (written by hidden_kernel
+        // for this pass) into the resident 128 B swizzled K chunks; chunk kc of
+        // the next tile is reloaded as soon as the last vocabulary chunk of the
+        // current tile has consumed it.
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            bool issued[kMaxKChunks];
+            uint32_t ipar[kMaxKChunks];
+#pragma unroll
+            for (int k = 0; k < kMaxKChunks; ++k) issued[k] = false, ipar[k] = 0;
+            for (int unit = unit0; ok && unit < nunits; unit += units_stride, ++it) {
+                const int row0 = (unit * kCta + (int)rank) * kBM;  // pass-relative H row
+                for (int kc = 0; kc < g.kchunks; ++kc) {
+                    if (it > 0 && !mbar_wait_cluster(&sm.a_empty[kc], (it - 1) & 1, err, 7)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* dst = sm.a + (size_t)kc * kAChunkBytes;
+                    if (kCta == 2) {
+                        if (leader) mbar_arrive_expect_tx(&sm.a_full[kc], 2 * kAChunkBytes);
+                        tma_load_2d_pair(dst, &map_h, kc * kAK, row0, in_leader(&sm.a_full[kc]));
+                    } else {
+                        mbar_arrive_expect_tx(&sm.a_full[kc], kAChunkBytes);
+                        tma_load_2d(dst, &map_h, kc * kAK, row0, &sm.a_full[kc]);
+                    }
+                    issued[kc] = true;
+                    ipar[kc] = it & 1;
+                }
             }
-            const float* er = P.a.enc + eo;
-            const float* dr = P.a.dec + dofs;
-            for (int kc = 0; kc < g.kchunks; ++kc) {
-                // warp-uniform outcome: lanes must not leave the loop separately
-                const bool got =
-                    __all_sync(0xffffffffu, it == 0 || mbar_wait_cluster(&sm.a_empty[kc], (it - 1) & 1, err, 7));
-                if (!got) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* arow = sm.a + (size_t)kc * kAChunkBytes + row_off;
-                const int kbase = kc * kAK + half * 32;
-                float h[32];
-                if (valid && vec4 && kbase + 32 <= P.a.d) {
-                    float4 e[8], dd[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        e[i] = __ldg(reinterpret_cast<const float4*>(er + kbase) + i);
-                        dd[i] = __ldg(reinterpret_cast<const float4*>(dr + kbase) + i);
-                    }
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        h[4 * i + 0] = tanh_fast(e[i].x + dd[i].x);
-                        h[4 * i + 1] = tanh_fast(e[i].y + dd[i].y);
-                        h[4 * i + 2] = tanh_fast(e[i].z + dd[i].z);
-                        h[4 * i + 3] = tanh_fast(e[i].w + dd[i].w);
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int k = kbase + i;
-                        h[i] = (valid && k < P.a.d) ? tanh_fast(__ldg(er + k) + __ldg(dr + k)) : 0.f;
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int u = half * 4 + q;  // 16-byte unit within the 128-byte row
-                    uint4 w;
-                    w.x = pack_bf16(h[8 * q + 0], h[8 * q + 1]);
-                    w.y = pack_bf16(h[8 * q + 2], h[8 * q + 3]);
-                    w.z = pack_bf16(h[8 * q + 4], h[8 * q + 5]);
-                    w.w = pack_bf16(h[8 * q + 6], h[8 * q + 7]);
-                    *reinterpret_cast<uint4*>(arow + ((u ^ (r & 7)) << 4)) = w;
-                    if (kBwd) *reinterpret_cast<uint4*>(P.H + (int64_t)(n - begin) * g.kpad + kbase + 8 * q) = w;
-                }
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    if (kCta == 2)
-                        mbar_arrive_cluster(in_leader(&sm.a_full[kc]));
-                    else
-                        mbar_arrive(&sm.a_full[kc]);
-                }
+            // drain: every issued copy has landed before the CTA may exit
+            if (leader) {
+                for (int kc = 0; kc < g.kchunks; ++kc)
+                    if (issued[kc]) mbar_wait_cluster(&sm.a_full[kc], ipar[kc], err, 17);
             }
         }
-    } else {
+    } else if (warp >= kEpilogueWarp0) {
         // --------------------------------------------------------------- epilogue
         const int lane_base = 32 * (warp & 3);
         const int row = lane_base + lane;
@@ -639,6 +596,144 @@ int dyn_smem_limit() {
     return v;
 }
 
+// ------------------------------------------------------------------ passes
+//
+// Both directions run over passes of at most kMaxPassNodes nodes (or the
+// ASR_B200_BWD_PASS_NODES override: a tuning knob, small values exercise
+// multi-pass runs), so the per-pass bf16 buffers (H, and G in the backward)
+// stay bounded whatever the batch.
+constexpr int64_t kMaxPassNodes = 4 << 20;
+constexpr int kPassAlign = 256;  // pass rows are padded to whole 256-row tiles
+
+int64_t pass_nodes_limit() {
+    const char* env = std::getenv("ASR_B200_BWD_PASS_NODES");
+    if (env) {
+        const long long v = std::atoll(env);
+        if (v > 0) return v;
+    }
+    return kMaxPassNodes;
+}
+
+struct PassPlan {
+    int64_t step;  // nodes per pass (multiple of kPassAlign) = rows of the per-pass buffers
+    int passes;
+};
+
+PassPlan pass_plan(int64_t cap) {
+    PassPlan pp;
+    const int64_t want = std::max<int64_t>(1, std::min<int64_t>(cap, pass_nodes_limit()));
+    pp.step = (want + kPassAlign - 1) / kPassAlign * kPassAlign;
+    pp.passes = (int)std::max<int64_t>(1, (cap + pp.step - 1) / pp.step);
+    return pp;
+}
+
+// bounds[p] = first node of pass p (p = 0..P), clamped to the node count.
+__global__ void plan_passes_kernel(LatticeMeta m, int B, int P, int64_t step, int32_t* __restrict__ bounds) {
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p > P) return;
+    const int N = total_nodes(m, B);
+    bounds[p] = (p == P) ? N : (int)std::min<int64_t>((int64_t)p * step, N);
+}
+
+// H[r, k] = bf16(tanh(enc[b, t, k] + dec[b, u, k])) for the pass's node r (row
+// r = node - pass start, k < kpad, zero for k >= d), 16-byte stores. Each warp
+// walks a run of kHiddenRun consecutive rows (one coordinate search per run,
+// then (t, u) increments), so consecutive nodes of a frame share their enc row
+// and neighbouring dec rows in L1. Rows from the pass end up to the next
+// 256-row boundary are zeroed: the joint kernels read whole tiles. HBM bound
+// (1280 B written per node at d = 640).
+constexpr int kHiddenRun = 64;
+
+__global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, const float* __restrict__ enc,
+                                                        const float* __restrict__ dec, int T, int U, int d, int kpad,
+                                                        const int32_t* __restrict__ bounds, int pass,
+                                                        __nv_bfloat16* __restrict__ H) {
+    const int N = total_nodes(m, B);
+    const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
+    const int rows = e - s;
+    const int rows_pad = (rows + kPassAlign - 1) / kPassAlign * kPassAlign;
+    const int c8n = kpad / 8;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int r0 = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kHiddenRun; r0 < rows_pad;
+         r0 += nwarps * kHiddenRun) {
+        const int r1 = min(r0 + kHiddenRun, rows_pad);
+        NodeCoord c{};
+        int Tb = 0;
+        if (r0 < rows) {
+            c = node_coord(m, B, s + r0);
+            Tb = __ldg(m.Tb + c.b);
+        }
+        for (int r = r0; r < r1; ++r) {
+            uint4* dst = reinterpret_cast<uint4*>(H + (int64_t)r * kpad);
+            if (r >= rows) {
+                for (int k8 = lane; k8 < c8n; k8 += 32) dst[k8] = make_uint4(0, 0, 0, 0);
+                continue;
+            }
+            const float* er = enc + ((int64_t)c.b * T + c.t) * d;
+            const float* dr = dec + ((int64_t)c.b * U + c.u) * d;
+            if ((d & 7) == 0 && c8n <= 3 * 32) {
+                // up to three 8-column groups per lane (d % 8 == 0, kpad <= 768): every
+                // load of the row in flight at once; groups at or past d stay zero
+                float4 ev[3][2], dv[3][2];
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    const int k = (lane + 32 * j) * 8;
+                    if (k + 8 <= d) {
+                        ev[j][0] = __ldg(reinterpret_cast<const float4*>(er + k));
+                        ev[j][1] = __ldg(reinterpret_cast<const float4*>(er + k) + 1);
+                        dv[j][0] = __ldg(reinterpret_cast<const float4*>(dr + k));
+                        dv[j][1] = __ldg(reinterpret_cast<const float4*>(dr + k) + 1);
+                    } else {
+                        ev[j][0] = ev[j][1] = dv[j][0] = dv[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    const int k8 = lane + 32 * j;
+                    if (k8 >= c8n) break;
+                    // columns d..kpad of the last group stay zero (tanh(0) = 0)
+                    uint4 w;
+                    w.x = pack_bf16(tanh_fast(ev[j][0].x + dv[j][0].x), tanh_fast(ev[j][0].y + dv[j][0].y));
+                    w.y = pack_bf16(tanh_fast(ev[j][0].z + dv[j][0].z), tanh_fast(ev[j][0].w + dv[j][0].w));
+                    w.z = pack_bf16(tanh_fast(ev[j][1].x + dv[j][1].x), tanh_fast(ev[j][1].y + dv[j][1].y));
+                    w.w = pack_bf16(tanh_fast(ev[j][1].z + dv[j][1].z), tanh_fast(ev[j][1].w + dv[j][1].w));
+                    dst[k8] = w;
+                }
+            } else {
+                for (int k8 = lane; k8 < c8n; k8 += 32) {
+                    const int k = k8 * 8;
+                    float h[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        h[i] = k + i < d ? tanh_fast(__ldg(er + k + i) + __ldg(dr + k + i)) : 0.f;
+                    uint4 w;
+                    w.x = pack_bf16(h[0], h[1]);
+                    w.y = pack_bf16(h[2], h[3]);
+                    w.z = pack_bf16(h[4], h[5]);
+                    w.w = pack_bf16(h[6], h[7]);
+                    dst[k8] = w;
+                }
+            }
+            // next node: next label position, next frame, or the next utterance
+            if (++c.u == c.Ub) {
+                c.u = 0;
+                if (++c.t == Tb && r + 1 < rows) {
+                    c = node_coord(m, B, s + r + 1);
+                    Tb = __ldg(m.Tb + c.b);
+                }
+            }
+        }
+    }
+}
+
+int launch_hidden(const JointArgs& a, int kpad, const int32_t* bounds, int pass, __nv_bfloat16* H, cudaStream_t st) {
+    KernelTimer kt("joint_hidden", st);
+    hidden_kernel<<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.dec, a.T, a.U, a.d, kpad, bounds, pass, H);
+    ASR_LAUNCH_CHECK();
+    return ASR_OK;
+}
+
 // CTA pairs (cta_group::2) for the joint kernel when ASR_B200_JOINT_PAIRS=1. Off
 // by default: on B200 the single-CTA kernel measured faster (5.9 vs 7.1 ms for
 // the config-5-like B = 128 forward), the pair paying cross-CTA barrier traffic
@@ -662,13 +757,13 @@ bool joint_weight_maps(const Geom& g, const __nv_bfloat16* Wf, bool pairs, CUten
 // Persistent launch over `tiles` 128-node tiles (at most one CTA per SM).
 template <bool kBwd>
 int launch_joint(bool pairs, int64_t tiles, size_t smem, const CUtensorMap& mfull, const CUtensorMap& mtail,
-                 const TcParams& P, cudaStream_t st) {
+                 const CUtensorMap& mh, const TcParams& P, cudaStream_t st) {
     const int sms = sm_count();
     if (!pairs) {
         ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem));
         const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sms));
-        tc_joint_kernel<kBwd, 1><<<grid, kThreads, smem, st>>>(mfull, mtail, P);
+        tc_joint_kernel<kBwd, 1><<<grid, kThreads, smem, st>>>(mfull, mtail, mh, P);
         ASR_LAUNCH_CHECK();
         return ASR_OK;
     }
@@ -688,7 +783,7 @@ int launch_joint(bool pairs, int64_t tiles, size_t smem, const CUtensorMap& mful
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ASR_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc_joint_kernel<kBwd, 2>, mfull, mtail, P));
+    ASR_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc_joint_kernel<kBwd, 2>, mfull, mtail, mh, P));
     return ASR_OK;
 }
 
@@ -700,37 +795,73 @@ bool tc_supported(const JointArgs& a) {
            (int)smem_bytes_for(g.kchunks) <= dyn_smem_limit();
 }
 
-// Forward scratch: bf16 weights + the kernel error word.
-size_t tc_forward_scratch_bytes(const JointArgs& a) {
+// Forward scratch: bf16 weights, the per-pass hidden rows, pass bounds, error word.
+struct FwdLayout {
+    PassPlan pp;
+    size_t wf, h, bounds, err, total;
+};
+
+FwdLayout fwd_layout(const JointArgs& a, int64_t cap) {
     const Geom g = make_geom(a);
-    return al256(sizeof(__nv_bfloat16) * (size_t)g.vpad * g.kpad) + 256;
+    FwdLayout L;
+    L.pp = pass_plan(cap);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += al256(bytes);
+        return o;
+    };
+    L.wf = take(sizeof(__nv_bfloat16) * (size_t)g.vpad * g.kpad);
+    L.h = take(sizeof(__nv_bfloat16) * (size_t)L.pp.step * g.kpad);
+    L.bounds = take(sizeof(int32_t) * (L.pp.passes + 1));
+    L.err = take(sizeof(int));
+    L.total = off;
+    return L;
 }
 
-int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, void* scratch, size_t scratch_bytes,
+size_t tc_forward_scratch_bytes(const JointArgs& a, int node_capacity) {
+    return fwd_layout(a, node_capacity).total + 256;
+}
+
+int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity, void* scratch, size_t scratch_bytes,
                      cudaStream_t st) {
     const Geom g = make_geom(a);
-    if (scratch_bytes < tc_forward_scratch_bytes(a)) return ASR_ERR_WORKSPACE;
-    auto* Wf = reinterpret_cast<__nv_bfloat16*>(scratch);
-    int* err = reinterpret_cast<int*>(reinterpret_cast<char*>(scratch) + al256(sizeof(__nv_bfloat16) * (size_t)g.vpad * g.kpad));
+    const FwdLayout L = fwd_layout(a, node_capacity);
+    if (scratch_bytes < L.total) return ASR_ERR_WORKSPACE;
+    char* base = reinterpret_cast<char*>(scratch);
+    auto* Wf = reinterpret_cast<__nv_bfloat16*>(base + L.wf);
+    auto* H = reinterpret_cast<__nv_bfloat16*>(base + L.h);
+    auto* bounds = reinterpret_cast<int32_t*>(base + L.bounds);
+    int* err = reinterpret_cast<int*>(base + L.err);
     ASR_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
     {
         KernelTimer kt("joint_prep_weights", st);
         prep_weights_kernel<<<sm_count() * 4, 256, 0, st>>>(a.W, a.Wd, a.V, a.n_dur, a.d, g.vpad, g.kpad, Wf,
                                                              nullptr);
         ASR_LAUNCH_CHECK();
+        plan_passes_kernel<<<(L.pp.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, L.pp.passes, L.pp.step, bounds);
+        ASR_LAUNCH_CHECK();
     }
     const bool pairs = joint_pairs();
-    CUtensorMap mfull, mtail;
+    CUtensorMap mfull, mtail, mh;
     if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
+    if (!make_map(&mh, H, (int)L.pp.step, g.kpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
     TcParams P;
     std::memset(&P, 0, sizeof(P));
     P.a = a;
     P.g = g;
     P.fwd = o;
+    P.range.bounds = bounds;
     P.err = err;
-    const int64_t cap_tiles = ((int64_t)a.B * a.T * a.U + kBM - 1) / kBM;
-    KernelTimer kt("joint_fwd_tc", st);
-    return launch_joint<false>(pairs, cap_tiles, smem_bytes_for(g.kchunks), mfull, mtail, P, st);
+    for (int p = 0; p < L.pp.passes; ++p) {
+        P.range.pass = p;
+        int rc = launch_hidden(a, g.kpad, bounds, p, H, st);
+        if (rc != ASR_OK) return rc;
+        KernelTimer kt("joint_fwd_tc", st);
+        rc = launch_joint<false>(pairs, L.pp.step / kBM, smem_bytes_for(g.kchunks), mfull, mtail, mh, P, st);
+        if (rc != ASR_OK) return rc;
+    }
+    return ASR_OK;
 }
 
 // =================================================================== backward
@@ -765,16 +896,6 @@ constexpr int kDwM = 128;         // vocabulary rows per dW work item (UMMA M)
 constexpr int kDwN = 320;         // hidden columns per dW work item (UMMA N = 256 + 64)
 constexpr int kBwdThreads = 192;  // TMA, MMA, 4 epilogue warps
 constexpr int kDwStageBytes = (2 + kDwN / 64) * 64 * 64 * 2;  // 2 + 5 boxes of 64 x 64, 56 KB
-constexpr int64_t kMaxPassNodes = 4 << 20;
-
-// bounds[p] = first node of pass p (p = 0..P), clamped to the node count.
-__global__ void plan_passes_kernel(LatticeMeta m, int B, int P, int64_t step, int32_t* __restrict__ bounds) {
-    const int p = blockIdx.x * blockDim.x + threadIdx.x;
-    if (p > P) return;
-    const int N = total_nodes(m, B);
-    bounds[p] = (p == P) ? N : (int)std::min<int64_t>((int64_t)p * step, N);
-}
-
 struct DhParams {
     JointArgs a;
     Geom g;
@@ -1234,28 +1355,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // ---------------------------------------------------------- backward host side
 
 struct BwdLayout {
-    int64_t step;  // nodes per pass (multiple of kDhNodes) = rows of the G / H buffers
+    int64_t step;  // nodes per pass (multiple of kPassAlign = kDhNodes) = rows of the G / H buffers
     int passes;
     size_t wf, wt, g, h, bounds, err, total;
 };
 
-// Nodes per backward pass: at most kMaxPassNodes, or the ASR_B200_BWD_PASS_NODES
-// environment override (a tuning knob; small values exercise multi-pass runs).
-int64_t pass_nodes_limit() {
-    const char* env = std::getenv("ASR_B200_BWD_PASS_NODES");
-    if (env) {
-        const long long v = std::atoll(env);
-        if (v > 0) return v;
-    }
-    return kMaxPassNodes;
-}
-
 BwdLayout bwd_layout(const JointArgs& a, int64_t cap) {
     const Geom g = make_geom(a);
     BwdLayout L;
-    const int64_t want = std::max<int64_t>(1, std::min<int64_t>(cap, pass_nodes_limit()));
-    L.step = (want + kDhNodes - 1) / kDhNodes * kDhNodes;
-    L.passes = (int)std::max<int64_t>(1, (cap + L.step - 1) / L.step);
+    const PassPlan pp = pass_plan(cap);
+    L.step = pp.step;
+    L.passes = pp.passes;
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
@@ -1317,8 +1427,9 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     // tensor maps
     const int rows = (int)L.step;
     const bool pairs = joint_pairs();
-    CUtensorMap mfull, mtail, m_wt, m_g, m_gmn, m_hmn;
+    CUtensorMap mfull, mtail, m_h, m_wt, m_g, m_gmn, m_hmn;
     if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
+    if (!make_map(&m_h, H, rows, g.kpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
     if (!make_map(&m_wt, Wt, g.kpad, g.vpad, kDhK, kDhM, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
     if (!make_map(&m_g, G, rows, g.vpad, kDhK, kDhNodes, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
     if (!make_map(&m_gmn, G, rows, g.vpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
@@ -1331,7 +1442,6 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     TP.g = g;
     TP.bwd = in;
     TP.G = G;
-    TP.H = H;
     TP.range.bounds = bounds;
     TP.err = err;
     const size_t smem_fw = smem_bytes_for(g.kchunks);
@@ -1375,7 +1485,9 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
         WP.pass = p;
         {
             KernelTimer kt("joint_dlogits_tc", st);
-            const int rc = launch_joint<true>(pairs, L.step / kBM, smem_fw, mfull, mtail, TP, st);
+            int rc = launch_hidden(a, g.kpad, bounds, p, H, st);
+            if (rc != ASR_OK) return rc;
+            rc = launch_joint<true>(pairs, L.step / kBM, smem_fw, mfull, mtail, m_h, TP, st);
             if (rc != ASR_OK) return rc;
         }
         {
