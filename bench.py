@@ -161,13 +161,18 @@ GEMM_KERNELS = ("joint_fwd_tc", "joint_dlogits_tc", "joint_dhidden_tc", "joint_d
                 "joint_fwd_simt", "joint_dlogits_simt", "joint_dhidden_simt", "joint_dweight_simt")
 
 
-def kernel_work(name, N, d, Vf, n_dur):
+def kernel_work(name, N, d, Vf, n_dur, frames=0, labels=0):
     """Algorithmic work of one step of kernel `name`: ('tensor', flops) or ('hbm', bytes).
     Joint GEMMs: 2 * N * d * Vf each (forward, backward recompute, d_hidden, dW).
+    Hidden rows (forward and backward): bf16 H written (2 * ceil64(d) bytes per
+    node) plus the fp32 enc / dec rows read once (frames + labels rows of d floats).
     Recursions: per node, the 4-byte lattice weights read plus the float64 alpha
     written (alpha) or read (beta) plus the 4-byte posteriors written (beta)."""
     if name in GEMM_KERNELS:
         return "tensor", 2.0 * N * d * Vf
+    if name == "joint_hidden":
+        kpad = (d + 63) // 64 * 64
+        return "hbm", 2.0 * (N * 2.0 * kpad + (frames + labels) * d * 4.0)
     if name == "tdt_alpha":
         return "hbm", N * (4.0 * (2 + n_dur) + 8.0)
     if name == "tdt_beta_posteriors":
@@ -403,7 +408,8 @@ def main():
     per_kernel = {}
     total_ms = max(sum(v[1] for v in prof.values()), 1e-9)
     for name, (launches, kms) in prof.items():
-        bound, work = kernel_work(name, N_local, D_MODEL, Vf, len(DURATIONS))
+        bound, work = kernel_work(name, N_local, D_MODEL, Vf, len(DURATIONS), frames=int(host["in_lens"].sum()),
+                                  labels=int((host["tgt_lens"] + 1).sum()))
         per_launch_ms = kms / max(launches, 1)
         steps_launches = launches / args.steps
         work_per_launch = work / max(steps_launches, 1)
