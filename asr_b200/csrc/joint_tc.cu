@@ -882,7 +882,7 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
 //               the fp32 activations (a register copy of the frame's enc value
 //               and a shared copy of the utterance's dec rows).
 //   dW  kernel: split-K over the pass rows, D = G^T H (M = 128 vocabulary rows,
-//               N = 320 hidden columns, both operands MN-major straight from G
+//               N = 320 hidden columns as 192 + 128, both operands MN-major from G
 //               and H), added to dW / dW_dur once per CTA.
 
 namespace {
@@ -893,7 +893,7 @@ constexpr int kDhK = 32;                           // vocabulary per stage (64 B
 constexpr int kDhABytes = kDhM * kDhK * 2;         // 8 KB
 constexpr int kDhStageBytes = kDhABytes + kDhNodes * kDhK * 2;  // 24 KB (4 stages beat 2 of 48 KB here)
 constexpr int kDwM = 128;         // vocabulary rows per dW work item (UMMA M)
-constexpr int kDwN = 320;         // hidden columns per dW work item (UMMA N = 256 + 64)
+constexpr int kDwN = 320;         // hidden columns per dW work item (UMMA N = 192 + 128)
 constexpr int kBwdThreads = 192;  // TMA, MMA, 4 epilogue warps
 constexpr int kDwStageBytes = (2 + kDwN / 64) * 64 * 64 * 2;  // 2 + 5 boxes of 64 x 64, 56 KB
 struct DhParams {
@@ -1232,9 +1232,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int nvt = (P.g.vpad + kDwM - 1) / kDwM;
     const int nkt = (P.g.kpad + kDwN - 1) / kDwN;
     const int item = blockIdx.x;
-    const int split = item % P.splits;
-    const int kt = (item / P.splits) % nkt;
-    const int vt = item / (P.splits * nkt);
+    // split slowest: the CTAs of one row range run side by side and share its G / H rows in L2
+    const int vt = item % nvt;
+    const int kt = (item / nvt) % nkt;
+    const int split = item / (nvt * nkt);
     const int s = P.bounds[P.pass], e = P.bounds[P.pass + 1];
     const int rows = e > s ? (e - s + 63) / 64 * 64 : 0;  // zero rows pad the pass to 64
     const int per = ((rows / 64 + P.splits - 1) / P.splits) * 64;
@@ -1286,8 +1287,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t id256 = idesc_bf16(kDwM, 256, true, true);
-            const uint32_t id64 = idesc_bf16(kDwM, 64, true, true);
+            // N = 320 as 192 + 128 (both start on a 64-column block; an N = 64 MMA
+            // would be issue-bound)
+            const uint32_t id_a = idesc_bf16(kDwM, 192, true, true);
+            const uint32_t id_b = idesc_bf16(kDwM, 128, true, true);
             const uint32_t sbase = smem_u32(stages);
             int stage = 0;
             uint32_t phase = 0;
@@ -1303,10 +1306,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 for (int ks = 0; ks < 4; ++ks) {  // 16 rows (K) per MMA
                     const uint64_t ad = desc_mn128(st + ks * 2048, kBox);
                     const uint64_t b0 = desc_mn128(st + 2 * kBox + ks * 2048, kBox);
-                    const uint64_t b1 = desc_mn128(st + 6 * kBox + ks * 2048, kBox);
+                    const uint64_t b1 = desc_mn128(st + 5 * kBox + ks * 2048, kBox);
                     const uint32_t acc = (i | ks) != 0 ? 1u : 0u;
-                    mma_bf16(tmem_base, ad, b0, id256, acc);
-                    mma_bf16(tmem_base + 256, ad, b1, id64, acc);
+                    mma_bf16(tmem_base, ad, b0, id_a, acc);
+                    mma_bf16(tmem_base + 192, ad, b1, id_b, acc);
                 }
                 mma_commit(&b_empty[stage]);
                 if (++stage == kDwStages) {
@@ -1475,7 +1478,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     WP.dWd = o.dWd;
     WP.err = err;
     const int nvt = (g.vpad + kDwM - 1) / kDwM, nkt = (g.kpad + kDwN - 1) / kDwN;
-    WP.splits = std::max(1, (sms + nvt * nkt - 1) / (nvt * nkt));
+    WP.splits = std::max(1, sms / (nvt * nkt));  // one wave: a CTA fills an SM's shared memory
     const size_t smem_dw = dw_smem_bytes();
     ASR_CUDA_TRY(cudaFuncSetAttribute(tc_dw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dw));
 
