@@ -95,18 +95,32 @@ struct Smem {
     uint32_t* tmem_slot;
 };
 
-__host__ __device__ constexpr size_t smem_bytes_for(int kchunks) {
-    return 1024 /* alignment slack */ + (size_t)kchunks * kAChunkBytes + (size_t)kStages * kBStageBytes +
+// Streamed-A variant (d > 64 * kMaxKChunks: the 128-row hidden tile no longer
+// fits in shared memory): every ring stage carries one hidden chunk and one
+// weight chunk, so the tile's hidden rows are re-read from L2 once per
+// vocabulary chunk instead of staying resident.
+constexpr int kStreamStages = 4;
+constexpr int kStreamStageBytes = kAChunkBytes + kBStageBytes;  // 48 KB
+
+__host__ __device__ constexpr size_t smem_bytes_for(int kchunks, bool stream = false) {
+    return 1024 /* alignment slack */ +
+           (stream ? (size_t)kStreamStages * kStreamStageBytes
+                   : (size_t)kchunks * kAChunkBytes + (size_t)kStages * kBStageBytes) +
            8 * (4 * kStages + 2 * kMaxKChunks + 5) + 16;
 }
 
-__device__ __forceinline__ Smem carve_smem(uint8_t* raw, int kchunks) {
+__device__ __forceinline__ Smem carve_smem(uint8_t* raw, int kchunks, bool stream = false) {
     Smem s;
     uint8_t* p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     s.a = p;
-    p += (size_t)kchunks * kAChunkBytes;
-    s.b = p;
-    p += (size_t)kStages * kBStageBytes;
+    if (stream) {
+        s.b = p;
+        p += (size_t)kStreamStages * kStreamStageBytes;
+    } else {
+        p += (size_t)kchunks * kAChunkBytes;
+        s.b = p;
+        p += (size_t)kStages * kBStageBytes;
+    }
     uint64_t* bars = reinterpret_cast<uint64_t*>(p);
     s.b_full = bars;
     s.b_empty = bars + 2 * kStages;
@@ -148,15 +162,16 @@ __host__ __device__ constexpr int b_stage_bytes() { return kNC / kCta * kBK * 2;
 template <int kCta>
 __host__ __device__ constexpr int b_stages() { return kStages * kCta; }
 
-template <bool kBwd, int kCta>
+template <bool kBwd, int kCta, bool kStream>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_joint_kernel(const __grid_constant__ CUtensorMap map_full, const __grid_constant__ CUtensorMap map_tail,
                     const __grid_constant__ CUtensorMap map_h, TcParams P) {
+    static_assert(!kStream || kCta == 1, "the streamed-A variant runs single CTAs");
     extern __shared__ uint8_t smem_raw[];
-    constexpr int SB = b_stage_bytes<kCta>();
-    constexpr int NS = b_stages<kCta>();
+    constexpr int SB = kStream ? kStreamStageBytes : b_stage_bytes<kCta>();
+    constexpr int NS = kStream ? kStreamStages : b_stages<kCta>();
     const Geom g = P.g;
-    Smem sm = carve_smem(smem_raw, g.kchunks);
+    Smem sm = carve_smem(smem_raw, g.kchunks, kStream);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* err = P.err;
     const uint32_t rank = kCta == 2 ? cluster_ctarank() : 0;
@@ -225,7 +240,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         uint8_t* dst = sm.b + (size_t)stage * SB;
                         const CUtensorMap* map = width == g.cw ? &map_full : &map_tail;
-                        if (kCta == 2) {
+                        if (kStream) {  // hidden chunk (tile rows x 64) then weight chunk
+                            mbar_arrive_expect_tx(&sm.b_full[stage], kAChunkBytes + (uint32_t)width * kBK * 2);
+                            tma_load_2d(dst, &map_h, ks * kAK, unit * kBM, &sm.b_full[stage]);
+                            tma_load_2d(dst + kAChunkBytes, map, ks * kBK, col, &sm.b_full[stage]);
+                        } else if (kCta == 2) {
                             if (leader) mbar_arrive_expect_tx(&sm.b_full[stage], (uint32_t)width * kBK * 2);
                             tma_load_2d_pair(dst, map, ks * kBK, col + (int)rank * rows, in_leader(&sm.b_full[stage]));
                         } else {
@@ -281,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t d_tmem = tmem_base + buf * kNC;
                     const uint32_t idesc = width == g.cw ? idesc_full : idesc_tail;
                     for (int kc = 0; kc < g.kchunks; ++kc) {
-                        if (j == 0 && !mbar_wait_cluster(&sm.a_full[kc], it & 1, err, 4)) {
+                        if (!kStream && j == 0 && !mbar_wait_cluster(&sm.a_full[kc], it & 1, err, 4)) {
                             ok = false;
                             break;
                         }
@@ -292,15 +311,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_fence_after();
 #pragma unroll
                         for (int kk = 0; kk < kBK / 16; ++kk) {
-                            const uint64_t ad = desc_k128(a_base + kc * kAChunkBytes + kk * 32);
-                            const uint64_t bd = desc_k128(b_base + stage * SB + kk * 32);
+                            const uint32_t sa = kStream ? b_base + stage * SB : a_base + kc * kAChunkBytes;
+                            const uint32_t sb = b_base + stage * SB + (kStream ? kAChunkBytes : 0);
+                            const uint64_t ad = desc_k128(sa + kk * 32);
+                            const uint64_t bd = desc_k128(sb + kk * 32);
                             if (kCta == 2)
                                 mma_bf16_pair(d_tmem, ad, bd, idesc, (kc | kk) != 0 ? 1u : 0u);
                             else
                                 mma_bf16(d_tmem, ad, bd, idesc, (kc | kk) != 0 ? 1u : 0u);
                         }
                         commit_both(&sm.b_empty[stage]);
-                        if (j == g.nchunks - 1) commit_both(&sm.a_empty[kc]);
+                        if (!kStream && j == g.nchunks - 1) commit_both(&sm.a_empty[kc]);
                         if (++stage == NS) {
                             stage = 0;
                             phase ^= 1;
@@ -320,8 +341,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The tile's rows of H = bf16(tanh(enc + dec)) (written by hidden_kernel
         // for this pass) into the resident 128 B swizzled K chunks; chunk kc of
         // the next tile is reloaded as soon as the last vocabulary chunk of the
-        // current tile has consumed it.
-        if (lane == 0) {
+        // current tile has consumed it. (The streamed variant loads them with the
+        // weights instead.)
+        if (!kStream && lane == 0) {
             uint32_t it = 0;
             bool ok = true;
             bool issued[kMaxKChunks];
@@ -672,13 +694,14 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
             }
             const float* er = enc + ((int64_t)c.b * T + c.t) * d;
             const float* dr = dec + ((int64_t)c.b * U + c.u) * d;
-            if ((d & 7) == 0 && c8n <= 3 * 32) {
-                // up to three 8-column groups per lane (d % 8 == 0, kpad <= 768): every
-                // load of the row in flight at once; groups at or past d stay zero
+            if ((d & 7) == 0) {
+              // three 8-column groups per lane at a time (d % 8 == 0): all their loads
+              // in flight at once; groups at or past d stay zero
+              for (int g0 = 0; g0 < c8n; g0 += 3 * 32) {
                 float4 ev[3][2], dv[3][2];
 #pragma unroll
                 for (int j = 0; j < 3; ++j) {
-                    const int k = (lane + 32 * j) * 8;
+                    const int k = (g0 + lane + 32 * j) * 8;
                     if (k + 8 <= d) {
                         ev[j][0] = __ldg(reinterpret_cast<const float4*>(er + k));
                         ev[j][1] = __ldg(reinterpret_cast<const float4*>(er + k) + 1);
@@ -690,7 +713,7 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
                 }
 #pragma unroll
                 for (int j = 0; j < 3; ++j) {
-                    const int k8 = lane + 32 * j;
+                    const int k8 = g0 + lane + 32 * j;
                     if (k8 >= c8n) break;
                     // columns d..kpad of the last group stay zero (tanh(0) = 0)
                     uint4 w;
@@ -700,6 +723,7 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
                     w.w = pack_bf16(tanh_fast(ev[j][1].z + dv[j][1].z), tanh_fast(ev[j][1].w + dv[j][1].w));
                     dst[k8] = w;
                 }
+              }
             } else {
                 for (int k8 = lane; k8 < c8n; k8 += 32) {
                     const int k = k8 * 8;
@@ -759,16 +783,24 @@ template <bool kBwd>
 int launch_joint(bool pairs, int64_t tiles, size_t smem, const CUtensorMap& mfull, const CUtensorMap& mtail,
                  const CUtensorMap& mh, const TcParams& P, cudaStream_t st) {
     const int sms = sm_count();
-    if (!pairs) {
-        ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem));
-        const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sms));
-        tc_joint_kernel<kBwd, 1><<<grid, kThreads, smem, st>>>(mfull, mtail, mh, P);
+    const int grid1 = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sms));
+    if (P.g.kchunks > kMaxKChunks) {  // streamed hidden tiles
+        const size_t smem_s = smem_bytes_for(P.g.kchunks, true);
+        ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem_s));
+        tc_joint_kernel<kBwd, 1, true><<<grid1, kThreads, smem_s, st>>>(mfull, mtail, mh, P);
         ASR_LAUNCH_CHECK();
         return ASR_OK;
     }
-    ASR_CUDA_TRY(
-        cudaFuncSetAttribute(tc_joint_kernel<kBwd, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (!pairs) {
+        ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 1, false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        tc_joint_kernel<kBwd, 1, false><<<grid1, kThreads, smem, st>>>(mfull, mtail, mh, P);
+        ASR_LAUNCH_CHECK();
+        return ASR_OK;
+    }
+    ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
     const int64_t units = (tiles + 1) / 2;
     const int clusters = (int)std::max<int64_t>(1, std::min<int64_t>(units, sms / 2));
     cudaLaunchConfig_t cfg = {};
@@ -783,16 +815,21 @@ int launch_joint(bool pairs, int64_t tiles, size_t smem, const CUtensorMap& mful
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ASR_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc_joint_kernel<kBwd, 2>, mfull, mtail, mh, P));
+    ASR_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc_joint_kernel<kBwd, 2, false>, mfull, mtail, mh, P));
     return ASR_OK;
 }
 
 }  // namespace
 
+// Hidden dimensions up to 64 * kMaxKChunks keep the hidden tile resident; larger
+// ones (up to 4096) stream it.
+constexpr int kMaxStreamKChunks = 64;
+
 bool tc_supported(const JointArgs& a) {
     const Geom g = make_geom(a);
-    return g.kchunks <= kMaxKChunks && a.n_dur <= kMaxDurCols && tensor_map_encoder() != nullptr &&
-           (int)smem_bytes_for(g.kchunks) <= dyn_smem_limit();
+    const bool stream = g.kchunks > kMaxKChunks;
+    return g.kchunks <= kMaxStreamKChunks && a.n_dur <= kMaxDurCols && tensor_map_encoder() != nullptr &&
+           (int)smem_bytes_for(g.kchunks, stream) <= dyn_smem_limit();
 }
 
 // Forward scratch: bf16 weights, the per-pass hidden rows, pass bounds, error word.
@@ -842,7 +879,7 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
         plan_passes_kernel<<<(L.pp.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, L.pp.passes, L.pp.step, bounds);
         ASR_LAUNCH_CHECK();
     }
-    const bool pairs = joint_pairs();
+    const bool pairs = joint_pairs() && g.kchunks <= kMaxKChunks;  // the streamed variant runs single CTAs
     CUtensorMap mfull, mtail, mh;
     if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
     if (!make_map(&mh, H, (int)L.pp.step, g.kpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
@@ -1429,7 +1466,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     }
     // tensor maps
     const int rows = (int)L.step;
-    const bool pairs = joint_pairs();
+    const bool pairs = joint_pairs() && g.kchunks <= kMaxKChunks;  // the streamed variant runs single CTAs
     CUtensorMap mfull, mtail, m_h, m_wt, m_g, m_gmn, m_hmn;
     if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
     if (!make_map(&m_h, H, rows, g.kpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;

@@ -404,3 +404,53 @@ def test_capi_ctc_direct():
     torch.cuda.synchronize()
     np.testing.assert_allclose((-logz).double().cpu().numpy(), c["loss"], rtol=1e-5, atol=2e-5)
     assert_grad(grad, c["grad_logits"], "grad_logits")
+
+
+def test_rnnt_bf16_wide_hidden_streams_the_hidden_tile():
+    """Joint dim 1024 (the large-batch RNN-T configuration): the 128-row hidden
+    tile no longer fits in shared memory, so the tensor-core joint streams it
+    with the weights; the gradients still track the fp32 path."""
+    from asr_b200 import _lib
+
+    assert _lib.joint_uses_tensor_cores(1024, 0, 1024)
+    c = transducer_case(39, 3, (30, 60), (20, 40), 1024, 1024)
+    l16, *g16 = run_rnnt(c, tf32=True)
+    l32, *g32 = run_rnnt(c, tf32=False)
+    np.testing.assert_allclose(l16.detach().cpu().numpy(), l32.detach().cpu().numpy(), rtol=2e-3)
+    for name, a, b in zip(("d_enc", "d_dec", "dW"), g16, g32):
+        assert _rel(a, b) < 1e-2, f"{name}: {_rel(a, b):.3e}"
+
+
+_PAIR_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from tests.gpu_cases import transducer_case
+from asr_b200.loss.tdt import tdt_loss
+c = transducer_case(40, 5, (40, 90), (10, 40), 1024, 640, n_dur=5)
+L = [torch.tensor(c[k], device="cuda", requires_grad=True) for k in ("enc", "dec", "W", "W_dur")]
+I = [torch.tensor(c[k], device="cuda") for k in ("targets", "in_lens", "tgt_lens")]
+loss = tdt_loss(*L, *I, list(range(5)), 0, 0.05, True)
+loss.sum().backward()
+np.savez(sys.argv[2], loss=loss.detach().cpu().numpy(), *[t.grad.cpu().numpy() for t in L])
+"""
+
+
+def test_tdt_bf16_cta_pairs_match_single_ctas(tmp_path):
+    """The opt-in CTA-pair joint kernel (ASR_B200_JOINT_PAIRS=1, one M = 256 MMA
+    per pair of SMs) computes the same sums as the single-CTA kernel."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = str(Path(__file__).resolve().parents[1])
+    out = {}
+    for pairs in ("0", "1"):
+        f = tmp_path / f"pairs{pairs}.npz"
+        env = dict(os.environ, ASR_B200_JOINT_PAIRS=pairs)
+        subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, root, str(f)], check=True, env=env, timeout=300)
+        out[pairs] = np.load(f)
+    np.testing.assert_allclose(out["1"]["loss"], out["0"]["loss"], rtol=1e-6)
+    for k in ("arr_0", "arr_1", "arr_2", "arr_3"):
+        a, b = out["1"][k].astype(np.float64), out["0"][k].astype(np.float64)
+        assert np.linalg.norm(a - b) <= 1e-5 * np.linalg.norm(b), k
