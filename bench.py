@@ -268,6 +268,173 @@ def cpu_baseline_leg(in_lens, tgt_lens, W, Wd, sample=2):
                       f"U={list(map(int, tgt_lens[:sample]))}), fwd+bwd, float64 C oracle, {threads} threads"}
 
 
+# ------------------------------------------------ other BASELINE configurations
+#
+# `--workload c1..c4` times the other four BASELINE configurations on one GPU
+# through the same public loss API (seeded synthetic inputs with the configs'
+# shapes and distributions). They are secondary lines for the per-config
+# table; the default workload (c5) is the headline.
+
+CONFIGS = {
+    "c1": {"name": "c1_ctc_char", "kind": "ctc", "B": 8, "T": (150, 200), "U": (20, 60), "V": 29},
+    "c2": {"name": "c2_rnnt_char", "kind": "rnnt", "B": 32, "T": (100, 400), "U": (30, 150), "V": 30, "d": 640},
+    "c3": {"name": "c3_tdt_bpe1024", "kind": "tdt", "B": 32, "T": (100, 400), "U": (10, 80), "V": 1024, "d": 640},
+    "c4": {"name": "c4_rnnt_bpe1024_stress", "kind": "rnnt", "B": 128, "T": (400, 400), "U": (40, 100), "V": 1024,
+           "d": 1024},
+}
+
+
+def config_inputs(cfg, seed=SEED):
+    rng = np.random.default_rng([seed, 77])
+    B = cfg["B"]
+    in_lens = rng.integers(cfg["T"][0], cfg["T"][1] + 1, size=B).astype(np.int32)
+    tgt_lens = rng.integers(cfg["U"][0], cfg["U"][1] + 1, size=B).astype(np.int32)
+    T, U, V = int(in_lens.max()), int(tgt_lens.max()), cfg["V"]
+    x = {"in_lens": in_lens, "tgt_lens": tgt_lens, "targets": rng.integers(1, V, size=(B, U)).astype(np.int32)}
+    if cfg["kind"] == "ctc":
+        x["logits"] = rng.standard_normal((B, T, V)).astype(np.float32)
+        return x
+    d = cfg["d"]
+
+    def xavier(r, c):
+        b = np.sqrt(6.0 / (r + c))
+        return rng.uniform(-b, b, size=(r, c)).astype(np.float32)
+
+    x["enc"] = (rng.standard_normal((B, T, d)) / np.sqrt(d)).astype(np.float32)
+    x["dec"] = (rng.standard_normal((B, U + 1, d)) / np.sqrt(d)).astype(np.float32)
+    x["W"] = xavier(V, d)
+    if cfg["kind"] == "tdt":
+        x["W_dur"] = xavier(len(DURATIONS), d)
+    return x
+
+
+def run_config(args):
+    import torch
+
+    from asr_b200 import _lib
+
+    cfg = CONFIGS[args.workload]
+    dev = torch.device("cuda", 0)
+    host = config_inputs(cfg)
+    kind = cfg["kind"]
+    tf32 = bool(args.tf32)
+    B = cfg["B"]
+    float_keys = ["logits"] if kind == "ctc" else (["enc", "dec", "W"] + (["W_dur"] if kind == "tdt" else []))
+    dev_in = {k: torch.tensor(v, device=dev) for k, v in host.items()}
+
+    def step(t):
+        leaves = [t[k].requires_grad_(True) if k in ("logits", "enc", "dec") else t[k] for k in float_keys]
+        for v in leaves:
+            v.grad = None
+        if kind == "ctc":
+            from asr_b200.loss.ctc import CTCLoss
+
+            loss = CTCLoss()(leaves[0], t["targets"], t["in_lens"], t["tgt_lens"])
+        elif kind == "rnnt":
+            from asr_b200.loss.rnnt import rnnt_loss
+
+            loss = rnnt_loss(*leaves, t["targets"], t["in_lens"], t["tgt_lens"], 0, tf32) / t["tgt_lens"].clamp_min(1)
+        else:
+            from asr_b200.loss.tdt import tdt_loss
+
+            loss = tdt_loss(*leaves, t["targets"], t["in_lens"], t["tgt_lens"], DURATIONS, 0, SIGMA, tf32)
+            loss = loss / t["tgt_lens"].clamp_min(1)
+        total = loss.mean()
+        total.backward()
+        return total.detach()
+
+    for k in ("W", "W_dur"):
+        if k in dev_in:
+            dev_in[k].requires_grad_(True)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def timed(run, k):
+        times = []
+        for _ in range(k):
+            flush.fill_(1)
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            run()
+            s1.record(stream)
+            times.append((s0, s1))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in times)
+
+    for _ in range(args.warmup):
+        step(dev_in)
+    torch.cuda.synchronize()
+    lib = _lib.capi_ops()
+    lib.asr_profiler_report(None, 0, 1)
+    clocks = ClockSampler(args.clocks_log)
+    clocks.start()
+    time.sleep(0.3)
+    lib.asr_profiler_enable(1)
+    ms = timed(lambda: step(dev_in), args.steps) / args.steps
+    lib.asr_profiler_enable(0)
+    clock_info = clocks.stop()
+    prof = profiler_report(clear=True)
+
+    pinned = {k: torch.from_numpy(v).pin_memory() for k, v in host.items()}
+    res = torch.empty(1, dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pinned.values())
+
+    def e2e():
+        t = {k: v.to(dev, non_blocking=True) for k, v in pinned.items()}
+        res.copy_(step(t).reshape(1), non_blocking=True)
+
+    e2e()
+    torch.cuda.synchronize()
+    e2e_ms = timed(e2e, args.steps) / args.steps
+
+    N = int((host["in_lens"].astype(np.int64) * (host["tgt_lens"] + 1)).sum())
+    d = cfg.get("d", 0)
+    Vf = cfg["V"] + (len(DURATIONS) if kind == "tdt" else 0)
+    n_dur = len(DURATIONS) if kind == "tdt" else 0
+    peaks = measured_peaks()
+    kernels, roof = {}, None
+    total_ms = max(sum(v[1] for v in prof.values()), 1e-9)
+    for name, (launches, kms) in prof.items():
+        bound, work = kernel_work(name, N, d, Vf, n_dur, frames=int(host["in_lens"].sum()),
+                                  labels=int((host["tgt_lens"] + 1).sum()))
+        if name.startswith("ctc_"):
+            tv = int(host["in_lens"].sum()) * cfg["V"] * 4.0
+            states = int((host["in_lens"].astype(np.int64) * (2 * host["tgt_lens"] + 1)).sum()) * 8.0
+            bound, work = "hbm", (tv + states) if name == "ctc_alpha" else (2 * tv + states)
+        e = {"launches_per_step": launches / args.steps, "ms_per_step": round(kms / args.steps, 4),
+             "share": round(kms / total_ms, 4)}
+        if bound:
+            sec = kms / args.steps / 1000.0
+            ach = work / sec / (1e12 if bound == "tensor" else 1e9)
+            pk = peaks["bf16_tflops_sustained"] if bound == "tensor" else peaks["hbm_gbs"]
+            e.update({"bound": bound, "achieved": round(ach, 2), "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
+                      "frac": round(ach / pk, 4)})
+        kernels[name] = e
+    if prof:
+        top = max(prof.items(), key=lambda kv: kv[1][1])[0]
+        k = kernels[top]
+        roof = {"kernel": top, "bound": k.get("bound"), "achieved": k.get("achieved"),
+                "peak": peaks["bf16_tflops_sustained"] if k.get("bound") == "tensor" else peaks["hbm_gbs"],
+                "unit": k.get("unit"), "frac": k.get("frac"), "traffic": None, "share": k["share"]}
+    tc = kind != "ctc" and tf32 and _lib.joint_uses_tensor_cores(cfg["V"], n_dur, d)
+    line = {
+        "metric": "fused joint+loss fwd+bwd utterances/s" if kind != "ctc" else "CTC loss fwd+bwd utterances/s",
+        "value": round(B / (ms / 1000.0), 3), "unit": "utterances/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16" if tc else "f32", "data": "synthetic",
+        "config": {"workload": cfg["name"], "batch": B, "T": list(cfg["T"]), "U": list(cfg["U"]), "vocab": cfg["V"],
+                   "d_model": d or None, "lattice_nodes": N if kind != "ctc" else None,
+                   "l2": "flushed between timed steps (256 MB write)",
+                   "joint_path": None if kind == "ctc" else ("tcgen05 bf16" if tc else "SIMT fp32")},
+        "roofline": roof, "cpu_baseline": None,
+        "e2e": {"value": round(B / (e2e_ms / 1000.0), 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": int(sum(v[0] for v in prof.values())), "kernels": kernels, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -279,7 +446,14 @@ def main():
     ap.add_argument("--clocks-log", default=None)
     ap.add_argument("--batch", type=int, default=None,
                     help="profiling aid: run only the first BATCH utterances of the workload")
+    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"],
+                    help="c5 (default): the headline config-5 workload; c1..c4: the other BASELINE configs, 1 GPU")
     args = ap.parse_args()
+    if args.workload != "c5":
+        if args.impl == "reference" or int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            raise SystemExit("--workload c1..c4 runs our implementation on one GPU only")
+        run_config(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
