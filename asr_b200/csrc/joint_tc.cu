@@ -494,9 +494,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         w1.y = pack_bf16(gv[10], gv[11]);
                         w1.z = pack_bf16(gv[12], gv[13]);
                         w1.w = pack_bf16(gv[14], gv[15]);
-                        uint4* dst = reinterpret_cast<uint4*>(P.G + (int64_t)(n - begin) * g.vpad + c0);
-                        dst[0] = w0;
-                        dst[1] = w1;
+                        // one 32-byte store (a whole sector): rows are vpad * 2 bytes, a multiple
+                        // of 32, and groups start on 16-column boundaries
+                        st_global_32B(P.G + (int64_t)(n - begin) * g.vpad + c0, w0, w1);
                     }
                 }
                 tc_fence_before();
