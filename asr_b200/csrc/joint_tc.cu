@@ -52,6 +52,10 @@ constexpr int kAChunkBytes = kBM * kAK * 2;   // 16 KB
 constexpr int kBStageBytes = kNC * kBK * 2;   // 32 KB
 constexpr int kMaxDurCols = 16;
 constexpr int kTmemCols = 512;
+constexpr int kMaxRing = 8;           // barrier slots per ring
+constexpr int kStreamStagesMax = 6;
+constexpr int kSmemBudget = 227 * 1024;
+constexpr int kBarBytes = 8 * (2 * kMaxRing + 2 * kMaxKChunks + 5) + 16;
 
 struct Geom {
     int kchunks;  // ceil(d / 64)
@@ -60,6 +64,8 @@ struct Geom {
     int cw;       // vocabulary columns of a chunk (multiple of 16, <= 256)
     int lw;       // columns of the last chunk (multiple of 16, <= cw)
     int nchunks;  // chunks per tile
+    int sstage;   // streamed variant: bytes of one ring stage (hidden chunk + weight chunk)
+    int nstream;  // streamed variant: ring stages
 };
 
 // The vocabulary is cut into equal chunks (e.g. 1040 = 5 x 208): every chunk
@@ -74,6 +80,12 @@ Geom make_geom(const JointArgs& a) {
     g.cw = ((g.vpad + g.nchunks - 1) / g.nchunks + 15) / 16 * 16;
     g.nchunks = (g.vpad + g.cw - 1) / g.cw;
     g.lw = g.vpad - (g.nchunks - 1) * g.cw;
+    g.sstage = kAChunkBytes + g.cw * kBK * 2;  // a multiple of 2 KB: stage bases stay 1024-aligned
+    g.nstream = std::min(kStreamStagesMax, (kSmemBudget - 1024 - kBarBytes) / g.sstage);
+    if (const char* e = std::getenv("ASR_B200_JOINT_RING")) {  // tuning knob: fewer streamed stages
+        const int r = std::atoi(e);
+        if (r >= 2 && r < g.nstream) g.nstream = r;
+    }
     return g;
 }
 
@@ -95,27 +107,28 @@ struct Smem {
     uint32_t* tmem_slot;
 };
 
-// Streamed-A variant (d > 64 * kMaxKChunks: the 128-row hidden tile no longer
-// fits in shared memory): every ring stage carries one hidden chunk and one
-// weight chunk, so the tile's hidden rows are re-read from L2 once per
-// vocabulary chunk instead of staying resident.
-constexpr int kStreamStages = 4;
-constexpr int kStreamStageBytes = kAChunkBytes + kBStageBytes;  // 48 KB
+// Streamed-A variant (the default; required when d > 64 * kMaxKChunks, where
+// the 128-row hidden tile no longer fits in shared memory): every ring stage
+// carries one hidden chunk (16 KB) and one weight chunk (cw x 128 B), so the
+// tile's hidden rows are re-read from L2 once per vocabulary chunk, and the ring
+// gets as many stages as shared memory holds (5 of 42.5 KB at cw = 208). On B200
+// this measured faster than keeping the hidden tile resident behind a 2-stage
+// weight ring (d = 640, B = 128: dlogits 6.2 vs 6.8 ms, forward 4.4 vs 4.5 ms).
 
-__host__ __device__ constexpr size_t smem_bytes_for(int kchunks, bool stream = false) {
+__host__ __device__ constexpr size_t smem_bytes_for(int kchunks, bool stream = false, int sstage = 0,
+                                                    int nstream = 0) {
     return 1024 /* alignment slack */ +
-           (stream ? (size_t)kStreamStages * kStreamStageBytes
-                   : (size_t)kchunks * kAChunkBytes + (size_t)kStages * kBStageBytes) +
-           8 * (4 * kStages + 2 * kMaxKChunks + 5) + 16;
+           (stream ? (size_t)nstream * sstage : (size_t)kchunks * kAChunkBytes + (size_t)kStages * kBStageBytes) +
+           kBarBytes;
 }
 
-__device__ __forceinline__ Smem carve_smem(uint8_t* raw, int kchunks, bool stream = false) {
+__device__ __forceinline__ Smem carve_smem(uint8_t* raw, int kchunks, bool stream = false, int ring_bytes = 0) {
     Smem s;
     uint8_t* p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     s.a = p;
     if (stream) {
         s.b = p;
-        p += (size_t)kStreamStages * kStreamStageBytes;
+        p += (size_t)ring_bytes;
     } else {
         p += (size_t)kchunks * kAChunkBytes;
         s.b = p;
@@ -123,10 +136,10 @@ __device__ __forceinline__ Smem carve_smem(uint8_t* raw, int kchunks, bool strea
     }
     uint64_t* bars = reinterpret_cast<uint64_t*>(p);
     s.b_full = bars;
-    s.b_empty = bars + 2 * kStages;
-    s.a_full = bars + 4 * kStages;
-    s.a_empty = bars + 4 * kStages + kMaxKChunks;
-    s.t_full = bars + 4 * kStages + 2 * kMaxKChunks;
+    s.b_empty = bars + kMaxRing;
+    s.a_full = bars + 2 * kMaxRing;
+    s.a_empty = bars + 2 * kMaxRing + kMaxKChunks;
+    s.t_full = bars + 2 * kMaxRing + 2 * kMaxKChunks;
     s.t_empty = s.t_full + 2;
     s.done = s.t_empty + 2;
     s.tmem_slot = reinterpret_cast<uint32_t*>(s.done + 1);
@@ -168,10 +181,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap map_h, TcParams P) {
     static_assert(!kStream || kCta == 1, "the streamed-A variant runs single CTAs");
     extern __shared__ uint8_t smem_raw[];
-    constexpr int SB = kStream ? kStreamStageBytes : b_stage_bytes<kCta>();
-    constexpr int NS = kStream ? kStreamStages : b_stages<kCta>();
     const Geom g = P.g;
-    Smem sm = carve_smem(smem_raw, g.kchunks, kStream);
+    const int SB = kStream ? g.sstage : b_stage_bytes<kCta>();
+    const int NS = kStream ? g.nstream : b_stages<kCta>();
+    Smem sm = carve_smem(smem_raw, g.kchunks, kStream, g.sstage * g.nstream);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* err = P.err;
     const uint32_t rank = kCta == 2 ? cluster_ctarank() : 0;
@@ -223,8 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            uint32_t issued_parity[NS];
-            bool issued[NS];
+            uint32_t issued_parity[kMaxRing];
+            bool issued[kMaxRing];
 #pragma unroll
             for (int s = 0; s < NS; ++s) issued[s] = false, issued_parity[s] = 0;
             bool ok = true;
@@ -770,6 +783,19 @@ bool joint_pairs() {
     return pairs;
 }
 
+// Streamed hidden tiles: the default (see kStreamStagesMax); required above
+// 64 * kMaxKChunks hidden columns. ASR_B200_JOINT_STREAM=0, or CTA pairs (which
+// split the resident tile's MMA across two SMs), keep the hidden tile resident.
+bool joint_stream(const Geom& g) {
+    if (g.kchunks > kMaxKChunks) return true;
+    static const int force = [] {
+        const char* e = std::getenv("ASR_B200_JOINT_STREAM");
+        return e ? (e[0] == '1' ? 1 : 0) : -1;
+    }();
+    if (force == 0) return false;
+    return force == 1 || !joint_pairs();
+}
+
 // Weight tensor maps of the joint kernel: a regular chunk and the last chunk,
 // each split across the pair when pairs are used.
 bool joint_weight_maps(const Geom& g, const __nv_bfloat16* Wf, bool pairs, CUtensorMap* mfull, CUtensorMap* mtail) {
@@ -784,8 +810,8 @@ int launch_joint(bool pairs, int64_t tiles, size_t smem, const CUtensorMap& mful
                  const CUtensorMap& mh, const TcParams& P, cudaStream_t st) {
     const int sms = sm_count();
     const int grid1 = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sms));
-    if (P.g.kchunks > kMaxKChunks) {  // streamed hidden tiles
-        const size_t smem_s = smem_bytes_for(P.g.kchunks, true);
+    if (joint_stream(P.g)) {  // streamed hidden tiles
+        const size_t smem_s = smem_bytes_for(P.g.kchunks, true, P.g.sstage, P.g.nstream);
         ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem_s));
         tc_joint_kernel<kBwd, 1, true><<<grid1, kThreads, smem_s, st>>>(mfull, mtail, mh, P);
@@ -829,7 +855,7 @@ bool tc_supported(const JointArgs& a) {
     const Geom g = make_geom(a);
     const bool stream = g.kchunks > kMaxKChunks;
     return g.kchunks <= kMaxStreamKChunks && a.n_dur <= kMaxDurCols && tensor_map_encoder() != nullptr &&
-           (int)smem_bytes_for(g.kchunks, stream) <= dyn_smem_limit();
+           (int)smem_bytes_for(g.kchunks, stream, g.sstage, g.nstream) <= dyn_smem_limit();
 }
 
 // Forward scratch: bf16 weights, the per-pass hidden rows, pass bounds, error word.
@@ -879,7 +905,7 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
         plan_passes_kernel<<<(L.pp.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, L.pp.passes, L.pp.step, bounds);
         ASR_LAUNCH_CHECK();
     }
-    const bool pairs = joint_pairs() && g.kchunks <= kMaxKChunks;  // the streamed variant runs single CTAs
+    const bool pairs = joint_pairs() && !joint_stream(g);  // pairs use the resident hidden tile
     CUtensorMap mfull, mtail, mh;
     if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
     if (!make_map(&mh, H, (int)L.pp.step, g.kpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
@@ -1466,7 +1492,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     }
     // tensor maps
     const int rows = (int)L.step;
-    const bool pairs = joint_pairs() && g.kchunks <= kMaxKChunks;  // the streamed variant runs single CTAs
+    const bool pairs = joint_pairs() && !joint_stream(g);  // pairs use the resident hidden tile
     CUtensorMap mfull, mtail, m_h, m_wt, m_g, m_gmn, m_hmn;
     if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
     if (!make_map(&m_h, H, rows, g.kpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;

@@ -435,22 +435,27 @@ np.savez(sys.argv[2], loss=loss.detach().cpu().numpy(), *[t.grad.cpu().numpy() f
 """
 
 
-def test_tdt_bf16_cta_pairs_match_single_ctas(tmp_path):
-    """The opt-in CTA-pair joint kernel (ASR_B200_JOINT_PAIRS=1, one M = 256 MMA
-    per pair of SMs) computes the same sums as the single-CTA kernel."""
+def test_tdt_bf16_joint_variants_agree(tmp_path):
+    """The joint kernel's variants compute the same sums: streamed hidden tiles
+    (the default), the resident hidden tile (ASR_B200_JOINT_STREAM=0) and the
+    opt-in CTA pairs (ASR_B200_JOINT_PAIRS=1, one M = 256 MMA per pair of SMs).
+    Each runs in its own process: the switches are read once per process."""
     import os
     import subprocess
     import sys
     from pathlib import Path
 
     root = str(Path(__file__).resolve().parents[1])
+    variants = {"stream": {}, "resident": {"ASR_B200_JOINT_STREAM": "0"}, "pairs": {"ASR_B200_JOINT_PAIRS": "1"}}
     out = {}
-    for pairs in ("0", "1"):
-        f = tmp_path / f"pairs{pairs}.npz"
-        env = dict(os.environ, ASR_B200_JOINT_PAIRS=pairs)
+    for name, extra in variants.items():
+        f = tmp_path / f"{name}.npz"
+        env = {k: v for k, v in os.environ.items() if not k.startswith("ASR_B200_JOINT_")}
+        env.update(extra)
         subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, root, str(f)], check=True, env=env, timeout=300)
-        out[pairs] = np.load(f)
-    np.testing.assert_allclose(out["1"]["loss"], out["0"]["loss"], rtol=1e-6)
-    for k in ("arr_0", "arr_1", "arr_2", "arr_3"):
-        a, b = out["1"][k].astype(np.float64), out["0"][k].astype(np.float64)
-        assert np.linalg.norm(a - b) <= 1e-5 * np.linalg.norm(b), k
+        out[name] = np.load(f)
+    for name in ("resident", "pairs"):
+        np.testing.assert_allclose(out[name]["loss"], out["stream"]["loss"], rtol=1e-6)
+        for k in ("arr_0", "arr_1", "arr_2", "arr_3"):
+            a, b = out[name][k].astype(np.float64), out["stream"][k].astype(np.float64)
+            assert np.linalg.norm(a - b) <= 1e-5 * np.linalg.norm(b), (name, k)
