@@ -11,6 +11,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include "asr_b200.h"
@@ -135,8 +136,12 @@ inline int sm_count() {
     return n;
 }
 
-// Host-side launcher declared in lattice.cu.
+// Host-side launchers defined in lattice.cu.
 int launch_lattice_prep(const int32_t* in_lens, const int32_t* tgt_lens, int B, int T, int U, int S,
                         const LatticeMeta& m, cudaStream_t stream);
+// bf16 <-> fp32 element conversions of n contiguous values (bf16 activations and
+// their gradients).
+int launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n, cudaStream_t stream);
+int launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream);
 
 }  // namespace asr

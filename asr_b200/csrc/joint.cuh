@@ -7,13 +7,18 @@
 // head (joint_W_dur). No launcher ever writes the (nodes x Vf) logits to HBM.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace asr {
 
 struct JointArgs {
-    const float* enc;      // (B, T, d)
+    const float* enc;      // (B, T, d) fp32 activations, or nullptr when enc16 is set
     const float* dec;      // (B, U, d)
+    const __nv_bfloat16* enc16;  // bf16 activations (the tensor-core path reads them directly)
+    const __nv_bfloat16* dec16;
+    int vec;               // d % 8 == 0 and 16-byte aligned activation bases: vector row loads
     const float* W;        // (V, d)
     const float* Wd;       // (n_dur, d) or nullptr
     const int32_t* targets;  // (B, S)

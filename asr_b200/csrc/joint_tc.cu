@@ -679,9 +679,28 @@ __global__ void plan_passes_kernel(LatticeMeta m, int B, int P, int64_t step, in
 // (1280 B written per node at d = 640).
 constexpr int kHiddenRun = 64;
 
-__global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, const float* __restrict__ enc,
-                                                        const float* __restrict__ dec, int T, int U, int d, int kpad,
-                                                        const int32_t* __restrict__ bounds, int pass,
+// Eight consecutive activations as fp32 (16-byte aligned source).
+__device__ __forceinline__ void load8(const float* __restrict__ p, float (&x)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* __restrict__ p, float (&x)[8]) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        x[2 * i] = f.x, x[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ float load1(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float load1(const __nv_bfloat16* p) { return __bfloat162float(p[0]); }
+
+template <typename TA>
+__global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, const TA* __restrict__ enc,
+                                                        const TA* __restrict__ dec, int T, int U, int d, int kpad,
+                                                        int vec, const int32_t* __restrict__ bounds, int pass,
                                                         __nv_bfloat16* __restrict__ H) {
     const int N = total_nodes(m, B);
     const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
@@ -705,45 +724,42 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
                 for (int k8 = lane; k8 < c8n; k8 += 32) dst[k8] = make_uint4(0, 0, 0, 0);
                 continue;
             }
-            const float* er = enc + ((int64_t)c.b * T + c.t) * d;
-            const float* dr = dec + ((int64_t)c.b * U + c.u) * d;
-            if ((d & 7) == 0) {
-              // three 8-column groups per lane at a time (d % 8 == 0): all their loads
-              // in flight at once; groups at or past d stay zero
-              for (int g0 = 0; g0 < c8n; g0 += 3 * 32) {
-                float4 ev[3][2], dv[3][2];
+            const TA* er = enc + ((int64_t)c.b * T + c.t) * d;
+            const TA* dr = dec + ((int64_t)c.b * U + c.u) * d;
+            if (vec) {
+                // three 8-column groups per lane at a time (d % 8 == 0, aligned rows):
+                // all their loads in flight at once; groups at or past d stay zero
+                for (int g0 = 0; g0 < c8n; g0 += 3 * 32) {
+                    float ev[3][8], dv[3][8];
 #pragma unroll
-                for (int j = 0; j < 3; ++j) {
-                    const int k = (g0 + lane + 32 * j) * 8;
-                    if (k + 8 <= d) {
-                        ev[j][0] = __ldg(reinterpret_cast<const float4*>(er + k));
-                        ev[j][1] = __ldg(reinterpret_cast<const float4*>(er + k) + 1);
-                        dv[j][0] = __ldg(reinterpret_cast<const float4*>(dr + k));
-                        dv[j][1] = __ldg(reinterpret_cast<const float4*>(dr + k) + 1);
-                    } else {
-                        ev[j][0] = ev[j][1] = dv[j][0] = dv[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int j = 0; j < 3; ++j) {
+                        const int k = (g0 + lane + 32 * j) * 8;
+                        if (k + 8 <= d) {
+                            load8(er + k, ev[j]);
+                            load8(dr + k, dv[j]);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) ev[j][i] = dv[j][i] = 0.f;
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 3; ++j) {
+                        const int k8 = g0 + lane + 32 * j;
+                        if (k8 >= c8n) break;
+                        uint4 w;
+                        w.x = pack_bf16(tanh_fast(ev[j][0] + dv[j][0]), tanh_fast(ev[j][1] + dv[j][1]));
+                        w.y = pack_bf16(tanh_fast(ev[j][2] + dv[j][2]), tanh_fast(ev[j][3] + dv[j][3]));
+                        w.z = pack_bf16(tanh_fast(ev[j][4] + dv[j][4]), tanh_fast(ev[j][5] + dv[j][5]));
+                        w.w = pack_bf16(tanh_fast(ev[j][6] + dv[j][6]), tanh_fast(ev[j][7] + dv[j][7]));
+                        dst[k8] = w;
                     }
                 }
-#pragma unroll
-                for (int j = 0; j < 3; ++j) {
-                    const int k8 = g0 + lane + 32 * j;
-                    if (k8 >= c8n) break;
-                    // columns d..kpad of the last group stay zero (tanh(0) = 0)
-                    uint4 w;
-                    w.x = pack_bf16(tanh_fast(ev[j][0].x + dv[j][0].x), tanh_fast(ev[j][0].y + dv[j][0].y));
-                    w.y = pack_bf16(tanh_fast(ev[j][0].z + dv[j][0].z), tanh_fast(ev[j][0].w + dv[j][0].w));
-                    w.z = pack_bf16(tanh_fast(ev[j][1].x + dv[j][1].x), tanh_fast(ev[j][1].y + dv[j][1].y));
-                    w.w = pack_bf16(tanh_fast(ev[j][1].z + dv[j][1].z), tanh_fast(ev[j][1].w + dv[j][1].w));
-                    dst[k8] = w;
-                }
-              }
             } else {
                 for (int k8 = lane; k8 < c8n; k8 += 32) {
                     const int k = k8 * 8;
                     float h[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        h[i] = k + i < d ? tanh_fast(__ldg(er + k + i) + __ldg(dr + k + i)) : 0.f;
+                    for (int i = 0; i < 8; ++i) h[i] = k + i < d ? tanh_fast(load1(er + k + i) + load1(dr + k + i)) : 0.f;
                     uint4 w;
                     w.x = pack_bf16(h[0], h[1]);
                     w.y = pack_bf16(h[2], h[3]);
@@ -766,7 +782,12 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
 
 int launch_hidden(const JointArgs& a, int kpad, const int32_t* bounds, int pass, __nv_bfloat16* H, cudaStream_t st) {
     KernelTimer kt("joint_hidden", st);
-    hidden_kernel<<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.dec, a.T, a.U, a.d, kpad, bounds, pass, H);
+    if (a.enc16)
+        hidden_kernel<__nv_bfloat16><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc16, a.dec16, a.T, a.U, a.d, kpad,
+                                                                     a.vec, bounds, pass, H);
+    else
+        hidden_kernel<float><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.dec, a.T, a.U, a.d, kpad, a.vec,
+                                                             bounds, pass, H);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
@@ -973,6 +994,11 @@ struct DhParams {
     int* err;
 };
 
+// One activation as fp32 from the fp32 or the bf16 copy.
+__device__ __forceinline__ float act(const float* f32, const __nv_bfloat16* b16, int64_t i) {
+    return b16 ? __bfloat162float(b16[i]) : __ldg(f32 + i);
+}
+
 // Walk state of one epilogue thread over consecutive nodes (warp-uniform except
 // the per-column values).
 struct DhWalk {
@@ -992,11 +1018,11 @@ struct DhEpilogue {
     float* sacc;       // [dec_rows][kDhM] d_dec sums
 
     __device__ float enc_at(int b, int t) const {
-        return col_ok ? __ldg(P.a.enc + ((int64_t)b * P.a.T + t) * P.a.d + col) : 0.f;
+        return col_ok ? act(P.a.enc, P.a.enc16, ((int64_t)b * P.a.T + t) * P.a.d + col) : 0.f;
     }
     __device__ float dec_at(const DhWalk& w, int u) const {
         if (kSmemDec) return sdin[u * kDhM + cl];
-        return col_ok ? __ldg(P.a.dec + ((int64_t)w.b * P.a.U + u) * P.a.d + col) : 0.f;
+        return col_ok ? act(P.a.dec, P.a.dec16, ((int64_t)w.b * P.a.U + u) * P.a.d + col) : 0.f;
     }
     __device__ void add_dec(const DhWalk& w, int u, float x) const {
         if (kSmemDec)
@@ -1014,7 +1040,7 @@ struct DhEpilogue {
         w.e_nxt = t + 1 < w.Tb ? enc_at(b, t + 1) : 0.f;
         if (kSmemDec) {
             for (int u = 0; u < w.Ub; ++u) {
-                sdin[u * kDhM + cl] = col_ok ? __ldg(P.a.dec + ((int64_t)b * P.a.U + u) * P.a.d + col) : 0.f;
+                sdin[u * kDhM + cl] = col_ok ? act(P.a.dec, P.a.dec16, ((int64_t)b * P.a.U + u) * P.a.d + col) : 0.f;
                 sacc[u * kDhM + cl] = 0.f;
             }
         }

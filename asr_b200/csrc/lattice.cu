@@ -86,7 +86,34 @@ __global__ void __launch_bounds__(kPrepThreads)
     }
 }
 
+// Grid-stride element conversions (bandwidth bound; 8 elements per thread step).
+__global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ src, float* __restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __bfloat162float(src[i]);
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2bfloat16_rn(src[i]);
+}
+
 }  // namespace
+
+int launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n, cudaStream_t stream) {
+    if (n <= 0) return ASR_OK;
+    KernelTimer kt("act_convert", stream);
+    bf16_to_f32_kernel<<<sm_count() * 8, 256, 0, stream>>>(src, dst, n);
+    ASR_LAUNCH_CHECK();
+    return ASR_OK;
+}
+
+int launch_f32_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream) {
+    if (n <= 0) return ASR_OK;
+    KernelTimer kt("act_convert", stream);
+    f32_to_bf16_kernel<<<sm_count() * 8, 256, 0, stream>>>(src, dst, n);
+    ASR_LAUNCH_CHECK();
+    return ASR_OK;
+}
 
 int launch_lattice_prep(const int32_t* in_lens, const int32_t* tgt_lens, int B, int T, int U, int S,
                         const LatticeMeta& m, cudaStream_t stream) {

@@ -2,7 +2,9 @@
 // exact schemas of the reference (src/asr/loss/csrc/ctc_bindings.cpp:16-22,
 // rnnt_bindings.cpp:22-30, tdt_bindings.cpp:26-36), so the reference's Python
 // loss modules run on this library unchanged. Each op validates its tensors
-// like the reference (CUDA, contiguous, float32 / int32), allocates outputs and
+// like the reference (CUDA, contiguous, float32 / int32; the transducer ops also
+// take bf16 encoder / decoder activations and return bf16 gradients for them),
+// allocates outputs and
 // workspace through the torch caching allocator, and calls the C ABI of
 // include/asr_b200.h on the current stream of the input's device.
 #include <torch/csrc/inductor/aoti_torch/c/shim.h>
@@ -34,6 +36,17 @@ namespace {
     STD_TORCH_CHECK(x.is_cuda(), #x " must be a CUDA tensor");                                             \
     STD_TORCH_CHECK(x.is_contiguous(), #x " must be contiguous");                                          \
     STD_TORCH_CHECK(x.scalar_type() == ScalarType::Int, #x " must be int")
+
+// Encoder / decoder activations: float32 (the reference's contract) or bf16 (a
+// system's autocast activations, no float32 copies); both the same type.
+int act_dtype(const Tensor& encoder, const Tensor& decoder) {
+    STD_TORCH_CHECK(encoder.is_cuda() && decoder.is_cuda(), "encoder and decoder must be CUDA tensors");
+    STD_TORCH_CHECK(encoder.is_contiguous() && decoder.is_contiguous(), "encoder and decoder must be contiguous");
+    const ScalarType t = encoder.scalar_type();
+    STD_TORCH_CHECK(t == ScalarType::Float || t == ScalarType::BFloat16, "encoder must be float32 or bfloat16");
+    STD_TORCH_CHECK(decoder.scalar_type() == t, "decoder must have the encoder's dtype");
+    return t == ScalarType::BFloat16 ? ASR_DTYPE_BF16 : ASR_DTYPE_F32;
+}
 
 asr_stream_t current_stream(const Tensor& t) {
     void* s = nullptr;
@@ -98,8 +111,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> rnnt_forward(const Tensor& en
                                                                 const Tensor& joint_W, const Tensor& targets,
                                                                 const Tensor& in_lens, const Tensor& tgt_lens,
                                                                 int64_t blank_idx, int64_t tf32) {
-    ASR_CHECK_F32(encoder);
-    ASR_CHECK_F32(decoder);
+    const int act = act_dtype(encoder, decoder);
     ASR_CHECK_F32(joint_W);
     ASR_CHECK_I32(targets);
     ASR_CHECK_I32(in_lens);
@@ -108,14 +120,14 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> rnnt_forward(const Tensor& en
     const int B = dim(encoder, 0), T = dim(encoder, 1), d = dim(encoder, 2), U = dim(decoder, 1);
     const int V = dim(joint_W, 0), S = target_cols(targets);
     STD_TORCH_CHECK(dim(decoder, 0) == B && dim(decoder, 2) == d && dim(joint_W, 1) == d, "rnnt_forward: shape mismatch");
-    Tensor loss = torch::stable::new_empty(encoder, {B});
-    Tensor log_prob = torch::stable::new_empty(encoder, {B});
+    Tensor loss = torch::stable::new_empty(encoder, {B}, ScalarType::Float);
+    Tensor log_prob = torch::stable::new_empty(encoder, {B}, ScalarType::Float);
     Tensor alpha = torch::stable::new_empty(encoder, {B, T, U}, ScalarType::Double);
-    Tensor log_P_blank = torch::stable::new_empty(encoder, {2, B, T, U});
-    Tensor log_P_y = torch::stable::new_empty(encoder, {B, T, U});
-    const size_t wsb = asr_rnnt_workspace_bytes(B, T, U, V, d, (int)tf32, 0);
+    Tensor log_P_blank = torch::stable::new_empty(encoder, {2, B, T, U}, ScalarType::Float);
+    Tensor log_P_y = torch::stable::new_empty(encoder, {B, T, U}, ScalarType::Float);
+    const size_t wsb = asr_rnnt_workspace_bytes_ex(B, T, U, V, d, (int)tf32, 0, act);
     Tensor ws = workspace(encoder, wsb);
-    check_rc(asr_rnnt_forward(encoder.const_data_ptr<float>(), decoder.const_data_ptr<float>(),
+    check_rc(asr_rnnt_forward_ex(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
                               joint_W.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
                               in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, U, V, d, S,
                               (int)blank_idx, (int)tf32, loss.mutable_data_ptr<float>(),
@@ -131,8 +143,7 @@ std::tuple<Tensor, Tensor, Tensor> rnnt_backward(const Tensor& encoder, const Te
                                                  const Tensor& tgt_lens, int64_t blank_idx, const Tensor& alpha,
                                                  const Tensor& log_P_blank, const Tensor& log_P_y,
                                                  const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32) {
-    ASR_CHECK_F32(encoder);
-    ASR_CHECK_F32(decoder);
+    const int act = act_dtype(encoder, decoder);
     ASR_CHECK_F32(joint_W);
     ASR_CHECK_I32(targets);
     ASR_CHECK_I32(in_lens);
@@ -149,15 +160,15 @@ std::tuple<Tensor, Tensor, Tensor> rnnt_backward(const Tensor& encoder, const Te
     Tensor g_enc = torch::stable::new_empty(encoder, {B, T, d});
     Tensor g_dec = torch::stable::new_empty(encoder, {B, U, d});
     Tensor g_W = torch::stable::new_empty(joint_W, {V, d});
-    const size_t wsb = asr_rnnt_workspace_bytes(B, T, U, V, d, (int)tf32, 1);
+    const size_t wsb = asr_rnnt_workspace_bytes_ex(B, T, U, V, d, (int)tf32, 1, act);
     Tensor ws = workspace(encoder, wsb);
-    check_rc(asr_rnnt_backward(encoder.const_data_ptr<float>(), decoder.const_data_ptr<float>(),
+    check_rc(asr_rnnt_backward_ex(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
                                joint_W.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
                                in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, U, V, d,
                                S, (int)blank_idx, alpha.const_data_ptr<double>(), log_P_blank.const_data_ptr<float>(),
                                log_P_y.const_data_ptr<float>(), log_prob.const_data_ptr<float>(),
-                               grad_loss.const_data_ptr<float>(), (int)tf32, g_enc.mutable_data_ptr<float>(),
-                               g_dec.mutable_data_ptr<float>(), g_W.mutable_data_ptr<float>(), ws.mutable_data_ptr(),
+                               grad_loss.const_data_ptr<float>(), (int)tf32, g_enc.mutable_data_ptr(),
+                               g_dec.mutable_data_ptr(), g_W.mutable_data_ptr<float>(), ws.mutable_data_ptr(),
                                wsb, current_stream(encoder)),
              "asr::rnnt_backward");
     return {g_enc, g_dec, g_W};
@@ -169,8 +180,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> tdt_forward(
     const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
     const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
     int64_t max_duration, int64_t has_zero, int64_t blank_idx, double sigma, int64_t tf32) {
-    ASR_CHECK_F32(encoder);
-    ASR_CHECK_F32(decoder);
+    const int act = act_dtype(encoder, decoder);
     ASR_CHECK_F32(joint_W);
     ASR_CHECK_F32(joint_W_dur);
     ASR_CHECK_I32(targets);
@@ -181,15 +191,15 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> tdt_forward(
     const int B = dim(encoder, 0), T = dim(encoder, 1), d = dim(encoder, 2), U = dim(decoder, 1);
     const int V = dim(joint_W, 0), Dn = dim(joint_W_dur, 0), S = target_cols(targets);
     STD_TORCH_CHECK(durations.numel() == Dn, "tdt_forward: durations must have one entry per joint_W_dur row");
-    Tensor loss = torch::stable::new_empty(encoder, {B});
-    Tensor log_prob = torch::stable::new_empty(encoder, {B});
+    Tensor loss = torch::stable::new_empty(encoder, {B}, ScalarType::Float);
+    Tensor log_prob = torch::stable::new_empty(encoder, {B}, ScalarType::Float);
     Tensor alpha = torch::stable::new_empty(encoder, {B, T + 1, U}, ScalarType::Double);
-    Tensor log_P_blank = torch::stable::new_empty(encoder, {2, B, T, U});
-    Tensor log_P_y = torch::stable::new_empty(encoder, {B, T, U});
-    Tensor log_P_dur = torch::stable::new_empty(encoder, {B, T, U, Dn});
-    const size_t wsb = asr_tdt_workspace_bytes(B, T, U, V, Dn, d, (int)tf32, 0);
+    Tensor log_P_blank = torch::stable::new_empty(encoder, {2, B, T, U}, ScalarType::Float);
+    Tensor log_P_y = torch::stable::new_empty(encoder, {B, T, U}, ScalarType::Float);
+    Tensor log_P_dur = torch::stable::new_empty(encoder, {B, T, U, Dn}, ScalarType::Float);
+    const size_t wsb = asr_tdt_workspace_bytes_ex(B, T, U, V, Dn, d, (int)tf32, 0, act);
     Tensor ws = workspace(encoder, wsb);
-    check_rc(asr_tdt_forward(encoder.const_data_ptr<float>(), decoder.const_data_ptr<float>(),
+    check_rc(asr_tdt_forward_ex(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
                              joint_W.const_data_ptr<float>(), joint_W_dur.const_data_ptr<float>(),
                              targets.const_data_ptr<int32_t>(), in_lens.const_data_ptr<int32_t>(),
                              tgt_lens.const_data_ptr<int32_t>(), durations.const_data_ptr<int32_t>(), Dn,
@@ -207,8 +217,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward(
     const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
     int64_t max_duration, int64_t has_zero, int64_t blank_idx, const Tensor& alpha, const Tensor& log_P_blank,
     const Tensor& log_P_y, const Tensor& log_P_dur, const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32) {
-    ASR_CHECK_F32(encoder);
-    ASR_CHECK_F32(decoder);
+    const int act = act_dtype(encoder, decoder);
     ASR_CHECK_F32(joint_W);
     ASR_CHECK_F32(joint_W_dur);
     ASR_CHECK_I32(targets);
@@ -229,9 +238,9 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward(
     Tensor g_dec = torch::stable::new_empty(encoder, {B, U, d});
     Tensor g_W = torch::stable::new_empty(joint_W, {V, d});
     Tensor g_Wd = torch::stable::new_empty(joint_W_dur, {Dn, d});
-    const size_t wsb = asr_tdt_workspace_bytes(B, T, U, V, Dn, d, (int)tf32, 1);
+    const size_t wsb = asr_tdt_workspace_bytes_ex(B, T, U, V, Dn, d, (int)tf32, 1, act);
     Tensor ws = workspace(encoder, wsb);
-    check_rc(asr_tdt_backward(encoder.const_data_ptr<float>(), decoder.const_data_ptr<float>(),
+    check_rc(asr_tdt_backward_ex(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
                               joint_W.const_data_ptr<float>(), joint_W_dur.const_data_ptr<float>(),
                               targets.const_data_ptr<int32_t>(), in_lens.const_data_ptr<int32_t>(),
                               tgt_lens.const_data_ptr<int32_t>(), durations.const_data_ptr<int32_t>(), Dn,
@@ -239,7 +248,7 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward(
                               alpha.const_data_ptr<double>(), log_P_blank.const_data_ptr<float>(),
                               log_P_y.const_data_ptr<float>(), log_P_dur.const_data_ptr<float>(),
                               log_prob.const_data_ptr<float>(), grad_loss.const_data_ptr<float>(), (int)tf32,
-                              g_enc.mutable_data_ptr<float>(), g_dec.mutable_data_ptr<float>(),
+                              g_enc.mutable_data_ptr(), g_dec.mutable_data_ptr(),
                               g_W.mutable_data_ptr<float>(), g_Wd.mutable_data_ptr<float>(), ws.mutable_data_ptr(),
                               wsb, current_stream(encoder)),
              "asr::tdt_backward");

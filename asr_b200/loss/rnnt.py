@@ -43,7 +43,9 @@ class RNNTLossFn(torch.autograd.Function):
 
 
 def rnnt_loss(encoder, decoder, joint_W, targets, in_lens, tgt_lens, blank_idx: int = 0, tf32: bool = False):
-    """Per-utterance RNN-T loss ``-log P(y|x)`` (float32 CUDA tensors).
+    """Per-utterance RNN-T loss ``-log P(y|x)`` (CUDA tensors; encoder / decoder
+    float32, or bfloat16 to pass a system's autocast activations without float32
+    copies: their gradients then come back in bfloat16).
 
     encoder (B, T, d), decoder (B, U, d) with U = max target length + 1 (the
     caller prepends <sos>), joint_W (V, d), targets (B, S >= U-1),

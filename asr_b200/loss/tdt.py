@@ -63,7 +63,10 @@ def tdt_loss(encoder, decoder, joint_W, joint_W_dur, targets, in_lens, tgt_lens,
 
     ``durations`` lists the frame advance of each joint_W_dur row; it must be
     non-negative and contain 1. ``sigma`` (>= 0) is the logit under-normalisation
-    subtracted from every token log-prob (Xu et al. 2023, sec. 3.3).
+    subtracted from every token log-prob (Xu et al. 2023, sec. 3.3). encoder /
+    decoder may be float32 or bfloat16 (a system's autocast activations, passed
+    without float32 copies; their gradients then come back in bfloat16); the
+    joint weights stay float32.
     """
     durations = list(durations)
     if len(durations) != joint_W_dur.shape[0]:

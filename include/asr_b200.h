@@ -43,6 +43,13 @@ typedef enum {
     ASR_ERR_SCRATCH_LIMIT = 5     /* problem needs more than the fixed scratch of a *_noalloc entry point */
 } asr_status_t;
 
+/* Element type of the encoder / decoder activations and of their gradients in
+ * the *_ex entry points (the joint weights and every other array stay float32). */
+typedef enum {
+    ASR_DTYPE_F32 = 0,
+    ASR_DTYPE_BF16 = 1
+} asr_dtype_t;
+
 /* Human-readable name of a status code. */
 const char* asr_status_string(int status);
 
@@ -125,6 +132,47 @@ int asr_tdt_backward(const float* encoder, const float* decoder, const float* jo
                      const float* log_P_y, const float* log_P_dur, const float* log_prob, const float* grad_loss,
                      int tf32, float* grad_encoder, float* grad_decoder, float* grad_joint_W,
                      float* grad_joint_W_dur, void* workspace, size_t workspace_bytes, asr_stream_t stream);
+
+/* ------------------------------------------- bf16 activations (*_ex variants)
+ *
+ * The entry points above with the encoder / decoder activations (and, in the
+ * backward, their gradients) of element type act_dtype (asr_dtype_t): bf16 lets a
+ * system pass its autocast activations without float32 copies. The tensor-core
+ * joint (tf32 != 0) reads bf16 activations directly; the fp32 path reads float32
+ * copies that the call makes in its workspace. bf16 gradients are summed in
+ * float32 in the workspace and rounded once. Activation rows must be 16-byte
+ * aligned for the vector loads (otherwise a scalar path is taken). With act_dtype =
+ * ASR_DTYPE_F32 each is identical to its float32 entry point. No counterpart in
+ * the reference, whose ops take float32 only (the systems' .float() copies,
+ * system/rnnt.py:51, system/tdt.py:59). */
+size_t asr_rnnt_workspace_bytes_ex(int B, int T, int U, int V, int d, int tf32, int backward, int act_dtype);
+int asr_rnnt_forward_ex(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                        const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens, int B, int T,
+                        int U, int V, int d, int S, int blank_idx, int tf32, float* loss, double* alpha,
+                        float* log_P_blank, float* log_P_y, float* log_prob, void* workspace,
+                        size_t workspace_bytes, asr_stream_t stream);
+int asr_rnnt_backward_ex(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                         const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens, int B, int T,
+                         int U, int V, int d, int S, int blank_idx, const double* alpha, const float* log_P_blank,
+                         const float* log_P_y, const float* log_prob, const float* grad_loss, int tf32,
+                         void* grad_encoder, void* grad_decoder, float* grad_joint_W, void* workspace,
+                         size_t workspace_bytes, asr_stream_t stream);
+size_t asr_tdt_workspace_bytes_ex(int B, int T, int U, int V, int n_dur, int d, int tf32, int backward,
+                                  int act_dtype);
+int asr_tdt_forward_ex(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                       const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                       const int32_t* tgt_lens, const int32_t* durations, int n_dur, int max_duration, int has_zero,
+                       int B, int T, int U, int V, int d, int S, int blank_idx, float sigma, int tf32, float* loss,
+                       double* alpha, float* log_P_blank, float* log_P_y, float* log_P_dur, float* log_prob,
+                       void* workspace, size_t workspace_bytes, asr_stream_t stream);
+int asr_tdt_backward_ex(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                        const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                        const int32_t* tgt_lens, const int32_t* durations, int n_dur, int max_duration, int has_zero,
+                        int B, int T, int U, int V, int d, int S, int blank_idx, const double* alpha,
+                        const float* log_P_blank, const float* log_P_y, const float* log_P_dur,
+                        const float* log_prob, const float* grad_loss, int tf32, void* grad_encoder,
+                        void* grad_decoder, float* grad_joint_W, float* grad_joint_W_dur, void* workspace,
+                        size_t workspace_bytes, asr_stream_t stream);
 
 /* Bytes of the scratch array compiled into the library for asr_tdt_forward_noalloc. */
 #define ASR_TDT_FORWARD_NOALLOC_SCRATCH_BYTES (4u << 20)

@@ -57,7 +57,7 @@ def test_status_strings_and_version():
     lib.asr_status_string.restype = ctypes.c_char_p
     assert lib.asr_status_string(0) == b"ok"
     assert b"workspace" in lib.asr_status_string(2)
-    assert lib.asr_abi_version() == 1
+    assert lib.asr_abi_version() == 2
 
 
 def _ws(lib, fn, *args):
@@ -73,6 +73,25 @@ def test_workspace_sizes_monotone():
     assert 0 < small < big
     assert _ws(lib, "asr_tdt_workspace_bytes", 4, 50, 10, 64, 5, 32, 0, 0) < small
     assert _ws(lib, "asr_rnnt_workspace_bytes", 4, 0, 10, 64, 32, 0, 0) == 0  # T < 1 is invalid
+
+
+def test_bf16_activation_workspace_and_dtype_checks():
+    """The *_ex entry points: bf16 activations add fp32 staging to the workspace
+    (gradient sums in the backward), float32 matches the plain entry points, and an
+    unknown activation dtype is rejected on the host."""
+    lib = _lib.capi()
+    for fn, base, args in (("asr_tdt_workspace_bytes_ex", "asr_tdt_workspace_bytes", (4, 50, 10, 64, 5, 32, 0)),
+                           ("asr_rnnt_workspace_bytes_ex", "asr_rnnt_workspace_bytes", (4, 50, 10, 64, 32, 0))):
+        for bwd in (0, 1):
+            f32 = _ws(lib, fn, *args, bwd, 0)
+            assert f32 == _ws(lib, base, *args, bwd)
+            assert _ws(lib, fn, *args, bwd, 1) > f32
+            assert _ws(lib, fn, *args, bwd, 7) == 0
+    null = ctypes.c_void_p(0)
+    fake = ctypes.c_void_p(0x1000)
+    args = [fake, fake, ctypes.c_int(7)] + [fake] * 4 + [ctypes.c_int(v) for v in (2, 4, 3, 5, 8, 2, 0, 0)] + \
+        [fake] * 5 + [null, ctypes.c_size_t(0), null]
+    assert lib.asr_rnnt_forward_ex(*args) == 1
 
 
 def test_invalid_arguments_rejected_on_host():

@@ -459,3 +459,53 @@ def test_tdt_bf16_joint_variants_agree(tmp_path):
         for k in ("arr_0", "arr_1", "arr_2", "arr_3"):
             a, b = out[name][k].astype(np.float64), out["stream"][k].astype(np.float64)
             assert np.linalg.norm(a - b) <= 1e-5 * np.linalg.norm(b), (name, k)
+
+
+@pytest.mark.parametrize("tf32", [True, False])
+def test_tdt_bf16_activations_match_float32_on_the_same_values(tf32):
+    """bf16 encoder / decoder activations (what an autocast system produces) go in
+    without float32 copies: the loss equals the float32 path fed the same values,
+    the activation gradients come back in bf16 within their rounding, and the
+    joint-weight gradients match. Both joint paths: tensor cores read bf16
+    directly, the fp32 path reads a float32 copy made in the workspace."""
+    from asr_b200.loss.tdt import tdt_loss
+
+    c = transducer_case(41, 4, (40, 90), (10, 40), 1024, 640, n_dur=5)
+    enc16 = torch.tensor(c["enc"]).to(torch.bfloat16).cuda()
+    dec16 = torch.tensor(c["dec"]).to(torch.bfloat16).cuda()
+    args = [cuda(c[k]) for k in ("targets", "in_lens", "tgt_lens")]
+    gl = cuda(c["grad_loss"])
+    out = {}
+    for name, e0, d0 in (("bf16", enc16, dec16), ("f32", enc16.float(), dec16.float())):
+        e, d = e0.clone().requires_grad_(True), d0.clone().requires_grad_(True)
+        w, wd = leaf(c["W"]), leaf(c["W_dur"])
+        loss = tdt_loss(e, d, w, wd, *args, [int(x) for x in c["durations"]], 0, 0.05, tf32)
+        (loss * gl).sum().backward()
+        out[name] = (loss.detach(), e.grad, d.grad, w.grad, wd.grad)
+    lb, eb, db, wb, wdb = out["bf16"]
+    lf, ef, df, wf, wdf = out["f32"]
+    assert lb.dtype == torch.float32 and eb.dtype == torch.bfloat16 and db.dtype == torch.bfloat16
+    torch.testing.assert_close(lb, lf, rtol=1e-6, atol=1e-6)
+    assert _rel(eb.float(), ef) < 1e-2 and _rel(db.float(), df) < 1e-2
+    assert _rel(wb, wf) < 1e-5 and _rel(wdb, wdf) < 1e-5
+
+
+def test_rnnt_bf16_activations_module():
+    """RNNTLoss on bf16 activations through autograd (tensor-core joint)."""
+    from asr_b200.loss.rnnt import RNNTLoss, rnnt_loss
+
+    c = transducer_case(42, 3, (30, 60), (10, 30), 256, 320)
+    e = torch.tensor(c["enc"]).to(torch.bfloat16).cuda().requires_grad_(True)
+    d = torch.tensor(c["dec"]).to(torch.bfloat16).cuda().requires_grad_(True)
+    w = leaf(c["W"])
+    args = [cuda(c[k]) for k in ("targets", "in_lens", "tgt_lens")]
+    loss = RNNTLoss(tf32=True)(e, d, w, *args)
+    loss.sum().backward()
+    e32 = e.detach().float().requires_grad_(True)
+    d32 = d.detach().float().requires_grad_(True)
+    w32 = leaf(c["W"])
+    ref = rnnt_loss(e32, d32, w32, *args, 0, True) / args[2].clamp_min(1)
+    ref.sum().backward()
+    torch.testing.assert_close(loss.detach(), ref.detach(), rtol=1e-6, atol=1e-6)
+    assert e.grad.dtype == torch.bfloat16 and _rel(e.grad.float(), e32.grad) < 1e-2
+    assert _rel(w.grad, w32.grad) < 1e-5
