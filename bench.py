@@ -446,6 +446,8 @@ def main():
     ap.add_argument("--clocks-log", default=None)
     ap.add_argument("--batch", type=int, default=None,
                     help="profiling aid: run only the first BATCH utterances of the workload")
+    ap.add_argument("--act-dtype", default="f32", choices=["f32", "bf16"],
+                    help="encoder / decoder activation dtype (bf16: a system's autocast activations, no float32 copies)")
     ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"],
                     help="c5 (default): the headline config-5 workload; c1..c4: the other BASELINE configs, 1 GPU")
     args = ap.parse_args()
@@ -490,8 +492,9 @@ def main():
     N_local = int((host["in_lens"].astype(np.int64) * (host["tgt_lens"] + 1)).sum())
     N_global = int((in_lens.astype(np.int64) * (tgt_lens + 1)).sum())
 
-    enc = torch.tensor(host["enc"], device=dev, requires_grad=True)
-    dec = torch.tensor(host["dec"], device=dev, requires_grad=True)
+    act_dt = torch.bfloat16 if args.act_dtype == "bf16" else torch.float32
+    enc = torch.tensor(host["enc"], device=dev).to(act_dt).requires_grad_(True)
+    dec = torch.tensor(host["dec"], device=dev).to(act_dt).requires_grad_(True)
     W = torch.tensor(W_np, device=dev, requires_grad=True)
     Wd = torch.tensor(Wd_np, device=dev, requires_grad=True)
     targets = torch.tensor(host["targets"], device=dev)
@@ -547,6 +550,8 @@ def main():
 
     # ---- end to end: pinned host inputs copied in, loss read back, every step
     pinned = {k: torch.from_numpy(v).pin_memory() for k, v in host.items()}
+    pinned["enc"] = pinned["enc"].to(act_dt).pin_memory()
+    pinned["dec"] = pinned["dec"].to(act_dt).pin_memory()
     res_host = torch.empty(1, dtype=torch.float32).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in pinned.values())
 
@@ -635,7 +640,7 @@ def main():
                        "lattice_nodes_rank0": N_local, "shard_imbalance": round(shard_imbalance(
                            in_lens, tgt_lens, shards), 4), "parallelism": f"dp{world}",
                        "l2": "flushed between timed steps (256 MB write)",
-                       "joint_path": "tcgen05 bf16" if tc else "SIMT fp32"},
+                       "joint_path": "tcgen05 bf16" if tc else "SIMT fp32", "activations": args.act_dtype},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4)},
