@@ -435,6 +435,218 @@ def run_config(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------- greedy decoding
+#
+# `--workload decode-tdt | decode-rnnt` times batched greedy decoding
+# (asr_b200.decode.{tdt,rnnt}.greedy_decode) on one GPU: decode-tdt on the
+# config-5 shapes (B=512, T ~ U[200, 500], d=640, V=1024, durations 0..4),
+# decode-rnnt on the config-4 shapes (B=128, T=400, d=1024, V=1024). The encoder
+# output is synthetic, N(0, 0.8^2) with a constant component the blank row of
+# the joint weight reads, so that blank wins most steps (about 0.25 tokens per
+# frame, as a trained BPE model emits); the predictor is the reference system's
+# Embedding + 2-layer LSTM(batch_first=False), random-initialised, called once
+# per emitted token and utterance as the reference decoder calls it
+# (--decode-predict batched: a batch_first LSTM called once per scan on all
+# emitting utterances instead).
+
+DECODE = {
+    "decode-tdt": {"name": "decode_tdt_bpe1024", "B": 512, "T": T_RANGE, "d": 640, "V": 1024, "n_dur": 5,
+                   "blank_bias": 6.0},
+    "decode-rnnt": {"name": "decode_rnnt_bpe1024", "B": 128, "T": (400, 400), "d": 1024, "V": 1024, "n_dur": 0,
+                    "blank_bias": 8.0},
+}
+
+
+def decode_inputs(cfg, seed=SEED):
+    rng = np.random.default_rng([seed, 91])
+    B, d, V = cfg["B"], cfg["d"], cfg["V"]
+    in_lens = rng.integers(cfg["T"][0], cfg["T"][1] + 1, size=B).astype(np.int32)
+    T = int(in_lens.max())
+    enc = (rng.standard_normal((B, T, d), dtype=np.float32) * 0.8).astype(np.float32)
+    enc[..., 0] = 2.0
+    W = (rng.standard_normal((V, d)) * (3.0 / np.sqrt(d))).astype(np.float32)
+    W[0, 0] += cfg["blank_bias"]
+    Wd = None
+    if cfg["n_dur"]:
+        Wd = (rng.standard_normal((cfg["n_dur"], d)) * (3.0 / np.sqrt(d))).astype(np.float32)
+        Wd[1, 0] += 0.5
+    return {"enc": enc, "in_lens": in_lens, "W": W, "W_dur": Wd}
+
+
+def decode_predictor(cfg, device, batch_first=False, seed=SEED):
+    import torch
+
+    g = torch.Generator().manual_seed(seed + 5)
+    d, V = cfg["d"], cfg["V"]
+    emb = torch.nn.Embedding(V, d, padding_idx=0)
+    lstm = torch.nn.LSTM(input_size=d, hidden_size=d, num_layers=2, batch_first=batch_first)
+    with torch.no_grad():
+        for p in list(emb.parameters()) + list(lstm.parameters()):
+            p.copy_(torch.randn(p.shape, generator=g) * (1.0 / np.sqrt(d)))
+    emb, lstm = emb.to(device).eval(), lstm.to(device).eval()
+
+    def predict(tokens):
+        return lstm(emb(tokens))[0]
+
+    return predict
+
+
+def decode_cpu_sample(cfg, host, sample):
+    """The reference greedy algorithm restated in numpy (oracle/greedy.py) with the
+    same predictor on the CPU, on the first `sample` utterances."""
+    import torch
+
+    from oracle import greedy
+
+    predict_t = decode_predictor(cfg, "cpu")
+
+    def predict(prefix):
+        with torch.no_grad():
+            return predict_t(torch.as_tensor(np.asarray(prefix), dtype=torch.int64)[None])[0, -1].numpy()
+
+    enc, lens = host["enc"][:sample], host["in_lens"][:sample]
+    t0 = time.perf_counter()
+    if cfg["n_dur"]:
+        greedy.greedy_tdt(enc, lens, predict, host["W"], host["W_dur"], cfg["n_dur"] - 1)
+    else:
+        greedy.greedy_rnnt(enc, lens, predict, host["W"])
+    return time.perf_counter() - t0
+
+
+def run_decode(args):
+    import ctypes
+
+    import torch
+
+    from asr_b200 import _lib
+    from asr_b200.decode import rnnt as dec_rnnt
+    from asr_b200.decode import tdt as dec_tdt
+
+    cfg = DECODE[args.workload]
+    host = decode_inputs(cfg)
+    sample = 1  # ~10-30 s of CPU work: the reference re-runs the predictor on the whole prefix per token
+    if args.impl == "reference":
+        torch.set_num_threads(os.cpu_count() or 1)
+        decode_cpu_sample(cfg, host, 1)  # warm-up
+        dt = sum(decode_cpu_sample(cfg, host, sample) for _ in range(max(1, args.steps // 5)))
+        value = sample * max(1, args.steps // 5) / dt
+        base = {"value": round(value, 4), "unit": "utterances/s", "cores": torch.get_num_threads(), "kind": "port",
+                "sample": f"utterances 0..{sample - 1} per step, numpy restatement of the reference greedy decoder "
+                          "with the same LSTM predictor on the CPU (torch, float32)"}
+        print(json.dumps({"impl": "reference", "metric": "greedy decode utterances/s", "value": base["value"],
+                          "unit": "utterances/s", "n_gpus": 1, "steps": max(1, args.steps // 5), "warmup": 1,
+                          "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                          "config": {"workload": cfg["name"]}, "cpu_baseline": base,
+                          "e2e": {"value": base["value"], "unit": "utterances/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+
+    dev = torch.device("cuda", 0)
+    batched = args.decode_predict == "batched"
+    predict = decode_predictor(cfg, dev, batch_first=batched)
+    enc = torch.tensor(host["enc"], device=dev)
+    lens = torch.tensor(host["in_lens"], device=dev)
+    W = torch.tensor(host["W"], device=dev)
+    Wd = torch.tensor(host["W_dur"], device=dev) if cfg["n_dur"] else None
+    B = cfg["B"]
+
+    def decode(e, ln):
+        if cfg["n_dur"]:
+            return dec_tdt.greedy_decode(e, ln, predict, W, Wd, cfg["n_dur"] - 1, batch_predict=batched)
+        return dec_rnnt.greedy_decode(e, ln, predict, W, batch_predict=batched), None
+
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    out = {}
+
+    def timed(run, k):
+        times = []
+        for _ in range(k):
+            flush.fill_(1)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            run()
+            s1.record(stream)
+            times.append((s0, s1))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in times)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            out["r"] = decode(enc, lens)
+        torch.cuda.synchronize()
+        lib = _lib.capi()
+        lib.asr_profiler_report(None, 0, 1)
+        clocks = ClockSampler(args.clocks_log)
+        clocks.start()
+        time.sleep(0.3)
+        lib.asr_profiler_enable(1)
+        ms = timed(lambda: out.__setitem__("r", decode(enc, lens)), args.steps) / args.steps
+        lib.asr_profiler_enable(0)
+        clock_info = clocks.stop()
+        n = lib.asr_profiler_report(None, 0, 0)
+        buf = ctypes.create_string_buffer(max(n, 0) + 1)
+        lib.asr_profiler_report(buf, len(buf), 1)
+        prof = parse_profile(buf.value.decode())
+
+        pinned = {"enc": torch.from_numpy(host["enc"]).pin_memory(), "in_lens": torch.from_numpy(host["in_lens"])}
+        h2d = pinned["enc"].numel() * 4
+
+        def e2e():
+            out["r"] = decode(pinned["enc"].to(dev, non_blocking=True), pinned["in_lens"])
+
+        e2e()
+        e2e_ms = timed(e2e, args.steps) / args.steps
+
+    hyps, durs = out["r"]
+    n_tok = sum(map(len, hyps))
+    frames = int(host["in_lens"].sum())
+    # Joint evaluations the reference decoder makes: one per TDT step (the recorded
+    # durations); for RNN-T one per emitted token plus one blank per frame.
+    steps = sum(map(len, durs)) if durs is not None else n_tok + frames
+    d2h = 8 * (n_tok + (steps if durs is not None else 0)) + 16 * B
+    Vf = cfg["V"] + cfg["n_dur"]
+    kernels = {}
+    total_ms = max(sum(v[1] for v in prof.values()), 1e-9)
+    sm_mhz = (clock_info or {}).get("sm_mhz") or 1965.0
+    fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12  # FFMA lanes x 2 flops x SM clock
+    for name, (launches, kms) in prof.items():
+        e = {"launches_per_step": launches / args.steps, "ms_per_step": round(kms / args.steps, 4),
+             "share": round(kms / total_ms, 4)}
+        if name == "greedy_scan":
+            flops = 2.0 * steps * cfg["d"] * Vf
+            ach = flops / (kms / args.steps / 1000.0) / 1e12
+            e.update({"bound": "fp32", "achieved": round(ach, 2), "unit": "TFLOP/s", "frac": round(ach / fp32_peak, 4)})
+        kernels[name] = e
+    scan = kernels.get("greedy_scan", {})
+    roof = {"kernel": "greedy_scan", "bound": "fp32", "achieved": scan.get("achieved"),
+            "peak": round(fp32_peak, 2), "unit": "TFLOP/s", "frac": scan.get("frac"), "traffic": None,
+            "peak_source": f"nominal FP32 FFMA rate of 148 SMs at the sampled SM clock ({sm_mhz:.0f} MHz)",
+            "work": "2 * d * (V + n_dur) flops per reference decoding step"}
+    cpu = None
+    if not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        dt = decode_cpu_sample(cfg, host, sample)
+        cpu = {"value": round(sample / dt, 4), "unit": "utterances/s", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": f"utterances 0..{sample - 1}: numpy restatement of the reference greedy "
+                                         "decoder with the same LSTM predictor on the CPU"}
+    line = {
+        "metric": "greedy decode utterances/s", "value": round(B / (ms / 1000.0), 3), "unit": "utterances/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["name"], "batch": B, "T": list(cfg["T"]), "d_model": cfg["d"], "vocab": cfg["V"],
+                   "n_dur": cfg["n_dur"], "predictor": "Embedding + LSTM(2 layers, " +
+                   ("batch_first=True), one call per scan" if batched else "batch_first=False), one call per token"),
+                   "tokens": n_tok, "frames": frames, "decoding_steps": steps,
+                   "l2": "flushed between timed steps (256 MB write)"},
+        "roofline": roof, "cpu_baseline": cpu,
+        "e2e": {"value": round(B / (e2e_ms / 1000.0), 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": int(sum(v[0] for v in prof.values()) / args.steps), "kernels": kernels, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -448,9 +660,16 @@ def main():
                     help="profiling aid: run only the first BATCH utterances of the workload")
     ap.add_argument("--act-dtype", default="f32", choices=["f32", "bf16"],
                     help="encoder / decoder activation dtype (bf16: a system's autocast activations, no float32 copies)")
-    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"],
-                    help="c5 (default): the headline config-5 workload; c1..c4: the other BASELINE configs, 1 GPU")
+    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5", *DECODE],
+                    help="c5 (default): the headline config-5 workload; c1..c4: the other BASELINE configs, 1 GPU; "
+                         "decode-tdt / decode-rnnt: batched greedy decoding, 1 GPU")
+    ap.add_argument("--decode-predict", default="per-utterance", choices=["per-utterance", "batched"])
     args = ap.parse_args()
+    if args.workload in DECODE:
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            raise SystemExit("--workload decode-* runs on one GPU")
+        run_decode(args)
+        return
     if args.workload != "c5":
         if args.impl == "reference" or int(os.environ.get("WORLD_SIZE", "1")) > 1:
             raise SystemExit("--workload c1..c4 runs our implementation on one GPU only")

@@ -194,6 +194,55 @@ int asr_tdt_forward_noalloc(const float* encoder, const float* decoder, const fl
                             int tf32, float* loss, double* alpha, float* log_P_blank, float* log_P_y,
                             float* log_P_dur, float* log_prob, asr_stream_t stream);
 
+/* ------------------------------------------------ greedy transducer decoding */
+
+/* Batched greedy decoding for RNN-T and TDT. Replaces the per-utterance,
+ * per-symbol joint calls of the reference decoders (src/asr/decode/rnnt.py:12-37
+ * greedy_decode; src/asr/decode/tdt.py:14-62 greedy_decode), whose joint is
+ * Linear(tanh(enc_t + pred_u)) without bias (src/asr/system/rnnt.py:29-34,
+ * src/asr/system/tdt.py:31-43). The reference has no C interface for decoding;
+ * these entry points are driven by a host loop (asr_b200/decode/_greedy.py):
+ *
+ *   asr_greedy_pack_weights(W -> Wt); asr_greedy_init(state, prefix);
+ *   pred[b] = predictor output for the prefix [<sos>], every b;
+ *   loop: asr_greedy_scan(...); read report (B,);
+ *         stop when no report[b] > 0; otherwise, for every b with
+ *         report[b] = L > 0, pred[b] = predictor output at position L-1 of
+ *         prefix[b, :L].
+ *
+ * Buffers, all device memory, row-major:
+ *   state  (B, 4) int32   per utterance: frame t, symbols emitted at t, hypothesis
+ *                         length, number of recorded durations;
+ *   prefix (B, hyp_cap+1) int64  <sos> followed by the emitted tokens;
+ *   durs   (B, dur_cap) int32   TDT only: the argmax duration of every step,
+ *                         blanks included (the reference's second return value);
+ *   report (B,) int32     after a scan: L = prefix length when utterance b emitted a
+ *                         token and needs a new predictor output, 0 when it has
+ *                         finished, -1 when hyp_cap or dur_cap was too small.
+ * hyp_cap = dur_cap = T * max_symbols_per_frame can never overflow. */
+
+/* joint_Wt (d, ldw) = transpose of joint_W (V, d), columns V..ldw-1 zeroed.
+ * ldw >= V, a multiple of 4; joint_Wt 16-byte aligned. */
+int asr_greedy_pack_weights(const float* joint_W, int V, int d, float* joint_Wt, int ldw, asr_stream_t stream);
+
+/* Zeroes state and writes <sos> = sos_id at prefix[b, 0]. */
+int asr_greedy_init(int32_t* state, int64_t* prefix, int B, int hyp_cap, int sos_id, asr_stream_t stream);
+
+/* Advances every unfinished utterance from its state to its next emitted token
+ * or to its end (frame t >= in_lens[b]) with the predictor output pred (B, d).
+ * encoder (B, T, d) float32; joint_Wt from asr_greedy_pack_weights;
+ * joint_W_dur (n_dur, d) float32 selects TDT when n_dur > 0 (duration value =
+ * argmax index, the reference's durations = range(max_duration + 1)); n_dur = 0
+ * and joint_W_dur = NULL select RNN-T. Ties take the lowest index and NaN counts
+ * as the maximum (torch.argmax). max_symbols_per_frame <= 0 finishes every
+ * utterance without emitting, as the reference's empty per-frame loop does.
+ * in_lens outside [0, T] are clamped. d <= 4096 and n_dur <= 64, else
+ * ASR_ERR_UNSUPPORTED. */
+int asr_greedy_scan(const float* encoder, const float* pred, const float* joint_Wt, int ldw,
+                    const float* joint_W_dur, const int32_t* in_lens, int32_t* state, int64_t* prefix,
+                    int32_t* durs, int32_t* report, int B, int T, int d, int V, int n_dur, int blank_idx,
+                    int max_symbols_per_frame, int hyp_cap, int dur_cap, asr_stream_t stream);
+
 /* ----------------------------------------------------------- diagnostics */
 
 /* Copies the device status word of a workspace used by the last call on it

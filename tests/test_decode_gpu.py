@@ -1,0 +1,193 @@
+"""Parity of the batched GPU greedy decoders with the reference decoders.
+
+Decoding is integer output (token and duration indices), so the bar is exact
+equality: (a) with the golden vectors produced by the reference's own
+greedy_decode (tests/golden/make_decode_golden.py), (b) with the numpy oracle
+(oracle/greedy.py) on seeded inputs at the benchmark's joint shapes. The float32
+joint of the kernel and of the oracle differ only in summation order (relative
+error ~1e-6), so every comparison first checks, on the oracle side, that no
+argmax it took had a top-2 gap below MARGIN; such a near-tie could legitimately
+resolve either way.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from asr_b200.decode import rnnt, tdt
+from oracle import greedy
+from tests.decode_cases import DECODE, expected, params, random_decode_case
+
+pytestmark = pytest.mark.gpu
+
+MARGIN = 1e-4
+
+
+def cuda(x):
+    return torch.as_tensor(np.ascontiguousarray(x), device="cuda")
+
+
+def table_predictor(P, Q, calls=None):
+    """Torch form of oracle.greedy.table_predictor (same float32 values)."""
+    Pt, Qt = cuda(P), cuda(Q)
+
+    def predict(tokens):
+        assert tokens.dtype == torch.int64 and tokens.dim() == 2
+        if calls is not None:
+            calls.extend(tuple(r) for r in tokens.cpu().numpy().tolist())
+        pos = (torch.arange(tokens.shape[-1], device=tokens.device) + 1) % Qt.shape[0]
+        return Pt[tokens] + Qt[pos]
+
+    return predict
+
+
+def run(c, batch_predict=False, joint_form="tensor", calls=None):
+    blank, sos, max_sym, max_duration = params(c)
+    pred = table_predictor(c["P"], c["Q"], calls)
+    W = cuda(c["W"])
+    if joint_form == "linear":
+        lin = torch.nn.Linear(W.shape[1], W.shape[0], bias=False, device="cuda")
+        lin.weight.data.copy_(W)
+        W = lin
+    if str(c["kind"]) == "rnnt":
+        return rnnt.greedy_decode(cuda(c["enc"]), cuda(c["in_lens"]), pred, W, blank_id=blank, sos_id=sos,
+                                  max_symbols_per_frame=max_sym, batch_predict=batch_predict), None
+    return tdt.greedy_decode(cuda(c["enc"]), cuda(c["in_lens"]), pred, W, cuda(c["W_dur"]), max_duration,
+                             blank_id=blank, sos_id=sos, max_symbols_per_frame=max_sym, batch_predict=batch_predict)
+
+
+@pytest.mark.parametrize("name", sorted(DECODE))
+def test_greedy_matches_reference_golden(name):
+    c = DECODE[name]
+    hyps, durs = run(c)
+    want_hyps, want_durs = expected(c)
+    assert hyps == want_hyps
+    assert durs == want_durs
+
+
+@pytest.mark.parametrize("name", ["rnnt_small", "rnnt_char30", "tdt_bpe_like", "tdt_wide_vocab", "ref_frame_skip"])
+def test_batched_predictor_calls_give_the_same_result(name):
+    """batch_predict=True (one call on padded prefixes) with a row-independent,
+    causal predictor, and the joint given as the system's nn.Linear."""
+    c = DECODE[name]
+    want_hyps, want_durs = expected(c)
+    hyps, durs = run(c, batch_predict=True, joint_form="linear")
+    assert hyps == want_hyps
+    assert durs == want_durs
+
+
+@pytest.mark.parametrize("kind", ["rnnt", "tdt"])
+def test_predictor_sees_the_reference_prefixes(kind):
+    """The default mode calls the predictor with exactly the (1, L) prefixes the
+    reference decoder passes (apart from its B repeated [<sos>] calls, made once)."""
+    c = DECODE["rnnt_odd_dim" if kind == "rnnt" else "tdt_bpe_like"]
+    blank, sos, max_sym, max_duration = params(c)
+    ours = []
+    run(c, calls=ours)
+    theirs = []
+    base = greedy.table_predictor(c["P"], c["Q"])
+
+    def logged(prefix):
+        theirs.append(tuple(np.asarray(prefix).tolist()))
+        return base(prefix)
+
+    if kind == "rnnt":
+        greedy.greedy_rnnt(c["enc"], c["in_lens"], logged, c["W"], blank, sos, max_sym)
+    else:
+        greedy.greedy_tdt(c["enc"], c["in_lens"], logged, c["W"], c["W_dur"], max_duration, blank, sos, max_sym)
+    start = (sos,)
+    assert ours.count(start) == 1
+    assert sorted(p for p in ours if p != start) == sorted(p for p in theirs if p != start)
+
+
+def _oracle(c, kind, max_sym, margins):
+    predict = greedy.table_predictor(c["P"], c["Q"])
+    if kind == "rnnt":
+        return greedy.greedy_rnnt(c["enc"], c["in_lens"], predict, c["W"], 0, 1, max_sym, margins), None
+    return greedy.greedy_tdt(c["enc"], c["in_lens"], predict, c["W"], c["W_dur"], c["W_dur"].shape[0] - 1, 0, 1,
+                             max_sym, margins)
+
+
+# (kind, V, d, blank bias, max_symbols_per_frame, seed): 0.2-0.4 tokens per frame
+@pytest.mark.parametrize("kind,V,d,bias,max_sym,seed", [("tdt", 1024, 640, 6.0, 10, 1677), ("rnnt", 1024, 640, 8.0, 10, 1677),
+                                                         ("rnnt", 30, 640, 6.0, 4, 682), ("tdt", 1029, 1024, 6.5, 3, 2064)])
+def test_greedy_matches_oracle_at_benchmark_shapes(kind, V, d, bias, max_sym, seed):
+    c = random_decode_case(seed, 12, 90, V, d, 5 if kind == "tdt" else 0, bias, lo=1)
+    margins = []
+    want_hyps, want_durs = _oracle(c, kind, max_sym, margins)
+    assert min(margins) > MARGIN, "seeded draw has a float32 near-tie; pick another seed"
+    assert sum(map(len, want_hyps)) > 0
+    cc = dict(c, kind=np.array(kind), params=np.array([0, 1, max_sym, 4], np.int32))
+    hyps, durs = run(cc)
+    assert hyps == want_hyps
+    assert durs == want_durs
+
+
+def test_full_batch_matches_oracle_on_a_sample():
+    """Config-5-sized batch (B=512, T up to 500, V=1024, d=640, 5 durations): every
+    utterance is decoded independently, so a seeded sample of 6 utterances checked
+    against the oracle pins the whole batch run."""
+    c = random_decode_case(7, 512, 500, 1024, 640, 5, 6.0, lo=200)
+    cc = dict(c, kind=np.array("tdt"), params=np.array([0, 1, 10, 4], np.int32))
+    hyps, durs = run(cc, batch_predict=True)
+    pick = np.random.default_rng(0).choice(512, size=6, replace=False)
+    sub = dict(c, enc=c["enc"][pick], in_lens=c["in_lens"][pick])
+    margins = []
+    want_hyps, want_durs = _oracle(sub, "tdt", 10, margins)
+    assert min(margins) > MARGIN
+    assert [hyps[i] for i in pick] == want_hyps
+    assert [durs[i] for i in pick] == want_durs
+    assert all(len(d) > 0 for d in durs)
+
+
+def test_reference_lstm_predictor_per_utterance():
+    """The reference's predictor, Embedding + LSTM(batch_first=False) as in
+    model/lstm.py:8-15, through the default per-utterance calls: the oracle runs
+    the same module on the CPU in float32."""
+    torch.manual_seed(3)
+    V, d = 48, 64
+    emb = torch.nn.Embedding(V, d, padding_idx=0)
+    lstm = torch.nn.LSTM(input_size=d, hidden_size=d, num_layers=2, batch_first=False)
+    c = random_decode_case(21, 6, 40, V, d, 5, 4.0, lo=5)
+
+    def cpu_predict(prefix):
+        with torch.no_grad():
+            x = emb(torch.as_tensor(np.asarray(prefix), dtype=torch.int64)[None])
+            return lstm(x)[0][0, -1].numpy()
+
+    margins = []
+    want_hyps, want_durs = greedy.greedy_tdt(c["enc"], c["in_lens"], cpu_predict, c["W"], c["W_dur"], 4, 0, 1, 10,
+                                             margins)
+    assert min(margins) > MARGIN
+    emb_g, lstm_g = emb.cuda(), lstm.cuda()
+
+    def gpu_predict(tokens):
+        return lstm_g(emb_g(tokens))[0]
+
+    hyps, durs = tdt.greedy_decode(cuda(c["enc"]), cuda(c["in_lens"]), gpu_predict, cuda(c["W"]), cuda(c["W_dur"]), 4)
+    assert hyps == want_hyps
+    assert durs == want_durs
+
+
+def test_bf16_encoder_output_is_decoded_in_float32():
+    c = DECODE["tdt_bpe_like"]
+    blank, sos, max_sym, max_duration = params(c)
+    enc16 = cuda(c["enc"]).bfloat16()
+    pred = table_predictor(c["P"], c["Q"])
+    a = tdt.greedy_decode(enc16, cuda(c["in_lens"]), pred, cuda(c["W"]), cuda(c["W_dur"]), max_duration)
+    b = tdt.greedy_decode(enc16.float(), cuda(c["in_lens"]), pred, cuda(c["W"]), cuda(c["W_dur"]), max_duration)
+    assert a == b
+
+
+def test_empty_and_degenerate_batches():
+    c = DECODE["rnnt_small"]
+    pred = table_predictor(c["P"], c["Q"])
+    W = cuda(c["W"])
+    enc = cuda(c["enc"])
+    assert rnnt.greedy_decode(enc[:0], cuda(c["in_lens"][:0]), pred, W) == []
+    assert rnnt.greedy_decode(enc, torch.zeros(3, dtype=torch.int32, device="cuda"), pred, W) == [[], [], []]
+    assert rnnt.greedy_decode(enc, cuda(c["in_lens"]), pred, W, max_symbols_per_frame=0) == [[], [], []]
+    with pytest.raises(ValueError, match="in_lens"):
+        rnnt.greedy_decode(enc, cuda(np.array([13, 1, 1], np.int32)), pred, W)
+    with pytest.raises(ValueError, match="blank_id"):
+        rnnt.greedy_decode(enc, cuda(c["in_lens"]), pred, W, blank_id=W.shape[0])
