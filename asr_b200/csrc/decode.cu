@@ -8,47 +8,65 @@
 // once per decoding step, re-running the predictor after every emitted token.
 // Between two emissions the predictor output of an utterance is fixed, so every
 // step until the next emission depends only on the frames it visits. One launch
-// of greedy_scan_kernel therefore advances EVERY active utterance (one CTA
-// each) from its current state to its next emitted token or to its end:
-//   * the hidden rows tanh(enc[b, t..t+kWin) + pred) of a window of frames are
+// of greedy_scan_kernel therefore advances every utterance of the active list
+// from its current state to its next emitted token or to its end:
+//   * the hidden rows tanh(enc[b, t..t+NF) + pred) of a window of NF frames are
 //     built in shared memory (the joint row is never written to HBM);
 //   * the window's logits come from one pass over the transposed joint weight
-//     (L2-resident, read once per window and reused for all kWin frames from
-//     registers), each thread owning 8 vocab columns x kWin frames;
-//   * the first maximal index per frame (torch.argmax semantics; NaN counts as
-//     the maximum) is reduced across the CTA, the duration head likewise;
-//   * one thread then replays the reference's state machine over the window
-//     (blank advances a frame, TDT durations jump frames, max_symbols_per_frame
-//     forces progress), recording every TDT duration, until a token is emitted
-//     (the host must run the predictor) or the utterance ends. Frames past the
-//     stopping point were computed speculatively and are discarded.
+//     (L2-resident, read once per window and reused for all NF frames from
+//     registers), each thread owning CPT vocab columns x NF frames;
+//   * one utterance is served by a thread-block cluster of C CTAs, CTA r owning
+//     the r-th slice of the vocabulary: every CTA reduces its slice to the first
+//     maximal index per frame (torch.argmax semantics; NaN counts as the maximum)
+//     and stores the candidate into every CTA of the cluster (distributed shared
+//     memory, double-buffered by window parity so one cluster barrier per window
+//     suffices); every CTA then reduces the C candidates identically. C is
+//     chosen per launch from the number of active utterances: C = 1 while they
+//     fill the GPU (throughput), up to 4 when few remain (the per-window latency
+//     falls with the number of SMs that share the vocabulary);
+//   * every CTA replays the reference's state machine over the window (blank
+//     advances a frame, TDT durations jump frames, max_symbols_per_frame forces
+//     progress), recording every TDT duration, until a token is emitted (the
+//     host must run the predictor) or the utterance ends. Frames past the
+//     stopping point were computed speculatively and are discarded. Rank 0
+//     writes the outputs;
+//   * an utterance may scan at most max_windows windows per launch: a long run
+//     of blanks pauses and continues in the next launch with the same predictor
+//     output, so one utterance's long run does not hold every other utterance's
+//     next predictor step.
 // The host loop (asr_b200/decode) thus runs one launch per emitted-token level
 // instead of one joint call per step and utterance.
+#include <algorithm>
 #include <climits>
+#include <cstdlib>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace asr {
 namespace {
 
-constexpr int kWin = 8;                                   // frames per window
-constexpr int kScanThreads = 128;                         // 4 warps
+constexpr int kScanThreads = 256;  // 8 warps: two CTAs per SM, four warps per scheduler
 constexpr int kScanWarps = kScanThreads / 32;
-constexpr int kColTile = kScanThreads * 8;                // vocab columns per pass
-constexpr int kMaxScanDim = 4096;                         // joint dim limit (shared memory)
-constexpr int kMaxScanDur = 64;                           // duration head width limit
+constexpr int kMaxScanDim = 2048;  // joint dim limit (shared memory: hidden rows + weight ring)
+constexpr int kMaxScanDur = 64;    // duration head width limit
+constexpr int kMaxCluster = 4;
+constexpr int kMaxFrames = 8;
 
 struct ScanArgs {
-    const float* enc;     // (B, T, D)
-    const float* pred;    // (B, D)
-    const float* wt;      // (D, ldw): transposed joint weight, columns >= V ignored
-    const float* wdur;    // (n_dur, D) or null
+    const float* enc;      // (B, T, D)
+    const float* pred;     // (B, D)
+    const float* wt;       // (D, ldw): transposed joint weight, columns >= V ignored
+    const float* wdur;     // (n_dur, D) or null
     const int32_t* in_lens;
-    int32_t* state;       // (B, 4): t, k (symbols at frame t), hyp_len, n_steps
-    int64_t* prefix;      // (B, hyp_cap + 1): <sos> then the emitted tokens
-    int32_t* durs;        // (B, dur_cap) or null
-    int32_t* report;      // (B,): prefix length after an emission, 0 finished, -1 error
+    const int32_t* active;  // (n_active,) utterance indices, or null for 0..B-1
+    int32_t* state;        // (B, 4): t, k (symbols at frame t), hyp_len, n_steps
+    int64_t* prefix;       // (B, hyp_cap + 1): <sos> then the emitted tokens
+    int32_t* durs;         // (B, dur_cap) or null
+    int32_t* report;       // (B,): prefix length after an emission, 0 finished, -1 error
     int B, T, D, V, ldw, n_dur, blank, max_symbols, hyp_cap, dur_cap;
+    int max_windows;  // windows one utterance may scan in this launch (0: no limit)
+    int stages;       // weight ring stages (kStageBytes each)
 };
 
 // a beats b under torch.argmax: NaN is the maximum, ties go to the lower index.
@@ -70,24 +88,107 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
     }
 }
 
-__device__ __forceinline__ void fma4(float (&acc)[8], const float4 w, const float h, const int base) {
-    acc[base + 0] = fmaf(w.x, h, acc[base + 0]);
-    acc[base + 1] = fmaf(w.y, h, acc[base + 1]);
-    acc[base + 2] = fmaf(w.z, h, acc[base + 2]);
-    acc[base + 3] = fmaf(w.w, h, acc[base + 3]);
+
+__device__ __forceinline__ void st_cluster_pair(uint32_t addr, float v, int i) {
+    asm volatile("st.shared::cluster.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(__float_as_uint(v)), "r"(i)
+                 : "memory");
 }
 
-__global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
+// ------------------------------------------------ joint weight stream
+//
+// The window's pass over the transposed joint weight is a per-thread cp.async
+// pipeline: every thread copies its own CPT columns of the next rows into a
+// private part of a shared-memory ring of `stages` 16 KB stages and later reads
+// back only what it copied, so no CTA barrier is needed. Each weight row feeds
+// only NF frames, so the stream runs at the L2 rate only with deep lookahead:
+// the ring takes the shared memory the hidden rows leave (up to kMaxRingStages,
+// one CTA per SM), keeping (stages - 1) stages of reads in flight.
+constexpr int kMaxRingStages = 6;
+constexpr int kMinRingStages = 2;
+constexpr int kStageBytes = 16 * 1024;
+constexpr size_t kScanSmemBudget = 110 * 1024;  // two CTAs per SM
+
+template <int CPT>
+struct Ring {
+    static constexpr int kVec = CPT;                       // floats per copy (one per row and thread)
+    static constexpr int kRows = kStageBytes / (4 * CPT * kScanThreads);  // weight rows per stage
+    static constexpr int kStageFloats = kRows * CPT * kScanThreads;
+};
+
+template <int N>
+__device__ __forceinline__ void cp_async(float* dst, const float* src, bool ok) {
+    const uint32_t d = tc::smem_u32(dst);
+    const int n = ok ? 4 * N : 0;  // 0: zero-fill, nothing read
+    if constexpr (N == 4)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+    else if constexpr (N == 2)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// cp.async.wait_group takes an immediate: dispatch the (uniform) runtime count.
+__device__ __forceinline__ void cp_async_wait_n(int n) {
+    switch (n) {
+        case 0: cp_async_wait<0>(); break;
+        case 1: cp_async_wait<1>(); break;
+        case 2: cp_async_wait<2>(); break;
+        case 3: cp_async_wait<3>(); break;
+        case 4: cp_async_wait<4>(); break;
+        case 5: cp_async_wait<5>(); break;
+        case 6: cp_async_wait<6>(); break;
+        case 7: cp_async_wait<7>(); break;
+        case 8: cp_async_wait<8>(); break;
+        default: cp_async_wait<9>(); break;
+    }
+}
+
+// Issues this thread's copies of weight rows [chunk * kRows, +kRows) into ring slot chunk % stages.
+template <int CPT>
+__device__ __forceinline__ void issue_chunk(float* ring, int stages, int chunk, int D, const float* wt, int ldw,
+                                            int col, int tid) {
+    using R = Ring<CPT>;
+    float* base = ring + (size_t)(chunk % stages) * R::kStageFloats;
+    const int j0 = chunk * R::kRows;
+#pragma unroll
+    for (int r = 0; r < R::kRows; ++r) {
+        const int j = j0 + r;
+        if (j < D) {
+            const bool ok = col < ldw;
+            cp_async<R::kVec>(base + ((size_t)r * kScanThreads + tid) * R::kVec, wt + (size_t)j * ldw + (ok ? col : 0),
+                              ok);
+        }
+    }
+    cp_async_commit();
+}
+
+template <int C, int NF>
+__global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a) {
+    constexpr int CPT = 4 / C;                        // consecutive vocab columns per thread and pass
+    constexpr int kPass = CPT * kScanThreads;
+    using R = Ring<CPT>;
     extern __shared__ __align__(16) float smem[];
-    float* hs = smem;                       // (D, kWin): hidden rows, frame-minor
-    float* ps = smem + (size_t)a.D * kWin;  // (D,): predictor output
-    __shared__ float red_v[kWin][kScanWarps];
-    __shared__ int red_i[kWin][kScanWarps];
-    __shared__ float dur_v[kWin][kMaxScanDur];
-    __shared__ int best_tok[kWin], best_dur[kWin];
+    float* ring = smem;                                // per-thread weight stream stages
+    float* hs = smem + (size_t)a.stages * R::kStageFloats;  // (D, NF): hidden rows, frame-minor
+    float* ps = hs + (size_t)a.D * NF;                 // (D,): predictor output
+    __shared__ float red_v[kMaxFrames][kScanWarps];
+    __shared__ int red_i[kMaxFrames][kScanWarps];
+    __shared__ __align__(8) int2 cand[2][kMaxCluster][kMaxFrames];  // (value bits, index) per rank
+    __shared__ float dur_v[kMaxFrames][kMaxScanDur];
+    __shared__ int best_tok[kMaxFrames], best_dur[kMaxFrames];
     __shared__ int s_t, s_k, s_len, s_steps, s_go;
 
-    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rank = C > 1 ? (int)tc::cluster_ctarank() : 0;
+    const int slot = blockIdx.x / C;
+    const int b = a.active ? a.active[slot] : slot;
     const int Tb = min(max(a.in_lens[b], 0), a.T);
     int32_t* st = a.state + 4 * b;
     if (tid == 0) {
@@ -100,8 +201,8 @@ __global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
     const float* pr = a.pred + (size_t)b * a.D;
     for (int j = tid; j < a.D; j += kScanThreads) ps[j] = pr[j];
     __syncthreads();
-    if (s_t >= Tb) {
-        if (tid == 0) {
+    if (s_t >= Tb) {  // uniform over the cluster: every CTA read the same state
+        if (tid == 0 && rank == 0) {
             st[0] = s_t;
             a.report[b] = 0;
         }
@@ -109,94 +210,130 @@ __global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
     }
     const float* encb = a.enc + (size_t)b * a.T * a.D;
     const bool tdt = a.n_dur > 0;
+    // This CTA's vocabulary slice [lo, hi).
+    const int slice = ((a.V + C - 1) / C + 3) / 4 * 4;
+    const int lo = rank * slice, hi = min(a.V, lo + slice);
+    int parity = 0, windows = 0;
 
     for (;;) {
         const int t0 = s_t;
-        const int nf = min(kWin, Tb - t0);
-        // Hidden rows of the window, frame-minor so one 32-byte read serves all frames.
+        const int nf = min(NF, Tb - t0);
+        // Hidden rows of the window, frame-minor so one vector read serves all frames.
         for (int j = tid; j < a.D; j += kScanThreads) {
             const float p = ps[j];
-            float hv[kWin];
+            float hv[NF];
 #pragma unroll
-            for (int f = 0; f < kWin; ++f) hv[f] = f < nf ? tanhf(encb[(size_t)(t0 + f) * a.D + j] + p) : 0.f;
-            float4* dst = reinterpret_cast<float4*>(hs + (size_t)j * kWin);
-            dst[0] = make_float4(hv[0], hv[1], hv[2], hv[3]);
-            dst[1] = make_float4(hv[4], hv[5], hv[6], hv[7]);
+            for (int f = 0; f < NF; ++f) hv[f] = f < nf ? tanhf(encb[(size_t)(t0 + f) * a.D + j] + p) : 0.f;
+            float4* dst = reinterpret_cast<float4*>(hs + (size_t)j * NF);
+#pragma unroll
+            for (int q = 0; q < NF / 4; ++q) dst[q] = make_float4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
         }
         __syncthreads();
 
-        float bv[kWin];
-        int bi[kWin];
+        float bv[NF];
+        int bi[NF];
 #pragma unroll
-        for (int f = 0; f < kWin; ++f) {
+        for (int f = 0; f < NF; ++f) {
             bv[f] = -INFINITY;
             bi[f] = INT_MAX;
         }
-        for (int c0 = 0; c0 < a.V; c0 += kColTile) {
-            const int ca = c0 + 4 * tid, cb = ca + 4 * kScanThreads;
-            const bool va = ca < a.ldw, vb = cb < a.ldw;
-            float acc[kWin][8];
+        for (int c0 = lo; c0 < hi; c0 += kPass) {
+            const int col = c0 + CPT * tid;
+            float acc[NF][CPT];
 #pragma unroll
-            for (int f = 0; f < kWin; ++f)
+            for (int f = 0; f < NF; ++f)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[f][c] = 0.f;
-            const float* wa = a.wt + ca;
-            const float* wb = a.wt + cb;
-#pragma unroll 4
-            for (int j = 0; j < a.D; ++j) {
-                const size_t row = (size_t)j * a.ldw;
-                const float4 w0 = va ? __ldg(reinterpret_cast<const float4*>(wa + row)) : make_float4(0, 0, 0, 0);
-                const float4 w1 = vb ? __ldg(reinterpret_cast<const float4*>(wb + row)) : make_float4(0, 0, 0, 0);
-                const float4 h0 = *reinterpret_cast<const float4*>(hs + (size_t)j * kWin);
-                const float4 h1 = *reinterpret_cast<const float4*>(hs + (size_t)j * kWin + 4);
-                const float hf[kWin] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-#pragma unroll
-                for (int f = 0; f < kWin; ++f) {
-                    fma4(acc[f], w0, hf[f], 0);
-                    fma4(acc[f], w1, hf[f], 4);
+                for (int c = 0; c < CPT; ++c) acc[f][c] = 0.f;
+            // Lanes that stream weights (a partial last pass leaves some idle).
+            const unsigned live = __ballot_sync(0xffffffffu, col < hi);
+            if (col < hi) {
+                const int nch = (a.D + R::kRows - 1) / R::kRows;
+                for (int c = 0; c < a.stages - 1; ++c) {
+                    if (c < nch)
+                        issue_chunk<CPT>(ring, a.stages, c, a.D, a.wt, a.ldw, col, tid);
+                    else
+                        cp_async_commit();
                 }
+                for (int ch = 0; ch < nch; ++ch) {
+                    const int nx = ch + a.stages - 1;
+                    // The slot refilled now was read in the previous iteration: order those
+                    // shared-memory reads before the asynchronous writes.
+                    __syncwarp(live);
+                    if (nx < nch)
+                        issue_chunk<CPT>(ring, a.stages, nx, a.D, a.wt, a.ldw, col, tid);
+                    else
+                        cp_async_commit();
+                    cp_async_wait_n(a.stages - 1);  // this thread's copies of chunk ch have landed
+                    const float* base = ring + (size_t)(ch % a.stages) * R::kStageFloats;
+#pragma unroll
+                    for (int r = 0; r < R::kRows; ++r) {
+                        const int j = ch * R::kRows + r;
+                        if (j < a.D) {
+                            float w[CPT];
+                            const float* src = base + ((size_t)r * kScanThreads + tid) * CPT;
+                            if constexpr (CPT == 4) {
+                                const float4 v = *reinterpret_cast<const float4*>(src);
+                                w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+                            } else if constexpr (CPT == 2) {
+                                const float2 v = *reinterpret_cast<const float2*>(src);
+                                w[0] = v.x, w[1] = v.y;
+                            } else {
+                                w[0] = *src;
+                            }
+                            float hf[NF];
+#pragma unroll
+                            for (int q = 0; q < NF / 4; ++q) {
+                                const float4 h = *reinterpret_cast<const float4*>(hs + (size_t)j * NF + 4 * q);
+                                hf[4 * q] = h.x, hf[4 * q + 1] = h.y, hf[4 * q + 2] = h.z, hf[4 * q + 3] = h.w;
+                            }
+#pragma unroll
+                            for (int f = 0; f < NF; ++f)
+#pragma unroll
+                                for (int c = 0; c < CPT; ++c) acc[f][c] = fmaf(w[c], hf[f], acc[f][c]);
+                        }
+                    }
+                }
+                cp_async_wait<0>();
             }
 #pragma unroll
-            for (int f = 0; f < kWin; ++f)
+            for (int f = 0; f < NF; ++f)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const int col = (c < 4 ? ca : cb) + (c & 3);
-                    if (col < a.V && beats(acc[f][c], col, bv[f], bi[f])) {
+                for (int c = 0; c < CPT; ++c) {
+                    const int cc = col + c;
+                    if (cc < hi && beats(acc[f][c], cc, bv[f], bi[f])) {
                         bv[f] = acc[f][c];
-                        bi[f] = col;
+                        bi[f] = cc;
                     }
                 }
         }
 #pragma unroll
-        for (int f = 0; f < kWin; ++f) {
+        for (int f = 0; f < NF; ++f) {
             warp_argmax(bv[f], bi[f]);
             if (lane == 0) {
                 red_v[f][warp] = bv[f];
                 red_i[f][warp] = bi[f];
             }
         }
-        // Duration head: warp w owns columns w, w + 4, ...; lanes split the joint dim.
+        // Duration head (every CTA, a few columns): warp w owns columns w, w + 4, ...
         if (tdt) {
             for (int c = warp; c < a.n_dur; c += kScanWarps) {
                 const float* wd = a.wdur + (size_t)c * a.D;
-                float s[kWin];
+                float s[NF];
 #pragma unroll
-                for (int f = 0; f < kWin; ++f) s[f] = 0.f;
+                for (int f = 0; f < NF; ++f) s[f] = 0.f;
                 for (int j = lane; j < a.D; j += 32) {
                     const float w = __ldg(wd + j);
-                    const float4 h0 = *reinterpret_cast<const float4*>(hs + (size_t)j * kWin);
-                    const float4 h1 = *reinterpret_cast<const float4*>(hs + (size_t)j * kWin + 4);
-                    s[0] = fmaf(w, h0.x, s[0]);
-                    s[1] = fmaf(w, h0.y, s[1]);
-                    s[2] = fmaf(w, h0.z, s[2]);
-                    s[3] = fmaf(w, h0.w, s[3]);
-                    s[4] = fmaf(w, h1.x, s[4]);
-                    s[5] = fmaf(w, h1.y, s[5]);
-                    s[6] = fmaf(w, h1.z, s[6]);
-                    s[7] = fmaf(w, h1.w, s[7]);
+#pragma unroll
+                    for (int q = 0; q < NF / 4; ++q) {
+                        const float4 h = *reinterpret_cast<const float4*>(hs + (size_t)j * NF + 4 * q);
+                        s[4 * q] = fmaf(w, h.x, s[4 * q]);
+                        s[4 * q + 1] = fmaf(w, h.y, s[4 * q + 1]);
+                        s[4 * q + 2] = fmaf(w, h.z, s[4 * q + 2]);
+                        s[4 * q + 3] = fmaf(w, h.w, s[4 * q + 3]);
+                    }
                 }
 #pragma unroll
-                for (int f = 0; f < kWin; ++f) {
+                for (int f = 0; f < NF; ++f) {
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) s[f] += __shfl_xor_sync(0xffffffffu, s[f], o);
                     if (lane == 0) dur_v[f][c] = s[f];
@@ -204,7 +341,7 @@ __global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
             }
         }
         __syncthreads();
-        if (tid < kWin) {
+        if (tid < NF) {
             float v = red_v[tid][0];
             int i = red_i[tid][0];
             for (int w = 1; w < kScanWarps; ++w)
@@ -212,7 +349,13 @@ __global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
                     v = red_v[tid][w];
                     i = red_i[tid][w];
                 }
-            best_tok[tid] = i;
+            if constexpr (C > 1) {
+                const uint32_t local = tc::smem_u32(&cand[parity][rank][tid]);
+#pragma unroll
+                for (int r = 0; r < C; ++r) st_cluster_pair(tc::mapa_shared(local, r), v, i);
+            } else {
+                best_tok[tid] = i;
+            }
             if (tdt) {
                 float dv = dur_v[tid][0];
                 int di = 0;
@@ -224,10 +367,30 @@ __global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
                 best_dur[tid] = di;  // durations are range(max_duration + 1): index == value
             }
         }
+        if constexpr (C > 1) {
+            tc::cluster_sync();  // candidates of every rank have landed in every CTA
+            if (tid < NF) {
+                float v = __int_as_float(cand[parity][0][tid].x);
+                int i = cand[parity][0][tid].y;
+#pragma unroll
+                for (int r = 1; r < C; ++r) {
+                    const float rv = __int_as_float(cand[parity][r][tid].x);
+                    const int ri = cand[parity][r][tid].y;
+                    if (beats(rv, ri, v, i)) {
+                        v = rv;
+                        i = ri;
+                    }
+                }
+                best_tok[tid] = i;
+            }
+            parity ^= 1;
+        }
         __syncthreads();
 
-        // The reference state machine over the window (one thread; a few steps).
+        // The reference state machine over the window (one thread per CTA; identical
+        // in every CTA of the cluster, rank 0 writes the outputs).
         if (tid == 0) {
+            const bool out = rank == 0;
             int t = t0, k = s_k, len = s_len, steps = s_steps;
             int emitted = 0, err = 0;
             int64_t* pre = a.prefix + (size_t)b * (a.hyp_cap + 1);
@@ -243,7 +406,8 @@ __global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
                         err = 1;
                         break;
                     }
-                    pre[1 + len++] = tok;
+                    if (out) pre[1 + len] = tok;
+                    ++len;
                     emitted = 1;
                     if (++k >= a.max_symbols) {  // rnnt.py:29 loop exhausted: next frame
                         ++t;
@@ -256,13 +420,15 @@ __global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
                     err = 1;
                     break;
                 }
-                a.durs[(size_t)b * a.dur_cap + steps++] = dv;  // tdt.py:45
-                if (tok != a.blank) {                          // tdt.py:46-49
+                if (out) a.durs[(size_t)b * a.dur_cap + steps] = dv;  // tdt.py:45
+                ++steps;
+                if (tok != a.blank) {  // tdt.py:46-49
                     if (len >= a.hyp_cap) {
                         err = 1;
                         break;
                     }
-                    pre[1 + len++] = tok;
+                    if (out) pre[1 + len] = tok;
+                    ++len;
                     emitted = 1;
                 }
                 if (dv > 0) {  // tdt.py:50-52
@@ -281,18 +447,21 @@ __global__ void __launch_bounds__(kScanThreads) greedy_scan_kernel(ScanArgs a) {
             s_k = k;
             s_len = len;
             s_steps = steps;
-            const int done = err || emitted || t >= Tb;
-            s_go = !done;
-            if (done) {
+            const bool finished = err || emitted || t >= Tb;
+            // A long run of blanks is continued by the next launch: the launch's
+            // duration is set by its longest chain of windows.
+            const bool paused = !finished && a.max_windows > 0 && ++windows >= a.max_windows;
+            s_go = !(finished || paused);
+            if ((finished || paused) && out) {
                 st[0] = t;
                 st[1] = k;
                 st[2] = len;
                 st[3] = steps;
-                a.report[b] = err ? -1 : (emitted ? len + 1 : 0);
+                a.report[b] = err ? -1 : (emitted ? len + 1 : (paused ? -2 : 0));
             }
         }
         __syncthreads();
-        if (!s_go) return;
+        if (!s_go) return;  // every CTA of the cluster stops after the same window
     }
 }
 
@@ -310,11 +479,52 @@ __global__ void pack_weights_kernel(const float* __restrict__ W, int V, int D, f
     }
 }
 
+// Zeroes the state and fills every prefix position with <sos>: position 0 is the
+// reference's start token, and positions past a hypothesis then hold a valid token
+// id for predictors that are run on right-padded prefixes.
 __global__ void greedy_init_kernel(int32_t* state, int64_t* prefix, int B, int hyp_cap, int sos) {
-    const int b = blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= B) return;
-    for (int i = 0; i < 4; ++i) state[4 * b + i] = 0;
-    prefix[(size_t)b * (hyp_cap + 1)] = sos;
+    const size_t n = (size_t)B * (hyp_cap + 1), ns = 4 * (size_t)B;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n || i < ns; i += (size_t)gridDim.x * blockDim.x) {
+        if (i < n) prefix[i] = sos;
+        if (i < ns) state[i] = 0;
+    }
+}
+
+using ScanKernel = void (*)(ScanArgs);
+
+template <int C, int NF>
+int launch_scan(const ScanArgs& a, int n_slots, size_t smem, cudaStream_t stream) {
+    ScanKernel k = greedy_scan_kernel<C, NF>;
+    if (smem > 48 * 1024)
+        ASR_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_slots * C);
+    cfg.blockDim = dim3(kScanThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = C > 1 ? 1 : 0;
+    ASR_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, a));
+    return ASR_OK;
+}
+
+template <int NF>
+int launch_scan_c(int C, const ScanArgs& a, int n_slots, size_t smem, cudaStream_t stream) {
+    switch (C) {
+        case 1: return launch_scan<1, NF>(a, n_slots, smem, stream);
+        case 2: return launch_scan<2, NF>(a, n_slots, smem, stream);
+        default: return launch_scan<4, NF>(a, n_slots, smem, stream);
+    }
+}
+
+int env_choice(const char* name, int fallback) {
+    const char* e = std::getenv(name);
+    return e ? std::atoi(e) : fallback;
 }
 
 }  // namespace
@@ -339,29 +549,50 @@ extern "C" int asr_greedy_init(int32_t* state, int64_t* prefix, int B, int hyp_c
     if (B == 0) return ASR_OK;
     if (!state || !prefix) return ASR_ERR_INVALID_ARGUMENT;
     KernelTimer kt("greedy_init", stream);
-    greedy_init_kernel<<<(B + 127) / 128, 128, 0, stream>>>(state, prefix, B, hyp_cap, sos_id);
+    const size_t n = std::max((size_t)B * (hyp_cap + 1), 4 * (size_t)B);
+    const int grid = (int)std::min<size_t>((n + 255) / 256, (size_t)sm_count() * 8);
+    greedy_init_kernel<<<grid, 256, 0, stream>>>(state, prefix, B, hyp_cap, sos_id);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
 
+
 extern "C" int asr_greedy_scan(const float* encoder, const float* pred, const float* joint_Wt, int ldw,
-                               const float* joint_W_dur, const int32_t* in_lens, int32_t* state, int64_t* prefix,
-                               int32_t* durs, int32_t* report, int B, int T, int d, int V, int n_dur,
-                               int blank_idx, int max_symbols, int hyp_cap, int dur_cap, asr_stream_t stream) {
+                               const float* joint_W_dur, const int32_t* in_lens, const int32_t* active,
+                               int n_active, int32_t* state, int64_t* prefix, int32_t* durs, int32_t* report, int B,
+                               int T, int d, int V, int n_dur, int blank_idx, int max_symbols, int hyp_cap,
+                               int dur_cap, int max_windows, asr_stream_t stream) {
     if (B < 0 || T < 1 || d < 1 || V < 1 || n_dur < 0 || hyp_cap < 0 || dur_cap < 0) return ASR_ERR_INVALID_ARGUMENT;
-    if (ldw < V || ldw % 4 != 0 || blank_idx < 0 || blank_idx >= V) return ASR_ERR_INVALID_ARGUMENT;
-    if (B == 0) return ASR_OK;
+    if (ldw < V || ldw % 4 != 0 || blank_idx < 0 || blank_idx >= V || max_windows < 0) return ASR_ERR_INVALID_ARGUMENT;
+    const int n_slots = active ? n_active : B;
+    if (n_slots < 0 || n_slots > B) return ASR_ERR_INVALID_ARGUMENT;
+    if (n_slots == 0) return ASR_OK;
     if (!encoder || !pred || !joint_Wt || !in_lens || !state || !prefix || !report) return ASR_ERR_INVALID_ARGUMENT;
     if (n_dur > 0 && (!joint_W_dur || !durs)) return ASR_ERR_INVALID_ARGUMENT;
     if (reinterpret_cast<uintptr_t>(joint_Wt) % 16 != 0) return ASR_ERR_INVALID_ARGUMENT;
     if (d > kMaxScanDim || n_dur > kMaxScanDur) return ASR_ERR_UNSUPPORTED;
-    ScanArgs a{encoder, pred, joint_Wt, joint_W_dur, in_lens, state, prefix, durs, report,
-               B, T, d, V, ldw, n_dur, blank_idx, max_symbols, hyp_cap, dur_cap};
-    const size_t smem = sizeof(float) * (size_t)d * (kWin + 1);
-    if (smem > 48 * 1024)
-        ASR_CUDA_TRY(cudaFuncSetAttribute(greedy_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    ScanArgs a{encoder, pred, joint_Wt, joint_W_dur, in_lens, active, state, prefix, durs, report,
+               B, T, d, V, ldw, n_dur, blank_idx, max_symbols, hyp_cap, dur_cap, max_windows, 0};
+    // Cluster width: one CTA per utterance while the active utterances fill the
+    // GPU; otherwise split the vocabulary over up to kMaxCluster SMs per utterance.
+    static const int env_c = env_choice("ASR_B200_DECODE_CLUSTER", 0);
+    static const int env_f = env_choice("ASR_B200_DECODE_FRAMES", 0);
+    int C = 1;
+    if (env_c == 1 || env_c == 2 || env_c == 4) {
+        C = env_c;
+    } else if (V >= 512) {
+        const int sms = sm_count();
+        while (C < kMaxCluster && n_slots * C * 2 <= sms) C *= 2;
+    }
+    const int NF = env_f == 4 ? 4 : 8;
+    // Shared memory: hidden rows + predictor row, the rest of the budget for the ring.
+    const size_t rows = sizeof(float) * (size_t)d * (NF + 1);
+    const int stages = rows + kMinRingStages * kStageBytes > kScanSmemBudget
+                           ? kMinRingStages
+                           : (int)std::min<size_t>(kMaxRingStages, (kScanSmemBudget - rows) / kStageBytes);
+    if (stages < kMinRingStages) return ASR_ERR_UNSUPPORTED;
+    a.stages = stages;
+    const size_t smem = rows + (size_t)stages * kStageBytes;
     KernelTimer kt("greedy_scan", stream);
-    greedy_scan_kernel<<<B, kScanThreads, smem, stream>>>(a);
-    ASR_LAUNCH_CHECK();
-    return ASR_OK;
+    return NF == 4 ? launch_scan_c<4>(C, a, n_slots, smem, stream) : launch_scan_c<8>(C, a, n_slots, smem, stream);
 }

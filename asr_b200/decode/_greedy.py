@@ -10,12 +10,19 @@ is the longest hypothesis plus one.
 
 The predictor is called exactly as the reference calls it: on the (1, L) int64
 prefix ``[<sos>, tokens...]`` of one utterance, taking the output at the last
-position. ``batch_predict=True`` instead makes one call per launch on the
-right-padded (n, L_max) prefixes of all utterances that emitted and reads row i
-at position L_i - 1; that is only equivalent for predictors whose rows are
-independent and causal along the sequence (a batch_first LSTM, a causal
-transformer). The reference's own LSTM predictor (model/lstm.py:8-15) is built
-with batch_first=False and so mixes rows; keep the default for it.
+position (``batch_predict=False``). Two batched forms make one call per launch
+for all utterances that emitted:
+  * ``batch_predict=True``: ``predict`` on the right-padded (n, L_max) prefixes,
+    row i read at position L_i - 1. Equivalent only for predictors whose rows
+    are independent and causal along the sequence (a batch_first LSTM, a causal
+    transformer). The reference's own LSTM predictor (model/lstm.py:8-15) is
+    built with batch_first=False and mixes rows under this form.
+  * ``batch_predict=f``, a callable ``f(tokens, lengths) -> (n, d)`` given the
+    right-padded (n, L_max) int64 prefixes and their (n,) int64 lengths, whose
+    row i must equal ``predict(tokens[i:i+1, :lengths[i]])[0, -1]``. For the
+    reference's LSTM predictor that output depends only on the last token (its
+    (1, L) input is read as L independent one-step sequences), so
+    ``last_token_predictor(predict)`` is an exact batched form of it.
 """
 
 from __future__ import annotations
@@ -31,6 +38,11 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _bound = False
 
+# Windows of 8 frames one utterance scans per launch before it pauses (see
+# asr_greedy_scan): bounds each launch by a short chain instead of the longest
+# run of blanks in the batch.
+MAX_WINDOWS = 1
+
 
 def _capi() -> ctypes.CDLL:
     global _bound
@@ -38,7 +50,7 @@ def _capi() -> ctypes.CDLL:
     if not _bound:
         lib.asr_greedy_pack_weights.argtypes = [_P, _I, _I, _P, _I, _P]
         lib.asr_greedy_init.argtypes = [_P, _P, _I, _I, _I, _P]
-        lib.asr_greedy_scan.argtypes = [_P] * 3 + [_I] + [_P] * 6 + [_I] * 9 + [_P]
+        lib.asr_greedy_scan.argtypes = [_P] * 3 + [_I] + [_P] * 3 + [_I] + [_P] * 4 + [_I] * 10 + [_P]
         lib.asr_status_string.restype = ctypes.c_char_p
         _bound = True
     return lib
@@ -47,6 +59,19 @@ def _capi() -> ctypes.CDLL:
 def _check(lib, rc: int, what: str) -> None:
     if rc != 0:
         raise RuntimeError(f"{what} failed: {lib.asr_status_string(rc).decode()} (status {rc})")
+
+
+def last_token_predictor(predict):
+    """Batched form of a predictor whose output at the last prefix position depends
+    only on the last token, as the reference's LSTM(batch_first=False) predictor
+    behaves on a (1, L) prefix: the last tokens of all n prefixes are passed as one
+    (1, n) call, i.e. n independent one-step sequences."""
+
+    def f(tokens, lengths):
+        last = tokens.gather(1, (lengths - 1).unsqueeze(1))  # (n, 1)
+        return predict(last.reshape(1, -1))[0]
+
+    return f
 
 
 def joint_weight(joint, name: str) -> torch.Tensor:
@@ -111,34 +136,56 @@ def decode(encoder_out, in_lens, predict, W, W_dur, max_duration, blank_id, sos_
         durs = torch.empty(B, cap, device=dev, dtype=torch.int32) if tdt else None
         report = torch.empty(B, device=dev, dtype=torch.int32)
         report_h = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        # One upload per scan: [active list | utterances that emitted | their prefix lengths].
+        active_h = torch.empty(3 * B, dtype=torch.int32, pin_memory=True)
+        active_d = torch.empty(3 * B, dtype=torch.int32, device=dev)
         _check(lib, lib.asr_greedy_init(state.data_ptr(), prefix.data_ptr(), B, cap, sos_id, sp), "asr_greedy_init")
 
         # Every utterance starts from the same prefix [<sos>]: one predictor call.
         start = predict(torch.tensor([[sos_id]], device=dev))[0, -1]
         pred = start.float().reshape(1, D).expand(B, D).contiguous()
-        scan_args = (enc.data_ptr(), pred.data_ptr(), Wt.data_ptr(), ldw, Wd.data_ptr() if tdt else None,
-                     lens.data_ptr(), state.data_ptr(), prefix.data_ptr(), durs.data_ptr() if tdt else None,
-                     report.data_ptr(), B, T, D, V, n_dur, blank_id, int(max_symbols_per_frame), cap, cap, sp)
-        for _ in range(cap + 2):
-            _check(lib, lib.asr_greedy_scan(*scan_args), "asr_greedy_scan")
+        active = np.arange(B, dtype=np.int32)
+        active_h[:B].copy_(torch.from_numpy(active))
+        active_d[:B].copy_(active_h[:B], non_blocking=True)
+        for _ in range(cap * B + 2):
+            n = active.size
+            _check(lib, lib.asr_greedy_scan(
+                enc.data_ptr(), pred.data_ptr(), Wt.data_ptr(), ldw, Wd.data_ptr() if tdt else None, lens.data_ptr(),
+                active_d.data_ptr(), n, state.data_ptr(), prefix.data_ptr(), durs.data_ptr() if tdt else None,
+                report.data_ptr(), B, T, D, V, n_dur, blank_id, int(max_symbols_per_frame), cap, cap, MAX_WINDOWS, sp),
+                "asr_greedy_scan")
             report_h.copy_(report, non_blocking=True)
             stream.synchronize()
-            r = report_h.numpy()
-            if (r < 0).any():
+            r = report_h.numpy()[active]
+            if (r == -1).any():
                 raise RuntimeError("asr_greedy_scan: hypothesis buffer overflow")
-            emit = np.flatnonzero(r > 0)
-            if emit.size == 0:
+            keep = (r > 0) | (r == -2)
+            emitted = r[keep] > 0
+            active, r = active[keep], r[keep]
+            if active.size == 0:
                 break
-            if batch_predict:
-                Ls = r[emit].astype(np.int64)
-                idx = torch.from_numpy(emit.astype(np.int64)).to(dev)
+            # Utterances that emitted or paused form the next scan's active list;
+            # the predictor runs for those that emitted.
+            n, Ls = active.size, r[emitted]
+            upd = active[emitted]
+            m = upd.size
+            hb = active_h.numpy()
+            hb[:n], hb[n: n + m], hb[n + m: n + 2 * m] = active, upd, Ls
+            active_d[: n + 2 * m].copy_(active_h[: n + 2 * m], non_blocking=True)
+            if m == 0:
+                continue
+            if batch_predict is not False:
+                idx = active_d[n: n + m].long()
+                lens_t = active_d[n + m: n + 2 * m].long()
                 rows = prefix[:, : int(Ls.max())].index_select(0, idx)
-                out = predict(rows)
-                last = torch.from_numpy(Ls - 1).to(dev)
-                pred.index_copy_(0, idx, out[torch.arange(emit.size, device=dev), last].float())
+                if callable(batch_predict):
+                    new = batch_predict(rows, lens_t)
+                else:
+                    new = predict(rows)[torch.arange(upd.size, device=dev), lens_t - 1]
+                pred.index_copy_(0, idx, new.float())
             else:
-                for b in emit.tolist():
-                    out = predict(prefix[b: b + 1, : int(r[b])])
+                for b, L in zip(upd.tolist(), Ls.tolist()):
+                    out = predict(prefix[b: b + 1, :L])
                     pred[b].copy_(out[0, -1])
         else:
             raise RuntimeError("asr_greedy_scan: decoding did not terminate")

@@ -9,7 +9,7 @@ from asr_b200.decode._greedy import decode, joint_weight
 
 @torch.no_grad()
 def greedy_decode(encoder_out, in_lens, predict, joint, blank_id: int = 0, sos_id: int = 1,
-                  max_symbols_per_frame: int = 10, *, batch_predict: bool = False) -> list[list[int]]:
+                  max_symbols_per_frame: int = 10, *, batch_predict=False) -> list[list[int]]:
     """Greedy RNN-T decode of a batch; same results as the reference decoder.
 
     encoder_out (B, T, d) on the GPU (decoded in float32, as the systems pass

@@ -10,7 +10,7 @@ from asr_b200.decode._greedy import decode, joint_weight
 @torch.no_grad()
 def greedy_decode(encoder_out, in_lens, predict, joint, joint_dur, max_duration: int, blank_id: int = 0,
                   sos_id: int = 1, max_symbols_per_frame: int = 10, *,
-                  batch_predict: bool = False) -> tuple[list[list[int]], list[list[int]]]:
+                  batch_predict=False) -> tuple[list[list[int]], list[list[int]]]:
     """Greedy TDT decode of a batch; same results as the reference decoder.
 
     Arguments as ``asr_b200.decode.rnnt.greedy_decode``, plus ``joint_dur``

@@ -442,18 +442,22 @@ def run_config(args):
 # config-5 shapes (B=512, T ~ U[200, 500], d=640, V=1024, durations 0..4),
 # decode-rnnt on the config-4 shapes (B=128, T=400, d=1024, V=1024). The encoder
 # output is synthetic, N(0, 0.8^2) with a constant component the blank row of
-# the joint weight reads, so that blank wins most steps (about 0.25 tokens per
+# the joint weight reads, so that blank wins most steps (about 0.2 tokens per
 # frame, as a trained BPE model emits); the predictor is the reference system's
-# Embedding + 2-layer LSTM(batch_first=False), random-initialised, called once
-# per emitted token and utterance as the reference decoder calls it
-# (--decode-predict batched: a batch_first LSTM called once per scan on all
-# emitting utterances instead).
+# Embedding + 2-layer LSTM(batch_first=False), random-initialised. Predictor
+# calls (--decode-predict):
+#   last-token (default): one call per scan for all utterances that emitted,
+#     through asr_b200.decode.last_token_predictor, which gives this predictor's
+#     outputs exactly (its (1, L) prefix input is read as L one-step sequences);
+#   per-utterance: one call per emitted token and utterance on the whole prefix,
+#     as the reference decoder calls it;
+#   batched: a batch_first LSTM (another model) on the padded prefixes.
 
 DECODE = {
     "decode-tdt": {"name": "decode_tdt_bpe1024", "B": 512, "T": T_RANGE, "d": 640, "V": 1024, "n_dur": 5,
-                   "blank_bias": 6.0},
+                   "blank_bias": 7.5},
     "decode-rnnt": {"name": "decode_rnnt_bpe1024", "B": 128, "T": (400, 400), "d": 1024, "V": 1024, "n_dur": 0,
-                    "blank_bias": 8.0},
+                    "blank_bias": 9.5},
 }
 
 
@@ -519,6 +523,7 @@ def run_decode(args):
     import torch
 
     from asr_b200 import _lib
+    from asr_b200.decode import last_token_predictor
     from asr_b200.decode import rnnt as dec_rnnt
     from asr_b200.decode import tdt as dec_tdt
 
@@ -544,6 +549,8 @@ def run_decode(args):
     dev = torch.device("cuda", 0)
     batched = args.decode_predict == "batched"
     predict = decode_predictor(cfg, dev, batch_first=batched)
+    mode = {"per-utterance": False, "batched": True,
+            "last-token": last_token_predictor(predict)}[args.decode_predict]
     enc = torch.tensor(host["enc"], device=dev)
     lens = torch.tensor(host["in_lens"], device=dev)
     W = torch.tensor(host["W"], device=dev)
@@ -552,8 +559,8 @@ def run_decode(args):
 
     def decode(e, ln):
         if cfg["n_dur"]:
-            return dec_tdt.greedy_decode(e, ln, predict, W, Wd, cfg["n_dur"] - 1, batch_predict=batched)
-        return dec_rnnt.greedy_decode(e, ln, predict, W, batch_predict=batched), None
+            return dec_tdt.greedy_decode(e, ln, predict, W, Wd, cfg["n_dur"] - 1, batch_predict=mode)
+        return dec_rnnt.greedy_decode(e, ln, predict, W, batch_predict=mode), None
 
     stream = torch.cuda.current_stream()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
@@ -635,8 +642,12 @@ def run_decode(args):
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": cfg["name"], "batch": B, "T": list(cfg["T"]), "d_model": cfg["d"], "vocab": cfg["V"],
-                   "n_dur": cfg["n_dur"], "predictor": "Embedding + LSTM(2 layers, " +
-                   ("batch_first=True), one call per scan" if batched else "batch_first=False), one call per token"),
+                   "n_dur": cfg["n_dur"], "predictor": {
+                       "per-utterance": "Embedding + LSTM(2 layers, batch_first=False), one call per token",
+                       "last-token": "Embedding + LSTM(2 layers, batch_first=False), one call per scan "
+                                     "(last_token_predictor)",
+                       "batched": "Embedding + LSTM(2 layers, batch_first=True), one call per scan on padded "
+                                  "prefixes"}[args.decode_predict],
                    "tokens": n_tok, "frames": frames, "decoding_steps": steps,
                    "l2": "flushed between timed steps (256 MB write)"},
         "roofline": roof, "cpu_baseline": cpu,
@@ -663,7 +674,7 @@ def main():
     ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5", *DECODE],
                     help="c5 (default): the headline config-5 workload; c1..c4: the other BASELINE configs, 1 GPU; "
                          "decode-tdt / decode-rnnt: batched greedy decoding, 1 GPU")
-    ap.add_argument("--decode-predict", default="per-utterance", choices=["per-utterance", "batched"])
+    ap.add_argument("--decode-predict", default="last-token", choices=["last-token", "per-utterance", "batched"])
     args = ap.parse_args()
     if args.workload in DECODE:
         if int(os.environ.get("WORLD_SIZE", "1")) > 1:

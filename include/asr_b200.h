@@ -205,10 +205,11 @@ int asr_tdt_forward_noalloc(const float* encoder, const float* decoder, const fl
  *
  *   asr_greedy_pack_weights(W -> Wt); asr_greedy_init(state, prefix);
  *   pred[b] = predictor output for the prefix [<sos>], every b;
- *   loop: asr_greedy_scan(...); read report (B,);
- *         stop when no report[b] > 0; otherwise, for every b with
- *         report[b] = L > 0, pred[b] = predictor output at position L-1 of
- *         prefix[b, :L].
+ *   active = all b;
+ *   loop: asr_greedy_scan(active, ...); read report (B,);
+ *         active = the b of the list with report[b] > 0 or == -2; stop when
+ *         empty; for every b with report[b] = L > 0, pred[b] = predictor
+ *         output at position L-1 of prefix[b, :L].
  *
  * Buffers, all device memory, row-major:
  *   state  (B, 4) int32   per utterance: frame t, symbols emitted at t, hypothesis
@@ -218,30 +219,42 @@ int asr_tdt_forward_noalloc(const float* encoder, const float* decoder, const fl
  *                         blanks included (the reference's second return value);
  *   report (B,) int32     after a scan: L = prefix length when utterance b emitted a
  *                         token and needs a new predictor output, 0 when it has
- *                         finished, -1 when hyp_cap or dur_cap was too small.
+ *                         finished, -2 when it stopped at max_windows (scan it
+ *                         again, pred unchanged), -1 when hyp_cap or dur_cap was
+ *                         too small.
  * hyp_cap = dur_cap = T * max_symbols_per_frame can never overflow. */
 
 /* joint_Wt (d, ldw) = transpose of joint_W (V, d), columns V..ldw-1 zeroed.
  * ldw >= V, a multiple of 4; joint_Wt 16-byte aligned. */
 int asr_greedy_pack_weights(const float* joint_W, int V, int d, float* joint_Wt, int ldw, asr_stream_t stream);
 
-/* Zeroes state and writes <sos> = sos_id at prefix[b, 0]. */
+/* Zeroes state and fills prefix with <sos> = sos_id: prefix[b, 0] is the start
+ * token, and positions past a hypothesis hold sos_id (a valid token id when a
+ * predictor is run on right-padded prefixes). */
 int asr_greedy_init(int32_t* state, int64_t* prefix, int B, int hyp_cap, int sos_id, asr_stream_t stream);
 
-/* Advances every unfinished utterance from its state to its next emitted token
- * or to its end (frame t >= in_lens[b]) with the predictor output pred (B, d).
+/* Advances each utterance of the active list (n_active indices into the batch;
+ * active = NULL: all B) from its state to its next emitted token or to its end
+ * (frame t >= in_lens[b]) with the predictor output pred (B, d); report[b] is
+ * written for those utterances only. Utterances that reported 0 are finished and
+ * may be left out of later lists; a finished utterance in the list reports 0
+ * again.
  * encoder (B, T, d) float32; joint_Wt from asr_greedy_pack_weights;
  * joint_W_dur (n_dur, d) float32 selects TDT when n_dur > 0 (duration value =
  * argmax index, the reference's durations = range(max_duration + 1)); n_dur = 0
  * and joint_W_dur = NULL select RNN-T. Ties take the lowest index and NaN counts
  * as the maximum (torch.argmax). max_symbols_per_frame <= 0 finishes every
  * utterance without emitting, as the reference's empty per-frame loop does.
- * in_lens outside [0, T] are clamped. d <= 4096 and n_dur <= 64, else
- * ASR_ERR_UNSUPPORTED. */
+ * in_lens outside [0, T] are clamped. d <= 2048 and n_dur <= 64, else
+ * ASR_ERR_UNSUPPORTED. max_windows > 0 bounds the frames one utterance scans in
+ * this call to max_windows windows of 8 frames: an utterance that reaches it
+ * without emitting or finishing reports -2 and continues, from its saved state
+ * and with the same pred row, when it is next in the active list (0: no bound). */
 int asr_greedy_scan(const float* encoder, const float* pred, const float* joint_Wt, int ldw,
-                    const float* joint_W_dur, const int32_t* in_lens, int32_t* state, int64_t* prefix,
-                    int32_t* durs, int32_t* report, int B, int T, int d, int V, int n_dur, int blank_idx,
-                    int max_symbols_per_frame, int hyp_cap, int dur_cap, asr_stream_t stream);
+                    const float* joint_W_dur, const int32_t* in_lens, const int32_t* active, int n_active,
+                    int32_t* state, int64_t* prefix, int32_t* durs, int32_t* report, int B, int T, int d, int V,
+                    int n_dur, int blank_idx, int max_symbols_per_frame, int hyp_cap, int dur_cap,
+                    int max_windows, asr_stream_t stream);
 
 /* ----------------------------------------------------------- diagnostics */
 

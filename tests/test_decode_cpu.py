@@ -43,10 +43,11 @@ def test_golden_cases_cover_the_edges():
 
 def _scan(lib, **kw):
     f = lib.asr_greedy_scan
-    f.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] + [ctypes.c_void_p] * 6 + [ctypes.c_int] * 9 + [
-        ctypes.c_void_p]
-    a = dict(enc=0x1000, pred=0x1000, wt=0x1000, ldw=8, wdur=None, lens=0x1000, state=0x1000, prefix=0x1000,
-             durs=None, report=0x1000, B=2, T=4, d=8, V=6, n_dur=0, blank=0, max_sym=10, hyp_cap=40, dur_cap=40)
+    f.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] + [
+        ctypes.c_void_p] * 4 + [ctypes.c_int] * 10 + [ctypes.c_void_p]
+    a = dict(enc=0x1000, pred=0x1000, wt=0x1000, ldw=8, wdur=None, lens=0x1000, active=None, n_active=0,
+             state=0x1000, prefix=0x1000, durs=None, report=0x1000, B=2, T=4, d=8, V=6, n_dur=0, blank=0, max_sym=10,
+             hyp_cap=40, dur_cap=40, max_windows=0)
     a.update(kw)
     return f(*a.values(), None)
 
@@ -60,6 +61,9 @@ def test_scan_rejects_bad_arguments_on_host():
     assert _scan(lib, n_dur=3) == 1            # TDT without duration weight / buffer
     assert _scan(lib, d=5000) == 3             # joint dim beyond the shared-memory tile
     assert _scan(lib, B=0, enc=None) == 0      # empty batch: nothing to do
+    assert _scan(lib, active=0x1000, n_active=0, enc=None) == 0  # empty active list
+    assert _scan(lib, active=0x1000, n_active=3) == 1            # longer than the batch
+    assert _scan(lib, max_windows=-1) == 1                       # negative window budget
 
 
 def test_pack_and_init_reject_bad_arguments_on_host():

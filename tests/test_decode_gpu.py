@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from asr_b200.decode import rnnt, tdt
+from asr_b200.decode import last_token_predictor, rnnt, tdt
 from oracle import greedy
 from tests.decode_cases import DECODE, expected, params, random_decode_case
 
@@ -109,8 +109,10 @@ def _oracle(c, kind, max_sym, margins):
 
 
 # (kind, V, d, blank bias, max_symbols_per_frame, seed): 0.2-0.4 tokens per frame
-@pytest.mark.parametrize("kind,V,d,bias,max_sym,seed", [("tdt", 1024, 640, 6.0, 10, 1677), ("rnnt", 1024, 640, 8.0, 10, 1677),
-                                                         ("rnnt", 30, 640, 6.0, 4, 682), ("tdt", 1029, 1024, 6.5, 3, 2064)])
+@pytest.mark.parametrize("kind,V,d,bias,max_sym,seed", [("tdt", 1024, 640, 6.0, 10, 1677),
+                                                         ("rnnt", 1024, 640, 8.0, 10, 1677),
+                                                         ("rnnt", 30, 640, 6.0, 4, 682),
+                                                         ("tdt", 1029, 1024, 6.5, 3, 2064)])
 def test_greedy_matches_oracle_at_benchmark_shapes(kind, V, d, bias, max_sym, seed):
     c = random_decode_case(seed, 12, 90, V, d, 5 if kind == "tdt" else 0, bias, lo=1)
     margins = []
@@ -140,10 +142,12 @@ def test_full_batch_matches_oracle_on_a_sample():
     assert all(len(d) > 0 for d in durs)
 
 
-def test_reference_lstm_predictor_per_utterance():
+@pytest.mark.parametrize("mode", ["per-utterance", "last-token"])
+def test_reference_lstm_predictor(mode):
     """The reference's predictor, Embedding + LSTM(batch_first=False) as in
-    model/lstm.py:8-15, through the default per-utterance calls: the oracle runs
-    the same module on the CPU in float32."""
+    model/lstm.py:8-15, through the default per-utterance calls and through its
+    exact batched form (last_token_predictor): the oracle runs the same module on
+    the CPU in float32, called on whole prefixes as the reference decoder does."""
     torch.manual_seed(3)
     V, d = 48, 64
     emb = torch.nn.Embedding(V, d, padding_idx=0)
@@ -164,7 +168,24 @@ def test_reference_lstm_predictor_per_utterance():
     def gpu_predict(tokens):
         return lstm_g(emb_g(tokens))[0]
 
-    hyps, durs = tdt.greedy_decode(cuda(c["enc"]), cuda(c["in_lens"]), gpu_predict, cuda(c["W"]), cuda(c["W_dur"]), 4)
+    batch = last_token_predictor(gpu_predict) if mode == "last-token" else False
+    hyps, durs = tdt.greedy_decode(cuda(c["enc"]), cuda(c["in_lens"]), gpu_predict, cuda(c["W"]), cuda(c["W_dur"]), 4,
+                                   batch_predict=batch)
+    assert hyps == want_hyps
+    assert durs == want_durs
+
+
+@pytest.mark.parametrize("max_windows", [0, 1, 3])
+@pytest.mark.parametrize("name", ["ref_blank_duration_skips", "rnnt_char30", "tdt_bpe_like", "tdt_odd_dim"])
+def test_window_budget_does_not_change_results(monkeypatch, name, max_windows):
+    """Pausing long blank runs at a per-launch window budget (and resuming them in
+    the next launch with the same predictor output) gives the reference's results."""
+    from asr_b200.decode import _greedy
+
+    monkeypatch.setattr(_greedy, "MAX_WINDOWS", max_windows)
+    c = DECODE[name]
+    want_hyps, want_durs = expected(c)
+    hyps, durs = run(c)
     assert hyps == want_hyps
     assert durs == want_durs
 
