@@ -527,8 +527,11 @@ def run_decode(args):
     from asr_b200.decode import rnnt as dec_rnnt
     from asr_b200.decode import tdt as dec_tdt
 
-    cfg = DECODE[args.workload]
+    cfg = dict(DECODE[args.workload])
     host = decode_inputs(cfg)
+    if args.batch:  # profiling aid: the first BATCH utterances
+        cfg["B"] = min(args.batch, cfg["B"])
+        host["enc"], host["in_lens"] = host["enc"][: cfg["B"]], host["in_lens"][: cfg["B"]]
     sample = 1  # ~10-30 s of CPU work: the reference re-runs the predictor on the whole prefix per token
     if args.impl == "reference":
         torch.set_num_threads(os.cpu_count() or 1)
