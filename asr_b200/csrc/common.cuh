@@ -139,6 +139,11 @@ inline int sm_count() {
 // Host-side launchers defined in lattice.cu.
 int launch_lattice_prep(const int32_t* in_lens, const int32_t* tgt_lens, int B, int T, int U, int S,
                         const LatticeMeta& m, cudaStream_t stream);
+// CTC beta + gradient (ctc.cu). post_only = 1 writes grad_loss * (state posterior
+// mass per column) instead of d loss / d logits.
+int ctc_grad_dispatch(const double* alpha, const float* log_probs, const int32_t* targets, const int32_t* in_lens,
+                      const int32_t* tgt_lens, const float* grad_loss, int zero_infinity, int post_only, int B, int T,
+                      int V, int S, float* grad, cudaStream_t st);
 // bf16 <-> fp32 element conversions of n contiguous values (bf16 activations and
 // their gradients).
 int launch_bf16_to_f32(const __nv_bfloat16* src, float* dst, int64_t n, cudaStream_t stream);

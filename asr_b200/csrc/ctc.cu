@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
     ctc_grad_kernel(const double* __restrict__ alpha, const float* __restrict__ lp,
                     const int32_t* __restrict__ targets, const int32_t* __restrict__ in_lens,
                     const int32_t* __restrict__ tgt_lens, const float* __restrict__ grad_loss, int zero_infinity,
-                    int B, int T, int V, int S, float* __restrict__ grad) {
+                    int post_only, int B, int T, int V, int S, float* __restrict__ grad) {
     extern __shared__ float smem_rows[];
     const int lane = threadIdx.x & 31;
     const int w = threadIdx.x >> 5;
@@ -183,7 +183,9 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
         __syncwarp();
         for (int v = lane; v < V; v += 32) {
             const int64_t idx = (int64_t)t * V + v;
-            gb[idx] = gl * (__expf(lpb[idx]) - row[v]);
+            // post_only: the posterior mass per column only (the fused CTC head adds
+            // the softmax part inside its joint kernel)
+            gb[idx] = post_only ? gl * row[v] : gl * (__expf(lpb[idx]) - row[v]);
             row[v] = 0.f;
         }
         __syncwarp();
@@ -220,7 +222,8 @@ int launch_ctc_alpha(const float* lp, const int32_t* tg, const int32_t* il, cons
 
 template <int KS>
 int launch_ctc_grad(const double* alpha, const float* lp, const int32_t* tg, const int32_t* il, const int32_t* tl,
-                    const float* gl, int zinf, int B, int T, int V, int S, float* grad, cudaStream_t st) {
+                    const float* gl, int zinf, int post_only, int B, int T, int V, int S, float* grad,
+                    cudaStream_t st) {
     const int blocks = (B + kCtcWarps - 1) / kCtcWarps;
     const size_t smem = sizeof(float) * (size_t)V * kCtcWarps;
     if (smem > 48 * 1024) {
@@ -229,7 +232,8 @@ int launch_ctc_grad(const double* alpha, const float* lp, const int32_t* tg, con
             return ASR_ERR_UNSUPPORTED;
     }
     KernelTimer kt("ctc_beta_grad", st);
-    ctc_grad_kernel<KS><<<blocks, 32 * kCtcWarps, smem, st>>>(alpha, lp, tg, il, tl, gl, zinf, B, T, V, S, grad);
+    ctc_grad_kernel<KS><<<blocks, 32 * kCtcWarps, smem, st>>>(alpha, lp, tg, il, tl, gl, zinf, post_only, B, T, V, S,
+                                                             grad);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
@@ -268,6 +272,26 @@ extern "C" int asr_ctc_alpha(const float* log_probs, const int32_t* targets, con
     }
 }
 
+namespace asr {
+
+int ctc_grad_dispatch(const double* alpha, const float* log_probs, const int32_t* targets, const int32_t* in_lens,
+                      const int32_t* tgt_lens, const float* grad_loss, int zero_infinity, int post_only, int B, int T,
+                      int V, int S, float* grad, cudaStream_t st) {
+    const int z = zero_infinity ? 1 : 0;
+    const int p = post_only ? 1 : 0;
+    switch (ctc_ks(S)) {
+        case 1: return launch_ctc_grad<1>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 2: return launch_ctc_grad<2>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 4: return launch_ctc_grad<4>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 8: return launch_ctc_grad<8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 16: return launch_ctc_grad<16>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 32: return launch_ctc_grad<32>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        default: return ASR_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace asr
+
 extern "C" int asr_ctc_grad(const double* alpha, const float* log_Z, const float* log_probs, const int32_t* targets,
                             const int32_t* in_lens, const int32_t* tgt_lens, const float* grad_loss,
                             int zero_infinity, int B, int T, int V, int S, float* grad_logits, asr_stream_t stream) {
@@ -276,15 +300,6 @@ extern "C" int asr_ctc_grad(const double* alpha, const float* log_Z, const float
     if (!alpha || !log_Z || !log_probs || !in_lens || !tgt_lens || !grad_loss || !grad_logits ||
         (S > 0 && !targets))
         return ASR_ERR_INVALID_ARGUMENT;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int z = zero_infinity ? 1 : 0;
-    switch (ctc_ks(S)) {
-        case 1: return launch_ctc_grad<1>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
-        case 2: return launch_ctc_grad<2>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
-        case 4: return launch_ctc_grad<4>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
-        case 8: return launch_ctc_grad<8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
-        case 16: return launch_ctc_grad<16>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
-        case 32: return launch_ctc_grad<32>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, B, T, V, S, grad_logits, st);
-        default: return ASR_ERR_UNSUPPORTED;
-    }
+    return ctc_grad_dispatch(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, zero_infinity, 0, B, T, V, S,
+                             grad_logits, reinterpret_cast<cudaStream_t>(stream));
 }

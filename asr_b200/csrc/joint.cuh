@@ -25,6 +25,14 @@ struct JointArgs {
     LatticeMeta m;
     int B, T, U, V, n_dur, d, S, blank;
     float sigma;
+    // CTC head mode (head = 1, tensor-core path only): the lattice has one label
+    // position per frame (U_b = 1) and the hidden row is RMSNorm(enc) * rms_g
+    // instead of tanh(enc + dec); with `bias` the GEMM gains a ones column whose
+    // weight column is the bias (K = d + 1). dec / targets are unused.
+    int head;
+    const float* rms_g;  // (d,) RMSNorm weight
+    float rms_eps;
+    const float* bias;   // (V,) or nullptr
 };
 
 // Forward epilogue outputs (compact per-node arrays).
@@ -44,10 +52,11 @@ struct JointBwdIn {
 };
 
 struct JointBwdOut {
-    float* d_enc;  // (B, T, d), accumulated
-    float* d_dec;  // (B, U, d), accumulated
+    float* d_enc;  // (B, T, d), accumulated (CTC head mode: d loss / d hidden row, before RMSNorm)
+    float* d_dec;  // (B, U, d), accumulated (unused in CTC head mode)
     float* dW;     // (V, d), accumulated
     float* dWd;    // (n_dur, d), accumulated, or nullptr
+    float* dbias;  // (V,), accumulated: CTC head mode with a bias, else nullptr
 };
 
 // ---- fp32 SIMT path -----------------------------------------------------------

@@ -73,7 +73,8 @@ struct Geom {
 // remainder chunk paying a full ring of weight stages for a few columns.
 Geom make_geom(const JointArgs& a) {
     Geom g;
-    g.kchunks = (a.d + kAK - 1) / kAK;
+    const int kd = a.d + (a.head && a.bias ? 1 : 0);  // CTC head: bias as a ones column
+    g.kchunks = (kd + kAK - 1) / kAK;
     g.kpad = g.kchunks * kAK;
     g.vpad = (a.V + a.n_dur + 15) / 16 * 16;
     g.nchunks = (g.vpad + kNC - 1) / kNC;
@@ -558,9 +559,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // [joint_W; joint_W_dur] -> bf16 (vpad, kpad), zero padded; optionally also the
 // transpose (kpad, vpad) used as the K-major B operand of dH.
-__global__ void prep_weights_kernel(const float* __restrict__ W, const float* __restrict__ Wd, int V, int n_dur,
-                                    int d, int vpad, int kpad, __nv_bfloat16* __restrict__ Wf,
-                                    __nv_bfloat16* __restrict__ Wt) {
+__global__ void prep_weights_kernel(const float* __restrict__ W, const float* __restrict__ Wd,
+                                    const float* __restrict__ bias, int V, int n_dur, int d, int vpad, int kpad,
+                                    __nv_bfloat16* __restrict__ Wf, __nv_bfloat16* __restrict__ Wt) {
     const int64_t total = (int64_t)vpad * kpad;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int r = (int)(i / kpad), k = (int)(i % kpad);
@@ -570,6 +571,8 @@ __global__ void prep_weights_kernel(const float* __restrict__ W, const float* __
                 x = W[(int64_t)r * d + k];
             else if (r < V + n_dur)
                 x = Wd[(int64_t)(r - V) * d + k];
+        } else if (k == d && bias && r < V) {
+            x = bias[r];  // CTC head: the weight of the ones column
         }
         const __nv_bfloat16 b = __float2bfloat16_rn(x);
         Wf[i] = b;
@@ -780,8 +783,60 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
     }
 }
 
+// CTC head hidden rows: one warp per frame row, H = bf16(x * rsqrt(mean(x^2) + eps)
+// * g) (torch's rms_norm: fp32 statistics, the result rounded to bf16 as the
+// autocast Linear rounds its input), then a ones column at k = d when the head has
+// a bias; columns past it and rows up to the next 256-row boundary are zero.
+template <typename TA>
+__global__ void __launch_bounds__(256) rms_hidden_kernel(LatticeMeta m, int B, const TA* __restrict__ enc,
+                                                         const float* __restrict__ g, float eps, int ones, int T,
+                                                         int d, int kpad, const int32_t* __restrict__ bounds, int pass,
+                                                         __nv_bfloat16* __restrict__ H) {
+    const int N = total_nodes(m, B);
+    const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
+    const int rows = e - s;
+    const int rows_pad = (rows + kPassAlign - 1) / kPassAlign * kPassAlign;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows_pad; r += nwarps) {
+        __nv_bfloat16* dst = H + (int64_t)r * kpad;
+        if (r >= rows) {
+            for (int k = lane; k < kpad; k += 32) dst[k] = __float2bfloat16_rn(0.f);
+            continue;
+        }
+        const NodeCoord c = node_coord(m, B, s + r);  // U_b = 1: node = frame
+        const TA* x = enc + ((int64_t)c.b * T + c.t) * d;
+        float ss = 0.f;
+        for (int k = lane; k < d; k += 32) {
+            const float v = load1(x + k);
+            ss = fmaf(v, v, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rstd = rsqrtf(ss / (float)d + eps);
+        for (int k = lane; k < kpad; k += 32) {
+            float h = 0.f;
+            if (k < d)
+                h = load1(x + k) * rstd * __ldg(g + k);
+            else if (k == d && ones)
+                h = 1.f;
+            dst[k] = __float2bfloat16_rn(h);
+        }
+    }
+}
+
 int launch_hidden(const JointArgs& a, int kpad, const int32_t* bounds, int pass, __nv_bfloat16* H, cudaStream_t st) {
     KernelTimer kt("joint_hidden", st);
+    if (a.head) {
+        if (a.enc16)
+            rms_hidden_kernel<__nv_bfloat16><<<sm_count() * 8, 256, 0, st>>>(
+                a.m, a.B, a.enc16, a.rms_g, a.rms_eps, a.bias ? 1 : 0, a.T, a.d, kpad, bounds, pass, H);
+        else
+            rms_hidden_kernel<float><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.rms_g, a.rms_eps,
+                                                                     a.bias ? 1 : 0, a.T, a.d, kpad, bounds, pass, H);
+        ASR_LAUNCH_CHECK();
+        return ASR_OK;
+    }
     if (a.enc16)
         hidden_kernel<__nv_bfloat16><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc16, a.dec16, a.T, a.U, a.d, kpad,
                                                                      a.vec, bounds, pass, H);
@@ -920,8 +975,8 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
     ASR_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
     {
         KernelTimer kt("joint_prep_weights", st);
-        prep_weights_kernel<<<sm_count() * 4, 256, 0, st>>>(a.W, a.Wd, a.V, a.n_dur, a.d, g.vpad, g.kpad, Wf,
-                                                             nullptr);
+        prep_weights_kernel<<<sm_count() * 4, 256, 0, st>>>(a.W, a.Wd, a.head ? a.bias : nullptr, a.V, a.n_dur,
+                                                             a.d, g.vpad, g.kpad, Wf, nullptr);
         ASR_LAUNCH_CHECK();
         plan_passes_kernel<<<(L.pp.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, L.pp.passes, L.pp.step, bounds);
         ASR_LAUNCH_CHECK();
@@ -1018,6 +1073,7 @@ struct DhEpilogue {
     float* sacc;       // [dec_rows][kDhM] d_dec sums
 
     __device__ float enc_at(int b, int t) const {
+        if (P.a.head) return 0.f;  // CTC head: d hidden itself, no tanh' to recompute
         return col_ok ? act(P.a.enc, P.a.enc16, ((int64_t)b * P.a.T + t) * P.a.d + col) : 0.f;
     }
     __device__ float dec_at(const DhWalk& w, int u) const {
@@ -1073,6 +1129,11 @@ struct DhEpilogue {
     }
     // One node at a time (any U_b, utterance changes inside the group).
     __device__ void node(DhWalk& w, float g) const {
+        if (P.a.head) {  // CTC head: one node per frame, d_hidden = G Wf
+            w.acc_e += g;
+            if (++w.u == w.Ub) end_frame(w);
+            return;
+        }
         const float h = tanh_fast(w.e_cur + dec_at(w, w.u));
         const float x = g * (1.f - h * h);
         w.acc_e += x;
@@ -1300,6 +1361,7 @@ struct DwParams {
     int splits;
     float* dW;
     float* dWd;
+    float* dbias;  // CTC head: column d of the product (the ones column)
     int* err;
 };
 
@@ -1431,7 +1493,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int k = kt * kDwN + gi * 16 + i;
-                        if (k < a.d) atomicAdd(dst + k, acc[i]);
+                        if (k < a.d)
+                            atomicAdd(dst + k, acc[i]);
+                        else if (k == a.d && P.dbias && v < a.V)
+                            atomicAdd(P.dbias + v, acc[i]);
                     }
                 }
             }
@@ -1508,7 +1573,8 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     ASR_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), st));
     {
         KernelTimer kt("joint_prep_weights", st);
-        prep_weights_kernel<<<sms * 4, 256, 0, st>>>(a.W, a.Wd, a.V, a.n_dur, a.d, g.vpad, g.kpad, Wf, Wt);
+        prep_weights_kernel<<<sms * 4, 256, 0, st>>>(a.W, a.Wd, a.head ? a.bias : nullptr, a.V, a.n_dur, a.d,
+                                                     g.vpad, g.kpad, Wf, Wt);
         ASR_LAUNCH_CHECK();
     }
     {
@@ -1551,7 +1617,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     DP.ndt = (g.kpad + kDhM - 1) / kDhM;
     DP.groups = std::max(1, sms / DP.ndt);
     const int limit = dyn_smem_limit();
-    DP.dec_rows = (int)dh_smem_bytes(2, a.U) <= limit ? a.U : 0;
+    DP.dec_rows = !a.head && (int)dh_smem_bytes(2, a.U) <= limit ? a.U : 0;
     DP.stages = 2;
     while (DP.stages < 8 && (int)dh_smem_bytes(DP.stages + 1, DP.dec_rows) <= limit) ++DP.stages;
     const size_t smem_dh = dh_smem_bytes(DP.stages, DP.dec_rows);
@@ -1565,6 +1631,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     WP.bounds = bounds;
     WP.dW = o.dW;
     WP.dWd = o.dWd;
+    WP.dbias = a.head ? o.dbias : nullptr;
     WP.err = err;
     const int nvt = (g.vpad + kDwM - 1) / kDwM, nkt = (g.kpad + kDwN - 1) / kDwN;
     WP.splits = std::max(1, sms / (nvt * nkt));  // one wave: a CTA fills an SM's shared memory

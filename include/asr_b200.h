@@ -194,6 +194,40 @@ int asr_tdt_forward_noalloc(const float* encoder, const float* decoder, const fl
                             int tf32, float* loss, double* alpha, float* log_P_blank, float* log_P_y,
                             float* log_P_dur, float* log_prob, asr_stream_t stream);
 
+/* ------------------------------------------------------- fused CTC head */
+
+/* The CTC system's head and loss in one pass: Linear(RMSNorm(enc)) (reference
+ * src/asr/system/ctc.py:21-24: torch.nn.RMSNorm(d) then torch.nn.Linear(d, V),
+ * run under bf16 autocast) followed by CTCLoss (src/asr/loss/ctc.py:11-30:
+ * log_softmax in fp32, the CTC recursion, blank = 0, zero_infinity), without the
+ * (B, T, V) logits, log-probs or their gradient in HBM. No counterpart in the
+ * reference, which materialises all three.
+ * encoder (B, T, d) float32 or bfloat16 (act_dtype; grad_encoder has the same
+ * type); rms_weight (d,); weight (V, d); bias (V,) or NULL; targets (B, S) int32
+ * labels in [1, V); in_lens in [1, T]; tgt_lens in [0, S]. The GEMM runs on bf16
+ * tcgen05 tensor cores with fp32 accumulation: bf16(RMSNorm(enc)) and bf16(weight,
+ * bias), the operands the autocast Linear uses. rms_eps: torch's default is
+ * FLT_EPSILON.
+ * loss (B,) = -log P(targets | enc), 0 where zero_infinity drops an infeasible
+ * utterance (not divided by tgt_lens; CTCLoss divides by tgt_lens.clamp_min(1)).
+ * The forward leaves what the backward needs in the workspace: call
+ * asr_ctc_head_backward with the same workspace and inputs before reusing it.
+ * 2S + 1 <= 1024 and asr_ctc_head_supported(V, d), else ASR_ERR_UNSUPPORTED. */
+size_t asr_ctc_head_workspace_bytes(int B, int T, int S, int V, int d, int act_dtype);
+int asr_ctc_head_supported(int V, int d);
+int asr_ctc_head_forward(const void* encoder, int act_dtype, const float* rms_weight, float rms_eps,
+                         const float* weight, const float* bias, const int32_t* targets, const int32_t* in_lens,
+                         const int32_t* tgt_lens, int B, int T, int S, int V, int d, int zero_infinity, float* loss,
+                         void* workspace, size_t workspace_bytes, asr_stream_t stream);
+/* Writes (overwrites) grad_encoder (B, T, d), zero past in_lens; grad_rms_weight
+ * (d,); grad_weight (V, d); grad_bias (V,) when bias is given. grad_loss (B,)
+ * scales each utterance. */
+int asr_ctc_head_backward(const void* encoder, int act_dtype, const float* rms_weight, float rms_eps,
+                          const float* weight, const float* bias, const int32_t* targets, const int32_t* in_lens,
+                          const int32_t* tgt_lens, int B, int T, int S, int V, int d, int zero_infinity,
+                          const float* grad_loss, void* grad_encoder, float* grad_rms_weight, float* grad_weight,
+                          float* grad_bias, void* workspace, size_t workspace_bytes, asr_stream_t stream);
+
 /* ------------------------------------------------ greedy transducer decoding */
 
 /* Batched greedy decoding for RNN-T and TDT. Replaces the per-utterance,
