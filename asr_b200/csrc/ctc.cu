@@ -168,18 +168,40 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
         be[j] = (in[j] && (s == ut.L - 1 || s == ut.L - 2)) ? 0.0 : -INFINITY;
     }
     float lpt[KS];
+    double acur[KS];  // alpha of the current step, loaded one step ahead
 #pragma unroll
-    for (int j = 0; j < KS; ++j) lpt[j] = in[j] ? lpb[(int64_t)(ut.Tb - 1) * V + lab[j]] : 0.f;
+    for (int j = 0; j < KS; ++j) {
+        lpt[j] = in[j] ? lpb[(int64_t)(ut.Tb - 1) * V + lab[j]] : 0.f;
+        acur[j] = in[j] ? ab[(int64_t)(ut.Tb - 1) * Lmax + lane * KS + j] : -INFINITY;
+    }
     __syncwarp();
     for (int t = ut.Tb - 1; t >= 0; --t) {
-        // state posteriors scattered to vocabulary bins (ctc.cu:152-165)
+        // state posteriors scattered to vocabulary bins (ctc.cu:152-165); the blank
+        // states (every even s, about half of them) share bin 0, so their mass is
+        // summed over the warp first instead of contending for one address
+        float pblank = 0.f;
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
             if (in[j]) {
-                const float post = __expf((float)(ab[(int64_t)t * Lmax + lane * KS + j] + be[j] - logZ));
-                atomicAdd(row + lab[j], post);
+                const float post = __expf((float)(acur[j] + be[j] - logZ));
+                if ((lane * KS + j) & 1)
+                    atomicAdd(row + lab[j], post);
+                else
+                    pblank += post;
             }
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) pblank += __shfl_xor_sync(0xffffffffu, pblank, o);
+        if (lane == 0) atomicAdd(row, pblank);
+        // next step's alpha and emissions, in flight during the row writes and the recursion
+        if (t > 0) {
+#pragma unroll
+            for (int j = 0; j < KS; ++j)
+                if (in[j]) acur[j] = ab[(int64_t)(t - 1) * Lmax + lane * KS + j];
+        }
+        float lnx[KS];
+#pragma unroll
+        for (int j = 0; j < KS; ++j) lnx[j] = (in[j] && t > 0) ? lpb[(int64_t)(t - 1) * V + lab[j]] : 0.f;
         __syncwarp();
         for (int v = lane; v < V; v += 32) {
             const int64_t idx = (int64_t)t * V + v;
@@ -206,7 +228,7 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
             be[j] = in[j] ? lse3_d(c[j], n1, skip[j] ? n2 : -INFINITY) : -INFINITY;
         }
 #pragma unroll
-        for (int j = 0; j < KS; ++j) lpt[j] = in[j] ? lpb[(int64_t)(t - 1) * V + lab[j]] : 0.f;
+        for (int j = 0; j < KS; ++j) lpt[j] = lnx[j];
     }
 }
 

@@ -47,35 +47,45 @@ __device__ __forceinline__ float ld_act(const TA* p) {
 // (vocabulary id 0), slots 1..K_b-1 the distinct target labels; slot_tg maps each
 // target position to its slot. Labels outside [0, V) are clamped into it so no
 // weight-row access leaves the matrix (the reference leaves them undefined). One
-// thread per utterance (S is at most a few hundred).
-__global__ void slot_prep_kernel(const int32_t* __restrict__ targets, const int32_t* __restrict__ tgt_lens, int B,
-                                 int S, int K, int V, int32_t* __restrict__ labels, int32_t* __restrict__ kb,
-                                 int32_t* __restrict__ slot_tg) {
-    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+// warp per utterance: the lanes compare a label against 32 known slots at a time
+// in shared memory.
+constexpr int kSlotWarps = 4;
+
+__global__ void __launch_bounds__(32 * kSlotWarps) slot_prep_kernel(const int32_t* __restrict__ targets,
+                                                                    const int32_t* __restrict__ tgt_lens, int B,
+                                                                    int S, int K, int V, int32_t* __restrict__ labels,
+                                                                    int32_t* __restrict__ kb,
+                                                                    int32_t* __restrict__ slot_tg) {
+    extern __shared__ int32_t slot_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int b = blockIdx.x * kSlotWarps + warp;
     if (b >= B) return;
+    int32_t* L = slot_smem + warp * K;
     const int Sb = min(max(tgt_lens[b], 0), S);
-    int32_t* L = labels + (int64_t)b * K;
     int n = 1;
-    L[0] = 0;
+    if (lane == 0) L[0] = 0;
+    __syncwarp();
     for (int s = 0; s < S; ++s) {
         int slot = 0;
         if (s < Sb) {
             const int y = min(max(targets[(int64_t)b * S + s], 0), V - 1);
             slot = -1;
-            for (int j = 0; j < n; ++j)
-                if (L[j] == y) {
-                    slot = j;
-                    break;
-                }
+            for (int j0 = 0; j0 < n && slot < 0; j0 += 32) {
+                const int j = j0 + lane;
+                const unsigned hit = __ballot_sync(0xffffffffu, j < n && L[j] == y);
+                if (hit) slot = j0 + __ffs(hit) - 1;
+            }
             if (slot < 0) {
                 slot = n;
-                L[n++] = y;
+                if (lane == 0) L[n] = y;
+                ++n;
             }
+            __syncwarp();
         }
-        slot_tg[(int64_t)b * S + s] = slot;
+        if (lane == 0) slot_tg[(int64_t)b * S + s] = slot;
     }
-    for (int j = n; j < K; ++j) L[j] = 0;
-    kb[b] = n;
+    for (int j = lane; j < K; j += 32) labels[(int64_t)b * K + j] = j < n ? L[j] : 0;
+    if (lane == 0) kb[b] = n;
 }
 
 // rstd of the frames [t0, t0 + nf) of utterance b into rs[] (one warp per frame).
@@ -415,8 +425,10 @@ int head_forward(const JointArgs& a, const HeadWs& w, const TA* enc, const int32
     if (rc) return rc;
     {
         KernelTimer kt("ctc_head_slots", st);
-        slot_prep_kernel<<<(B + 127) / 128, 128, 0, st>>>(targets, tgt_lens, B, S, K, a.V, w.labels, w.kb,
-                                                          w.slot_tg);
+        const size_t smem = sizeof(int32_t) * (size_t)K * kSlotWarps;
+        ASR_CUDA_TRY(cudaFuncSetAttribute(slot_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        slot_prep_kernel<<<(B + kSlotWarps - 1) / kSlotWarps, 32 * kSlotWarps, smem, st>>>(
+            targets, tgt_lens, B, S, K, a.V, w.labels, w.kb, w.slot_tg);
         ASR_LAUNCH_CHECK();
     }
     JointFwdOut o{w.lpb, w.lse, w.lpy, nullptr};

@@ -661,6 +661,208 @@ def run_decode(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------ fused CTC head
+#
+# `--workload ctc-head` times the CTC system's head + loss fused into one op
+# (asr_b200.loss.ctc_head.FusedCTCHead, forward + backward) on one GPU: B = 64
+# utterances, T ~ U[200, 500] frames, S ~ U[20, 120] labels, d = 512 (the reference
+# encoder width), V = 1024 (BPE), zero_infinity (the reference ctc.yaml), bf16
+# encoder output as the system's autocast produces it. Beside it, in the same run,
+# the unfused path of the reference system: Sequential(RMSNorm, Linear) under bf16
+# autocast, fp32 log_softmax and the CTC loss module (asr_b200.loss.CTCLoss, the
+# drop-in of the reference's), which writes the (B, T, V) logits, log-probs and
+# their gradient to HBM.
+
+CTC_HEAD = {"name": "ctc_head_bpe1024", "B": 64, "T": (200, 500), "S": (20, 120), "d": 512, "V": 1024}
+
+
+def ctc_head_inputs(cfg, seed=SEED):
+    rng = np.random.default_rng([seed, 53])
+    B, d, V = cfg["B"], cfg["d"], cfg["V"]
+    il = rng.integers(cfg["T"][0], cfg["T"][1] + 1, size=B).astype(np.int32)
+    tl = rng.integers(cfg["S"][0], cfg["S"][1] + 1, size=B).astype(np.int32)
+    T, S = int(il.max()), int(tl.max())
+    return {"enc": rng.standard_normal((B, T, d), dtype=np.float32), "in_lens": il, "tgt_lens": tl,
+            "targets": rng.integers(1, V, size=(B, S)).astype(np.int32)}
+
+
+def run_ctc_head(args):
+    import ctypes
+
+    import torch
+
+    from asr_b200 import _lib
+    from asr_b200.loss import CTCLoss
+    from asr_b200.loss.ctc_head import FusedCTCHead
+
+    cfg = CTC_HEAD
+    host = ctc_head_inputs(cfg)
+    B, d, V = cfg["B"], cfg["d"], cfg["V"]
+    if args.impl == "reference":
+        from oracle import ctc_head as oracle_head
+
+        torch.manual_seed(SEED)
+        ref = torch.nn.Sequential(torch.nn.RMSNorm(d), torch.nn.Linear(d, V))
+        g, W, b = (p.detach().numpy() for p in (ref[0].weight, ref[1].weight, ref[1].bias))
+        sample = 2
+
+        def one():
+            oracle_head.ctc_head(host["enc"][:sample], g, W, b, host["targets"][:sample], host["in_lens"][:sample],
+                                 host["tgt_lens"][:sample], zero_infinity=True)
+
+        one()
+        steps = max(1, args.steps // 2)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one()
+        value = sample * steps / (time.perf_counter() - t0)
+        base = {"value": round(value, 4), "unit": "utterances/s", "cores": os.cpu_count() or 1, "kind": "port",
+                "sample": f"utterances 0..{sample - 1} per step: float64 numpy head + the C CTC oracle"}
+        print(json.dumps({"impl": "reference", "metric": "fused CTC head + loss fwd+bwd utterances/s",
+                          "value": base["value"], "unit": "utterances/s", "n_gpus": 1, "steps": steps, "warmup": 1,
+                          "higher_is_better": True, "dtype": "f64", "data": "synthetic",
+                          "config": {"workload": cfg["name"]}, "cpu_baseline": base,
+                          "e2e": {"value": base["value"], "unit": "utterances/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(SEED)
+    head = FusedCTCHead(d, V, zero_infinity=True).to(dev)
+    ref = torch.nn.Sequential(torch.nn.RMSNorm(d), torch.nn.Linear(d, V)).to(dev)
+    ref.load_state_dict(head.state_dict())
+    ctc = CTCLoss(zero_infinity=True)
+    enc = torch.tensor(host["enc"], device=dev).bfloat16()
+    tg = torch.tensor(host["targets"], device=dev)
+    il = torch.tensor(host["in_lens"], device=dev)
+    tl = torch.tensor(host["tgt_lens"], device=dev)
+
+    def fused(e, t, i, l):
+        e = e.detach().requires_grad_(True)
+        for p in head.parameters():
+            p.grad = None
+        loss = head(e, t, i, l).mean()
+        loss.backward()
+        return loss.detach()
+
+    def unfused(e, t, i, l):
+        e = e.detach().requires_grad_(True)
+        for p in ref.parameters():
+            p.grad = None
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = ref(e)
+        loss = ctc(logits, t, i, l).mean()
+        loss.backward()
+        return loss.detach()
+
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def timed(run, k):
+        times = []
+        for _ in range(k):
+            flush.fill_(1)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            run()
+            s1.record(stream)
+            times.append((s0, s1))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in times) / k
+
+    for _ in range(args.warmup):
+        fused(enc, tg, il, tl)
+        unfused(enc, tg, il, tl)
+    torch.cuda.synchronize()
+    lib = _lib.capi()
+    lib.asr_profiler_report(None, 0, 1)
+    clocks = ClockSampler(args.clocks_log)
+    clocks.start()
+    time.sleep(0.3)
+    lib.asr_profiler_enable(1)
+    ms = timed(lambda: fused(enc, tg, il, tl), args.steps)
+    lib.asr_profiler_enable(0)
+    clock_info = clocks.stop()
+    n = lib.asr_profiler_report(None, 0, 0)
+    buf = ctypes.create_string_buffer(max(n, 0) + 1)
+    lib.asr_profiler_report(buf, len(buf), 1)
+    prof = parse_profile(buf.value.decode())
+    ms_unfused = timed(lambda: unfused(enc, tg, il, tl), args.steps)
+    peak_mem = {}
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats(dev)
+        base_mem = torch.cuda.memory_allocated(dev)
+        fn(enc, tg, il, tl)
+        torch.cuda.synchronize()
+        peak_mem[name] = int(torch.cuda.max_memory_allocated(dev) - base_mem)
+
+    pinned = {"enc": torch.from_numpy(host["enc"]).bfloat16().pin_memory(),
+              "targets": torch.from_numpy(host["targets"]).pin_memory(),
+              "in_lens": torch.from_numpy(host["in_lens"]).pin_memory(),
+              "tgt_lens": torch.from_numpy(host["tgt_lens"]).pin_memory()}
+    res = torch.empty(1, dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pinned.values())
+
+    def e2e():
+        t = {k: v.to(dev, non_blocking=True) for k, v in pinned.items()}
+        res.copy_(fused(t["enc"], t["targets"], t["in_lens"], t["tgt_lens"]).reshape(1), non_blocking=True)
+
+    e2e()
+    e2e_ms = timed(e2e, args.steps)
+
+    N = int(host["in_lens"].sum())
+    kd = (d + 1 + 63) // 64 * 64
+    peaks = measured_peaks()
+    kernels = {}
+    total_ms = max(sum(v[1] for v in prof.values()), 1e-9)
+    for name, (launches, kms) in prof.items():
+        e = {"launches_per_step": launches / args.steps, "ms_per_step": round(kms / args.steps, 4),
+             "share": round(kms / total_ms, 4)}
+        if name in GEMM_KERNELS:
+            fl = 2.0 * N * kd * V
+            ach = fl / (kms / args.steps / 1000.0) / 1e12
+            e.update({"bound": "tensor", "achieved": round(ach, 2), "unit": "TFLOP/s",
+                      "frac": round(ach / peaks["bf16_tflops_sustained"], 4)})
+        kernels[name] = e
+    top = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
+    gem = [k for k in kernels if k in GEMM_KERNELS]
+    gem_ms = sum(kernels[k]["ms_per_step"] for k in gem)
+    gem_ach = 4 * 2.0 * N * kd * V / (gem_ms / 1000.0) / 1e12 if gem_ms else None
+    roof = {"kernel": "joint GEMMs (fwd, dlogits, dhidden, dweight)", "bound": "tensor",
+            "achieved": round(gem_ach, 2) if gem_ach else None, "peak": peaks["bf16_tflops_sustained"],
+            "unit": "TFLOP/s", "frac": round(gem_ach / peaks["bf16_tflops_sustained"], 4) if gem_ach else None,
+            "traffic": None, "top_kernel": top, "top_share": kernels[top]["share"] if top else None,
+            "work": "2 * frames * ceil64(d + 1) * V flops per GEMM, 4 GEMMs per step"}
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import ctc_head as oracle_head
+
+        g, W, b = (p.detach().float().cpu().numpy() for p in (head[0].weight, head[1].weight, head[1].bias))
+        t0 = time.perf_counter()
+        oracle_head.ctc_head(host["enc"][:2], g, W, b, host["targets"][:2], host["in_lens"][:2],
+                             host["tgt_lens"][:2], zero_infinity=True)
+        cpu = {"value": round(2 / (time.perf_counter() - t0), 4), "unit": "utterances/s", "cores": 1,
+               "kind": "port", "sample": "utterances 0..1: float64 numpy head + the C CTC oracle"}
+    line = {
+        "metric": "fused CTC head + loss fwd+bwd utterances/s", "value": round(B / (ms / 1000.0), 3),
+        "unit": "utterances/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg["name"], "batch": B, "T": list(cfg["T"]), "S": list(cfg["S"]), "d_model": d,
+                   "vocab": V, "frames": N, "encoder_dtype": "bf16", "zero_infinity": True,
+                   "l2": "flushed between timed steps (256 MB write)"},
+        "unfused": {"value": round(B / (ms_unfused / 1000.0), 3), "unit": "utterances/s",
+                    "ms_per_step": round(ms_unfused, 4),
+                    "path": "Sequential(RMSNorm, Linear) under bf16 autocast + fp32 log_softmax + CTCLoss"},
+        "peak_memory_bytes": peak_mem,
+        "roofline": roof, "cpu_baseline": cpu,
+        "e2e": {"value": round(B / (e2e_ms / 1000.0), 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": int(sum(v[0] for v in prof.values()) / args.steps), "kernels": kernels, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -674,15 +876,15 @@ def main():
                     help="profiling aid: run only the first BATCH utterances of the workload")
     ap.add_argument("--act-dtype", default="f32", choices=["f32", "bf16"],
                     help="encoder / decoder activation dtype (bf16: a system's autocast activations, no float32 copies)")
-    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5", *DECODE],
+    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5", *DECODE, "ctc-head"],
                     help="c5 (default): the headline config-5 workload; c1..c4: the other BASELINE configs, 1 GPU; "
-                         "decode-tdt / decode-rnnt: batched greedy decoding, 1 GPU")
+                         "decode-tdt / decode-rnnt: batched greedy decoding, 1 GPU; ctc-head: the fused CTC head")
     ap.add_argument("--decode-predict", default="last-token", choices=["last-token", "per-utterance", "batched"])
     args = ap.parse_args()
-    if args.workload in DECODE:
+    if args.workload in DECODE or args.workload == "ctc-head":
         if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-            raise SystemExit("--workload decode-* runs on one GPU")
-        run_decode(args)
+            raise SystemExit("--workload decode-* / ctc-head runs on one GPU")
+        (run_decode if args.workload in DECODE else run_ctc_head)(args)
         return
     if args.workload != "c5":
         if args.impl == "reference" or int(os.environ.get("WORLD_SIZE", "1")) > 1:
