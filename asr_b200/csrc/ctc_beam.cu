@@ -1,0 +1,296 @@
+// CTC prefix beam search on the GPU: one CTA per utterance. Replaces the
+// reference's CPU op asr::beam_decode (src/asr/decode/csrc/ctc.cpp:46-137, a trie
+// of prefixes and a hash map of next-beam entries per frame, OpenMP over the
+// batch) with the same search:
+//   for every frame t < in_len, every beam entry (prefix, p_blank, p_nonblank)
+//   and every token v: v = blank keeps the prefix (p_blank += total + lp[v]); v =
+//   the prefix's last token keeps the prefix from p_nonblank and extends it from
+//   p_blank; any other v extends it from total; the beam_width candidates of
+//   highest total = p_blank (+) p_nonblank survive (+ = logaddexp, float32).
+//
+// Per frame, on the CTA:
+//   1. the frame's top (W + 1) non-blank tokens by log-prob (a bitonic sort of the
+//      row in shared memory). Only extensions by these tokens can survive: every
+//      other extension of an entry is beaten by at least W extensions of the same
+//      entry (same base score, larger log-prob, distinct prefixes), so the search
+//      keeps exactly the reference's candidates while scoring W (W + 2) of them
+//      instead of W x V;
+//   2. "stay" candidates (an entry keeping its prefix). A prefix reachable both by
+//      staying and by extending its parent (also in the beam) is one candidate:
+//      the parent's extension score is added into the stay, and the duplicate
+//      extension is dropped. Prefix identity uses a 64-bit polynomial hash of the
+//      token sequence plus its length, so prefixes that left the beam and came
+//      back still merge (the reference's trie nodes give the same identity);
+//   3. the W best candidates (a bitonic sort of their scores); new prefixes get a
+//      node (parent, token) in the utterance's node pool for the final backtrack.
+// Ties between equal scores resolve by candidate order (the reference's
+// nth_element leaves them unspecified).
+#include <algorithm>
+#include <climits>
+
+#include "common.cuh"
+
+namespace asr {
+namespace {
+
+constexpr int kBeamThreads = 256;
+constexpr int kMaxBeam = 64;
+constexpr int kMaxBeamVocab = 8192;
+constexpr unsigned long long kHashMul = 0x100000001B3ull;  // odd multiplier of the prefix hash
+
+// logaddexp as the reference computes it (ctc.cpp:28-34), in float32.
+__device__ __forceinline__ float lae_ref(float a, float b) {
+    if (a == -INFINITY) return b;
+    if (b == -INFINITY) return a;
+    const float hi = fmaxf(a, b), lo = fminf(a, b);
+    return hi + log1pf(expf(lo - hi));
+}
+
+// a sorts before b: valid entries (val >= 0) first, then larger key, then smaller val.
+__device__ __forceinline__ bool before(float ka, int va, float kb, int vb) {
+    if ((va >= 0) != (vb >= 0)) return va >= 0;
+    if (ka != kb) return ka > kb;
+    return va < vb;
+}
+
+// Bitonic sort of (key, val) pairs in shared memory, N a power of two, into
+// `before` order. Ends with a barrier.
+__device__ void bitonic(float* key, int* val, int N) {
+    for (int k = 2; k <= N; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < N; i += blockDim.x) {
+                const int p = i ^ j;
+                if (p > i) {
+                    const bool fwd = (i & k) == 0;
+                    const bool sw = fwd ? before(key[p], val[p], key[i], val[i]) : before(key[i], val[i], key[p], val[p]);
+                    if (sw) {
+                        const float tk = key[i];
+                        key[i] = key[p];
+                        key[p] = tk;
+                        const int tv = val[i];
+                        val[i] = val[p];
+                        val[p] = tv;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+struct Beam {
+    int node[kMaxBeam], len[kMaxBeam], last[kMaxBeam];
+    float pb[kMaxBeam], pnb[kMaxBeam];
+    unsigned long long hash[kMaxBeam];
+};
+
+__global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __restrict__ lp,
+                                                               const int32_t* __restrict__ in_lens, int T, int V,
+                                                               int W, int NT, int NC, int32_t* __restrict__ pool_par,
+                                                               int32_t* __restrict__ pool_tok, int64_t pool_cap,
+                                                               int32_t* __restrict__ out_tokens,
+                                                               int32_t* __restrict__ out_len) {
+    extern __shared__ __align__(16) unsigned char beam_smem[];
+    float* tkey = reinterpret_cast<float*>(beam_smem);  // NT: frame log-probs of tokens 1..V-1
+    int* tval = reinterpret_cast<int*>(tkey + NT);
+    float* ckey = reinterpret_cast<float*>(tval + NT);  // NC: candidate scores
+    int* cval = reinterpret_cast<int*>(ckey + NC);
+    __shared__ Beam bs[2];
+    __shared__ float spb[kMaxBeam], spnb[kMaxBeam];  // stay candidates (merged)
+    __shared__ int mpar[kMaxBeam], mpos[kMaxBeam];   // parent entry in the beam, its top-token slot
+    __shared__ int toks[kMaxBeam + 1];
+    __shared__ float tlp[kMaxBeam + 1];
+    __shared__ int s_n, s_cur, s_next;
+
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const int Tb = min(max(in_lens[b], 0), T);
+    int32_t* par = pool_par + (int64_t)b * pool_cap;
+    int32_t* tokp = pool_tok + (int64_t)b * pool_cap;
+    if (tid == 0) {
+        Beam& c = bs[0];
+        c.node[0] = 0;
+        c.len[0] = 0;
+        c.last[0] = -1;
+        c.pb[0] = 0.f;
+        c.pnb[0] = -INFINITY;
+        c.hash[0] = 0ull;
+        par[0] = -1;
+        tokp[0] = -1;
+        s_n = 1;
+        s_cur = 0;
+        s_next = 1;
+    }
+    __syncthreads();
+    const int ntop = min(W + 1, V - 1);
+    const int per = ntop + 1;  // candidates per entry: the stay, then one per top token
+
+    for (int t = 0; t < Tb; ++t) {
+        const float* row = lp + ((int64_t)b * T + t) * V;
+        const int cur = s_cur, n = s_n;
+        const Beam& c = bs[cur];
+        Beam& nx = bs[cur ^ 1];
+        // 1. the frame's top non-blank tokens
+        for (int i = tid; i < NT; i += blockDim.x) {
+            const int v = i + 1;
+            tkey[i] = v < V ? __ldg(row + v) : -INFINITY;
+            tval[i] = v < V ? v : -1;
+        }
+        __syncthreads();
+        bitonic(tkey, tval, NT);
+        if (tid < ntop) {
+            toks[tid] = tval[tid];
+            tlp[tid] = tkey[tid];
+        }
+        __syncthreads();
+        // 2. stay candidates, with the parent's extension merged in
+        if (tid < n) {
+            const int e = tid, last = c.last[e];
+            float pnb = last >= 0 ? c.pnb[e] + __ldg(row + last) : -INFINITY;
+            int pe = -1, pos = -1;
+            if (c.len[e] > 0) {
+                for (int q = 0; q < n; ++q)
+                    if (c.len[q] + 1 == c.len[e] && c.hash[q] * kHashMul + (unsigned long long)(last + 1) == c.hash[e]) {
+                        pe = q;
+                        break;
+                    }
+            }
+            if (pe >= 0) {
+                const float base = last == c.last[pe] ? c.pb[pe] : lae_ref(c.pb[pe], c.pnb[pe]);
+                pnb = lae_ref(pnb, base + __ldg(row + last));
+                for (int j = 0; j < ntop; ++j)
+                    if (toks[j] == last) {
+                        pos = j;
+                        break;
+                    }
+            }
+            spb[e] = lae_ref(c.pb[e], c.pnb[e]) + __ldg(row);
+            spnb[e] = pnb;
+            mpar[e] = pe;
+            mpos[e] = pos;
+        }
+        __syncthreads();
+        // 3. candidate scores
+        const int nc = n * per;
+        for (int i = tid; i < NC; i += blockDim.x) {
+            float key = -INFINITY;
+            int val = -1;
+            if (i < nc) {
+                const int e = i / per, j = i - e * per;
+                if (j == 0) {
+                    key = lae_ref(spb[e], spnb[e]);
+                    val = i;
+                } else {
+                    bool merged = false;
+                    for (int q = 0; q < n; ++q)
+                        if (mpar[q] == e && mpos[q] == j - 1) {
+                            merged = true;
+                            break;
+                        }
+                    if (!merged) {
+                        const int v = toks[j - 1];
+                        const float base = v == c.last[e] ? c.pb[e] : lae_ref(c.pb[e], c.pnb[e]);
+                        key = base + tlp[j - 1];
+                        val = i;
+                    }
+                }
+            }
+            ckey[i] = key;
+            cval[i] = val;
+        }
+        __syncthreads();
+        bitonic(ckey, cval, NC);
+        // 4. the next beam (W entries at most; new prefixes get pool nodes)
+        if (tid == 0) {
+            int k = 0, node = s_next;
+            for (; k < W && k < NC && cval[k] >= 0; ++k) {
+                const int i = cval[k], e = i / per, j = i - e * per;
+                if (j == 0) {
+                    nx.node[k] = c.node[e];
+                    nx.len[k] = c.len[e];
+                    nx.last[k] = c.last[e];
+                    nx.pb[k] = spb[e];
+                    nx.pnb[k] = spnb[e];
+                    nx.hash[k] = c.hash[e];
+                } else {
+                    const int v = toks[j - 1];
+                    par[node] = c.node[e];
+                    tokp[node] = v;
+                    nx.node[k] = node++;
+                    nx.len[k] = c.len[e] + 1;
+                    nx.last[k] = v;
+                    nx.pb[k] = -INFINITY;
+                    nx.pnb[k] = ckey[k];
+                    nx.hash[k] = c.hash[e] * kHashMul + (unsigned long long)(v + 1);
+                }
+            }
+            s_n = k;
+            s_next = node;
+            s_cur = cur ^ 1;
+        }
+        __syncthreads();
+    }
+    // 5. the best surviving prefix, backtracked through the node pool
+    if (tid == 0) {
+        const Beam& c = bs[s_cur];
+        int best = 0;
+        float bt = lae_ref(c.pb[0], c.pnb[0]);
+        for (int e = 1; e < s_n; ++e) {
+            const float x = lae_ref(c.pb[e], c.pnb[e]);
+            if (x > bt) {
+                bt = x;
+                best = e;
+            }
+        }
+        const int L = c.len[best];
+        int node = c.node[best];
+        out_len[b] = L;
+        for (int i = L - 1; i >= 0; --i) {
+            out_tokens[(int64_t)b * T + i] = tokp[node];
+            node = par[node];
+        }
+    }
+}
+
+int pow2_at_least(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+}  // namespace
+}  // namespace asr
+
+using namespace asr;
+
+extern "C" size_t asr_ctc_beam_workspace_bytes(int B, int T, int beam_width) {
+    if (B < 0 || T < 0 || beam_width < 1 || beam_width > kMaxBeam) return 0;
+    return sizeof(int32_t) * 2 * (size_t)B * (1 + (size_t)T * beam_width) + 256;
+}
+
+extern "C" int asr_ctc_beam_decode(const float* log_probs, const int32_t* in_lens, int B, int T, int V,
+                                   int beam_width, int32_t* tokens, int32_t* lengths, void* workspace,
+                                   size_t workspace_bytes, asr_stream_t stream) {
+    if (B < 0 || T < 0 || V < 1 || beam_width < 1) return ASR_ERR_INVALID_ARGUMENT;
+    if (B == 0) return ASR_OK;
+    if (!log_probs || !in_lens || !tokens || !lengths) return ASR_ERR_INVALID_ARGUMENT;
+    if (beam_width > kMaxBeam || V > kMaxBeamVocab) return ASR_ERR_UNSUPPORTED;
+    if (!workspace || workspace_bytes < asr_ctc_beam_workspace_bytes(B, T, beam_width)) return ASR_ERR_WORKSPACE;
+    const int ntop = std::min(beam_width + 1, V - 1);
+    const int NT = pow2_at_least(std::max(V - 1, 1));
+    const int NC = pow2_at_least(beam_width * (ntop + 1));
+    const int64_t cap = 1 + (int64_t)T * beam_width;
+    auto* base = reinterpret_cast<int32_t*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+    const size_t smem = sizeof(float) * 2 * (size_t)(NT + NC);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (smem > 48 * 1024)
+        ASR_CUDA_TRY(cudaFuncSetAttribute(ctc_beam_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (T == 0) {
+        ASR_CUDA_TRY(cudaMemsetAsync(lengths, 0, sizeof(int32_t) * B, st));
+        return ASR_OK;
+    }
+    KernelTimer kt("ctc_beam", st);
+    ctc_beam_kernel<<<B, kBeamThreads, smem, st>>>(log_probs, in_lens, T, V, beam_width, NT, NC, base,
+                                                   base + (size_t)B * cap, cap, tokens, lengths);
+    ASR_LAUNCH_CHECK();
+    return ASR_OK;
+}

@@ -228,6 +228,21 @@ int asr_ctc_head_backward(const void* encoder, int act_dtype, const float* rms_w
                           const float* grad_loss, void* grad_encoder, float* grad_rms_weight, float* grad_weight,
                           float* grad_bias, void* workspace, size_t workspace_bytes, asr_stream_t stream);
 
+/* --------------------------------------------------- CTC prefix beam search */
+
+/* Replaces the reference's CPU op asr::beam_decode (src/asr/decode/csrc/ctc.cpp:46-137;
+ * called by src/asr/decode/ctc.py:34-40 beam_decode): prefix beam search over
+ * log_probs (B, T, V) float32 on the device, blank = 0, frames t < in_lens[b]
+ * (clamped to [0, T]). Writes the best prefix of each utterance to tokens (B, T)
+ * int32 (row b holds lengths[b] tokens) and lengths (B,). Same search as the
+ * reference: ties between equal scores may resolve differently (the reference's
+ * nth_element leaves them unspecified). 1 <= beam_width <= 64 and V <= 8192, else
+ * ASR_ERR_UNSUPPORTED. Workspace: asr_ctc_beam_workspace_bytes. */
+size_t asr_ctc_beam_workspace_bytes(int B, int T, int beam_width);
+int asr_ctc_beam_decode(const float* log_probs, const int32_t* in_lens, int B, int T, int V, int beam_width,
+                        int32_t* tokens, int32_t* lengths, void* workspace, size_t workspace_bytes,
+                        asr_stream_t stream);
+
 /* ------------------------------------------------ greedy transducer decoding */
 
 /* Batched greedy decoding for RNN-T and TDT. Replaces the per-utterance,
