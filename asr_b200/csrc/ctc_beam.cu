@@ -9,8 +9,8 @@
 //   highest total = p_blank (+) p_nonblank survive (+ = logaddexp, float32).
 //
 // Per frame, on the CTA:
-//   1. the frame's top (W + 1) non-blank tokens by log-prob (a bitonic sort of the
-//      row in shared memory). Only extensions by these tokens can survive: every
+//   1. the frame's top (W + 1) non-blank tokens by log-prob (a block-wide radix
+//      select over the row in shared memory). Only extensions by these tokens can survive: every
 //      other extension of an entry is beaten by at least W extensions of the same
 //      entry (same base score, larger log-prob, distinct prefixes), so the search
 //      keeps exactly the reference's candidates while scoring W (W + 2) of them
@@ -21,7 +21,7 @@
 //      extension is dropped. Prefix identity uses a 64-bit polynomial hash of the
 //      token sequence plus its length, so prefixes that left the beam and came
 //      back still merge (the reference's trie nodes give the same identity);
-//   3. the W best candidates (a bitonic sort of their scores); new prefixes get a
+//   3. the W best candidates (the same radix select); new prefixes get a
 //      node (parent, token) in the utterance's node pool for the final backtrack.
 // Ties between equal scores resolve by candidate order (the reference's
 // nth_element leaves them unspecified).
@@ -78,6 +78,140 @@ __device__ void bitonic(float* key, int* val, int N) {
     }
 }
 
+// Order-preserving image of a float score (larger float -> larger unsigned).
+__device__ __forceinline__ unsigned key_bits(float x) {
+    const unsigned u = __float_as_uint(x);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// The K first pairs in `before` order of the n (key, val) pairs in shared memory
+// (val < 0 marks an invalid pair), written sorted to okey / oval; returns how many
+// (min(K, valid pairs)). A radix select on key_bits, one 8-bit digit per pass
+// (four passes at most), finds the K-th score; pairs above it are taken, pairs
+// equal to it in index order; then the <= kSelMax winners are bitonic-sorted.
+// All threads call it; it ends with a barrier.
+constexpr int kSelMax = 128;
+
+struct SelScratch {
+    int hist[256];
+    int warp_cnt[kBeamThreads / 32];
+    int digit, above, n_valid, n_out, n_tie_base;
+};
+
+__device__ int block_topk(const float* key, const int* val, int n, int K, float* okey, int* oval, SelScratch& sc) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // valid pairs
+    int cnt = 0;
+    for (int i = tid; i < n; i += blockDim.x) cnt += val[i] >= 0;
+    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (lane == 0) sc.warp_cnt[warp] = cnt;
+    __syncthreads();
+    if (tid == 0) {
+        int t = 0;
+        for (int w = 0; w < kBeamThreads / 32; ++w) t += sc.warp_cnt[w];
+        sc.n_valid = t;
+        sc.n_out = 0;
+    }
+    __syncthreads();
+    const int nv = sc.n_valid;
+    const int k = min(K, nv);
+    unsigned prefix = 0u, mask = 0u;
+    int need = k;  // pairs still to take among those matching prefix
+    bool all = k == nv;
+    if (!all) {
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int i = tid; i < 256; i += blockDim.x) sc.hist[i] = 0;
+            __syncthreads();
+            for (int i = tid; i < n; i += blockDim.x) {
+                if (val[i] < 0) continue;
+                const unsigned u = key_bits(key[i]);
+                if ((u & mask) == prefix) atomicAdd(&sc.hist[(u >> shift) & 255u], 1);
+            }
+            __syncthreads();
+            if (warp == 0) {  // digit d: count(digits > d) < need <= count(digits >= d)
+                int c[8], sum = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    c[q] = sc.hist[255 - (lane * 8 + q)];  // lane 0 holds the highest digits
+                    sum += c[q];
+                }
+                int incl = sum;  // inclusive scan over lanes (from the highest digits)
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                int run = incl - sum;  // count of digits above this lane's block
+                int found = -1, above = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    if (found < 0 && run + c[q] >= need) {
+                        found = 255 - (lane * 8 + q);
+                        above = run;
+                    }
+                    run += c[q];
+                }
+                const unsigned hit = __ballot_sync(0xffffffffu, found >= 0);
+                const int src = __ffs(hit) - 1;
+                const int d = __shfl_sync(0xffffffffu, found, src);
+                const int ab = __shfl_sync(0xffffffffu, above, src);
+                if (lane == 0) {
+                    sc.digit = d;
+                    sc.above = ab;
+                }
+            }
+            __syncthreads();
+            prefix |= (unsigned)sc.digit << shift;
+            mask |= 255u << shift;
+            need -= sc.above;
+            __syncthreads();
+        }
+    }
+    // gather: everything strictly above the threshold (any order), then `need` ties in index order
+    for (int i = tid; i < n; i += blockDim.x) {
+        if (val[i] < 0) continue;
+        if (all || key_bits(key[i]) > prefix) {
+            const int slot = atomicAdd(&sc.n_out, 1);
+            okey[slot] = key[i];
+            oval[slot] = val[i];
+        }
+    }
+    __syncthreads();
+    if (!all && need > 0) {
+        const int base = sc.n_out;
+        int taken = 0;  // ties taken by earlier passes over the array
+        for (int i0 = 0; i0 < n && taken < need; i0 += blockDim.x) {
+            const int i = i0 + tid;
+            const bool tie = i < n && val[i] >= 0 && key_bits(key[i]) == prefix;
+            const unsigned bal = __ballot_sync(0xffffffffu, tie);
+            if (lane == 0) sc.warp_cnt[warp] = __popc(bal);
+            __syncthreads();
+            int before_w = 0, total = 0;
+            for (int w = 0; w < kBeamThreads / 32; ++w) {
+                if (w < warp) before_w += sc.warp_cnt[w];
+                total += sc.warp_cnt[w];
+            }
+            const int rank = taken + before_w + __popc(bal & ((1u << lane) - 1u));
+            if (tie && rank < need) {
+                okey[base + rank] = key[i];
+                oval[base + rank] = val[i];
+            }
+            taken += total;
+            __syncthreads();
+        }
+    }
+    // sort the k winners (k <= kSelMax) into `before` order
+    int N = 1;
+    while (N < k) N <<= 1;
+    for (int i = k + tid; i < N; i += blockDim.x) {
+        okey[i] = -INFINITY;
+        oval[i] = -1;
+    }
+    __syncthreads();
+    bitonic(okey, oval, N);
+    return k;
+}
+
 struct Beam {
     int node[kMaxBeam], len[kMaxBeam], last[kMaxBeam];
     float pb[kMaxBeam], pnb[kMaxBeam];
@@ -95,6 +229,9 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
     int* tval = reinterpret_cast<int*>(tkey + NT);
     float* ckey = reinterpret_cast<float*>(tval + NT);  // NC: candidate scores
     int* cval = reinterpret_cast<int*>(ckey + NC);
+    __shared__ float skey[kSelMax];  // selected (sorted) top tokens / candidates
+    __shared__ int sval[kSelMax];
+    __shared__ SelScratch sc;
     __shared__ Beam bs[2];
     __shared__ float spb[kMaxBeam], spnb[kMaxBeam];  // stay candidates (merged)
     __shared__ int mpar[kMaxBeam], mpos[kMaxBeam];   // parent entry in the beam, its top-token slot
@@ -130,16 +267,15 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
         const Beam& c = bs[cur];
         Beam& nx = bs[cur ^ 1];
         // 1. the frame's top non-blank tokens
-        for (int i = tid; i < NT; i += blockDim.x) {
-            const int v = i + 1;
-            tkey[i] = v < V ? __ldg(row + v) : -INFINITY;
-            tval[i] = v < V ? v : -1;
+        for (int i = tid; i < V - 1; i += blockDim.x) {
+            tkey[i] = __ldg(row + i + 1);
+            tval[i] = i + 1;
         }
         __syncthreads();
-        bitonic(tkey, tval, NT);
+        block_topk(tkey, tval, V - 1, ntop, skey, sval, sc);
         if (tid < ntop) {
-            toks[tid] = tval[tid];
-            tlp[tid] = tkey[tid];
+            toks[tid] = sval[tid];
+            tlp[tid] = skey[tid];
         }
         __syncthreads();
         // 2. stay candidates, with the parent's extension merged in
@@ -171,7 +307,7 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
         __syncthreads();
         // 3. candidate scores
         const int nc = n * per;
-        for (int i = tid; i < NC; i += blockDim.x) {
+        for (int i = tid; i < nc; i += blockDim.x) {
             float key = -INFINITY;
             int val = -1;
             if (i < nc) {
@@ -198,12 +334,12 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
             cval[i] = val;
         }
         __syncthreads();
-        bitonic(ckey, cval, NC);
+        const int keep = block_topk(ckey, cval, nc, W, skey, sval, sc);
         // 4. the next beam (W entries at most; new prefixes get pool nodes)
         if (tid == 0) {
             int k = 0, node = s_next;
-            for (; k < W && k < NC && cval[k] >= 0; ++k) {
-                const int i = cval[k], e = i / per, j = i - e * per;
+            for (; k < keep; ++k) {
+                const int i = sval[k], e = i / per, j = i - e * per;
                 if (j == 0) {
                     nx.node[k] = c.node[e];
                     nx.len[k] = c.len[e];
@@ -219,7 +355,7 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
                     nx.len[k] = c.len[e] + 1;
                     nx.last[k] = v;
                     nx.pb[k] = -INFINITY;
-                    nx.pnb[k] = ckey[k];
+                    nx.pnb[k] = skey[k];
                     nx.hash[k] = c.hash[e] * kHashMul + (unsigned long long)(v + 1);
                 }
             }
@@ -251,12 +387,6 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
     }
 }
 
-int pow2_at_least(int x) {
-    int p = 1;
-    while (p < x) p <<= 1;
-    return p;
-}
-
 }  // namespace
 }  // namespace asr
 
@@ -276,8 +406,8 @@ extern "C" int asr_ctc_beam_decode(const float* log_probs, const int32_t* in_len
     if (beam_width > kMaxBeam || V > kMaxBeamVocab) return ASR_ERR_UNSUPPORTED;
     if (!workspace || workspace_bytes < asr_ctc_beam_workspace_bytes(B, T, beam_width)) return ASR_ERR_WORKSPACE;
     const int ntop = std::min(beam_width + 1, V - 1);
-    const int NT = pow2_at_least(std::max(V - 1, 1));
-    const int NC = pow2_at_least(beam_width * (ntop + 1));
+    const int NT = std::max(V - 1, 1);
+    const int NC = beam_width * (ntop + 1);
     const int64_t cap = 1 + (int64_t)T * beam_width;
     auto* base = reinterpret_cast<int32_t*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
     const size_t smem = sizeof(float) * 2 * (size_t)(NT + NC);

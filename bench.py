@@ -863,6 +863,139 @@ def run_ctc_head(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------ CTC prefix beam search
+#
+# `--workload ctc-beam` times CTC prefix beam search (asr_b200.decode.ctc.
+# beam_decode, beam 32 as the reference's default) on one GPU over log-probs of
+# B = 64 utterances, T ~ U[200, 500] frames, V = 1024 (BPE): log_softmax of
+# N(0, 4^2) logits with the blank raised by 6, peaked frames as a trained model
+# gives. The CPU baseline / reference arm is the reference's own op
+# (src/asr/decode/csrc/ctc.cpp) compiled into oracle/_ref by `make -C oracle ref`
+# (without OpenMP, so one thread; its own build parallelises over the batch).
+
+CTC_BEAM = {"name": "ctc_beam_bpe1024", "B": 64, "T": (200, 500), "V": 1024, "beam": 32}
+
+
+def ctc_beam_inputs(cfg, seed=SEED):
+    import torch
+
+    rng = np.random.default_rng([seed, 71])
+    il = rng.integers(cfg["T"][0], cfg["T"][1] + 1, size=cfg["B"]).astype(np.int32)
+    logits = rng.standard_normal((cfg["B"], int(il.max()), cfg["V"]), dtype=np.float32) * 4.0
+    logits[..., 0] += 6.0
+    return {"log_probs": torch.log_softmax(torch.from_numpy(logits), -1).numpy(), "in_lens": il}
+
+
+def run_ctc_beam(args):
+    import ctypes
+
+    import torch
+
+    from asr_b200 import _lib
+    from asr_b200.decode import ctc as ctc_dec
+    from oracle import ctc_beam as ref_beam
+
+    cfg = CTC_BEAM
+    host = ctc_beam_inputs(cfg)
+    B, W = cfg["B"], cfg["beam"]
+    sample = 2
+
+    def cpu_ref():
+        if not ref_beam.reference_available():
+            return None
+        lp, il = host["log_probs"][:sample], host["in_lens"][:sample]
+        ref_beam.reference_beam_decode(lp[:, :20], il * 0 + 20, W)  # load + warm
+        t0 = time.perf_counter()
+        out = ref_beam.reference_beam_decode(lp, il, W)
+        return sample / (time.perf_counter() - t0), out
+
+    if args.impl == "reference":
+        r = cpu_ref()
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable": "reference beam-search op not built into "
+                              "oracle/_ref (make -C oracle ref REF=<reference checkout>)"}), flush=True)
+            return
+        base = {"value": round(r[0], 4), "unit": "utterances/s", "cores": 1, "kind": "reference",
+                "sample": f"utterances 0..{sample - 1}, the reference op built without OpenMP (one thread)"}
+        print(json.dumps({"impl": "reference", "metric": "CTC beam decode utterances/s", "value": base["value"],
+                          "unit": "utterances/s", "n_gpus": 1, "steps": 1, "warmup": 1, "higher_is_better": True,
+                          "dtype": "f32", "data": "synthetic", "config": {"workload": cfg["name"], "beam": W},
+                          "cpu_baseline": base, "e2e": {"value": base["value"], "unit": "utterances/s",
+                                                         "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return
+
+    dev = torch.device("cuda", 0)
+    lp = torch.tensor(host["log_probs"], device=dev)
+    il = torch.tensor(host["in_lens"], device=dev)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    out = {}
+
+    def timed(run, k):
+        times = []
+        for _ in range(k):
+            flush.fill_(1)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            run()
+            s1.record(stream)
+            times.append((s0, s1))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in times) / k
+
+    for _ in range(args.warmup):
+        out["h"] = ctc_dec.beam_decode(lp, il, W)
+    torch.cuda.synchronize()
+    lib = _lib.capi()
+    lib.asr_profiler_report(None, 0, 1)
+    clocks = ClockSampler(args.clocks_log)
+    clocks.start()
+    time.sleep(0.3)
+    lib.asr_profiler_enable(1)
+    ms = timed(lambda: out.__setitem__("h", ctc_dec.beam_decode(lp, il, W)), args.steps)
+    lib.asr_profiler_enable(0)
+    clock_info = clocks.stop()
+    n = lib.asr_profiler_report(None, 0, 0)
+    buf = ctypes.create_string_buffer(max(n, 0) + 1)
+    lib.asr_profiler_report(buf, len(buf), 1)
+    prof = parse_profile(buf.value.decode())
+    pinned = torch.from_numpy(host["log_probs"]).pin_memory()
+    e2e_ms = timed(lambda: ctc_dec.beam_decode(pinned.to(dev, non_blocking=True), il, W), args.steps)
+    frames = int(host["in_lens"].sum())
+    kms = prof.get("ctc_beam", (0, 0.0))[1] / args.steps
+    bytes_read = frames * cfg["V"] * 4.0
+    peaks = measured_peaks()
+    ach = bytes_read / (kms / 1000.0) / 1e9 if kms else None
+    roof = {"kernel": "ctc_beam", "bound": "hbm", "achieved": round(ach, 2) if ach else None,
+            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(ach / peaks["hbm_gbs"], 5) if ach else None,
+            "traffic": None, "work": "the log-prob rows read once (frames x V x 4 bytes)",
+            "note": "latency-bound: two block-wide bitonic sorts per frame and utterance"}
+    cpu = None
+    r = None if args.no_cpu_baseline else cpu_ref()
+    agree = None
+    if r is not None:
+        cpu = {"value": round(r[0], 4), "unit": "utterances/s", "cores": 1, "kind": "reference",
+               "sample": f"utterances 0..{sample - 1}: the reference op (oracle/_ref, one thread)"}
+        agree = r[1] == out["h"][:sample]
+    kernels = {k: {"launches_per_step": v[0] / args.steps, "ms_per_step": round(v[1] / args.steps, 4)}
+               for k, v in prof.items()}
+    line = {
+        "metric": "CTC beam decode utterances/s", "value": round(B / (ms / 1000.0), 3), "unit": "utterances/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["name"], "batch": B, "T": list(cfg["T"]), "vocab": cfg["V"], "beam": W,
+                   "frames": frames, "l2": "flushed between timed steps (256 MB write)",
+                   "sample_matches_reference": agree},
+        "roofline": roof, "cpu_baseline": cpu,
+        "e2e": {"value": round(B / (e2e_ms / 1000.0), 3), "unit": "utterances/s",
+                "h2d_bytes_per_step": int(pinned.numel() * 4), "d2h_bytes_per_step": int(B * (lp.shape[1] + 1) * 4),
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": int(sum(v[0] for v in prof.values()) / args.steps), "kernels": kernels, "clocks": clock_info,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -876,15 +1009,17 @@ def main():
                     help="profiling aid: run only the first BATCH utterances of the workload")
     ap.add_argument("--act-dtype", default="f32", choices=["f32", "bf16"],
                     help="encoder / decoder activation dtype (bf16: a system's autocast activations, no float32 copies)")
-    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5", *DECODE, "ctc-head"],
+    ap.add_argument("--workload", default="c5",
+                    choices=["c1", "c2", "c3", "c4", "c5", *DECODE, "ctc-head", "ctc-beam"],
                     help="c5 (default): the headline config-5 workload; c1..c4: the other BASELINE configs, 1 GPU; "
-                         "decode-tdt / decode-rnnt: batched greedy decoding, 1 GPU; ctc-head: the fused CTC head")
+                         "decode-tdt / decode-rnnt: batched greedy decoding; ctc-head: the fused CTC head; "
+                         "ctc-beam: CTC prefix beam search (1 GPU each)")
     ap.add_argument("--decode-predict", default="last-token", choices=["last-token", "per-utterance", "batched"])
     args = ap.parse_args()
-    if args.workload in DECODE or args.workload == "ctc-head":
+    if args.workload in DECODE or args.workload in ("ctc-head", "ctc-beam"):
         if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-            raise SystemExit("--workload decode-* / ctc-head runs on one GPU")
-        (run_decode if args.workload in DECODE else run_ctc_head)(args)
+            raise SystemExit("--workload decode-* / ctc-head / ctc-beam runs on one GPU")
+        {"ctc-head": run_ctc_head, "ctc-beam": run_ctc_beam}.get(args.workload, run_decode)(args)
         return
     if args.workload != "c5":
         if args.impl == "reference" or int(os.environ.get("WORLD_SIZE", "1")) > 1:
