@@ -1,19 +1,19 @@
 // CTC forward (alpha) and backward (beta fused with d loss / d logits).
 //
-// One warp per utterance. The 2S+1 extended-label states are split into
-// lane-contiguous blocks of KS states held in registers; the stay / advance /
-// skip moves (ctc.cu:84-98 of the reference) need the two states just left of a
-// block, which come from the neighbouring lane by shuffle. Each time step is
-// therefore a handful of register ops plus two shuffles, with the next step's
-// emission log-probs prefetched while the current step computes.
-// The backward scatters state posteriors into a per-warp shared-memory row of
-// V bins (no global atomics, deterministic) and writes each gradient row once.
+// One CTA of up to 8 warps per utterance: the 2S+1 extended-label states are
+// split into thread-contiguous blocks of KS (about two) states held in
+// registers. The stay / advance / skip moves (ctc.cu:84-98 of the reference)
+// need the two states just left of a block (right, for beta): inside a warp they
+// come by shuffle, across warps through shared memory, so a time step is a few
+// register ops, two shuffles and one (alpha) or two (beta) CTA barriers, with the
+// next step's emission log-probs (and, for beta, alpha) prefetched meanwhile.
+// The backward scatters state posteriors into a shared-memory row of V bins
+// (the blank states' mass summed per warp first) and writes each gradient row
+// once.
 #include "common.cuh"
 
 namespace asr {
 namespace {
-
-constexpr int kCtcWarps = 4;  // utterances per block
 
 // log(exp(a) + exp(b) + exp(c)) with float64 state and an fp32 correction term.
 __device__ __forceinline__ double lse3_d(double a, double b, double c) {
@@ -34,17 +34,6 @@ __device__ __forceinline__ CtcUtt ctc_utt(const int32_t* in_lens, const int32_t*
     return u;
 }
 
-// Value held by state s = src_lane*KS + j of array a (register-resident), broadcast.
-template <int KS>
-__device__ __forceinline__ double warp_pick(const double (&a)[KS], int s) {
-    const int src = s / KS, jj = s - src * KS;
-    double v = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < KS; ++j)
-        if (j == jj) v = a[j];
-    return __shfl_sync(0xffffffffu, v, src);
-}
-
 // log Z from the last blank and last label state (ctc.cu:106-113).
 __device__ __forceinline__ double ctc_logz(double last, double prev, int L) {
     if (L == 1) return last;
@@ -55,14 +44,20 @@ __device__ __forceinline__ double ctc_logz(double last, double prev, int L) {
 
 // The forward variable is float64: on T ~ 10^2..10^3 frames |alpha| reaches 10^3,
 // where fp32 rounding along the recursion would cost ~1e-3 in the posteriors.
-template <int KS>
-__global__ void __launch_bounds__(32 * kCtcWarps)
+//
+// One CTA of NW warps per utterance, KS consecutive states per thread. The two
+// states left of a warp's first thread (for the stay / advance / skip moves) come
+// from the previous warp through shared memory, double-buffered by step parity so
+// one barrier per step suffices; inside a warp they come by shuffle.
+template <int KS, int NW>
+__global__ void __launch_bounds__(32 * NW)
     ctc_alpha_kernel(const float* __restrict__ lp, const int32_t* __restrict__ targets,
                      const int32_t* __restrict__ in_lens, const int32_t* __restrict__ tgt_lens, int B, int T, int V,
                      int S, double* __restrict__ alpha, float* __restrict__ log_Z) {
-    const int lane = threadIdx.x & 31;
-    const int b = blockIdx.x * kCtcWarps + (threadIdx.x >> 5);
-    if (b >= B) return;
+    __shared__ double bnd[2][NW][2];  // last two states of each warp (previous step)
+    __shared__ double fin[2];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = threadIdx.x;
+    const int b = blockIdx.x;
     const CtcUtt ut = ctc_utt(in_lens, tgt_lens, b, T, S);
     const int Lmax = 2 * S + 1;
     const int32_t* y = targets + (int64_t)b * S;
@@ -73,7 +68,7 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
     bool skip[KS], in[KS];
 #pragma unroll
     for (int j = 0; j < KS; ++j) {
-        const int s = lane * KS + j;
+        const int s = g * KS + j;
         in[j] = s < ut.L;
         const bool odd = s & 1;
         lab[j] = (odd && in[j]) ? y[s >> 1] : 0;
@@ -83,7 +78,7 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
     float nxt[KS];
 #pragma unroll
     for (int j = 0; j < KS; ++j) {
-        const int s = lane * KS + j;
+        const int s = g * KS + j;
         a[j] = (in[j] && s <= 1) ? (double)lpb[lab[j]] : -INFINITY;
         if (in[j]) ab[s] = a[j];
         nxt[j] = (in[j] && ut.Tb > 1) ? lpb[V + lab[j]] : 0.f;
@@ -96,42 +91,58 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
 #pragma unroll
             for (int j = 0; j < KS; ++j) nxt[j] = in[j] ? lpb[(int64_t)(t + 1) * V + lab[j]] : 0.f;
         }
-        // states s-1, s-2 left of this lane's block (previous time step)
+        // publish this warp's last two states, then gather the two states left of each block
+        const double e1 = __shfl_sync(0xffffffffu, a[KS - 1], 31);
+        const double e2 = KS >= 2 ? __shfl_sync(0xffffffffu, a[KS >= 2 ? KS - 2 : 0], 31)
+                                  : __shfl_sync(0xffffffffu, a[0], 30);
+        if (NW > 1 && lane == 0) {
+            bnd[t & 1][warp][0] = e1;
+            bnd[t & 1][warp][1] = e2;
+        }
+        if (NW > 1) __syncthreads();
         double x1 = __shfl_up_sync(0xffffffffu, a[KS - 1], 1);
         double x2 = (KS >= 2) ? __shfl_up_sync(0xffffffffu, a[KS >= 2 ? KS - 2 : 0], 1)
                               : __shfl_up_sync(0xffffffffu, a[0], 2);
-        if (lane == 0) x1 = x2 = -INFINITY;
-        if (KS == 1 && lane == 1) x2 = -INFINITY;
+        const double p1 = (NW > 1 && warp > 0) ? bnd[t & 1][warp > 0 ? warp - 1 : 0][0] : -INFINITY;
+        const double p2 = (NW > 1 && warp > 0) ? bnd[t & 1][warp > 0 ? warp - 1 : 0][1] : -INFINITY;
+        if (lane == 0) {
+            x1 = p1;
+            x2 = p2;
+        }
+        if (KS == 1 && lane == 1) x2 = p1;
         double na[KS];
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
-            const double p1 = (j >= 1) ? a[j >= 1 ? j - 1 : 0] : x1;
-            const double p2 = (j >= 2) ? a[j >= 2 ? j - 2 : 0] : (j == 1 ? x1 : x2);
-            na[j] = in[j] ? lse3_d(a[j], p1, skip[j] ? p2 : -INFINITY) + cur[j] : -INFINITY;
+            const double q1 = (j >= 1) ? a[j >= 1 ? j - 1 : 0] : x1;
+            const double q2 = (j >= 2) ? a[j >= 2 ? j - 2 : 0] : (j == 1 ? x1 : x2);
+            na[j] = in[j] ? lse3_d(a[j], q1, skip[j] ? q2 : -INFINITY) + cur[j] : -INFINITY;
         }
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
             a[j] = na[j];
-            if (in[j]) ab[(int64_t)t * Lmax + lane * KS + j] = a[j];
+            if (in[j]) ab[(int64_t)t * Lmax + g * KS + j] = a[j];
         }
     }
-    const double zl = warp_pick<KS>(a, ut.L - 1);
-    const double zp = (ut.L >= 2) ? warp_pick<KS>(a, ut.L - 2) : -INFINITY;
-    if (lane == 0) log_Z[b] = (float)ctc_logz(zl, zp, ut.L);
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+        const int s = g * KS + j;
+        if (s == ut.L - 1) fin[0] = a[j];
+        if (s == ut.L - 2) fin[1] = a[j];
+    }
+    __syncthreads();
+    if (g == 0) log_Z[b] = (float)ctc_logz(fin[0], ut.L >= 2 ? fin[1] : -INFINITY, ut.L);
 }
 
-template <int KS>
-__global__ void __launch_bounds__(32 * kCtcWarps)
+template <int KS, int NW>
+__global__ void __launch_bounds__(32 * NW)
     ctc_grad_kernel(const double* __restrict__ alpha, const float* __restrict__ lp,
                     const int32_t* __restrict__ targets, const int32_t* __restrict__ in_lens,
                     const int32_t* __restrict__ tgt_lens, const float* __restrict__ grad_loss, int zero_infinity,
                     int post_only, int B, int T, int V, int S, float* __restrict__ grad) {
-    extern __shared__ float smem_rows[];
-    const int lane = threadIdx.x & 31;
-    const int w = threadIdx.x >> 5;
-    const int b = blockIdx.x * kCtcWarps + w;
-    if (b >= B) return;
-    float* row = smem_rows + (int64_t)w * V;
+    extern __shared__ float row[];     // (V,) posterior mass of the current frame per column
+    __shared__ double bnd[2][NW][2];   // first two states of each warp (beta + emission)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = threadIdx.x;
+    const int b = blockIdx.x;
     const CtcUtt ut = ctc_utt(in_lens, tgt_lens, b, T, S);
     const int Lmax = 2 * S + 1;
     const int32_t* y = targets + (int64_t)b * S;
@@ -145,15 +156,15 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
 
     const bool dead = zero_infinity && !isfinite(logZ);
     // rows the recursion never reaches are zero (the reference zero-initialises)
-    for (int64_t i = (int64_t)(dead ? 0 : ut.Tb) * V + lane; i < (int64_t)T * V; i += 32) gb[i] = 0.f;
+    for (int64_t i = (int64_t)(dead ? 0 : ut.Tb) * V + g; i < (int64_t)T * V; i += blockDim.x) gb[i] = 0.f;
     if (dead) return;
-    for (int v = lane; v < V; v += 32) row[v] = 0.f;
+    for (int v = g; v < V; v += blockDim.x) row[v] = 0.f;
 
     int lab[KS];
     bool skip[KS], in[KS];
 #pragma unroll
     for (int j = 0; j < KS; ++j) {
-        const int s = lane * KS + j;
+        const int s = g * KS + j;
         in[j] = s < ut.L;
         const bool odd = s & 1;
         lab[j] = (odd && in[j]) ? y[s >> 1] : 0;
@@ -164,7 +175,7 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
     double be[KS];
 #pragma unroll
     for (int j = 0; j < KS; ++j) {
-        const int s = lane * KS + j;
+        const int s = g * KS + j;
         be[j] = (in[j] && (s == ut.L - 1 || s == ut.L - 2)) ? 0.0 : -INFINITY;
     }
     float lpt[KS];
@@ -172,9 +183,9 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
 #pragma unroll
     for (int j = 0; j < KS; ++j) {
         lpt[j] = in[j] ? lpb[(int64_t)(ut.Tb - 1) * V + lab[j]] : 0.f;
-        acur[j] = in[j] ? ab[(int64_t)(ut.Tb - 1) * Lmax + lane * KS + j] : -INFINITY;
+        acur[j] = in[j] ? ab[(int64_t)(ut.Tb - 1) * Lmax + g * KS + j] : -INFINITY;
     }
-    __syncwarp();
+    __syncthreads();
     for (int t = ut.Tb - 1; t >= 0; --t) {
         // state posteriors scattered to vocabulary bins (ctc.cu:152-165); the blank
         // states (every even s, about half of them) share bin 0, so their mass is
@@ -184,7 +195,7 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
         for (int j = 0; j < KS; ++j) {
             if (in[j]) {
                 const float post = __expf((float)(acur[j] + be[j] - logZ));
-                if ((lane * KS + j) & 1)
+                if ((g * KS + j) & 1)
                     atomicAdd(row + lab[j], post);
                 else
                     pblank += post;
@@ -197,77 +208,87 @@ __global__ void __launch_bounds__(32 * kCtcWarps)
         if (t > 0) {
 #pragma unroll
             for (int j = 0; j < KS; ++j)
-                if (in[j]) acur[j] = ab[(int64_t)(t - 1) * Lmax + lane * KS + j];
+                if (in[j]) acur[j] = ab[(int64_t)(t - 1) * Lmax + g * KS + j];
         }
         float lnx[KS];
 #pragma unroll
         for (int j = 0; j < KS; ++j) lnx[j] = (in[j] && t > 0) ? lpb[(int64_t)(t - 1) * V + lab[j]] : 0.f;
-        __syncwarp();
-        for (int v = lane; v < V; v += 32) {
+        __syncthreads();
+        for (int v = g; v < V; v += blockDim.x) {
             const int64_t idx = (int64_t)t * V + v;
             // post_only: the posterior mass per column only (the fused CTC head adds
             // the softmax part inside its joint kernel)
             gb[idx] = post_only ? gl * row[v] : gl * (__expf(lpb[idx]) - row[v]);
             row[v] = 0.f;
         }
-        __syncwarp();
         if (t == 0) break;
         // beta recursion (ctc.cu:180-204): c[s] = beta[s] + lp[t][lab(s)]
         double c[KS];
 #pragma unroll
         for (int j = 0; j < KS; ++j) c[j] = in[j] ? be[j] + lpt[j] : -INFINITY;
+        const double f1 = __shfl_sync(0xffffffffu, c[0], 0);
+        const double f2 = KS >= 2 ? __shfl_sync(0xffffffffu, c[KS >= 2 ? 1 : 0], 0) : __shfl_sync(0xffffffffu, c[0], 1);
+        if (NW > 1 && lane == 0) {
+            bnd[t & 1][warp][0] = f1;
+            bnd[t & 1][warp][1] = f2;
+        }
+        __syncthreads();  // the next warp's first states published; the row is clear
         double r1 = __shfl_down_sync(0xffffffffu, c[0], 1);
         double r2 = (KS >= 2) ? __shfl_down_sync(0xffffffffu, c[KS >= 2 ? 1 : 0], 1)
                               : __shfl_down_sync(0xffffffffu, c[0], 2);
-        if (lane == 31) r1 = r2 = -INFINITY;
-        if (KS == 1 && lane == 30) r2 = -INFINITY;
+        const double n1 = (NW > 1 && warp + 1 < NW) ? bnd[t & 1][warp + 1 < NW ? warp + 1 : 0][0] : -INFINITY;
+        const double n2 = (NW > 1 && warp + 1 < NW) ? bnd[t & 1][warp + 1 < NW ? warp + 1 : 0][1] : -INFINITY;
+        if (lane == 31) {
+            r1 = n1;
+            r2 = n2;
+        }
+        if (KS == 1 && lane == 30) r2 = n1;
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
-            const double n1 = (j + 1 < KS) ? c[j + 1 < KS ? j + 1 : 0] : r1;
-            const double n2 = (j + 2 < KS) ? c[j + 2 < KS ? j + 2 : 0] : (j + 1 < KS ? r1 : r2);
-            be[j] = in[j] ? lse3_d(c[j], n1, skip[j] ? n2 : -INFINITY) : -INFINITY;
+            const double q1 = (j + 1 < KS) ? c[j + 1 < KS ? j + 1 : 0] : r1;
+            const double q2 = (j + 2 < KS) ? c[j + 2 < KS ? j + 2 : 0] : (j + 1 < KS ? r1 : r2);
+            be[j] = in[j] ? lse3_d(c[j], q1, skip[j] ? q2 : -INFINITY) : -INFINITY;
         }
 #pragma unroll
         for (int j = 0; j < KS; ++j) lpt[j] = lnx[j];
     }
 }
 
-template <int KS>
+template <int KS, int NW>
 int launch_ctc_alpha(const float* lp, const int32_t* tg, const int32_t* il, const int32_t* tl, int B, int T, int V,
                      int S, double* alpha, float* logz, cudaStream_t st) {
-    const int blocks = (B + kCtcWarps - 1) / kCtcWarps;
     KernelTimer kt("ctc_alpha", st);
-    ctc_alpha_kernel<KS><<<blocks, 32 * kCtcWarps, 0, st>>>(lp, tg, il, tl, B, T, V, S, alpha, logz);
+    ctc_alpha_kernel<KS, NW><<<B, 32 * NW, 0, st>>>(lp, tg, il, tl, B, T, V, S, alpha, logz);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
 
-template <int KS>
+template <int KS, int NW>
 int launch_ctc_grad(const double* alpha, const float* lp, const int32_t* tg, const int32_t* il, const int32_t* tl,
                     const float* gl, int zinf, int post_only, int B, int T, int V, int S, float* grad,
                     cudaStream_t st) {
-    const int blocks = (B + kCtcWarps - 1) / kCtcWarps;
-    const size_t smem = sizeof(float) * (size_t)V * kCtcWarps;
+    const size_t smem = sizeof(float) * (size_t)V;
     if (smem > 48 * 1024) {
-        if (cudaFuncSetAttribute(ctc_grad_kernel<KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        if (cudaFuncSetAttribute(ctc_grad_kernel<KS, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
             return ASR_ERR_UNSUPPORTED;
     }
     KernelTimer kt("ctc_beta_grad", st);
-    ctc_grad_kernel<KS><<<blocks, 32 * kCtcWarps, smem, st>>>(alpha, lp, tg, il, tl, gl, zinf, post_only, B, T, V, S,
-                                                             grad);
+    ctc_grad_kernel<KS, NW><<<B, 32 * NW, smem, st>>>(alpha, lp, tg, il, tl, gl, zinf, post_only, B, T, V, S, grad);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
 
-int ctc_ks(int S) {
+// (KS states per thread, NW warps per utterance) for L = 2S + 1 states: about two
+// states per thread, up to 8 warps, then more states per thread.
+int ctc_shape(int S) {
     const int L = 2 * S + 1;
-    if (L <= 32) return 1;
-    if (L <= 64) return 2;
-    if (L <= 128) return 4;
-    if (L <= 256) return 8;
-    if (L <= 512) return 16;
-    if (L <= 1024) return 32;
+    if (L <= 32) return 11;
+    if (L <= 64) return 21;
+    if (L <= 128) return 22;
+    if (L <= 256) return 24;
+    if (L <= 512) return 28;
+    if (L <= 1024) return 48;
     return 0;
 }
 
@@ -283,13 +304,13 @@ extern "C" int asr_ctc_alpha(const float* log_probs, const int32_t* targets, con
     if (B == 0) return ASR_OK;
     if (!log_probs || !in_lens || !tgt_lens || !alpha || !log_Z || (S > 0 && !targets)) return ASR_ERR_INVALID_ARGUMENT;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    switch (ctc_ks(S)) {
-        case 1: return launch_ctc_alpha<1>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
-        case 2: return launch_ctc_alpha<2>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
-        case 4: return launch_ctc_alpha<4>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
-        case 8: return launch_ctc_alpha<8>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
-        case 16: return launch_ctc_alpha<16>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
-        case 32: return launch_ctc_alpha<32>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+    switch (ctc_shape(S)) {
+        case 11: return launch_ctc_alpha<1, 1>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 21: return launch_ctc_alpha<2, 1>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 22: return launch_ctc_alpha<2, 2>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 24: return launch_ctc_alpha<2, 4>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 28: return launch_ctc_alpha<2, 8>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 48: return launch_ctc_alpha<4, 8>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
         default: return ASR_ERR_UNSUPPORTED;
     }
 }
@@ -301,13 +322,13 @@ int ctc_grad_dispatch(const double* alpha, const float* log_probs, const int32_t
                       int V, int S, float* grad, cudaStream_t st) {
     const int z = zero_infinity ? 1 : 0;
     const int p = post_only ? 1 : 0;
-    switch (ctc_ks(S)) {
-        case 1: return launch_ctc_grad<1>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
-        case 2: return launch_ctc_grad<2>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
-        case 4: return launch_ctc_grad<4>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
-        case 8: return launch_ctc_grad<8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
-        case 16: return launch_ctc_grad<16>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
-        case 32: return launch_ctc_grad<32>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+    switch (ctc_shape(S)) {
+        case 11: return launch_ctc_grad<1, 1>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 21: return launch_ctc_grad<2, 1>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 22: return launch_ctc_grad<2, 2>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 24: return launch_ctc_grad<2, 4>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 28: return launch_ctc_grad<2, 8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 48: return launch_ctc_grad<4, 8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
         default: return ASR_ERR_UNSUPPORTED;
     }
 }
