@@ -123,11 +123,14 @@ __global__ void __launch_bounds__(kHeadThreads) label_logits_kernel(
     const int nf = min(kFrameTile, Tb - t0), Kb = __ldg(kb + b), off = __ldg(m.off + b);
     const int32_t* L = labels + (int64_t)b * K;
     frame_rstd(enc, b, T, d, t0, nf, eps, rs);
-    const int f = threadIdx.x % kFrameTile, lg = threadIdx.x / kFrameTile;  // 8 label groups of 16
+    // thread tile: frames fg*4 .. +3 x labels lg*4 .. +3 (8 frame groups x 32 label groups)
+    const int fg = threadIdx.x % 8, lg = threadIdx.x / 8;
     for (int l0 = 0; l0 < Kb; l0 += kLabelBlock) {
-        float acc[16];
+        float acc[4][4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[i][q] = 0.f;
         for (int k0 = 0; k0 < d; k0 += kColChunk) {
             __syncthreads();  // rs ready / previous chunk consumed
             for (int i = threadIdx.x; i < kFrameTile * kColChunk; i += kHeadThreads) {
@@ -145,24 +148,33 @@ __global__ void __launch_bounds__(kHeadThreads) label_logits_kernel(
             __syncthreads();
             const int kn = min(kColChunk, d - k0);
             for (int kk = 0; kk < kn; ++kk) {
-                const float h = hs[f][kk];
+                float h[4], w[4];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) acc[i] = fmaf(h, ws[lg * 16 + i][kk], acc[i]);
+                for (int i = 0; i < 4; ++i) h[i] = hs[fg * 4 + i][kk];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) w[q] = ws[lg * 4 + q][kk];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc[i][q] = fmaf(h[i], w[q], acc[i][q]);
             }
         }
-        if (f < nf) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int f = fg * 4 + i;
+            if (f >= nf) break;
             const int n = off + t0 + f;
             const float l_n = __ldg(lse + n);
             float* e = E + ((int64_t)b * T + t0 + f) * K;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int slot = l0 + lg * 16 + i;
+            for (int q = 0; q < 4; ++q) {
+                const int slot = l0 + lg * 4 + q;
                 if (slot >= Kb) break;
                 if (slot == 0) {
                     e[0] = __ldg(lpb + n);
                 } else {
                     const float bb = bias ? bf16r(__ldg(bias + __ldg(L + slot))) : 0.f;
-                    e[slot] = acc[i] + bb - l_n;
+                    e[slot] = acc[i][q] + bb - l_n;
                 }
             }
         }
@@ -201,8 +213,10 @@ __global__ void __launch_bounds__(kHeadThreads) sparse_bwd_kernel(
     const int b = blockIdx.y, k0 = blockIdx.x * kColChunk;
     const int Tb = __ldg(m.Tb + b), Kb = __ldg(kb + b);
     const int32_t* L = labels + (int64_t)b * K;
-    const int kk = threadIdx.x % kColChunk, half = threadIdx.x / kColChunk;  // 2 halves
-    const int k = k0 + kk;
+    // d hidden tile: frames dfg*4 .. +3 x columns dcg + 32q (q < 4)
+    const int dcg = threadIdx.x % 32, dfg = threadIdx.x / 32;
+    // dW tile: labels wlg*8 .. +7 x columns wcg + 16q (q < 8)
+    const int wcg = threadIdx.x % 16, wlg = threadIdx.x / 16;
     for (int l0 = 0; l0 < Kb; l0 += kLabelBlock) {
         const int nl = min(kLabelBlock, Kb - l0);
         __syncthreads();
@@ -212,9 +226,11 @@ __global__ void __launch_bounds__(kHeadThreads) sparse_bwd_kernel(
             if (l < nl && k0 + c < d) w = bf16r(__ldg(W + (int64_t)__ldg(L + l0 + l) * d + k0 + c));
             ws[l][c] = w;
         }
-        float dwacc[kLabelBlock / 2];  // labels half*64 .. +63 of this block, column k
+        float dwacc[8][8];
 #pragma unroll
-        for (int i = 0; i < kLabelBlock / 2; ++i) dwacc[i] = 0.f;
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dwacc[i][q] = 0.f;
         float dbacc = 0.f;  // thread l < nl of chunk 0: sum over frames of P[., l]
         for (int t0 = 0; t0 < Tb; t0 += kFrameTile) {
             const int nf = min(kFrameTile, Tb - t0);
@@ -233,33 +249,57 @@ __global__ void __launch_bounds__(kHeadThreads) sparse_bwd_kernel(
                 hs[ff][c] = h;
             }
             __syncthreads();
-            // d_hidden: frames half*16 .. +15 at column k
-            if (k < d) {
-                for (int j = 0; j < kFrameTile / 2; ++j) {
-                    const int ff = half * (kFrameTile / 2) + j;
+            // d hidden -= P W_labels
+            {
+                float acc[4][4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc[i][q] = 0.f;
+                for (int l = 0; l < nl; ++l) {
+                    float pv[4], wv[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) pv[i] = ps[dfg * 4 + i][l];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) wv[q] = ws[l][dcg + 32 * q];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) acc[i][q] = fmaf(pv[i], wv[q], acc[i][q]);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int ff = dfg * 4 + i;
                     if (ff >= nf) break;
-                    float s = 0.f;
-                    for (int l = 0; l < nl; ++l) s = fmaf(ps[ff][l], ws[l][kk], s);
-                    float* p = dh + ((int64_t)b * T + t0 + ff) * d + k;
-                    *p -= s;
+                    float* row = dh + ((int64_t)b * T + t0 + ff) * d + k0;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if (k0 + dcg + 32 * q < d) row[dcg + 32 * q] -= acc[i][q];
                 }
             }
-            // dW: labels half*64 .. +63 at column k
-#pragma unroll 4
+            // dW: labels x columns, summed over the frames of the tile
             for (int ff = 0; ff < nf; ++ff) {
-                const float h = hs[ff][kk];
+                float pv[8], hv[8];
 #pragma unroll
-                for (int i = 0; i < kLabelBlock / 2; ++i) dwacc[i] = fmaf(ps[ff][half * (kLabelBlock / 2) + i], h, dwacc[i]);
+                for (int i = 0; i < 8; ++i) pv[i] = ps[ff][wlg * 8 + i];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) hv[q] = hs[ff][wcg + 16 * q];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) dwacc[i][q] = fmaf(pv[i], hv[q], dwacc[i][q]);
             }
             if (blockIdx.x == 0 && threadIdx.x < nl)
                 for (int ff = 0; ff < nf; ++ff) dbacc += ps[ff][threadIdx.x];
         }
-        if (k < d) {
 #pragma unroll
-            for (int i = 0; i < kLabelBlock / 2; ++i) {
-                const int l = half * (kLabelBlock / 2) + i;
-                if (l < nl) atomicAdd(dW + (int64_t)__ldg(L + l0 + l) * d + k, -dwacc[i]);
-            }
+        for (int i = 0; i < 8; ++i) {
+            const int l = wlg * 8 + i;
+            if (l >= nl) break;
+            float* dst = dW + (int64_t)__ldg(L + l0 + l) * d + k0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (k0 + wcg + 16 * q < d) atomicAdd(dst + wcg + 16 * q, -dwacc[i][q]);
         }
         if (dbias && blockIdx.x == 0 && threadIdx.x < nl) atomicAdd(dbias + __ldg(L + l0 + threadIdx.x), -dbacc);
     }
