@@ -52,6 +52,7 @@ constexpr int kMaxScanDim = 2048;  // joint dim limit (shared memory: hidden row
 constexpr int kMaxScanDur = 64;    // duration head width limit
 constexpr int kMaxCluster = 4;
 constexpr int kMaxFrames = 8;
+constexpr int kMaxRows = 2 * kMaxFrames;  // frame rows of a window: up to two utterances x 8 frames
 
 struct ScanArgs {
     const float* enc;      // (B, T, D)
@@ -66,6 +67,7 @@ struct ScanArgs {
     int32_t* report;       // (B,): prefix length after an emission, 0 finished, -1 error
     int B, T, D, V, ldw, n_dur, blank, max_symbols, hyp_cap, dur_cap;
     int max_windows;  // windows one utterance may scan in this launch (0: no limit)
+    int n_active;     // entries of `active`
     int stages;       // weight ring stages (kStageBytes each)
 };
 
@@ -169,46 +171,64 @@ __device__ __forceinline__ void issue_chunk(float* ring, int stages, int chunk, 
     cp_async_commit();
 }
 
-template <int C, int NF>
+template <int C, int NF, int RU>
 __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a) {
+    static_assert(RU == 1 || C == 1, "utterance pairs run without clusters");
     constexpr int CPT = 4 / C;                        // consecutive vocab columns per thread and pass
     constexpr int kPass = CPT * kScanThreads;
+    constexpr int NR = RU * NF;                       // frame rows per window: RU utterances x NF frames
     using R = Ring<CPT>;
     extern __shared__ __align__(16) float smem[];
-    float* ring = smem;                                // per-thread weight stream stages
-    float* hs = smem + (size_t)a.stages * R::kStageFloats;  // (D, NF): hidden rows, frame-minor
-    float* ps = hs + (size_t)a.D * NF;                 // (D,): predictor output
-    __shared__ float red_v[kMaxFrames][kScanWarps];
-    __shared__ int red_i[kMaxFrames][kScanWarps];
-    __shared__ __align__(8) int2 cand[2][kMaxCluster][kMaxFrames];  // (value bits, index) per rank
-    __shared__ float dur_v[kMaxFrames][kMaxScanDur];
-    __shared__ int best_tok[kMaxFrames], best_dur[kMaxFrames];
-    __shared__ int s_t, s_k, s_len, s_steps, s_go;
+    float* ring = smem;                                     // per-thread weight stream stages
+    float* hs = smem + (size_t)a.stages * R::kStageFloats;  // RU x (D, NF): hidden rows, frame-minor
+    float* ps = hs + (size_t)RU * a.D * NF;                 // RU x (D,): predictor outputs
+    __shared__ float red_v[kMaxRows][kScanWarps];
+    __shared__ int red_i[kMaxRows][kScanWarps];
+    __shared__ __align__(8) int2 cand[2][kMaxCluster][kMaxRows];  // (value bits, index) per rank
+    __shared__ float dur_v[kMaxRows][kMaxScanDur];
+    __shared__ int best_tok[kMaxRows], best_dur[kMaxRows];
+    __shared__ int s_t[RU], s_k[RU], s_len[RU], s_steps[RU], s_go[RU], s_t0[RU], s_nf[RU];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rank = C > 1 ? (int)tc::cluster_ctarank() : 0;
-    const int slot = blockIdx.x / C;
-    const int b = a.active ? a.active[slot] : slot;
-    const int Tb = min(max(a.in_lens[b], 0), a.T);
-    int32_t* st = a.state + 4 * b;
-    if (tid == 0) {
-        s_t = st[0];
-        s_k = st[1];
-        s_len = st[2];
-        s_steps = st[3];
-        if (a.max_symbols <= 0) s_t = Tb;  // the reference's per-frame loop never runs
+    const int slot0 = (blockIdx.x / C) * RU;
+    const int n_slots = a.active ? a.n_active : a.B;
+    int bs[RU], Tbs[RU];
+#pragma unroll
+    for (int r = 0; r < RU; ++r) {
+        const int sl = slot0 + r;
+        bs[r] = sl < n_slots ? (a.active ? a.active[sl] : sl) : -1;
+        Tbs[r] = bs[r] >= 0 ? min(max(a.in_lens[bs[r]], 0), a.T) : 0;
     }
-    const float* pr = a.pred + (size_t)b * a.D;
-    for (int j = tid; j < a.D; j += kScanThreads) ps[j] = pr[j];
-    __syncthreads();
-    if (s_t >= Tb) {  // uniform over the cluster: every CTA read the same state
-        if (tid == 0 && rank == 0) {
-            st[0] = s_t;
-            a.report[b] = 0;
+    if (tid < RU) {
+        const int r = tid;
+        if (bs[r] >= 0) {
+            const int32_t* st = a.state + 4 * bs[r];
+            s_t[r] = st[0];
+            s_k[r] = st[1];
+            s_len[r] = st[2];
+            s_steps[r] = st[3];
+            if (a.max_symbols <= 0) s_t[r] = Tbs[r];  // the reference's per-frame loop never runs
+            s_go[r] = s_t[r] < Tbs[r];
+            if (!s_go[r] && rank == 0) {
+                a.state[4 * bs[r]] = s_t[r];
+                a.report[bs[r]] = 0;
+            }
+        } else {
+            s_go[r] = 0;
         }
-        return;
     }
-    const float* encb = a.enc + (size_t)b * a.T * a.D;
+#pragma unroll
+    for (int r = 0; r < RU; ++r) {
+        if (bs[r] < 0) continue;
+        const float* pr = a.pred + (size_t)bs[r] * a.D;
+        for (int j = tid; j < a.D; j += kScanThreads) ps[(size_t)r * a.D + j] = pr[j];
+    }
+    __syncthreads();
+    bool any = false;
+#pragma unroll
+    for (int r = 0; r < RU; ++r) any |= s_go[r] != 0;
+    if (!any) return;  // uniform over the cluster: every CTA read the same state
     const bool tdt = a.n_dur > 0;
     // This CTA's vocabulary slice [lo, hi).
     const int slice = ((a.V + C - 1) / C + 3) / 4 * 4;
@@ -216,32 +236,42 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
     int parity = 0, windows = 0;
 
     for (;;) {
-        const int t0 = s_t;
-        const int nf = min(NF, Tb - t0);
-        // Hidden rows of the window, frame-minor so one vector read serves all frames.
-        for (int j = tid; j < a.D; j += kScanThreads) {
-            const float p = ps[j];
-            float hv[NF];
+        if (tid < RU) {
+            s_t0[tid] = s_t[tid];
+            s_nf[tid] = s_go[tid] ? min(NF, Tbs[tid] - s_t[tid]) : 0;
+        }
+        __syncthreads();
+        // Hidden rows of the window, frame-minor so one vector read serves all frames;
+        // rows of a stopped utterance (or past its end) are zero.
 #pragma unroll
-            for (int f = 0; f < NF; ++f) hv[f] = f < nf ? tanhf(encb[(size_t)(t0 + f) * a.D + j] + p) : 0.f;
-            float4* dst = reinterpret_cast<float4*>(hs + (size_t)j * NF);
+        for (int r = 0; r < RU; ++r) {
+            const int t0 = s_t0[r], nf = s_nf[r];
+            const float* encb = a.enc + ((size_t)max(bs[r], 0) * a.T) * a.D;
+            for (int j = tid; j < a.D; j += kScanThreads) {
+                const float p = ps[(size_t)r * a.D + j];
+                float hv[NF];
 #pragma unroll
-            for (int q = 0; q < NF / 4; ++q) dst[q] = make_float4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
+                for (int f = 0; f < NF; ++f) hv[f] = f < nf ? tanhf(encb[(size_t)(t0 + f) * a.D + j] + p) : 0.f;
+                float4* dst = reinterpret_cast<float4*>(hs + ((size_t)r * a.D + j) * NF);
+#pragma unroll
+                for (int q = 0; q < NF / 4; ++q)
+                    dst[q] = make_float4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
+            }
         }
         __syncthreads();
 
-        float bv[NF];
-        int bi[NF];
+        float bv[NR];
+        int bi[NR];
 #pragma unroll
-        for (int f = 0; f < NF; ++f) {
+        for (int f = 0; f < NR; ++f) {
             bv[f] = -INFINITY;
             bi[f] = INT_MAX;
         }
         for (int c0 = lo; c0 < hi; c0 += kPass) {
             const int col = c0 + CPT * tid;
-            float acc[NF][CPT];
+            float acc[NR][CPT];
 #pragma unroll
-            for (int f = 0; f < NF; ++f)
+            for (int f = 0; f < NR; ++f)
 #pragma unroll
                 for (int c = 0; c < CPT; ++c) acc[f][c] = 0.f;
             // Lanes that stream weights (a partial last pass leaves some idle).
@@ -266,11 +296,11 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
                     cp_async_wait_n(a.stages - 1);  // this thread's copies of chunk ch have landed
                     const float* base = ring + (size_t)(ch % a.stages) * R::kStageFloats;
 #pragma unroll
-                    for (int r = 0; r < R::kRows; ++r) {
-                        const int j = ch * R::kRows + r;
+                    for (int rr = 0; rr < R::kRows; ++rr) {
+                        const int j = ch * R::kRows + rr;
                         if (j < a.D) {
                             float w[CPT];
-                            const float* src = base + ((size_t)r * kScanThreads + tid) * CPT;
+                            const float* src = base + ((size_t)rr * kScanThreads + tid) * CPT;
                             if constexpr (CPT == 4) {
                                 const float4 v = *reinterpret_cast<const float4*>(src);
                                 w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
@@ -280,23 +310,28 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
                             } else {
                                 w[0] = *src;
                             }
-                            float hf[NF];
 #pragma unroll
-                            for (int q = 0; q < NF / 4; ++q) {
-                                const float4 h = *reinterpret_cast<const float4*>(hs + (size_t)j * NF + 4 * q);
-                                hf[4 * q] = h.x, hf[4 * q + 1] = h.y, hf[4 * q + 2] = h.z, hf[4 * q + 3] = h.w;
+                            for (int r = 0; r < RU; ++r) {
+                                float hf[NF];
+#pragma unroll
+                                for (int q = 0; q < NF / 4; ++q) {
+                                    const float4 h =
+                                        *reinterpret_cast<const float4*>(hs + ((size_t)r * a.D + j) * NF + 4 * q);
+                                    hf[4 * q] = h.x, hf[4 * q + 1] = h.y, hf[4 * q + 2] = h.z, hf[4 * q + 3] = h.w;
+                                }
+#pragma unroll
+                                for (int f = 0; f < NF; ++f)
+#pragma unroll
+                                    for (int c = 0; c < CPT; ++c)
+                                        acc[r * NF + f][c] = fmaf(w[c], hf[f], acc[r * NF + f][c]);
                             }
-#pragma unroll
-                            for (int f = 0; f < NF; ++f)
-#pragma unroll
-                                for (int c = 0; c < CPT; ++c) acc[f][c] = fmaf(w[c], hf[f], acc[f][c]);
                         }
                     }
                 }
                 cp_async_wait<0>();
             }
 #pragma unroll
-            for (int f = 0; f < NF; ++f)
+            for (int f = 0; f < NR; ++f)
 #pragma unroll
                 for (int c = 0; c < CPT; ++c) {
                     const int cc = col + c;
@@ -307,41 +342,44 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
                 }
         }
 #pragma unroll
-        for (int f = 0; f < NF; ++f) {
+        for (int f = 0; f < NR; ++f) {
             warp_argmax(bv[f], bi[f]);
             if (lane == 0) {
                 red_v[f][warp] = bv[f];
                 red_i[f][warp] = bi[f];
             }
         }
-        // Duration head (every CTA, a few columns): warp w owns columns w, w + 4, ...
+        // Duration head (every CTA, a few columns): warp w owns columns w, w + 8, ...
         if (tdt) {
             for (int c = warp; c < a.n_dur; c += kScanWarps) {
                 const float* wd = a.wdur + (size_t)c * a.D;
-                float s[NF];
+                float sd[NR];
 #pragma unroll
-                for (int f = 0; f < NF; ++f) s[f] = 0.f;
+                for (int f = 0; f < NR; ++f) sd[f] = 0.f;
                 for (int j = lane; j < a.D; j += 32) {
                     const float w = __ldg(wd + j);
 #pragma unroll
-                    for (int q = 0; q < NF / 4; ++q) {
-                        const float4 h = *reinterpret_cast<const float4*>(hs + (size_t)j * NF + 4 * q);
-                        s[4 * q] = fmaf(w, h.x, s[4 * q]);
-                        s[4 * q + 1] = fmaf(w, h.y, s[4 * q + 1]);
-                        s[4 * q + 2] = fmaf(w, h.z, s[4 * q + 2]);
-                        s[4 * q + 3] = fmaf(w, h.w, s[4 * q + 3]);
-                    }
+                    for (int r = 0; r < RU; ++r)
+#pragma unroll
+                        for (int q = 0; q < NF / 4; ++q) {
+                            const float4 h = *reinterpret_cast<const float4*>(hs + ((size_t)r * a.D + j) * NF + 4 * q);
+                            const int f0 = r * NF + 4 * q;
+                            sd[f0] = fmaf(w, h.x, sd[f0]);
+                            sd[f0 + 1] = fmaf(w, h.y, sd[f0 + 1]);
+                            sd[f0 + 2] = fmaf(w, h.z, sd[f0 + 2]);
+                            sd[f0 + 3] = fmaf(w, h.w, sd[f0 + 3]);
+                        }
                 }
 #pragma unroll
-                for (int f = 0; f < NF; ++f) {
+                for (int f = 0; f < NR; ++f) {
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) s[f] += __shfl_xor_sync(0xffffffffu, s[f], o);
-                    if (lane == 0) dur_v[f][c] = s[f];
+                    for (int o = 16; o > 0; o >>= 1) sd[f] += __shfl_xor_sync(0xffffffffu, sd[f], o);
+                    if (lane == 0) dur_v[f][c] = sd[f];
                 }
             }
         }
         __syncthreads();
-        if (tid < NF) {
+        if (tid < NR) {
             float v = red_v[tid][0];
             int i = red_i[tid][0];
             for (int w = 1; w < kScanWarps; ++w)
@@ -369,7 +407,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
         }
         if constexpr (C > 1) {
             tc::cluster_sync();  // candidates of every rank have landed in every CTA
-            if (tid < NF) {
+            if (tid < NR) {
                 float v = __int_as_float(cand[parity][0][tid].x);
                 int i = cand[parity][0][tid].y;
 #pragma unroll
@@ -387,15 +425,21 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
         }
         __syncthreads();
 
-        // The reference state machine over the window (one thread per CTA; identical
-        // in every CTA of the cluster, rank 0 writes the outputs).
-        if (tid == 0) {
+        // The reference state machine over the window: thread 32 r walks utterance r
+        // (identical in every CTA of a cluster; rank 0 writes the outputs).
+        ++windows;
+        if ((tid & 31) == 0 && (tid >> 5) < RU && s_go[tid >> 5]) {
+            const int r = tid >> 5;
+            const int b = bs[r], Tb = Tbs[r];
+            const int t0 = s_t0[r], nf = s_nf[r];
+            const int* btok = best_tok + r * NF;
+            const int* bdur = best_dur + r * NF;
             const bool out = rank == 0;
-            int t = t0, k = s_k, len = s_len, steps = s_steps;
+            int t = t0, k = s_k[r], len = s_len[r], steps = s_steps[r];
             int emitted = 0, err = 0;
             int64_t* pre = a.prefix + (size_t)b * (a.hyp_cap + 1);
             while (t < t0 + nf) {
-                const int tok = best_tok[t - t0];
+                const int tok = btok[t - t0];
                 if (!tdt) {
                     if (tok == a.blank) {  // rnnt.py:31-32
                         ++t;
@@ -415,7 +459,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
                     }
                     break;
                 }
-                const int dv = best_dur[t - t0];
+                const int dv = bdur[t - t0];
                 if (steps >= a.dur_cap) {
                     err = 1;
                     break;
@@ -443,16 +487,17 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
                 }
                 if (emitted) break;
             }
-            s_t = t;
-            s_k = k;
-            s_len = len;
-            s_steps = steps;
+            s_t[r] = t;
+            s_k[r] = k;
+            s_len[r] = len;
+            s_steps[r] = steps;
             const bool finished = err || emitted || t >= Tb;
             // A long run of blanks is continued by the next launch: the launch's
             // duration is set by its longest chain of windows.
-            const bool paused = !finished && a.max_windows > 0 && ++windows >= a.max_windows;
-            s_go = !(finished || paused);
+            const bool paused = !finished && a.max_windows > 0 && windows >= a.max_windows;
+            s_go[r] = !(finished || paused);
             if ((finished || paused) && out) {
+                int32_t* st = a.state + 4 * b;
                 st[0] = t;
                 st[1] = k;
                 st[2] = len;
@@ -461,7 +506,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) greedy_scan_kernel(ScanArgs a
             }
         }
         __syncthreads();
-        if (!s_go) return;  // every CTA of the cluster stops after the same window
+        bool more = false;
+#pragma unroll
+        for (int r = 0; r < RU; ++r) more |= s_go[r] != 0;
+        if (!more) return;  // every CTA of the cluster stops after the same window
     }
 }
 
@@ -492,13 +540,13 @@ __global__ void greedy_init_kernel(int32_t* state, int64_t* prefix, int B, int h
 
 using ScanKernel = void (*)(ScanArgs);
 
-template <int C, int NF>
-int launch_scan(const ScanArgs& a, int n_slots, size_t smem, cudaStream_t stream) {
-    ScanKernel k = greedy_scan_kernel<C, NF>;
+template <int C, int NF, int RU>
+int launch_scan(const ScanArgs& a, int n_ctas, size_t smem, cudaStream_t stream) {
+    ScanKernel k = greedy_scan_kernel<C, NF, RU>;
     if (smem > 48 * 1024)
         ASR_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(n_slots * C);
+    cfg.gridDim = dim3(n_ctas * C);
     cfg.blockDim = dim3(kScanThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -514,11 +562,12 @@ int launch_scan(const ScanArgs& a, int n_slots, size_t smem, cudaStream_t stream
 }
 
 template <int NF>
-int launch_scan_c(int C, const ScanArgs& a, int n_slots, size_t smem, cudaStream_t stream) {
+int launch_scan_c(int C, int RU, const ScanArgs& a, int n_slots, size_t smem, cudaStream_t stream) {
+    if (RU == 2) return launch_scan<1, NF, 2>(a, (n_slots + 1) / 2, smem, stream);
     switch (C) {
-        case 1: return launch_scan<1, NF>(a, n_slots, smem, stream);
-        case 2: return launch_scan<2, NF>(a, n_slots, smem, stream);
-        default: return launch_scan<4, NF>(a, n_slots, smem, stream);
+        case 1: return launch_scan<1, NF, 1>(a, n_slots, smem, stream);
+        case 2: return launch_scan<2, NF, 1>(a, n_slots, smem, stream);
+        default: return launch_scan<4, NF, 1>(a, n_slots, smem, stream);
     }
 }
 
@@ -572,21 +621,28 @@ extern "C" int asr_greedy_scan(const float* encoder, const float* pred, const fl
     if (reinterpret_cast<uintptr_t>(joint_Wt) % 16 != 0) return ASR_ERR_INVALID_ARGUMENT;
     if (d > kMaxScanDim || n_dur > kMaxScanDur) return ASR_ERR_UNSUPPORTED;
     ScanArgs a{encoder, pred, joint_Wt, joint_W_dur, in_lens, active, state, prefix, durs, report,
-               B, T, d, V, ldw, n_dur, blank_idx, max_symbols, hyp_cap, dur_cap, max_windows, 0};
+               B, T, d, V, ldw, n_dur, blank_idx, max_symbols, hyp_cap, dur_cap, max_windows, 0, 0};
     // Cluster width: one CTA per utterance while the active utterances fill the
     // GPU; otherwise split the vocabulary over up to kMaxCluster SMs per utterance.
     static const int env_c = env_choice("ASR_B200_DECODE_CLUSTER", 0);
     static const int env_f = env_choice("ASR_B200_DECODE_FRAMES", 0);
+    static const int env_p = env_choice("ASR_B200_DECODE_PAIRS", -1);
+    const int sms = sm_count();
     int C = 1;
     if (env_c == 1 || env_c == 2 || env_c == 4) {
         C = env_c;
     } else if (V >= 512) {
-        const int sms = sm_count();
         while (C < kMaxCluster && n_slots * C * 2 <= sms) C *= 2;
     }
+    // Two utterances per CTA (one pass over the weight for both) halve the L2
+    // weight stream but measured slower on B200 (scan 41.4 vs 36.2 ms at config-5
+    // shapes): the saturated launches are issue-bound, not L2-bound. Opt-in only
+    // (ASR_B200_DECODE_PAIRS=1).
+    const int RU = (env_p == 1 && C == 1) ? 2 : 1;
+    a.n_active = n_slots;
     const int NF = env_f == 4 ? 4 : 8;
-    // Shared memory: hidden rows + predictor row, the rest of the budget for the ring.
-    const size_t rows = sizeof(float) * (size_t)d * (NF + 1);
+    // Shared memory: hidden rows + predictor rows, the rest of the budget for the ring.
+    const size_t rows = sizeof(float) * (size_t)RU * d * (NF + 1);
     const int stages = rows + kMinRingStages * kStageBytes > kScanSmemBudget
                            ? kMinRingStages
                            : (int)std::min<size_t>(kMaxRingStages, (kScanSmemBudget - rows) / kStageBytes);
@@ -594,5 +650,6 @@ extern "C" int asr_greedy_scan(const float* encoder, const float* pred, const fl
     a.stages = stages;
     const size_t smem = rows + (size_t)stages * kStageBytes;
     KernelTimer kt("greedy_scan", stream);
-    return NF == 4 ? launch_scan_c<4>(C, a, n_slots, smem, stream) : launch_scan_c<8>(C, a, n_slots, smem, stream);
+    return NF == 4 ? launch_scan_c<4>(C, RU, a, n_slots, smem, stream)
+                   : launch_scan_c<8>(C, RU, a, n_slots, smem, stream);
 }

@@ -212,3 +212,35 @@ def test_empty_and_degenerate_batches():
         rnnt.greedy_decode(enc, cuda(np.array([13, 1, 1], np.int32)), pred, W)
     with pytest.raises(ValueError, match="blank_id"):
         rnnt.greedy_decode(enc, cuda(c["in_lens"]), pred, W, blank_id=W.shape[0])
+
+
+_PAIRS_SCRIPT = """
+import json, sys
+import numpy as np, torch
+sys.path.insert(0, {root!r})
+from tests.decode_cases import DECODE, expected, params
+from tests.test_decode_gpu import run
+out = {{}}
+for name in ("rnnt_char30", "tdt_bpe_like", "tdt_wide_vocab", "ref_frame_skip"):
+    hyps, durs = run(DECODE[name])
+    out[name] = [hyps == expected(DECODE[name])[0], durs == expected(DECODE[name])[1]]
+print(json.dumps(out))
+"""
+
+
+def test_utterance_pairs_variant_matches_golden():
+    """The opt-in two-utterances-per-CTA scan (ASR_B200_DECODE_PAIRS=1, read once per
+    process) gives the reference's results."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = str(Path(__file__).resolve().parents[1])
+    env = dict(os.environ, ASR_B200_DECODE_PAIRS="1")
+    r = subprocess.run([sys.executable, "-c", _PAIRS_SCRIPT.format(root=root)], env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    assert all(all(v) for v in res.values()), res
