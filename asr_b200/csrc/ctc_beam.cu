@@ -39,6 +39,8 @@ constexpr int kMaxBeamVocab = 8192;
 constexpr unsigned long long kHashMul = 0x100000001B3ull;  // odd multiplier of the prefix hash
 
 // logaddexp as the reference computes it (ctc.cpp:28-34), in float32.
+__device__ __forceinline__ int lane_of(int tid) { return tid & 31; }
+
 __device__ __forceinline__ float lae_ref(float a, float b) {
     if (a == -INFINITY) return b;
     if (b == -INFINITY) return a;
@@ -53,31 +55,6 @@ __device__ __forceinline__ bool before(float ka, int va, float kb, int vb) {
     return va < vb;
 }
 
-// Bitonic sort of (key, val) pairs in shared memory, N a power of two, into
-// `before` order. Ends with a barrier.
-__device__ void bitonic(float* key, int* val, int N) {
-    for (int k = 2; k <= N; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < N; i += blockDim.x) {
-                const int p = i ^ j;
-                if (p > i) {
-                    const bool fwd = (i & k) == 0;
-                    const bool sw = fwd ? before(key[p], val[p], key[i], val[i]) : before(key[i], val[i], key[p], val[p]);
-                    if (sw) {
-                        const float tk = key[i];
-                        key[i] = key[p];
-                        key[p] = tk;
-                        const int tv = val[i];
-                        val[i] = val[p];
-                        val[p] = tv;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    }
-}
-
 // Order-preserving image of a float score (larger float -> larger unsigned).
 __device__ __forceinline__ unsigned key_bits(float x) {
     const unsigned u = __float_as_uint(x);
@@ -85,54 +62,111 @@ __device__ __forceinline__ unsigned key_bits(float x) {
 }
 
 // The K first pairs in `before` order of the n (key, val) pairs in shared memory
-// (val < 0 marks an invalid pair), written sorted to okey / oval; returns how many
-// (min(K, valid pairs)). A radix select on key_bits, one 8-bit digit per pass
-// (four passes at most), finds the K-th score; pairs above it are taken, pairs
-// equal to it in index order; then the <= kSelMax winners are bitonic-sorted.
-// All threads call it; it ends with a barrier.
+// (val < 0 marks an invalid pair; n_valid of them are valid), written sorted to
+// okey / oval; returns how many (min(K, n_valid)). A radix select on key_bits, one
+// 8-bit digit per pass (four passes at most, double-buffered histograms), finds the
+// K-th score; pairs above it are taken, pairs equal to it in index order; then one
+// warp sorts the <= kSelMax winners with shuffles. All threads call it; it ends with
+// a barrier.
 constexpr int kSelMax = 128;
 
 struct SelScratch {
-    int hist[256];
+    int hist[2][256];
     int warp_cnt[kBeamThreads / 32];
-    int digit, above, n_valid, n_out, n_tie_base;
+    int digit, above, n_out;
 };
 
-__device__ int block_topk(const float* key, const int* val, int n, int K, float* okey, int* oval, SelScratch& sc) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // valid pairs
-    int cnt = 0;
-    for (int i = tid; i < n; i += blockDim.x) cnt += val[i] >= 0;
-    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-    if (lane == 0) sc.warp_cnt[warp] = cnt;
-    __syncthreads();
-    if (tid == 0) {
-        int t = 0;
-        for (int w = 0; w < kBeamThreads / 32; ++w) t += sc.warp_cnt[w];
-        sc.n_valid = t;
-        sc.n_out = 0;
+// Sorts the k <= 32 E (key, val) pairs at key / val into `before` order: one warp,
+// E pairs per lane, a bitonic network over shuffles.
+template <int E>
+__device__ void warp_sort(float* key, int* val, int k) {
+    constexpr int N = 32 * E;
+    const int lane = threadIdx.x & 31;
+    float kk[E];
+    int vv[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = lane * E + e;
+        kk[e] = i < k ? key[i] : -INFINITY;
+        vv[e] = i < k ? val[i] : -1;
     }
-    __syncthreads();
-    const int nv = sc.n_valid;
-    const int k = min(K, nv);
+#pragma unroll
+    for (int ks = 2; ks <= N; ks <<= 1) {
+#pragma unroll
+        for (int j = ks >> 1; j > 0; j >>= 1) {
+            if (j < E) {  // both elements in this lane
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const int p = e ^ j;
+                    if (p > e) {
+                        const int i = lane * E + e;
+                        const bool fwd = (i & ks) == 0;
+                        const bool sw = fwd ? before(kk[p], vv[p], kk[e], vv[e]) : before(kk[e], vv[e], kk[p], vv[p]);
+                        if (sw) {
+                            const float tk = kk[e];
+                            kk[e] = kk[p];
+                            kk[p] = tk;
+                            const int tv = vv[e];
+                            vv[e] = vv[p];
+                            vv[p] = tv;
+                        }
+                    }
+                }
+            } else {  // the partner element sits in lane ^ (j / E), same slot
+                const int lm = j / E;
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    const float ok = __shfl_xor_sync(0xffffffffu, kk[e], lm);
+                    const int ov = __shfl_xor_sync(0xffffffffu, vv[e], lm);
+                    const int i = lane * E + e;
+                    const bool lower = (i & j) == 0;
+                    const bool fwd = (i & ks) == 0;
+                    // the lower index keeps the element that sorts first in this block's order
+                    const bool mine_first = before(kk[e], vv[e], ok, ov);
+                    const bool keep_mine = (lower == fwd) ? mine_first : !mine_first;
+                    if (!keep_mine) {
+                        kk[e] = ok;
+                        vv[e] = ov;
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = lane * E + e;
+        if (i < k) {
+            key[i] = kk[e];
+            val[i] = vv[e];
+        }
+    }
+}
+
+__device__ int block_topk(const float* key, const int* val, int n, int n_valid, int K, float* okey, int* oval,
+                          SelScratch& sc) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int k = min(K, n_valid);
+    const bool all = k == n_valid;
     unsigned prefix = 0u, mask = 0u;
     int need = k;  // pairs still to take among those matching prefix
-    bool all = k == nv;
     if (!all) {
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int i = tid; i < 256; i += blockDim.x) sc.hist[i] = 0;
-            __syncthreads();
+        for (int i = tid; i < 512; i += blockDim.x) (&sc.hist[0][0])[i] = 0;
+        if (tid == 0) sc.n_out = 0;
+        __syncthreads();
+        for (int pass = 0; pass < 4; ++pass) {
+            const int shift = 24 - 8 * pass;
+            int* hist = sc.hist[pass & 1];
             for (int i = tid; i < n; i += blockDim.x) {
                 if (val[i] < 0) continue;
                 const unsigned u = key_bits(key[i]);
-                if ((u & mask) == prefix) atomicAdd(&sc.hist[(u >> shift) & 255u], 1);
+                if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1);
             }
             __syncthreads();
             if (warp == 0) {  // digit d: count(digits > d) < need <= count(digits >= d)
                 int c[8], sum = 0;
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    c[q] = sc.hist[255 - (lane * 8 + q)];  // lane 0 holds the highest digits
+                    c[q] = hist[255 - (lane * 8 + q)];  // lane 0 holds the highest digits
                     sum += c[q];
                 }
                 int incl = sum;  // inclusive scan over lanes (from the highest digits)
@@ -159,13 +193,19 @@ __device__ int block_topk(const float* key, const int* val, int n, int K, float*
                     sc.digit = d;
                     sc.above = ab;
                 }
+            } else {
+                // the other buffer (last read by the previous pass's scan) for the next pass
+                int* next = sc.hist[(pass + 1) & 1];
+                for (int i = tid - 32; i < 256; i += blockDim.x - 32) next[i] = 0;
             }
             __syncthreads();
             prefix |= (unsigned)sc.digit << shift;
             mask |= 255u << shift;
             need -= sc.above;
-            __syncthreads();
         }
+    } else {
+        if (tid == 0) sc.n_out = 0;
+        __syncthreads();
     }
     // gather: everything strictly above the threshold (any order), then `need` ties in index order
     for (int i = tid; i < n; i += blockDim.x) {
@@ -200,16 +240,67 @@ __device__ int block_topk(const float* key, const int* val, int n, int K, float*
             __syncthreads();
         }
     }
-    // sort the k winners (k <= kSelMax) into `before` order
-    int N = 1;
-    while (N < k) N <<= 1;
-    for (int i = k + tid; i < N; i += blockDim.x) {
-        okey[i] = -INFINITY;
-        oval[i] = -1;
+    // sort the k winners into `before` order
+    if (warp == 0) {
+        if (k <= 64)
+            warp_sort<2>(okey, oval, k);
+        else
+            warp_sort<4>(okey, oval, k);
     }
     __syncthreads();
-    bitonic(okey, oval, N);
     return k;
+}
+
+// Top (K) non-blank tokens of every frame, in `before` order (larger log-prob,
+// then lower id), one warp per (utterance, frame) row: each lane holds its
+// strided share of the row in registers and K rounds of a warp argmax take the
+// next token. Only frames t < in_lens[b] are written. The frames are independent
+// of the beam, so this runs over the whole batch in parallel ahead of the search.
+constexpr int kTopPerLane = 64;  // vocabularies up to 32 * 64 + 1 columns
+
+__global__ void __launch_bounds__(256) top_tokens_kernel(const float* __restrict__ lp,
+                                                         const int32_t* __restrict__ in_lens, int B, int T, int V,
+                                                         int K, int32_t* __restrict__ top_tok,
+                                                         float* __restrict__ top_lp) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (r >= (int64_t)B * T) return;
+    const int b = (int)(r / T), t = (int)(r % T);
+    if (t >= min(max(in_lens[b], 0), T)) return;
+    const float* row = lp + r * V;
+    float x[kTopPerLane];
+#pragma unroll
+    for (int q = 0; q < kTopPerLane; ++q) {
+        const int v = 1 + lane + 32 * q;
+        x[q] = v < V ? __ldg(row + v) : -INFINITY;
+    }
+    unsigned long long taken = 0ull;
+    for (int k = 0; k < K; ++k) {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+#pragma unroll
+        for (int q = 0; q < kTopPerLane; ++q) {
+            const int v = 1 + lane + 32 * q;
+            if (v < V && !((taken >> q) & 1ull) && before(x[q], v, bv, bi)) {
+                bv = x[q];
+                bi = v;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (before(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (((bi - 1) & 31) == lane) taken |= 1ull << ((bi - 1) >> 5);
+        if (lane == 0) {
+            top_tok[r * K + k] = bi;
+            top_lp[r * K + k] = bv;
+        }
+    }
 }
 
 struct Beam {
@@ -223,21 +314,23 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
                                                                int W, int NT, int NC, int32_t* __restrict__ pool_par,
                                                                int32_t* __restrict__ pool_tok, int64_t pool_cap,
                                                                int32_t* __restrict__ out_tokens,
-                                                               int32_t* __restrict__ out_len) {
+                                                               int32_t* __restrict__ out_len,
+                                                               const int32_t* __restrict__ top_tok,
+                                                               const float* __restrict__ top_lp) {
     extern __shared__ __align__(16) unsigned char beam_smem[];
     float* tkey = reinterpret_cast<float*>(beam_smem);  // NT: frame log-probs of tokens 1..V-1
     int* tval = reinterpret_cast<int*>(tkey + NT);
     float* ckey = reinterpret_cast<float*>(tval + NT);  // NC: candidate scores
     int* cval = reinterpret_cast<int*>(ckey + NC);
+    unsigned char* mflag = reinterpret_cast<unsigned char*>(cval + NC);  // NC: extension merged into a stay
     __shared__ float skey[kSelMax];  // selected (sorted) top tokens / candidates
     __shared__ int sval[kSelMax];
     __shared__ SelScratch sc;
     __shared__ Beam bs[2];
     __shared__ float spb[kMaxBeam], spnb[kMaxBeam];  // stay candidates (merged)
-    __shared__ int mpar[kMaxBeam], mpos[kMaxBeam];   // parent entry in the beam, its top-token slot
     __shared__ int toks[kMaxBeam + 1];
     __shared__ float tlp[kMaxBeam + 1];
-    __shared__ int s_n, s_cur, s_next;
+    __shared__ int s_n, s_cur, s_next, s_valid, s_ext[2];
 
     const int b = blockIdx.x, tid = threadIdx.x;
     const int Tb = min(max(in_lens[b], 0), T);
@@ -266,19 +359,31 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
         const int cur = s_cur, n = s_n;
         const Beam& c = bs[cur];
         Beam& nx = bs[cur ^ 1];
-        // 1. the frame's top non-blank tokens
-        for (int i = tid; i < V - 1; i += blockDim.x) {
-            tkey[i] = __ldg(row + i + 1);
-            tval[i] = i + 1;
-        }
-        __syncthreads();
-        block_topk(tkey, tval, V - 1, ntop, skey, sval, sc);
-        if (tid < ntop) {
-            toks[tid] = sval[tid];
-            tlp[tid] = skey[tid];
+        // 1. the frame's top non-blank tokens (precomputed for the whole batch when the
+        // vocabulary fits the pre-pass, else selected here)
+        if (top_tok) {
+            if (tid < ntop) {
+                const int64_t o = ((int64_t)b * T + t) * ntop + tid;
+                toks[tid] = __ldg(top_tok + o);
+                tlp[tid] = __ldg(top_lp + o);
+            }
+        } else {
+            for (int i = tid; i < V - 1; i += blockDim.x) {
+                tkey[i] = __ldg(row + i + 1);
+                tval[i] = i + 1;
+            }
+            __syncthreads();
+            block_topk(tkey, tval, V - 1, V - 1, ntop, skey, sval, sc);
+            if (tid < ntop) {
+                toks[tid] = sval[tid];
+                tlp[tid] = skey[tid];
+            }
         }
         __syncthreads();
         // 2. stay candidates, with the parent's extension merged in
+        if (tid == 0) s_valid = 0;
+        for (int i = tid; i < n * per; i += blockDim.x) mflag[i] = 0;
+        __syncthreads();
         if (tid < n) {
             const int e = tid, last = c.last[e];
             float pnb = last >= 0 ? c.pnb[e] + __ldg(row + last) : -INFINITY;
@@ -301,11 +406,10 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
             }
             spb[e] = lae_ref(c.pb[e], c.pnb[e]) + __ldg(row);
             spnb[e] = pnb;
-            mpar[e] = pe;
-            mpos[e] = pos;
+            if (pe >= 0 && pos >= 0) mflag[pe * per + 1 + pos] = 1;  // that extension is this stay
         }
         __syncthreads();
-        // 3. candidate scores
+        // 3. candidate scores (s_valid counts the candidates that stay)
         const int nc = n * per;
         for (int i = tid; i < nc; i += blockDim.x) {
             float key = -INFINITY;
@@ -316,13 +420,7 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
                     key = lae_ref(spb[e], spnb[e]);
                     val = i;
                 } else {
-                    bool merged = false;
-                    for (int q = 0; q < n; ++q)
-                        if (mpar[q] == e && mpos[q] == j - 1) {
-                            merged = true;
-                            break;
-                        }
-                    if (!merged) {
+                    if (!mflag[i]) {
                         const int v = toks[j - 1];
                         const float base = v == c.last[e] ? c.pb[e] : lae_ref(c.pb[e], c.pnb[e]);
                         key = base + tlp[j - 1];
@@ -332,38 +430,49 @@ __global__ void __launch_bounds__(kBeamThreads) ctc_beam_kernel(const float* __r
             }
             ckey[i] = key;
             cval[i] = val;
+            if (val >= 0) atomicAdd(&s_valid, 1);
         }
         __syncthreads();
-        const int keep = block_topk(ckey, cval, nc, W, skey, sval, sc);
-        // 4. the next beam (W entries at most; new prefixes get pool nodes)
-        if (tid == 0) {
-            int k = 0, node = s_next;
-            for (; k < keep; ++k) {
-                const int i = sval[k], e = i / per, j = i - e * per;
-                if (j == 0) {
-                    nx.node[k] = c.node[e];
-                    nx.len[k] = c.len[e];
-                    nx.last[k] = c.last[e];
-                    nx.pb[k] = spb[e];
-                    nx.pnb[k] = spnb[e];
-                    nx.hash[k] = c.hash[e];
+        const int keep = block_topk(ckey, cval, nc, s_valid, W, skey, sval, sc);
+        // 4. the next beam (W entries at most): thread k builds entry k; new prefixes
+        // get pool nodes numbered in entry order (a ballot scan over warps 0-1)
+        {
+            const bool mine = tid < keep;
+            const int i = mine ? sval[tid] : 0, e = i / per, j = i - e * per;
+            const bool ext = mine && j != 0;
+            const unsigned bal = __ballot_sync(0xffffffffu, ext);
+            if (lane_of(tid) == 0 && tid < 64) s_ext[tid >> 5] = __popc(bal);
+            __syncthreads();
+            if (mine) {
+                if (!ext) {
+                    nx.node[tid] = c.node[e];
+                    nx.len[tid] = c.len[e];
+                    nx.last[tid] = c.last[e];
+                    nx.pb[tid] = spb[e];
+                    nx.pnb[tid] = spnb[e];
+                    nx.hash[tid] = c.hash[e];
                 } else {
+                    const int rank = (tid >= 32 ? s_ext[0] : 0) + __popc(bal & ((1u << (tid & 31)) - 1u));
+                    const int node = s_next + rank;
                     const int v = toks[j - 1];
                     par[node] = c.node[e];
                     tokp[node] = v;
-                    nx.node[k] = node++;
-                    nx.len[k] = c.len[e] + 1;
-                    nx.last[k] = v;
-                    nx.pb[k] = -INFINITY;
-                    nx.pnb[k] = skey[k];
-                    nx.hash[k] = c.hash[e] * kHashMul + (unsigned long long)(v + 1);
+                    nx.node[tid] = node;
+                    nx.len[tid] = c.len[e] + 1;
+                    nx.last[tid] = v;
+                    nx.pb[tid] = -INFINITY;
+                    nx.pnb[tid] = skey[tid];
+                    nx.hash[tid] = c.hash[e] * kHashMul + (unsigned long long)(v + 1);
                 }
             }
-            s_n = k;
-            s_next = node;
-            s_cur = cur ^ 1;
+            __syncthreads();
+            if (tid == 0) {
+                s_n = keep;
+                s_next += s_ext[0] + (keep > 32 ? s_ext[1] : 0);
+                s_cur = cur ^ 1;
+            }
+            __syncthreads();
         }
-        __syncthreads();
     }
     // 5. the best surviving prefix, backtracked through the node pool
     if (tid == 0) {
@@ -394,7 +503,9 @@ using namespace asr;
 
 extern "C" size_t asr_ctc_beam_workspace_bytes(int B, int T, int beam_width) {
     if (B < 0 || T < 0 || beam_width < 1 || beam_width > kMaxBeam) return 0;
-    return sizeof(int32_t) * 2 * (size_t)B * (1 + (size_t)T * beam_width) + 256;
+    // node pool (parent, token) + the per-frame top-token table (id, log-prob)
+    return sizeof(int32_t) * 2 * (size_t)B * (1 + (size_t)T * beam_width) +
+           sizeof(int32_t) * 2 * (size_t)B * T * (beam_width + 1) + 512;
 }
 
 extern "C" int asr_ctc_beam_decode(const float* log_probs, const int32_t* in_lens, int B, int T, int V,
@@ -410,7 +521,7 @@ extern "C" int asr_ctc_beam_decode(const float* log_probs, const int32_t* in_len
     const int NC = beam_width * (ntop + 1);
     const int64_t cap = 1 + (int64_t)T * beam_width;
     auto* base = reinterpret_cast<int32_t*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
-    const size_t smem = sizeof(float) * 2 * (size_t)(NT + NC);
+    const size_t smem = sizeof(float) * 2 * (size_t)(NT + NC) + (size_t)NC;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (smem > 48 * 1024)
         ASR_CUDA_TRY(cudaFuncSetAttribute(ctc_beam_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -418,9 +529,21 @@ extern "C" int asr_ctc_beam_decode(const float* log_probs, const int32_t* in_len
         ASR_CUDA_TRY(cudaMemsetAsync(lengths, 0, sizeof(int32_t) * B, st));
         return ASR_OK;
     }
+    int32_t* top_tok = nullptr;
+    float* top_lp = nullptr;
+    if (V - 1 <= 32 * kTopPerLane && ntop > 0) {
+        int32_t* tbl = base + 2 * (size_t)B * cap;
+        top_tok = tbl;
+        top_lp = reinterpret_cast<float*>(tbl + (size_t)B * T * ntop);
+        KernelTimer kt("ctc_beam_top_tokens", st);
+        const int64_t rows = (int64_t)B * T;
+        top_tokens_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(log_probs, in_lens, B, T, V, ntop, top_tok,
+                                                                      top_lp);
+        ASR_LAUNCH_CHECK();
+    }
     KernelTimer kt("ctc_beam", st);
     ctc_beam_kernel<<<B, kBeamThreads, smem, st>>>(log_probs, in_lens, T, V, beam_width, NT, NC, base,
-                                                   base + (size_t)B * cap, cap, tokens, lengths);
+                                                   base + (size_t)B * cap, cap, tokens, lengths, top_tok, top_lp);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
