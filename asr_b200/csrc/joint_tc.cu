@@ -674,36 +674,23 @@ __global__ void plan_passes_kernel(LatticeMeta m, int B, int P, int64_t step, in
 }
 
 // H[r, k] = bf16(tanh(enc[b, t, k] + dec[b, u, k])) for the pass's node r (row
-// r = node - pass start, k < kpad, zero for k >= d), 16-byte stores. Each warp
-// walks a run of kHiddenRun consecutive rows (one coordinate search per run,
-// then (t, u) increments), so consecutive nodes of a frame share their enc row
-// and neighbouring dec rows in L1. Rows from the pass end up to the next
-// 256-row boundary are zeroed: the joint kernels read whole tiles. HBM bound
-// (1280 B written per node at d = 640).
+// r = node - pass start, k < kpad, zero for k >= d). Rows from the pass end up
+// to the next 256-row boundary are zeroed: the joint kernels read whole tiles.
+// Bound by the H writes (1280 B per node at d = 640) and by the MUFU pipe (one
+// tanh per element plus one bf16 pack per pair).
+//
+// Scalar path (d % 8 != 0 or unaligned rows): each warp walks a run of
+// kHiddenRun consecutive rows (one coordinate search per run, then (t, u)
+// increments), element loads, 16-byte stores.
 constexpr int kHiddenRun = 64;
 
-// Eight consecutive activations as fp32 (16-byte aligned source).
-__device__ __forceinline__ void load8(const float* __restrict__ p, float (&x)[8]) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
-}
-__device__ __forceinline__ void load8(const __nv_bfloat16* __restrict__ p, float (&x)[8]) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        x[2 * i] = f.x, x[2 * i + 1] = f.y;
-    }
-}
 __device__ __forceinline__ float load1(const float* p) { return __ldg(p); }
 __device__ __forceinline__ float load1(const __nv_bfloat16* p) { return __bfloat162float(p[0]); }
 
 template <typename TA>
 __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, const TA* __restrict__ enc,
                                                         const TA* __restrict__ dec, int T, int U, int d, int kpad,
-                                                        int vec, const int32_t* __restrict__ bounds, int pass,
+                                                        const int32_t* __restrict__ bounds, int pass,
                                                         __nv_bfloat16* __restrict__ H) {
     const int N = total_nodes(m, B);
     const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
@@ -729,47 +716,17 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
             }
             const TA* er = enc + ((int64_t)c.b * T + c.t) * d;
             const TA* dr = dec + ((int64_t)c.b * U + c.u) * d;
-            if (vec) {
-                // three 8-column groups per lane at a time (d % 8 == 0, aligned rows):
-                // all their loads in flight at once; groups at or past d stay zero
-                for (int g0 = 0; g0 < c8n; g0 += 3 * 32) {
-                    float ev[3][8], dv[3][8];
+            for (int k8 = lane; k8 < c8n; k8 += 32) {
+                const int k = k8 * 8;
+                float h[8];
 #pragma unroll
-                    for (int j = 0; j < 3; ++j) {
-                        const int k = (g0 + lane + 32 * j) * 8;
-                        if (k + 8 <= d) {
-                            load8(er + k, ev[j]);
-                            load8(dr + k, dv[j]);
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) ev[j][i] = dv[j][i] = 0.f;
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < 3; ++j) {
-                        const int k8 = g0 + lane + 32 * j;
-                        if (k8 >= c8n) break;
-                        uint4 w;
-                        w.x = pack_bf16(tanh_fast(ev[j][0] + dv[j][0]), tanh_fast(ev[j][1] + dv[j][1]));
-                        w.y = pack_bf16(tanh_fast(ev[j][2] + dv[j][2]), tanh_fast(ev[j][3] + dv[j][3]));
-                        w.z = pack_bf16(tanh_fast(ev[j][4] + dv[j][4]), tanh_fast(ev[j][5] + dv[j][5]));
-                        w.w = pack_bf16(tanh_fast(ev[j][6] + dv[j][6]), tanh_fast(ev[j][7] + dv[j][7]));
-                        dst[k8] = w;
-                    }
-                }
-            } else {
-                for (int k8 = lane; k8 < c8n; k8 += 32) {
-                    const int k = k8 * 8;
-                    float h[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) h[i] = k + i < d ? tanh_fast(load1(er + k + i) + load1(dr + k + i)) : 0.f;
-                    uint4 w;
-                    w.x = pack_bf16(h[0], h[1]);
-                    w.y = pack_bf16(h[2], h[3]);
-                    w.z = pack_bf16(h[4], h[5]);
-                    w.w = pack_bf16(h[6], h[7]);
-                    dst[k8] = w;
-                }
+                for (int i = 0; i < 8; ++i) h[i] = k + i < d ? tanh_fast(load1(er + k + i) + load1(dr + k + i)) : 0.f;
+                uint4 w;
+                w.x = pack_bf16(h[0], h[1]);
+                w.y = pack_bf16(h[2], h[3]);
+                w.z = pack_bf16(h[4], h[5]);
+                w.w = pack_bf16(h[6], h[7]);
+                dst[k8] = w;
             }
             // next node: next label position, next frame, or the next utterance
             if (++c.u == c.Ub) {
@@ -781,6 +738,253 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
             }
         }
     }
+}
+
+// Vector path of the hidden rows (d % 8 == 0, 16-byte aligned rows). Each warp
+// takes a run of kFlatRun rows: lane i resolves row i's enc and dec row indices
+// once into shared memory, then the warp walks the run's rows x column chunks
+// as one flat index space. A chunk is the 16 bytes of input one lane loads from
+// each of enc and dec (4 fp32 or 8 bf16 columns), so every warp load covers 512
+// contiguous bytes (no sector is fetched half used) and no lane idles on a
+// partial column group. UNR chunks per lane are in flight at a time, all their
+// loads issued before the first tanh.
+constexpr int kFlatRun = 32;
+constexpr int kFlatWarps = 8;
+
+template <typename TA>
+struct Chunk;
+template <>
+struct Chunk<float> {  // 4 columns; 8 bytes of H
+    static constexpr int kCols = 4;
+    float4 v;
+    __device__ __forceinline__ void load(const float* __restrict__ p) { v = __ldg(reinterpret_cast<const float4*>(p)); }
+    __device__ __forceinline__ void get(float (&x)[kCols]) const { x[0] = v.x, x[1] = v.y, x[2] = v.z, x[3] = v.w; }
+};
+template <>
+struct Chunk<__nv_bfloat16> {  // 8 columns; 16 bytes of H
+    static constexpr int kCols = 8;
+    uint4 v;
+    __device__ __forceinline__ void load(const __nv_bfloat16* __restrict__ p) {
+        v = __ldg(reinterpret_cast<const uint4*>(p));
+    }
+    __device__ __forceinline__ void get(float (&x)[kCols]) const {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            x[2 * i] = f.x, x[2 * i + 1] = f.y;
+        }
+    }
+};
+
+__device__ __forceinline__ void store_h(__nv_bfloat16* p, const float (&h)[4]) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]));
+}
+__device__ __forceinline__ void store_h(__nv_bfloat16* p, const float (&h)[8]) {
+    *reinterpret_cast<uint4*>(p) =
+        make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]), pack_bf16(h[6], h[7]));
+}
+
+template <int UNR>
+constexpr int kFlatMinBlocks = UNR <= 4 ? 3 : 2;
+
+template <typename TA, int UNR>
+__global__ void __launch_bounds__(kFlatWarps * 32, kFlatMinBlocks<UNR>)
+    hidden_flat_kernel(LatticeMeta m, int B, const TA* __restrict__ enc, const TA* __restrict__ dec, int T, int U,
+                       int d, int kpad, const int32_t* __restrict__ bounds, int pass, __nv_bfloat16* __restrict__ H) {
+    constexpr int CE = Chunk<TA>::kCols;
+    __shared__ int2 rows_sm[kFlatWarps][kFlatRun];
+    const int N = total_nodes(m, B);
+    const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
+    const int rows = e - s;
+    const int rows_pad = (rows + kPassAlign - 1) / kPassAlign * kPassAlign;  // a multiple of kFlatRun
+    const int cn = kpad / CE, cd = d / CE;  // chunks per H row, chunks holding columns < d
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int nwarps = gridDim.x * kFlatWarps;
+    int2* rs = rows_sm[w];
+    const int total = kFlatRun * cn;  // chunks per run
+    for (int r0 = (blockIdx.x * kFlatWarps + w) * kFlatRun; r0 < rows_pad; r0 += nwarps * kFlatRun) {
+        {
+            const int r = r0 + lane;
+            int2 v = make_int2(-1, -1);  // padding row: zeros
+            if (r < rows) {
+                const NodeCoord c = node_coord(m, B, s + r);
+                v = make_int2(c.b * T + c.t, c.b * U + c.u);
+            }
+            rs[lane] = v;
+        }
+        __syncwarp();
+        __nv_bfloat16* dst = H + (int64_t)r0 * kpad;
+        int rr = 0, kc = lane;  // chunk q = lane + 32 i lies in row rr, column chunk kc
+        while (kc >= cn) kc -= cn, ++rr;
+        for (int q0 = 0; q0 < total; q0 += 32 * UNR) {
+            Chunk<TA> ev[UNR], dv[UNR];
+            int rj[UNR], kj[UNR];
+#pragma unroll
+            for (int j = 0; j < UNR; ++j) {
+                rj[j] = rr, kj[j] = kc;
+                const int2 v = rr < kFlatRun ? rs[rr] : make_int2(-1, -1);
+                if (v.x >= 0 && kc < cd) {
+                    ev[j].load(enc + (int64_t)v.x * d + kc * CE);
+                    dv[j].load(dec + (int64_t)v.y * d + kc * CE);
+                } else {
+                    kj[j] = -1 - kc;  // zero chunk (padding row or column)
+                }
+                kc += 32;
+                while (kc >= cn) kc -= cn, ++rr;
+            }
+#pragma unroll
+            for (int j = 0; j < UNR; ++j) {
+                if (rj[j] >= kFlatRun) break;
+                float h[CE];
+                int k = kj[j];
+                if (k >= 0) {
+                    float x[CE], y[CE];
+                    ev[j].get(x);
+                    dv[j].get(y);
+#pragma unroll
+                    for (int i = 0; i < CE; ++i) h[i] = tanh_fast(x[i] + y[i]);
+                } else {
+                    k = -1 - k;
+#pragma unroll
+                    for (int i = 0; i < CE; ++i) h[i] = 0.f;
+                }
+                store_h(dst + (int64_t)rj[j] * kpad + k * CE, h);
+            }
+        }
+        __syncwarp();  // rs is rewritten by the next run
+    }
+}
+
+// Row-stationary vector path for rows of at most 32 * 8 chunks (kpad <= 1024 for
+// fp32 activations, 2048 for bf16): lane l owns chunks l, l + 32, ..., l + 32 (J-1)
+// of every row, so the column offsets and their validity are fixed per lane and
+// a row costs one shared-memory descriptor read and a base address. Rows are
+// taken in groups of up to R consecutive rows of one frame: the group's R dec
+// rows are loaded together, and the frame's enc row is loaded only when the
+// frame changes and otherwise stays in registers, so the L1 data path carries
+// one input row per H row instead of two. Same run and descriptor scheme as the
+// flat kernel above.
+template <typename TA, int J, int R>
+constexpr int kRowsMinBlocks = (R + 1) * J * 4 <= 40 ? 3 : 2;
+
+template <typename TA, int J, int R>
+__global__ void __launch_bounds__(kFlatWarps * 32, (kRowsMinBlocks<TA, J, R>))
+    hidden_rows_kernel(LatticeMeta m, int B, const TA* __restrict__ enc, const TA* __restrict__ dec, int T, int U,
+                       int d, int kpad, const int32_t* __restrict__ bounds, int pass, __nv_bfloat16* __restrict__ H) {
+    constexpr int CE = Chunk<TA>::kCols;
+    __shared__ int2 rows_sm[kFlatWarps][kFlatRun + 1];
+    const int N = total_nodes(m, B);
+    const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
+    const int rows = e - s;
+    const int rows_pad = (rows + kPassAlign - 1) / kPassAlign * kPassAlign;
+    const int cn = kpad / CE, cd = d / CE;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int nwarps = gridDim.x * kFlatWarps;
+    int2* rs = rows_sm[w];
+    if (lane == 0) rs[kFlatRun] = make_int2(-2, -2);  // sentinel: ends every frame group
+    for (int r0 = (blockIdx.x * kFlatWarps + w) * kFlatRun; r0 < rows_pad; r0 += nwarps * kFlatRun) {
+        {
+            const int r = r0 + lane;
+            int2 v = make_int2(-1, -1);  // padding row: zeros
+            if (r < rows) {
+                const NodeCoord c = node_coord(m, B, s + r);
+                v = make_int2(c.b * T + c.t, c.b * U + c.u);
+            }
+            rs[lane] = v;
+        }
+        __syncwarp();
+        Chunk<TA> ev[J];
+        int ecur = -1;  // enc row held in ev (-1: none)
+        int rr = 0;
+#pragma unroll 1
+        while (rr < kFlatRun) {
+            const int erow = rs[rr].x;  // warp-uniform
+            int drow[R];
+            int n = 0;  // rows of this group: consecutive rows of frame erow, at most R
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                const int2 v = rs[rr + i < kFlatRun ? rr + i : kFlatRun];
+                drow[i] = v.y;
+                if (n == i && v.x == erow) n = i + 1;
+            }
+            Chunk<TA> dv[R][J];
+            if (erow >= 0) {
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    if (i < n) {
+                        const TA* db = dec + (int64_t)drow[i] * d + lane * CE;
+#pragma unroll
+                        for (int j = 0; j < J; ++j)
+                            if (lane + 32 * j < cd) dv[i][j].load(db + 32 * CE * j);
+                    }
+                }
+                if (erow != ecur) {
+                    const TA* eb = enc + (int64_t)erow * d + lane * CE;
+#pragma unroll
+                    for (int j = 0; j < J; ++j)
+                        if (lane + 32 * j < cd) ev[j].load(eb + 32 * CE * j);
+                    ecur = erow;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                if (i >= n) break;
+                __nv_bfloat16* out = H + (int64_t)(r0 + rr + i) * kpad + lane * CE;
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    if (lane + 32 * j >= cn) break;
+                    float h[CE];
+                    if (erow >= 0 && lane + 32 * j < cd) {
+                        float x[CE], y[CE];
+                        ev[j].get(x);
+                        dv[i][j].get(y);
+#pragma unroll
+                        for (int k = 0; k < CE; ++k) h[k] = tanh_fast(x[k] + y[k]);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < CE; ++k) h[k] = 0.f;
+                    }
+                    store_h(out + 32 * CE * j, h);
+                }
+            }
+            rr += n;
+        }
+        __syncwarp();  // rs is rewritten by the next run
+    }
+}
+
+template <typename TA, int J, int R>
+void launch_rows(const JointArgs& a, const TA* enc, const TA* dec, int kpad, const int32_t* bounds, int pass,
+                 __nv_bfloat16* H, cudaStream_t st) {
+    hidden_rows_kernel<TA, J, R><<<sm_count() * kRowsMinBlocks<TA, J, R>, kFlatWarps * 32, 0, st>>>(
+        a.m, a.B, enc, dec, a.T, a.U, a.d, kpad, bounds, pass, H);
+}
+
+// J = chunks per lane per row (1..8). Three rows in flight per warp where the
+// registers allow it (measured best on B200 for d = 640 in both activation
+// types), two for the widest rows.
+template <typename TA>
+bool launch_rows_j(int J, const JointArgs& a, const TA* enc, const TA* dec, int kpad, const int32_t* bounds, int pass,
+                   __nv_bfloat16* H, cudaStream_t st) {
+    switch (J) {
+        case 1: launch_rows<TA, 1, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        case 2: launch_rows<TA, 2, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        case 3: launch_rows<TA, 3, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        case 4: launch_rows<TA, 4, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        case 5: launch_rows<TA, 5, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        case 6: launch_rows<TA, 6, 2>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        case 7: launch_rows<TA, 7, 2>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        case 8: launch_rows<TA, 8, 2>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        default: return false;
+    }
+}
+
+template <typename TA, int UNR>
+void launch_flat(const JointArgs& a, const TA* enc, const TA* dec, int kpad, const int32_t* bounds, int pass,
+                 __nv_bfloat16* H, cudaStream_t st) {
+    hidden_flat_kernel<TA, UNR><<<sm_count() * kFlatMinBlocks<UNR>, kFlatWarps * 32, 0, st>>>(a.m, a.B, enc, dec, a.T, a.U, a.d, kpad,
+                                                                            bounds, pass, H);
 }
 
 // CTC head hidden rows: one warp per frame row, H = bf16(x * rsqrt(mean(x^2) + eps)
@@ -837,12 +1041,23 @@ int launch_hidden(const JointArgs& a, int kpad, const int32_t* bounds, int pass,
         ASR_LAUNCH_CHECK();
         return ASR_OK;
     }
-    if (a.enc16)
+    if (a.vec) {
+        // row-stationary kernel up to 8 chunks per lane, the flat kernel for wider rows
+        const int J = (kpad / (a.enc16 ? 8 : 4) + 31) / 32;
+        if (a.enc16) {
+            if (!launch_rows_j<__nv_bfloat16>(J, a, a.enc16, a.dec16, kpad, bounds, pass, H, st))
+                launch_flat<__nv_bfloat16, 4>(a, a.enc16, a.dec16, kpad, bounds, pass, H, st);
+        } else {
+            if (!launch_rows_j<float>(J, a, a.enc, a.dec, kpad, bounds, pass, H, st))
+                launch_flat<float, 4>(a, a.enc, a.dec, kpad, bounds, pass, H, st);
+        }
+    } else if (a.enc16) {
         hidden_kernel<__nv_bfloat16><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc16, a.dec16, a.T, a.U, a.d, kpad,
-                                                                     a.vec, bounds, pass, H);
-    else
-        hidden_kernel<float><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.dec, a.T, a.U, a.d, kpad, a.vec,
-                                                             bounds, pass, H);
+                                                                     bounds, pass, H);
+    } else {
+        hidden_kernel<float><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.dec, a.T, a.U, a.d, kpad, bounds, pass,
+                                                             H);
+    }
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }

@@ -509,3 +509,56 @@ def test_rnnt_bf16_activations_module():
     torch.testing.assert_close(loss.detach(), ref.detach(), rtol=1e-6, atol=1e-6)
     assert e.grad.dtype == torch.bfloat16 and _rel(e.grad.float(), e32.grad) < 1e-2
     assert _rel(w.grad, w32.grad) < 1e-5
+
+
+def _offset_view(x, dtype):
+    """`x` as a contiguous CUDA tensor of `dtype` whose data starts one element
+    past a 16-byte boundary, so the hidden-row kernels take their scalar path."""
+    flat = torch.empty(x.size + 1, dtype=dtype, device="cuda")
+    v = flat[1:].view(x.shape)
+    v.copy_(torch.as_tensor(np.ascontiguousarray(x)).to(dtype))
+    assert v.is_contiguous() and v.data_ptr() % 16 != 0
+    return v
+
+
+@pytest.mark.parametrize(
+    "act,d",
+    [
+        ("f32", 72),  # one 4-column chunk per lane, row-stationary kernel
+        ("f32", 640),  # five chunks per lane, three rows in flight
+        ("f32", 1100),  # nine chunks per lane: the flat kernel
+        ("bf16", 640),  # three 8-column chunks per lane
+        ("bf16", 2100),  # nine chunks per lane: the flat kernel
+    ],
+)
+def test_hidden_vector_paths_match_scalar_path(act, d):
+    """The vector hidden-row kernels (row-stationary and flat, fp32 and bf16
+    activations) write the same H as the element-wise path that unaligned rows
+    take: the tensor-core RNN-T loss is identical and the gradients agree to
+    accumulation order."""
+    from asr_b200 import _lib
+    from asr_b200.loss.rnnt import rnnt_loss
+
+    V = 256
+    assert _lib.joint_uses_tensor_cores(V, 0, d)
+    c = transducer_case(43, 3, (20, 50), (30, 70), V, d)
+    dt = torch.bfloat16 if act == "bf16" else torch.float32
+    args = [cuda(c[k]) for k in ("targets", "in_lens", "tgt_lens")]
+    gl = cuda(c["grad_loss"])
+    out = {}
+    for name in ("vector", "scalar"):
+        if name == "vector":
+            e0, d0 = cuda(c["enc"], dt), cuda(c["dec"], dt)
+            assert e0.data_ptr() % 16 == 0 and d0.data_ptr() % 16 == 0
+        else:
+            e0, d0 = _offset_view(c["enc"], dt), _offset_view(c["dec"], dt)
+        e, dd = e0.detach().requires_grad_(True), d0.detach().requires_grad_(True)
+        w = leaf(c["W"])
+        loss = rnnt_loss(e, dd, w, *args, 0, True)
+        (loss * gl).sum().backward()
+        out[name] = (loss.detach(), e.grad.float(), dd.grad.float(), w.grad)
+    lv, *gv = out["vector"]
+    ls, *gs = out["scalar"]
+    torch.testing.assert_close(lv, ls, rtol=1e-6, atol=1e-6)
+    for name, a, b in zip(("d_enc", "d_dec", "dW"), gv, gs):
+        assert _rel(a, b) < 1e-5, f"{name}: {_rel(a, b):.3e}"
