@@ -29,6 +29,7 @@ struct TrWorkspace {
     float* cb = nullptr;    // backward: (cap,)
     float* ct = nullptr;    // backward: (cap,)
     float* gdur = nullptr;  // backward TDT: (cap, n_dur)
+    double* beta = nullptr;  // backward TDT: (B, T + 1, U), the alpha array's shape
     void* joint = nullptr;  // joint-network scratch
     size_t joint_bytes = 0;
     // bf16 activations: fp32 copies for the SIMT path, fp32 gradient sums
@@ -54,6 +55,9 @@ size_t joint_scratch_bytes(const JointArgs& a, int64_t cap, bool tc, bool backwa
     return backward ? simt_backward_scratch_bytes(a.V + a.n_dur, (int)cap) : 0;
 }
 
+// Elements of the TDT alpha array (B, T + 1, U); beta has the same layout.
+size_t tdt_alpha_len(const JointArgs& a) { return (size_t)a.B * (a.T + 1) * a.U; }
+
 size_t tr_workspace_bytes(const JointArgs& a, int64_t cap, bool tc, bool backward, int act_dtype = ASR_DTYPE_F32) {
     size_t n = lattice_meta_bytes(a.B);
     const ActStaging sg = act_staging(act_dtype, tc, backward);
@@ -62,7 +66,10 @@ size_t tr_workspace_bytes(const JointArgs& a, int64_t cap, bool tc, bool backwar
     if (sg.grads) n += align256(ne) + align256(nd);
     if (backward) {
         n += 2 * align256(sizeof(float) * cap);
-        if (a.n_dur > 0) n += align256(sizeof(float) * cap * a.n_dur);
+        if (a.n_dur > 0) {
+            n += align256(sizeof(float) * cap * a.n_dur);
+            n += align256(sizeof(double) * tdt_alpha_len(a));
+        }
     }
     n += align256(joint_scratch_bytes(a, cap, tc, backward));
     return n + 256;  // slack for aligning the base pointer
@@ -94,6 +101,8 @@ TrWorkspace carve(void* ws, const JointArgs& a, int64_t cap, bool tc, bool backw
         if (a.n_dur > 0) {
             w.gdur = reinterpret_cast<float*>(p);
             p += align256(sizeof(float) * cap * a.n_dur);
+            w.beta = reinterpret_cast<double*>(p);
+            p += align256(sizeof(double) * tdt_alpha_len(a));
         }
     }
     w.joint = p;
@@ -422,7 +431,7 @@ int tdt_backward_impl(const void* encoder, const void* decoder, int act_dtype, c
     rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
     if (rc) return rc;
     rc = launch_tdt_beta(w.meta, B, U, max_duration, durations, n_dur, has_zero, log_P_blank, log_P_y, log_P_dur,
-                         alpha, grad_loss, w.cb, w.ct, w.gdur, st);
+                         alpha, grad_loss, w.cb, w.ct, w.gdur, w.beta, st);
     if (rc) return rc;
     float *ge, *gd;
     rc = zero_act_grads(a, w, grad_encoder, grad_decoder, &ge, &gd, st);

@@ -44,16 +44,27 @@ __device__ __forceinline__ double lae_d(double a, double b) {
 
 // Running log-sum-exp of float64 terms: max first, then one exp per term and a
 // single log (the terms of one lattice node are all known before the sum).
+// The max and the sum are pairwise trees, so the dependent chain of a node is
+// log2(N) deep rather than N.
 template <int N>
 __device__ __forceinline__ double lse_d(const double (&x)[N]) {
-    double m = x[0];
+    double mx[N];
 #pragma unroll
-    for (int i = 1; i < N; ++i) m = fmax(m, x[i]);
+    for (int i = 0; i < N; ++i) mx[i] = x[i];
+#pragma unroll
+    for (int w = 1; w < N; w *= 2)
+#pragma unroll
+        for (int i = 0; i + w < N; i += 2 * w) mx[i] = fmax(mx[i], mx[i + w]);
+    const double m = mx[0];
     if (m <= -1e29) return m;  // every term is the finite log-zero sentinel
-    float s = 0.f;
+    float e[N];
 #pragma unroll
-    for (int i = 0; i < N; ++i) s += __expf((float)(x[i] - m));
-    return m + (double)__logf(s);
+    for (int i = 0; i < N; ++i) e[i] = __expf((float)(x[i] - m));
+#pragma unroll
+    for (int w = 1; w < N; w *= 2)
+#pragma unroll
+        for (int i = 0; i + w < N; i += 2 * w) e[i] += e[i + w];
+    return m + (double)__logf(e[0]);
 }
 
 // Per-batch lattice bookkeeping produced by lattice_prep_kernel.

@@ -43,8 +43,9 @@ int launch_rnnt_beta(const LatticeMeta& m, int B, int U, const float* lpb, const
 int launch_tdt_alpha(const LatticeMeta& m, int B, int U, int max_duration, const int32_t* durations, int n_dur,
                      int has_zero, const float* lpb, const float* lpy, const float* lpd, double* alpha,
                      float* log_prob, float* loss, cudaStream_t st);
+// `beta` is scratch of the alpha array's size (sum over b of (T_b + 1) * U_b).
 int launch_tdt_beta(const LatticeMeta& m, int B, int U, int max_duration, const int32_t* durations, int n_dur,
                     int has_zero, const float* lpb, const float* lpy, const float* lpd, const double* alpha,
-                    const float* grad_loss, float* cb, float* ct, float* gdur, cudaStream_t st);
+                    const float* grad_loss, float* cb, float* ct, float* gdur, double* beta, cudaStream_t st);
 
 }  // namespace asr
