@@ -5,11 +5,11 @@
 // registers. The stay / advance / skip moves (ctc.cu:84-98 of the reference)
 // need the two states just left of a block (right, for beta): inside a warp they
 // come by shuffle, across warps through shared memory, so a time step is a few
-// register ops, two shuffles and one (alpha) or two (beta) CTA barriers, with the
-// next step's emission log-probs (and, for beta, alpha) prefetched meanwhile.
-// The backward scatters state posteriors into a shared-memory row of V bins
-// (the blank states' mass summed per warp first) and writes each gradient row
-// once.
+// register ops, two shuffles and one CTA barrier, with the next step's emission
+// log-probs (and, for beta, alpha) prefetched meanwhile. The backward scatters
+// state posteriors into a shared-memory row of V bins (the blank states' mass
+// summed per warp first; two rows, by step parity) and writes each gradient row
+// once, one step later, in the same block as the recursion.
 #include "common.cuh"
 
 namespace asr {
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(32 * NW)
                     const int32_t* __restrict__ targets, const int32_t* __restrict__ in_lens,
                     const int32_t* __restrict__ tgt_lens, const float* __restrict__ grad_loss, int zero_infinity,
                     int post_only, int B, int T, int V, int S, float* __restrict__ grad) {
-    extern __shared__ float row[];     // (V,) posterior mass of the current frame per column
+    extern __shared__ float row[];     // (2, V) posterior mass per column, by step parity
     __shared__ double bnd[2][NW][2];   // first two states of each warp (beta + emission)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = threadIdx.x;
     const int b = blockIdx.x;
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(32 * NW)
     // rows the recursion never reaches are zero (the reference zero-initialises)
     for (int64_t i = (int64_t)(dead ? 0 : ut.Tb) * V + g; i < (int64_t)T * V; i += blockDim.x) gb[i] = 0.f;
     if (dead) return;
-    for (int v = g; v < V; v += blockDim.x) row[v] = 0.f;
+    for (int v = g; v < 2 * V; v += blockDim.x) row[v] = 0.f;
 
     int lab[KS];
     bool skip[KS], in[KS];
@@ -185,43 +185,22 @@ __global__ void __launch_bounds__(32 * NW)
         lpt[j] = in[j] ? lpb[(int64_t)(ut.Tb - 1) * V + lab[j]] : 0.f;
         acur[j] = in[j] ? ab[(int64_t)(ut.Tb - 1) * Lmax + g * KS + j] : -INFINITY;
     }
-    __syncthreads();
-    for (int t = ut.Tb - 1; t >= 0; --t) {
-        // state posteriors scattered to vocabulary bins (ctc.cu:152-165); the blank
-        // states (every even s, about half of them) share bin 0, so their mass is
-        // summed over the warp first instead of contending for one address
-        float pblank = 0.f;
-#pragma unroll
-        for (int j = 0; j < KS; ++j) {
-            if (in[j]) {
-                const float post = __expf((float)(acur[j] + be[j] - logZ));
-                if ((g * KS + j) & 1)
-                    atomicAdd(row + lab[j], post);
-                else
-                    pblank += post;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) pblank += __shfl_xor_sync(0xffffffffu, pblank, o);
-        if (lane == 0) atomicAdd(row, pblank);
-        // next step's alpha and emissions, in flight during the row writes and the recursion
-        if (t > 0) {
-#pragma unroll
-            for (int j = 0; j < KS; ++j)
-                if (in[j]) acur[j] = ab[(int64_t)(t - 1) * Lmax + g * KS + j];
-        }
-        float lnx[KS];
-#pragma unroll
-        for (int j = 0; j < KS; ++j) lnx[j] = (in[j] && t > 0) ? lpb[(int64_t)(t - 1) * V + lab[j]] : 0.f;
-        __syncthreads();
+    // Step t: publish the recursion's boundary states, one barrier, then in one
+    // block (so their latencies overlap) the recursion to beta(t - 1), the state
+    // posteriors of step t scattered into the row buffer of parity t, and the
+    // gradient row of step t + 1, whose buffer every thread finished filling
+    // before the barrier.
+    auto write_row = [&](int tr) {
+        float* rw = row + (tr & 1) * V;
         for (int v = g; v < V; v += blockDim.x) {
-            const int64_t idx = (int64_t)t * V + v;
+            const int64_t idx = (int64_t)tr * V + v;
             // post_only: the posterior mass per column only (the fused CTC head adds
             // the softmax part inside its joint kernel)
-            gb[idx] = post_only ? gl * row[v] : gl * (__expf(lpb[idx]) - row[v]);
-            row[v] = 0.f;
+            gb[idx] = post_only ? gl * rw[v] : gl * (__expf(lpb[idx]) - rw[v]);
+            rw[v] = 0.f;
         }
-        if (t == 0) break;
+    };
+    for (int t = ut.Tb - 1; t >= 0; --t) {
         // beta recursion (ctc.cu:180-204): c[s] = beta[s] + lp[t][lab(s)]
         double c[KS];
 #pragma unroll
@@ -232,26 +211,58 @@ __global__ void __launch_bounds__(32 * NW)
             bnd[t & 1][warp][0] = f1;
             bnd[t & 1][warp][1] = f2;
         }
-        __syncthreads();  // the next warp's first states published; the row is clear
-        double r1 = __shfl_down_sync(0xffffffffu, c[0], 1);
-        double r2 = (KS >= 2) ? __shfl_down_sync(0xffffffffu, c[KS >= 2 ? 1 : 0], 1)
-                              : __shfl_down_sync(0xffffffffu, c[0], 2);
-        const double n1 = (NW > 1 && warp + 1 < NW) ? bnd[t & 1][warp + 1 < NW ? warp + 1 : 0][0] : -INFINITY;
-        const double n2 = (NW > 1 && warp + 1 < NW) ? bnd[t & 1][warp + 1 < NW ? warp + 1 : 0][1] : -INFINITY;
-        if (lane == 31) {
-            r1 = n1;
-            r2 = n2;
+        __syncthreads();  // boundary states published; the row of step t + 1 is complete
+        // state posteriors of step t (ctc.cu:152-165)
+        float post[KS];
+#pragma unroll
+        for (int j = 0; j < KS; ++j) post[j] = in[j] ? __expf((float)(acur[j] + be[j] - logZ)) : 0.f;
+        // next step's alpha and emissions, in flight during the rest of the step
+        float lnx[KS];
+        if (t > 0) {
+#pragma unroll
+            for (int j = 0; j < KS; ++j) {
+                if (in[j]) acur[j] = ab[(int64_t)(t - 1) * Lmax + g * KS + j];
+                lnx[j] = in[j] ? lpb[(int64_t)(t - 1) * V + lab[j]] : 0.f;
+            }
+            double r1 = __shfl_down_sync(0xffffffffu, c[0], 1);
+            double r2 = (KS >= 2) ? __shfl_down_sync(0xffffffffu, c[KS >= 2 ? 1 : 0], 1)
+                                  : __shfl_down_sync(0xffffffffu, c[0], 2);
+            const double n1 = (NW > 1 && warp + 1 < NW) ? bnd[t & 1][warp + 1 < NW ? warp + 1 : 0][0] : -INFINITY;
+            const double n2 = (NW > 1 && warp + 1 < NW) ? bnd[t & 1][warp + 1 < NW ? warp + 1 : 0][1] : -INFINITY;
+            if (lane == 31) {
+                r1 = n1;
+                r2 = n2;
+            }
+            if (KS == 1 && lane == 30) r2 = n1;
+#pragma unroll
+            for (int j = 0; j < KS; ++j) {
+                const double q1 = (j + 1 < KS) ? c[j + 1 < KS ? j + 1 : 0] : r1;
+                const double q2 = (j + 2 < KS) ? c[j + 2 < KS ? j + 2 : 0] : (j + 1 < KS ? r1 : r2);
+                be[j] = in[j] ? lse3_d(c[j], q1, skip[j] ? q2 : -INFINITY) : -INFINITY;
+            }
+#pragma unroll
+            for (int j = 0; j < KS; ++j) lpt[j] = lnx[j];
         }
-        if (KS == 1 && lane == 30) r2 = n1;
+        // the blank states (every even s, about half of them) share bin 0, so their
+        // mass is summed over the warp first instead of contending for one address
+        float* rw = row + (t & 1) * V;
+        float pblank = 0.f;
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
-            const double q1 = (j + 1 < KS) ? c[j + 1 < KS ? j + 1 : 0] : r1;
-            const double q2 = (j + 2 < KS) ? c[j + 2 < KS ? j + 2 : 0] : (j + 1 < KS ? r1 : r2);
-            be[j] = in[j] ? lse3_d(c[j], q1, skip[j] ? q2 : -INFINITY) : -INFINITY;
+            if (in[j]) {
+                if ((g * KS + j) & 1)
+                    atomicAdd(rw + lab[j], post[j]);
+                else
+                    pblank += post[j];
+            }
         }
 #pragma unroll
-        for (int j = 0; j < KS; ++j) lpt[j] = lnx[j];
+        for (int o = 16; o > 0; o >>= 1) pblank += __shfl_xor_sync(0xffffffffu, pblank, o);
+        if (lane == 0) atomicAdd(rw, pblank);
+        if (t + 1 < ut.Tb) write_row(t + 1);
     }
+    __syncthreads();  // the row of step 0 is complete
+    write_row(0);
 }
 
 template <int KS, int NW>
@@ -267,7 +278,7 @@ template <int KS, int NW>
 int launch_ctc_grad(const double* alpha, const float* lp, const int32_t* tg, const int32_t* il, const int32_t* tl,
                     const float* gl, int zinf, int post_only, int B, int T, int V, int S, float* grad,
                     cudaStream_t st) {
-    const size_t smem = sizeof(float) * (size_t)V;
+    const size_t smem = 2 * sizeof(float) * (size_t)V;
     if (smem > 48 * 1024) {
         if (cudaFuncSetAttribute(ctc_grad_kernel<KS, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
