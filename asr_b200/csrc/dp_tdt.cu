@@ -101,6 +101,26 @@ __device__ __forceinline__ DpSmem carve_dp(void* raw, int RV, int NT) {
     return s;
 }
 
+// Register copies of node n's weights (blank, label, duration classes: W <= R
+// values) and their store into ring slot `slot`: with unique duration classes
+// W <= MAXD + 3, and plain loads issued one diagonal ahead cost the step far
+// fewer instructions than per-word cp.async copies.
+template <int R>
+__device__ __forceinline__ void load_node(float (&w)[R], int W, int n, int n_dur, const float* lpb, const float* lpy,
+                                          const float* lpd) {
+    const float* src = lpd + (int64_t)n * n_dur;
+#pragma unroll
+    for (int k = 0; k < R; ++k)
+        if (k < W) w[k] = k == 0 ? __ldg(lpb + n) : (k == 1 ? __ldg(lpy + n) : __ldg(src + k - 2));
+}
+template <int R>
+__device__ __forceinline__ void store_node(const DpSmem& s, const float (&w)[R], int slot, int W, int NT, int u) {
+    float* dst = s.wring + (size_t)slot * W * NT + u;
+#pragma unroll
+    for (int k = 0; k < R; ++k)
+        if (k < W) dst[k * NT] = w[k];
+}
+
 // cp.async copies of node (t, u)'s weights into ring slot `slot`.
 __device__ __forceinline__ void prefetch_node(const DpSmem& s, int slot, int W, int NT, int u, int n, int n_dur,
                                               const float* lpb, const float* lpy, const float* lpd) {
@@ -133,17 +153,28 @@ __global__ void tdt_alpha_kernel(LatticeMeta m, int n_threads, const int32_t* __
     for (int i = u; i < RV * NT; i += NT) s.vring[i] = kNeg;
 
     const int last = Tb + Ub - 1;
-    // prefetch diagonal 0: node (0, 0) only
-    if (u == 0 && Tb > 0) prefetch_node(s, 0, W, NT, 0, off, n_dur, lpb, lpy, lpd);
-    cp_async_commit();
+    // Weights one diagonal ahead: registers stored into the ring (unique classes),
+    // else cp.async copies. Diagonal 0 is node (0, 0) only.
+    float wreg[MAXD + 3];
+    bool have = u == 0 && Tb > 0;
+    if (dt.uniq) {
+        if (have) load_node(wreg, W, off, n_dur, lpb, lpy, lpd);
+    } else {
+        if (have) prefetch_node(s, 0, W, NT, 0, off, n_dur, lpb, lpy, lpd);
+        cp_async_commit();
+    }
     for (int g = 0; g <= last; ++g) {
-        {
-            const int t1 = g + 1 - u;
-            if (g < last && lane_in && t1 >= 0 && t1 < Tb)
-                prefetch_node(s, (g + 1) % RW, W, NT, u, off + t1 * Ub + u, n_dur, lpb, lpy, lpd);
+        const int t1 = g + 1 - u;
+        const bool next = g < last && lane_in && t1 >= 0 && t1 < Tb;
+        if (dt.uniq) {
+            if (have) store_node(s, wreg, g % RW, W, NT, u);  // diagonal g, read from g + 1 on
+            if (next) load_node(wreg, W, off + t1 * Ub + u, n_dur, lpb, lpy, lpd);
+            have = next;
+        } else {
+            if (next) prefetch_node(s, (g + 1) % RW, W, NT, u, off + t1 * Ub + u, n_dur, lpb, lpy, lpd);
             cp_async_commit();
+            cp_async_wait_prev();
         }
-        cp_async_wait_prev();
         __syncthreads();  // weights of diagonal g and alpha of diagonal g - 1 are visible
         const int t = g - u;
         if (lane_in && t >= 0 && t <= Tb) {
@@ -243,16 +274,31 @@ __global__ void tdt_beta_kernel(LatticeMeta m, int n_threads, const int32_t* __r
     for (int i = u; i < RV * NT; i += NT) s.vring[i] = kNeg;
 
     const int first = Tb + Ub - 1;
-    auto prefetch = [&](int g) {
+    // The node's own weights one diagonal ahead: registers stored into the ring
+    // (unique classes), else cp.async copies.
+    auto node_in = [&](int g) {
         const int t = g - u;
-        if (g >= 0 && lane_in && t >= 0 && t < Tb)
-            prefetch_node(s, g & 1, W, NT, u, off + t * Ub + u, n_dur, lpb, lpy, lpd);
-        cp_async_commit();
+        return g >= 0 && lane_in && t >= 0 && t < Tb;
     };
-    prefetch(first);
+    float wreg[MAXD + 3];
+    bool have = node_in(first);
+    if (dt.uniq) {
+        if (have) load_node(wreg, W, off + (first - u) * Ub + u, n_dur, lpb, lpy, lpd);
+    } else {
+        if (have) prefetch_node(s, first & 1, W, NT, u, off + (first - u) * Ub + u, n_dur, lpb, lpy, lpd);
+        cp_async_commit();
+    }
     for (int g = first; g >= 0; --g) {
-        prefetch(g - 1);
-        cp_async_wait_prev();
+        const bool next = node_in(g - 1);
+        if (dt.uniq) {
+            if (have) store_node(s, wreg, g & 1, W, NT, u);
+            if (next) load_node(wreg, W, off + (g - 1 - u) * Ub + u, n_dur, lpb, lpy, lpd);
+            have = next;
+        } else {
+            if (next) prefetch_node(s, (g - 1) & 1, W, NT, u, off + (g - 1 - u) * Ub + u, n_dur, lpb, lpy, lpd);
+            cp_async_commit();
+            cp_async_wait_prev();
+        }
         __syncthreads();  // weights of diagonal g and beta of diagonal g + 1 are visible
         const int t = g - u;
         double be = kNeg;
@@ -395,6 +441,17 @@ __global__ void __launch_bounds__(256) tdt_posterior_kernel(
     }
 }
 
+// One CTA of NT threads per utterance must fit the SM's register file; wider
+// duration rings (MAXD 8, 16) use more registers per thread and so cap the label
+// axis lower than 1024 (a clean ASR_ERR_UNSUPPORTED instead of a failed launch).
+template <typename Kern>
+bool fits_registers(Kern k, int NT) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) return false;
+    const int regs = (fa.numRegs + 7) / 8 * 8;  // per-thread allocation granularity
+    return NT <= fa.maxThreadsPerBlock && (int64_t)regs * NT <= 65536;
+}
+
 template <typename Kern>
 int set_smem(Kern k, size_t bytes) {
     if (bytes > 227 * 1024) return ASR_ERR_UNSUPPORTED;
@@ -411,7 +468,8 @@ int tdt_alpha_launch(const LatticeMeta& m, int B, int U, const int32_t* dur, int
                      const float* lpy, const float* lpd, double* alpha, float* lp, float* loss, cudaStream_t st) {
     const int NT = dp_threads(U);
     const size_t smem = dp_smem_bytes(MAXD + 4, MAXD + 2, 2 + nd, NT);
-    if (set_smem(tdt_alpha_kernel<MAXD>, smem)) return ASR_ERR_UNSUPPORTED;
+    if (!fits_registers(tdt_alpha_kernel<MAXD>, NT) || set_smem(tdt_alpha_kernel<MAXD>, smem))
+        return ASR_ERR_UNSUPPORTED;
     KernelTimer kt("tdt_alpha", st);
     tdt_alpha_kernel<MAXD><<<B, NT, smem, st>>>(m, NT, dur, nd, hz, lpb, lpy, lpd, alpha, lp, loss);
     ASR_LAUNCH_CHECK();
@@ -424,7 +482,8 @@ int tdt_beta_launch(const LatticeMeta& m, int B, int U, const int32_t* dur, int 
                     float* gdur, double* beta, cudaStream_t st) {
     const int NT = dp_threads(U);
     const size_t smem = dp_smem_bytes(2, MAXD + 2, 2 + nd, NT);
-    if (set_smem(tdt_beta_kernel<MAXD>, smem)) return ASR_ERR_UNSUPPORTED;
+    if (!fits_registers(tdt_beta_kernel<MAXD>, NT) || set_smem(tdt_beta_kernel<MAXD>, smem))
+        return ASR_ERR_UNSUPPORTED;
     {
         KernelTimer kt("tdt_beta", st);
         tdt_beta_kernel<MAXD><<<B, NT, smem, st>>>(m, NT, dur, nd, hz, lpb, lpy, lpd, beta);
