@@ -246,6 +246,26 @@ def test_tdt_irregular_durations():
         assert_grad(g, o[name], name)
 
 
+def test_tdt_widest_duration_ring():
+    """Durations 0..16 (17 classes, the 16-diagonal ring of the recursions)."""
+    c = transducer_case(45, 2, (20, 30), (4, 9), 20, 24, n_dur=17, act_std=0.7)
+    loss, ge, gd, gw, gwd = run_tdt(c, sigma=0.05)
+    o = _tdt_oracle(c, 0.05)
+    assert_loss(loss, o["loss"])
+    for name, g in (("d_enc", ge), ("d_dec", gd), ("dW", gw), ("dW_dur", gwd)):
+        assert_grad(g, o[name], name)
+
+
+def test_tdt_wide_duration_ring_rejects_label_axis_beyond_register_file():
+    """With durations up to 16 a recursion thread holds 17 diagonals of state, so
+    one CTA per utterance (one thread per label position) fits the register file
+    only for a few hundred label positions: a longer label axis is reported as an
+    unsupported shape before any recursion is launched, never as a failed launch."""
+    c = transducer_case(46, 1, (20, 20), (600, 600), 16, 32, n_dur=17)
+    with pytest.raises(RuntimeError, match="supported kernel range"):
+        run_tdt(c, sigma=0.0)
+
+
 def test_tdt_no_zero_duration():
     c = transducer_case(33, 2, (15, 25), (3, 6), 16, 12, n_dur=3, act_std=0.7)
     c["durations"] = np.array([1, 2, 4], np.int32)
