@@ -1356,45 +1356,55 @@ struct DhEpilogue {
         w.dirty = true;
         if (++w.u == w.Ub) end_frame(w);
     }
-    // 16 consecutive nodes with U_b >= 16 that stay inside utterance b: the 16
-    // label positions are distinct, so their d_dec rows load and store together.
-    __device__ void group16(DhWalk& w, const float (&v)[16]) const {
+    // N consecutive nodes (N = 16 or 32) with U_b >= N that stay inside utterance
+    // b: the N label positions are distinct, so their d_dec rows load and store
+    // together, and at most one frame boundary falls inside the group. The N
+    // node chains are independent, so a larger N gives the single epilogue warp
+    // of a lane quarter more work to overlap its latencies with; the frame sums
+    // are pairwise trees.
+    template <int N>
+    __device__ void group(DhWalk& w, const float (&v)[N]) const {
         const int k = w.Ub - w.u;  // nodes left in frame t (at most one frame boundary here)
-        int idx[16];
+        int idx[N];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < N; ++i) {
             int ui = w.u + i;
             if (ui >= w.Ub) ui -= w.Ub;
             idx[i] = ui * kDhM + cl;
         }
-        float dv[16], sa[16];
+        float dv[N], sa[N];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) dv[i] = sdin[idx[i]];
+        for (int i = 0; i < N; ++i) dv[i] = sdin[idx[i]];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) sa[i] = sacc[idx[i]];
-        float lo = 0.f, hi = 0.f;
+        for (int i = 0; i < N; ++i) sa[i] = sacc[idx[i]];
+        float lo[N], hi[N];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < N; ++i) {
             const float h = tanh_fast((i < k ? w.e_cur : w.e_nxt) + dv[i]);
             const float x = v[i] * (1.f - h * h);
             sacc[idx[i]] = sa[i] + x;
-            if (i < k)
-                lo += x;
-            else
-                hi += x;
+            lo[i] = i < k ? x : 0.f;
+            hi[i] = i < k ? 0.f : x;
         }
+#pragma unroll
+        for (int s2 = 1; s2 < N; s2 *= 2)
+#pragma unroll
+            for (int i = 0; i + s2 < N; i += 2 * s2) {
+                lo[i] += lo[i + s2];
+                hi[i] += hi[i + s2];
+            }
         w.dirty = true;
-        if (k < 16) {  // frame t ends inside the group; frame t + 1 is in the same utterance
-            w.acc_e += lo;
+        if (k < N) {  // frame t ends inside the group; frame t + 1 is in the same utterance
+            w.acc_e += lo[0];
             flush_enc(w);
             ++w.t;
             w.e_cur = w.e_nxt;
             w.e_nxt = w.t + 1 < w.Tb ? enc_at(w.b, w.t + 1) : 0.f;
-            w.acc_e = hi;
-            w.u = 16 - k;
+            w.acc_e = hi[0];
+            w.u = N - k;
         } else {
-            w.acc_e += lo;
-            w.u += 16;
+            w.acc_e += lo[0];
+            w.u += N;
             if (w.u == w.Ub) end_frame(w);
         }
     }
@@ -1537,19 +1547,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tc_fence_after();
             const int cnt = min(kDhNodes, e - (s + tile * kDhNodes));
             const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + buf * kDhNodes;
-            for (int g16 = 0; g16 * 16 < cnt; ++g16) {
+            for (int g16 = 0; g16 * 16 < cnt;) {
+                const int left = cnt - g16 * 16;
+                if (kSmemDec && left >= 32 && w.Ub >= 32 && (w.t < w.Tb - 1 || w.Ub - w.u >= 32)) {
+                    float v[32];
+                    tmem_ld32(taddr + g16 * 16, v);
+                    ep.template group<32>(w, v);
+                    g16 += 2;
+                    continue;
+                }
                 float v[16];
                 tmem_ld16(taddr + g16 * 16, v);
-                const int left = cnt - g16 * 16;
                 const bool fast = kSmemDec && left >= 16 && w.Ub >= 16 &&
                                   (w.t < w.Tb - 1 || w.Ub - w.u >= 16);
                 if (fast) {
-                    ep.group16(w, v);
+                    ep.template group<16>(w, v);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 16; ++i)
                         if (i < left) ep.node(w, v[i]);
                 }
+                ++g16;
             }
             tc_fence_before();
             __syncwarp();
