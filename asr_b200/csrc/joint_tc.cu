@@ -433,6 +433,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + buf * kNC;
                 for (int gi = 0; gi < width / 16; ++gi) {
+                    if (!kBwd && gi + 1 < width / 16 && col + gi * 16 + 32 <= a.V) {
+                        // two token groups at once: one TMEM wait, and the max and the
+                        // sum of the online log-sum-exp as pairwise trees, so the chain
+                        // of this lane-quarter's single warp is 5 deep instead of 31
+                        const int c0 = col + gi * 16;
+                        float v[32], t[32];
+                        tmem_ld32(taddr + gi * 16, v);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) t[i] = v[i];
+#pragma unroll
+                        for (int s2 = 1; s2 < 32; s2 *= 2)
+#pragma unroll
+                            for (int i = 0; i + s2 < 32; i += 2 * s2) t[i] = fmaxf(t[i], t[i + s2]);
+                        if (t[0] > m) {
+                            s = (m == -INFINITY) ? 0.f : s * __expf(m - t[0]);
+                            m = t[0];
+                        }
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) t[i] = __expf(v[i] - m);
+#pragma unroll
+                        for (int s2 = 1; s2 < 32; s2 *= 2)
+#pragma unroll
+                            for (int i = 0; i + s2 < 32; i += 2 * s2) t[i] += t[i + s2];
+                        s += t[0];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (c0 + i == a.blank) lb = v[i];
+                            if (c0 + i == y) ly = v[i];
+                        }
+                        ++gi;
+                        continue;
+                    }
                     float v[16];
                     tmem_ld16(taddr + gi * 16, v);
                     const int c0 = col + gi * 16;
