@@ -13,9 +13,10 @@
 // The recursion variables of the last MAXD+2 diagonals live in a CTA-wide
 // shared-memory ring (float64), so a thread reads its neighbour label position
 // directly; one __syncthreads separates consecutive diagonals. Each thread
-// copies the weights of its next node (blank / label / duration log-probs) into
-// a shared-memory ring with cp.async one diagonal ahead, so the global-memory
-// latency overlaps the current diagonal. The edge posteriors need alpha and
+// fetches the weights of its next node (blank / label / duration log-probs) one
+// diagonal ahead into a shared-memory ring, by plain loads into registers when
+// the duration classes are unique and by cp.async otherwise, so the
+// global-memory latency overlaps the current diagonal. The edge posteriors need alpha and
 // beta but feed neither recursion: a separate kernel computes them for all
 // nodes in parallel once beta is complete.
 // Durations are arbitrary (duplicates allowed): for each duration value the
