@@ -256,11 +256,12 @@ def test_tdt_widest_duration_ring():
         assert_grad(g, o[name], name)
 
 
-def test_tdt_wide_duration_ring_rejects_label_axis_beyond_register_file():
-    """With durations up to 16 a recursion thread holds 17 diagonals of state, so
-    one CTA per utterance (one thread per label position) fits the register file
-    only for a few hundred label positions: a longer label axis is reported as an
-    unsupported shape before any recursion is launched, never as a failed launch."""
+def test_tdt_wide_duration_ring_rejects_label_axis_beyond_one_cta():
+    """With durations up to 16 the recursions keep 18-20 diagonals of state per
+    label position, so one CTA per utterance (one thread per label position) fits
+    one SM's shared memory and registers only up to about a hundred label
+    positions: a longer label axis is reported as an unsupported shape before any
+    recursion is launched, never as a failed launch."""
     c = transducer_case(46, 1, (20, 20), (600, 600), 16, 32, n_dur=17)
     with pytest.raises(RuntimeError, match="supported kernel range"):
         run_tdt(c, sigma=0.0)
