@@ -132,7 +132,11 @@ __device__ __forceinline__ void prefetch_node(const DpSmem& s, int slot, int W, 
     for (int k = 0; k < n_dur; ++k) cp_async4(dst + (2 + k) * NT, src + k);
 }
 
-template <int MAXD>
+// kGW: the edge weights are read from global memory (L1 / L2) at the source
+// nodes instead of from the shared-memory weight ring, so a label position costs
+// only its alpha ring in shared memory: the variant for label axes whose ring
+// would not fit (U above about 830 with five duration classes).
+template <int MAXD, bool kGW>
 __global__ void tdt_alpha_kernel(LatticeMeta m, int n_threads, const int32_t* __restrict__ durations, int n_dur,
                                  int has_zero, const float* __restrict__ lpb, const float* __restrict__ lpy,
                                  const float* __restrict__ lpd, double* __restrict__ alpha,
@@ -158,16 +162,19 @@ __global__ void tdt_alpha_kernel(LatticeMeta m, int n_threads, const int32_t* __
     // else cp.async copies. Diagonal 0 is node (0, 0) only.
     float wreg[MAXD + 3];
     bool have = u == 0 && Tb > 0;
-    if (dt.uniq) {
-        if (have) load_node(wreg, W, off, n_dur, lpb, lpy, lpd);
-    } else {
-        if (have) prefetch_node(s, 0, W, NT, 0, off, n_dur, lpb, lpy, lpd);
-        cp_async_commit();
+    if (!kGW) {
+        if (dt.uniq) {
+            if (have) load_node(wreg, W, off, n_dur, lpb, lpy, lpd);
+        } else {
+            if (have) prefetch_node(s, 0, W, NT, 0, off, n_dur, lpb, lpy, lpd);
+            cp_async_commit();
+        }
     }
     for (int g = 0; g <= last; ++g) {
         const int t1 = g + 1 - u;
         const bool next = g < last && lane_in && t1 >= 0 && t1 < Tb;
-        if (dt.uniq) {
+        if (kGW) {
+        } else if (dt.uniq) {
             if (have) store_node(s, wreg, g % RW, W, NT, u);  // diagonal g, read from g + 1 on
             if (next) load_node(wreg, W, off + t1 * Ub + u, n_dur, lpb, lpy, lpd);
             have = next;
@@ -193,12 +200,19 @@ __global__ void tdt_alpha_kernel(LatticeMeta m, int n_threads, const int32_t* __
                 double vsrc[2 * (MAXD + 1)];
 #pragma unroll
                 for (int dv = 0; dv <= MAXD; ++dv) {
-                    const float* wb = s.wring + (size_t)((g - dv + RW) % RW) * W * NT + u;       // (t - dv, u)
-                    const float* wt = s.wring + (size_t)((g - dv - 1 + RW) % RW) * W * NT + ul;  // (t - dv, u - 1)
                     const int kb = max(dt.single[dv], 0);
                     const int kt = max(dv == 0 ? dt.tok0_k : dt.single[dv], 0);
-                    wsum[dv] = wb[0] + wb[(2 + kb) * NT];
-                    wsum[MAXD + 1 + dv] = wt[NT] + wt[(2 + kt) * NT];
+                    if (kGW) {  // source rows clamped into the utterance; invalid terms are dropped below
+                        const int ts = min(max(t - dv, 0), Tb - 1);
+                        const int nb = off + ts * Ub + u, nt = off + ts * Ub + ul;
+                        wsum[dv] = __ldg(lpb + nb) + __ldg(lpd + (int64_t)nb * n_dur + kb);
+                        wsum[MAXD + 1 + dv] = __ldg(lpy + nt) + __ldg(lpd + (int64_t)nt * n_dur + kt);
+                    } else {
+                        const float* wb = s.wring + (size_t)((g - dv + RW) % RW) * W * NT + u;       // (t - dv, u)
+                        const float* wt = s.wring + (size_t)((g - dv - 1 + RW) % RW) * W * NT + ul;  // (t - dv, u - 1)
+                        wsum[dv] = wb[0] + wb[(2 + kb) * NT];
+                        wsum[MAXD + 1 + dv] = wt[NT] + wt[(2 + kt) * NT];
+                    }
                     vsrc[dv] = s.vring[((g - dv + RV) % RV) * NT + u];
                     vsrc[MAXD + 1 + dv] = s.vring[((g - dv - 1 + RV) % RV) * NT + ul];
                 }
@@ -222,8 +236,14 @@ __global__ void tdt_alpha_kernel(LatticeMeta m, int n_threads, const int32_t* __
 #pragma unroll
                 for (int dv = 1; dv <= MAXD; ++dv) {
                     if (dt.mask[dv] && t - dv >= 0 && t - dv < Tb) {
-                        const float* w = s.wring + (size_t)((g - dv) % RW) * W * NT + u;
-                        const float e = w[0] + dur_weight(w + 2 * NT, NT, dt.mask[dv], dt.single[dv]);
+                        float e;
+                        if (kGW) {
+                            const int n = off + (t - dv) * Ub + u;
+                            e = __ldg(lpb + n) + dur_weight(lpd + (int64_t)n * n_dur, 1, dt.mask[dv], dt.single[dv]);
+                        } else {
+                            const float* w = s.wring + (size_t)((g - dv) % RW) * W * NT + u;
+                            e = w[0] + dur_weight(w + 2 * NT, NT, dt.mask[dv], dt.single[dv]);
+                        }
                         terms[dv] = s.vring[((g - dv) % RV) * NT + u] + (double)e;
                     }
                 }
@@ -234,8 +254,14 @@ __global__ void tdt_alpha_kernel(LatticeMeta m, int n_threads, const int32_t* __
                         const uint32_t mk = dv == 0 ? dt.tok0 : dt.mask[dv];
                         const int sk = dv == 0 ? dt.tok0_k : dt.single[dv];
                         if (mk && t - dv >= 0 && t - dv < Tb) {
-                            const float* w = s.wring + (size_t)((g - dv - 1) % RW) * W * NT + (u - 1);
-                            const float e = w[NT] + dur_weight(w + 2 * NT, NT, mk, sk);
+                            float e;
+                            if (kGW) {
+                                const int n = off + (t - dv) * Ub + (u - 1);
+                                e = __ldg(lpy + n) + dur_weight(lpd + (int64_t)n * n_dur, 1, mk, sk);
+                            } else {
+                                const float* w = s.wring + (size_t)((g - dv - 1) % RW) * W * NT + (u - 1);
+                                e = w[NT] + dur_weight(w + 2 * NT, NT, mk, sk);
+                            }
                             terms[MAXD + 1 + dv] = s.vring[((g - dv - 1) % RV) * NT + u - 1] + (double)e;
                         }
                     }
@@ -469,10 +495,17 @@ int tdt_alpha_launch(const LatticeMeta& m, int B, int U, const int32_t* dur, int
                      const float* lpy, const float* lpd, double* alpha, float* lp, float* loss, cudaStream_t st) {
     const int NT = dp_threads(U);
     const size_t smem = dp_smem_bytes(MAXD + 4, MAXD + 2, 2 + nd, NT);
-    if (!fits_registers(tdt_alpha_kernel<MAXD>, NT) || set_smem(tdt_alpha_kernel<MAXD>, smem))
-        return ASR_ERR_UNSUPPORTED;
     KernelTimer kt("tdt_alpha", st);
-    tdt_alpha_kernel<MAXD><<<B, NT, smem, st>>>(m, NT, dur, nd, hz, lpb, lpy, lpd, alpha, lp, loss);
+    if (smem <= 227 * 1024) {  // weights in the shared-memory ring
+        if (!fits_registers(tdt_alpha_kernel<MAXD, false>, NT) || set_smem(tdt_alpha_kernel<MAXD, false>, smem))
+            return ASR_ERR_UNSUPPORTED;
+        tdt_alpha_kernel<MAXD, false><<<B, NT, smem, st>>>(m, NT, dur, nd, hz, lpb, lpy, lpd, alpha, lp, loss);
+    } else {  // long label axis: weights read at the source nodes, alpha ring only
+        const size_t smem_g = dp_smem_bytes(0, MAXD + 2, 2 + nd, NT);
+        if (!fits_registers(tdt_alpha_kernel<MAXD, true>, NT) || set_smem(tdt_alpha_kernel<MAXD, true>, smem_g))
+            return ASR_ERR_UNSUPPORTED;
+        tdt_alpha_kernel<MAXD, true><<<B, NT, smem_g, st>>>(m, NT, dur, nd, hz, lpb, lpy, lpd, alpha, lp, loss);
+    }
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }

@@ -256,6 +256,23 @@ def test_tdt_widest_duration_ring():
         assert_grad(g, o[name], name)
 
 
+def test_tdt_long_label_axis_reads_weights_from_global_memory():
+    """900 label positions with durations 0..4: the alpha sweep's shared-memory
+    weight ring would not fit one SM, so it reads the edge weights at the source
+    nodes instead; results still match the oracle. With 900 label positions the
+    gradients reach magnitudes of 10^2..10^3 and sum ~22 K nodes in float32, so
+    they are held to 2e-5 of their largest magnitude (measured: 5e-6, smoothly
+    growing with U from 7e-7 at U = 60 through 3e-6 at U = 700 on the ring path)."""
+    c = transducer_case(47, 2, (10, 14), (880, 899), 16, 32, n_dur=5, act_std=0.7)
+    loss, ge, gd, gw, gwd = run_tdt(c, sigma=0.05)
+    o = _tdt_oracle(c, 0.05)
+    assert_loss(loss, o["loss"])
+    for name, g in (("d_enc", ge), ("d_dec", gd), ("dW", gw), ("dW_dur", gwd)):
+        got, want = g.detach().double().cpu().numpy(), o[name]
+        err, scale = np.abs(got - want).max(), np.abs(want).max()
+        assert err <= 1e-4 + 2e-5 * scale, f"{name}: max-abs error {err:.3e}, largest magnitude {scale:.3e}"
+
+
 def test_tdt_wide_duration_ring_rejects_label_axis_beyond_one_cta():
     """With durations up to 16 the recursions keep 18-20 diagonals of state per
     label position, so one CTA per utterance (one thread per label position) fits
@@ -581,5 +598,9 @@ def test_hidden_vector_paths_match_scalar_path(act, d):
     lv, *gv = out["vector"]
     ls, *gs = out["scalar"]
     torch.testing.assert_close(lv, ls, rtol=1e-6, atol=1e-6)
+    # the backward sums with atomics, in a different order on each run: float32
+    # gradients differ by rounding, bf16 activation gradients by the odd bf16 ulp
+    # (4e-3 relative) where that rounding crosses a bf16 boundary
+    bar = 2e-4 if act == "bf16" else 1e-5
     for name, a, b in zip(("d_enc", "d_dec", "dW"), gv, gs):
-        assert _rel(a, b) < 1e-5, f"{name}: {_rel(a, b):.3e}"
+        assert _rel(a, b) < bar, f"{name}: {_rel(a, b):.3e}"
