@@ -10,36 +10,27 @@
 //
 // The scratch is one file-scope __device__ array of ASR_TDT_FORWARD_NOALLOC_SCRATCH_BYTES
 // bytes; every GPU that loads the library holds it until the process exits.
-// Host code cannot use the array's name as a device address, so its address is
-// looked up once per device with cudaGetSymbolAddress while that device is
-// current (the first call on a device does this; make that first call before
-// any stream capture). All calls share the array and it keeps the last call's
-// contents: the lattice bookkeeping kernel rewrites every byte the forward reads,
-// so nothing needs clearing, but calls that overlap on the GPU (other streams,
-// other host threads) race on it and must be serialised by the caller.
-#include <mutex>
-
+// Host code cannot use the array's name as a device address. A __device__
+// symbol's address belongs to the CUDA context that loaded the module, so it is
+// looked up with cudaGetSymbolAddress on every call, in the calling thread's
+// current context: any context that has the library loaded works, including a
+// primary context re-created after cudaDeviceReset and a driver-API context the
+// caller made current. The first call in a context loads the module there (make
+// it before any stream capture). All calls share the array and it keeps the last
+// call's contents: the lattice bookkeeping kernel rewrites every byte the forward
+// reads, so nothing needs clearing, but calls that overlap on the GPU (other
+// streams, other host threads) race on it and must be serialised by the caller.
 #include "asr_b200.h"
 
 namespace {
 
 static __device__ __align__(256) unsigned char g_tdt_forward_scratch[ASR_TDT_FORWARD_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mu;
-void* g_dev_ptr[kMaxDevices] = {};
-
-// Device address of the scratch array on the current device, or nullptr.
-void* scratch_on_current_device() {
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-    std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_dev_ptr[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_tdt_forward_scratch) != cudaSuccess) return nullptr;
-        g_dev_ptr[dev] = p;
-    }
-    return g_dev_ptr[dev];
+// Device address of the scratch array in the current context, or nullptr.
+void* scratch_in_current_context() {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tdt_forward_scratch) != cudaSuccess) return nullptr;
+    return p;
 }
 
 }  // namespace
@@ -54,7 +45,7 @@ extern "C" int asr_tdt_forward_noalloc(const float* encoder, const float* decode
     const size_t need = asr_tdt_workspace_bytes(B, T, U, V, n_dur, d, tf32, 0);
     if (need == 0 && B != 0) return ASR_ERR_INVALID_ARGUMENT;
     if (need > (size_t)ASR_TDT_FORWARD_NOALLOC_SCRATCH_BYTES) return ASR_ERR_SCRATCH_LIMIT;
-    void* scratch = scratch_on_current_device();
+    void* scratch = scratch_in_current_context();
     if (!scratch) return ASR_ERR_CUDA;
     return asr_tdt_forward(encoder, decoder, joint_W, joint_W_dur, targets, in_lens, tgt_lens, durations, n_dur,
                            max_duration, has_zero, B, T, U, V, d, S, blank_idx, sigma, tf32, loss, alpha,

@@ -183,8 +183,15 @@ int asr_tdt_backward_ex(const void* encoder, const void* decoder, int act_dtype,
  * No counterpart in the reference. Its scratch is a fixed array of
  * ASR_TDT_FORWARD_NOALLOC_SCRATCH_BYTES in device memory, held by every GPU that
  * loads the library; problems whose asr_tdt_workspace_bytes(..., backward = 0)
- * exceed it return ASR_ERR_SCRATCH_LIMIT without launching anything. The first
- * call on a device looks up the array's device address (make it before any stream
+ * exceed it return ASR_ERR_SCRATCH_LIMIT without launching anything. With
+ * tf32 = 0 that workspace is the per-utterance lattice bookkeeping (about 16
+ * bytes per utterance); with tf32 = 1 it also holds a bf16 copy of the joint
+ * weights (2 * ceil16(V + n_dur) * ceil64(d) bytes) and one bf16 hidden row per
+ * lattice node of capacity (2 * ceil64(d) bytes for each of B * T * U nodes), so
+ * at V = 1024 + 5 and d = 640 only B * T * U up to about 2,000 nodes fit. The
+ * array's device address is looked up on every call in the calling thread's
+ * current CUDA context, so any context that has loaded the library works; the
+ * first call in a context loads the module there (make it before any stream
  * capture). All calls share the array, so calls that overlap on the GPU race;
  * serialise them. Allocates nothing. */
 int asr_tdt_forward_noalloc(const float* encoder, const float* decoder, const float* joint_W,

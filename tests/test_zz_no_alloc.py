@@ -96,8 +96,9 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     null = ctypes.c_void_p(0)
     limit = 4 << 20
     lib.asr_tdt_workspace_bytes.restype = ctypes.c_size_t
-    # the forward's scratch is the per-utterance lattice bookkeeping (~16 bytes per
-    # utterance), so a batch of 400k short utterances needs more than the array holds
+    # with tf32 = 0 the forward's scratch is the per-utterance lattice bookkeeping
+    # (~16 bytes per utterance), so a batch of 400k short utterances needs more than
+    # the array holds (with tf32 = 1 the bf16 weights and hidden rows come on top)
     B, T, U, V, Dn, d = 400_000, 2, 2, 16, 5, 8
     assert lib.asr_tdt_workspace_bytes(B, T, U, V, Dn, d, 0, 0) > limit
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -106,3 +107,21 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     assert rc == 5
     lib.asr_status_string.restype = ctypes.c_char_p
     assert b"scratch" in lib.asr_status_string(rc)
+
+
+def test_noalloc_forward_takes_no_device_memory():
+    """After a first call in this context (which loads the module and so may map
+    memory), further calls leave the device's free memory as it was: no
+    cudaMalloc, no pool growth. Both joint paths. torch's caching allocator holds
+    the inputs and outputs, which are warmed up before the measurement."""
+    lib = _lib.capi()
+    c = TDT["wider"]
+    for tf32 in (0, 1):
+        _run(lib, c, tf32, noalloc=True)
+        torch.cuda.synchronize()
+        free0, _ = torch.cuda.mem_get_info()
+        for _ in range(3):
+            _run(lib, c, tf32, noalloc=True)
+        torch.cuda.synchronize()
+        free1, _ = torch.cuda.mem_get_info()
+        assert free1 >= free0, f"tf32={tf32}: free device memory fell by {free0 - free1} bytes"
