@@ -211,8 +211,34 @@ def profiler_report(clear=True):
 # ------------------------------------------------------------ reference arm
 
 
+CPU_SAMPLE = 8  # utterances in the fixed seeded CPU sample of the workload
+CPU_PER_STEP = 2  # of them per step of the reference arm (cycled)
+
+
+def cpu_sample(in_lens):
+    """The fixed seeded subsample of the workload that both CPU timings use."""
+    rng = np.random.default_rng([SEED, 99])
+    return np.sort(rng.choice(len(in_lens), size=min(CPU_SAMPLE, len(in_lens)), replace=False))
+
+
+def _oracle_utterances(idx, in_lens, tgt_lens, W, Wd, threads):
+    from oracle import oracle
+
+    b = make_batch(np.asarray(idx), in_lens, tgt_lens)
+    oracle.tdt(b["enc"], b["dec"], W, Wd, b["targets"], b["in_lens"], b["tgt_lens"], np.array(DURATIONS, np.int32),
+               sigma=SIGMA, grad_loss=np.ones(len(idx), np.float32), nthreads=threads)
+
+
+def _cpu_sample_text(idx, in_lens, tgt_lens, threads, per_step=None):
+    what = f"{per_step} of them per step, cycled" if per_step else "all of them once"
+    return (f"fixed seeded sample of {len(idx)} utterances of the workload (indices {list(map(int, idx))}, "
+            f"T={list(map(int, in_lens[idx]))}, U={list(map(int, tgt_lens[idx]))}), {what}; fwd+bwd, float64 C "
+            f"restatement of the reference's float64 oracles (tests/loss/tdt_reference.py), {threads} threads")
+
+
 def run_reference(args, rank):
-    """CPU restatement of the reference path (oracle/) on all host threads."""
+    """CPU restatement of the reference path (oracle/) on all host threads, over
+    the same fixed sample of utterances as the cpu_baseline leg of our arm."""
     if rank != 0:
         return
     from oracle import oracle
@@ -221,33 +247,32 @@ def run_reference(args, rank):
     in_lens, tgt_lens = workload_lengths()
     W, Wd = joint_weights()
     threads = os.cpu_count() or 1
-    order = np.argsort(in_lens * (tgt_lens + 1))[GLOBAL_B // 2:]  # median-and-up lattices, cycled
-
-    def one(i):
-        b = make_batch(np.array([i]), in_lens, tgt_lens)
-        oracle.tdt(b["enc"], b["dec"], W, Wd, b["targets"], b["in_lens"], b["tgt_lens"], np.array(DURATIONS, np.int32),
-                   sigma=SIGMA, grad_loss=np.ones(1, np.float32), nthreads=threads)
-
+    idx = cpu_sample(in_lens)
     k = 0
+
+    def one():
+        nonlocal k
+        _oracle_utterances([idx[(k + j) % len(idx)] for j in range(CPU_PER_STEP)], in_lens, tgt_lens, W, Wd, threads)
+        k += CPU_PER_STEP
+
     for _ in range(args.warmup):
-        one(int(order[k % len(order)]))
-        k += 1
+        one()
+    k = 0
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        one(int(order[k % len(order)]))
-        k += 1
+        one()
     dt = time.perf_counter() - t0
-    value = args.steps / dt
+    value = args.steps * CPU_PER_STEP / dt
     line = {
         "impl": "reference", "metric": "fused joint+loss fwd+bwd utterances/s", "value": round(value, 4),
         "unit": "utterances/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1000 * dt / args.steps, 3), "higher_is_better": True, "dtype": "f64",
         "data": "synthetic", "scaling": "strong",
         "config": {"workload": "tdt_bpe1024_sharded", "global_batch": GLOBAL_B, "vocab": VOCAB,
-                   "durations": DURATIONS, "d_model": D_MODEL, "sample": "1 utterance per step"},
+                   "durations": DURATIONS, "d_model": D_MODEL,
+                   "sample": f"{CPU_PER_STEP} utterances per step from a fixed sample of {len(idx)}"},
         "cpu_baseline": {"value": round(value, 4), "unit": "utterances/s", "cores": threads, "kind": "port",
-                         "sample": "1 utterance per step (median-or-longer lattice of the workload), fwd+bwd, "
-                                   "float64 C restatement of the reference algorithm"},
+                         "sample": _cpu_sample_text(idx, in_lens, tgt_lens, threads, CPU_PER_STEP)},
         "e2e": {"value": round(value, 4), "unit": "utterances/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -256,20 +281,67 @@ def run_reference(args, rank):
 # ----------------------------------------------------------------- our arm
 
 
-def cpu_baseline_leg(in_lens, tgt_lens, W, Wd, sample=2):
+def cpu_baseline_leg(in_lens, tgt_lens, W, Wd):
     from oracle import oracle
 
     oracle.build()
     threads = os.cpu_count() or 1
-    idx = np.arange(sample)
-    b = make_batch(idx, in_lens, tgt_lens)
+    idx = cpu_sample(in_lens)
     t0 = time.perf_counter()
-    oracle.tdt(b["enc"], b["dec"], W, Wd, b["targets"], b["in_lens"], b["tgt_lens"], np.array(DURATIONS, np.int32),
-               sigma=SIGMA, grad_loss=np.ones(sample, np.float32), nthreads=threads)
+    _oracle_utterances(idx, in_lens, tgt_lens, W, Wd, threads)
     dt = time.perf_counter() - t0
-    return {"value": round(sample / dt, 4), "unit": "utterances/s", "cores": threads, "kind": "port",
-            "sample": f"utterances 0..{sample - 1} of the workload (T={list(map(int, in_lens[:sample]))}, "
-                      f"U={list(map(int, tgt_lens[:sample]))}), fwd+bwd, float64 C oracle, {threads} threads"}
+    return {"value": round(len(idx) / dt, 4), "unit": "utterances/s", "cores": threads, "kind": "port",
+            "sample": _cpu_sample_text(idx, in_lens, tgt_lens, threads)}
+
+
+# ------------------------------------------- the reference's own CUDA op, same GPU
+#
+# The reference installed by its own build into baseline/_ref (its CUDA loss op
+# for sm_100a; cuBLAS joint GEMMs: fp32 with tf32 = 0, TF32 tensor cores with
+# tf32 = 1) is timed on the same workload and GPU, fwd+bwd with inputs resident
+# on the device, in a child process (its op library and ours both register the
+# asr:: namespace). A secondary baseline beside the reference arm.
+
+REF_ROOT = ROOT / "baseline" / "_ref"
+
+
+def reference_workload(name):
+    """Numpy inputs of a workload in the reference functional API's terms."""
+    if name == "c5":
+        in_lens, tgt_lens = workload_lengths()
+        W, Wd = joint_weights()
+        b = make_batch(np.arange(GLOBAL_B), in_lens, tgt_lens)
+        return dict(b, kind="tdt", W=W, W_dur=Wd, durations=np.array(DURATIONS, np.int32), sigma=SIGMA,
+                    grad_loss=np.full(GLOBAL_B, 1.0 / GLOBAL_B, np.float32))
+    cfg = CONFIGS[name]
+    x = config_inputs(cfg)
+    x["kind"] = cfg["kind"]
+    x["grad_loss"] = np.full(cfg["B"], 1.0 / cfg["B"], np.float32)
+    if cfg["kind"] == "tdt":
+        x.update(durations=np.array(DURATIONS, np.int32), sigma=SIGMA)
+    return x
+
+
+def reference_cuda_leg(workload, ours_value, steps=3, warmup=1, modes=(1, 0)):
+    if not any((REF_ROOT / "asr" / "loss").glob("_C*.so")):
+        return {"unavailable": "reference not installed in baseline/_ref (baseline/install_reference.py)"}
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as tmp:
+        spec = Path(tmp) / "spec.json"
+        spec.write_text(json.dumps({"bench_dir": str(ROOT), "workload": workload, "tf32": list(modes),
+                                    "steps": steps, "warmup": warmup}))
+        r = subprocess.run([sys.executable, str(ROOT / "baseline" / "ref_worker.py"), "time", str(REF_ROOT),
+                            str(spec)], capture_output=True, text=True, timeout=900)
+    if r.returncode != 0:
+        return {"unavailable": "reference worker failed: " + (r.stderr.strip().splitlines() or ["?"])[-1][:200]}
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    for v in out.values():
+        v["ours_over_reference"] = round(ours_value / v["utt_per_s"], 3)
+    out["what"] = ("the reference's own CUDA op (asr.loss._C built by its own setup.py for sm_100a), fwd+bwd on the "
+                   "same workload and GPU, inputs resident, CUDA events, median of the timed steps; tf32_1: TF32 "
+                   "cuBLAS joint GEMMs (the systems' setting), tf32_0: fp32")
+    return out
 
 
 # ------------------------------------------------ other BASELINE configurations
@@ -435,6 +507,7 @@ def run_config(args):
         "e2e": {"value": round(B / (e2e_ms / 1000.0), 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": int(sum(v[0] for v in prof.values())), "kernels": kernels, "clocks": clock_info,
+        "reference_cuda": None if args.no_reference_cuda else reference_cuda_leg(args.workload, B / (ms / 1000.0)),
     }
     print(json.dumps(line), flush=True)
 
@@ -1008,6 +1081,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tf32", type=int, default=1, help="1: bf16 tensor-core joint (the systems' setting)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-cuda", action="store_true",
+                    help="skip timing the reference's own CUDA op (baseline/_ref) on the same workload")
     ap.add_argument("--clocks-log", default=None)
     ap.add_argument("--batch", type=int, default=None,
                     help="profiling aid: run only the first BATCH utterances of the workload")
@@ -1246,6 +1321,9 @@ def main():
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline_leg(in_lens, tgt_lens, W_np, Wd_np)
+        ref_cuda = None
+        if world == 1 and not args.no_reference_cuda and not args.batch:
+            ref_cuda = reference_cuda_leg("c5", value)
         tc = bool(args.tf32) and _lib.joint_uses_tensor_cores(VOCAB, len(DURATIONS), D_MODEL)
         line = {
             "metric": "fused joint+loss fwd+bwd utterances/s", "value": round(value, 3), "unit": "utterances/s",
@@ -1266,7 +1344,7 @@ def main():
                     "serial": {"value": round(GLOBAL_B / (e2e_serial_ms / 1000.0), 3),
                                "ms_per_step": round(e2e_serial_ms, 4)}},
             "gpu_launches": launches_total, "kernels": per_kernel,
-            "clocks": clock_info,
+            "clocks": clock_info, "reference_cuda": ref_cuda,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -52,3 +52,22 @@ def ctc_case(seed, B, T_rng, V, S_rng):
         "tgt_lens": tgt_lens,
         "grad_loss": np.ones(B, np.float32),
     }
+
+
+def config_draws():
+    """Seeded draws with the shapes and distributions of BASELINE configs 1-5
+    (fewer utterances, so that the float64 oracle finishes in seconds): config 1
+    CTC char, 2 RNN-T char (T up to 400, U up to 150), 3 TDT BPE-1024, 4 RNN-T
+    BPE-1024 with d = 1024 and T = 400, 5 the long end of the sharded TDT
+    workload (T 450-500, U 100-120)."""
+    c1 = ctc_case(61, 8, (150, 200), 29, (20, 60))
+    c1["kind"] = "ctc"
+    c2 = transducer_case(62, 4, (300, 400), (120, 150), 30, 640)
+    c2["kind"] = "rnnt"
+    c3 = transducer_case(63, 3, (300, 400), (60, 80), 1024, 640, n_dur=5)
+    c3.update(kind="tdt", sigma=0.05)
+    c4 = transducer_case(64, 2, None, (40, 100), 1024, 1024, fixed_T=400)
+    c4["kind"] = "rnnt"
+    c5 = transducer_case(65, 4, (450, 500), (100, 120), 1024, 640, n_dur=5)
+    c5.update(kind="tdt", sigma=0.05)
+    return {"c1_ctc": c1, "c2_rnnt_char": c2, "c3_tdt_bpe": c3, "c4_rnnt_d1024": c4, "c5_tdt_long": c5}

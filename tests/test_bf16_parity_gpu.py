@@ -1,0 +1,160 @@
+"""The bf16 tensor-core path (tf32 = 1: the systems' setting and the benchmarked
+path) against the float64 oracle at the BASELINE configurations' shapes.
+
+The joint's operands are rounded to bf16 (8 significant bits: hidden rows H =
+tanh(enc + dec) and the joint weights; G = d loss / d logits in the backward)
+and every sum is accumulated in fp32, so the results differ from the exact ones
+by that rounding. The bf16 bar documented for this path is
+(BF16_LOSS_RTOL, BF16_GRAD_RELNORM):
+  * loss: relative error per utterance;
+  * gradients: relative Frobenius-norm error of d_enc, d_dec, dW (and dW_dur).
+Cases:
+  * configs 2-5 (tests.gpu_cases.config_draws): RNN-T char with T up to 400 and
+    U up to 150, TDT BPE-1024, RNN-T BPE-1024 with d = 1024 (the streamed hidden
+    tiles), and the long end of the config-5 workload (T 450-500, U 100-120);
+  * native bf16 activations (the *_ex entry points): the oracle is fed the same
+    bf16-rounded encoder / decoder values, so with tf32 = 0 the loss is held to
+    the fp32 bar and only the bf16 rounding of the returned activation
+    gradients remains;
+  * the full 512-utterance config-5 batch in one call, whose 12.66 M lattice
+    nodes run as several 4 M-node passes of the joint: the utterances that
+    straddle a pass boundary are checked against the oracle.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests.gpu_cases import config_draws
+
+pytestmark = pytest.mark.gpu
+
+BF16_LOSS_RTOL = 2e-3
+BF16_GRAD_RELNORM = 1e-2
+
+DRAWS = config_draws()
+
+
+def oracle_of(c, enc=None, dec=None, grad_loss=None):
+    enc = c["enc"] if enc is None else enc
+    dec = c["dec"] if dec is None else dec
+    gl = c["grad_loss"] if grad_loss is None else grad_loss
+    if c["kind"] == "rnnt":
+        return oracle.rnnt(enc, dec, c["W"], c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=gl)
+    return oracle.tdt(enc, dec, c["W"], c["W_dur"], c["targets"], c["in_lens"], c["tgt_lens"], c["durations"],
+                      sigma=float(c["sigma"]), grad_loss=gl)
+
+
+def run_ours(c, tf32, act=torch.float32):
+    dev = torch.device("cuda")
+    e = torch.tensor(c["enc"], device=dev).to(act).requires_grad_(True)
+    d = torch.tensor(c["dec"], device=dev).to(act).requires_grad_(True)
+    w = torch.tensor(c["W"], device=dev, requires_grad=True)
+    ints = [torch.tensor(c[k], device=dev) for k in ("targets", "in_lens", "tgt_lens")]
+    gl = torch.tensor(c["grad_loss"], device=dev)
+    if c["kind"] == "rnnt":
+        from asr_b200.loss.rnnt import rnnt_loss
+
+        loss = rnnt_loss(e, d, w, *ints, 0, tf32)
+        leaves = {"d_enc": e, "d_dec": d, "dW": w}
+    else:
+        from asr_b200.loss.tdt import tdt_loss
+
+        wd = torch.tensor(c["W_dur"], device=dev, requires_grad=True)
+        loss = tdt_loss(e, d, w, wd, *ints, [int(x) for x in c["durations"]], 0, float(c["sigma"]), tf32)
+        leaves = {"d_enc": e, "d_dec": d, "dW": w, "dW_dur": wd}
+    (loss * gl).sum().backward()
+    out = {"loss": loss.detach().double().cpu().numpy()}
+    out.update({k: v.grad.double().cpu().numpy() for k, v in leaves.items()})
+    return out
+
+
+def loss_rel(got, want):
+    return float((np.abs(got - want) / np.maximum(np.abs(want), 1e-30)).max())
+
+
+def relnorm(got, want):
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30))
+
+
+def check_bf16(name, got, want):
+    errs = {"loss": loss_rel(got["loss"], want["loss"])}
+    errs.update({k: relnorm(got[k], want[k]) for k in got if k != "loss"})
+    msg = f"{name}: " + ", ".join(f"{k} {v:.2e}" for k, v in errs.items())
+    print("\n" + msg, end="")
+    assert errs["loss"] <= BF16_LOSS_RTOL, msg
+    for k, v in errs.items():
+        if k != "loss":
+            assert v <= BF16_GRAD_RELNORM, msg
+
+
+@pytest.mark.parametrize("name", ["c2_rnnt_char", "c3_tdt_bpe", "c4_rnnt_d1024", "c5_tdt_long"])
+def test_bf16_path_matches_oracle_at_config_shapes(name):
+    c = DRAWS[name]
+    check_bf16(name, run_ours(c, True), oracle_of(c))
+
+
+def _bf16_values(x):
+    return torch.tensor(x).to(torch.bfloat16).float().numpy()
+
+
+@pytest.mark.parametrize("name", ["c3_tdt_bpe", "c5_tdt_long", "c2_rnnt_char"])
+@pytest.mark.parametrize("tf32", [False, True])
+def test_bf16_activations_match_oracle_on_the_rounded_values(name, tf32):
+    """Native bf16 encoder / decoder activations against the oracle fed the same
+    (bf16-representable) values. tf32 = 0: loss at the fp32 bar, dW to 1e-4 of
+    its largest magnitude, the bf16 activation gradients within their own
+    rounding (relative norm 4e-3: half an ulp is 2^-9 of each element).
+    tf32 = 1: the bf16 bar."""
+    c = DRAWS[name]
+    enc, dec = _bf16_values(c["enc"]), _bf16_values(c["dec"])
+    want = oracle_of(c, enc, dec)
+    got = run_ours(dict(c, enc=enc, dec=dec), tf32, act=torch.bfloat16)
+    if tf32:
+        check_bf16(name + "-bf16act", got, want)
+        return
+    rel = loss_rel(got["loss"], want["loss"])
+    assert rel <= 1e-5, f"loss relative error {rel:.3e}"
+    for k in ("d_enc", "d_dec"):
+        assert relnorm(got[k], want[k]) <= 4e-3, f"{k}: {relnorm(got[k], want[k]):.3e}"
+    for k in [k for k in ("dW", "dW_dur") if k in got]:
+        err, scale = np.abs(got[k] - want[k]).max(), np.abs(want[k]).max()
+        assert err <= 1e-4 * max(1.0, scale), f"{k}: max-abs {err:.3e} (|max| {scale:.3e})"
+
+
+def test_bf16_full_config5_batch_across_pass_boundaries():
+    """All 512 utterances of the benchmark workload in one call (the bench's
+    generator); the lattice is cut into node passes of 4 M nodes, and the
+    utterances whose nodes straddle a cut are compared with the oracle (loss and
+    their own rows of d_enc / d_dec)."""
+    import bench
+
+    in_lens, tgt_lens = bench.workload_lengths()
+    W, Wd = bench.joint_weights()
+    b = bench.make_batch(np.arange(bench.GLOBAL_B), in_lens, tgt_lens)
+    c = dict(b, kind="tdt", W=W, W_dur=Wd, durations=np.array(bench.DURATIONS, np.int32), sigma=bench.SIGMA,
+             grad_loss=np.ones(bench.GLOBAL_B, np.float32))
+    got = run_ours(c, True)
+    nodes = in_lens.astype(np.int64) * (tgt_lens + 1)
+    off = np.concatenate([[0], np.cumsum(nodes)])
+    step = 4 << 20
+    cuts = [k * step for k in range(1, int(off[-1] // step) + 1)]
+    assert len(cuts) >= 2, "the workload should span several passes"
+    owners = [int(np.searchsorted(off, x, side="right") - 1) for x in cuts]
+    assert all(off[i] < x < off[i + 1] for x, i in zip(cuts, owners)), "every cut lies inside an utterance"
+    pick = sorted(set(owners) | {0})
+    sub = bench.make_batch(np.array(pick), in_lens, tgt_lens)
+    want = oracle_of(dict(c, **sub, grad_loss=np.ones(len(pick), np.float32)))
+    errs = {}
+    for j, i in enumerate(pick):
+        T, U = int(in_lens[i]), int(tgt_lens[i]) + 1
+        errs[i] = (loss_rel(got["loss"][i:i + 1], want["loss"][j:j + 1]),
+                   relnorm(got["d_enc"][i, :T], want["d_enc"][j, :T]),
+                   relnorm(got["d_dec"][i, :U], want["d_dec"][j, :U]))
+    msg = "; ".join(f"utt {i}: loss {a:.2e} d_enc {e:.2e} d_dec {d:.2e}" for i, (a, e, d) in errs.items())
+    print("\n" + msg, end="")
+    for i, (a, e, d) in errs.items():
+        assert a <= BF16_LOSS_RTOL and e <= BF16_GRAD_RELNORM and d <= BF16_GRAD_RELNORM, msg

@@ -1,0 +1,148 @@
+"""Parity with the reference's own implementation, run on the same GPU.
+
+The reference is installed by its own build into baseline/_ref (its Python loss
+modules and its CUDA op asr.loss._C for sm_100a; baseline/install_reference.py).
+Its op library and ours both register the asr:: op namespace, so the reference
+always runs in a child process (baseline/ref_worker.py) that never loads ours.
+
+1. The reference's own loss modules (src/asr/loss/{ctc,rnnt,tdt}.py) run on our
+   op library: a scratch package holds copies of those modules with our
+   `_C.abi3.so` beside them, which their `_C*.so` glob loads
+   (src/asr/loss/tdt.py:8-9). Every golden case must come out as the goldens at
+   the fp32 bars of the other parity tests. This is the drop-in claim: the
+   reference's Python code, unchanged, on our kernels.
+2. Our fp32 path (tf32 = 0) against the reference op's fp32 path on identical
+   seeded inputs drawn from the BASELINE configurations, at the tolerance the
+   build is held to: loss relative error <= 1e-5 and gradient max-abs error
+   <= 1e-4, relative to the gradient's largest magnitude where that exceeds 1
+   (both sides sum the gradients in float32).
+
+Skipped when baseline/_ref holds no reference build.
+"""
+
+from __future__ import annotations
+
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from tests.golden_io import load_cases
+from tests.gpu_cases import config_draws
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parents[1]
+REF_ROOT = ROOT / "baseline" / "_ref"
+WORKER = ROOT / "baseline" / "ref_worker.py"
+HAVE_REF = any((REF_ROOT / "asr" / "loss").glob("_C*.so"))
+need_ref = pytest.mark.skipif(not HAVE_REF, reason="no reference build in baseline/_ref")
+
+GOLDEN = {kind: load_cases(kind) for kind in ("ctc", "rnnt", "tdt")}
+GRADS = {"ctc": ("grad_logits",), "rnnt": ("d_enc", "d_dec", "dW"), "tdt": ("d_enc", "d_dec", "dW", "dW_dur")}
+
+
+def run_worker(root: Path, cases: dict[str, dict], workdir: Path) -> dict[str, dict]:
+    workdir.mkdir(parents=True, exist_ok=True)
+    for name, c in cases.items():
+        np.savez(workdir / f"case_{name}.npz", **c)
+    subprocess.run([sys.executable, str(WORKER), "run", str(root), str(workdir)], check=True, timeout=1200)
+    out = {}
+    for name in cases:
+        with np.load(workdir / f"out_{name}.npz") as z:
+            out[name] = {k: z[k] for k in z.files}
+    return out
+
+
+# ------------------------------------------- the reference's modules on our op library
+
+
+@pytest.fixture(scope="module")
+def reference_modules_on_our_ops(tmp_path_factory):
+    pkg = tmp_path_factory.mktemp("refpkg")
+    (pkg / "asr" / "loss").mkdir(parents=True)
+    (pkg / "asr" / "__init__.py").write_text("")
+    for f in ("__init__.py", "ctc.py", "rnnt.py", "tdt.py"):
+        shutil.copy(REF_ROOT / "asr" / "loss" / f, pkg / "asr" / "loss" / f)
+    shutil.copy(ROOT / "asr_b200" / "_C.abi3.so", pkg / "asr" / "loss" / "_C.abi3.so")
+    cases = {f"{kind}__{name}": dict(c, kind=kind) for kind, g in GOLDEN.items() for name, c in g.items()}
+    return run_worker(pkg, cases, pkg / "cases")
+
+
+@need_ref
+@pytest.mark.parametrize("case", [f"{k}__{n}" for k, g in GOLDEN.items() for n in sorted(g)])
+def test_reference_modules_run_on_our_op_library(reference_modules_on_our_ops, case):
+    kind, name = case.split("__", 1)
+    want = GOLDEN[kind][name]
+    got = reference_modules_on_our_ops[case]
+    np.testing.assert_allclose(got["loss"], want["loss"], rtol=1e-5, atol=2e-5 if kind == "ctc" else 1e-5)
+    for g in GRADS[kind]:
+        excess = (np.abs(got[g].astype(np.float64) - want[g]) - (1e-4 + 1e-4 * np.abs(want[g]))).max(initial=-1)
+        assert excess <= 0, f"{case} {g}: max-abs error {np.abs(got[g] - want[g]).max():.3e}"
+
+
+# ------------------------------------------------ our fp32 path against the reference op
+
+DRAWS = config_draws()
+
+
+def ours(c: dict, tf32: bool = False) -> dict:
+    dev = torch.device("cuda")
+
+    def t(k, grad=False):
+        x = torch.tensor(np.ascontiguousarray(c[k]), device=dev)
+        return x.requires_grad_(True) if grad else x
+
+    gl = t("grad_loss")
+    kind = c["kind"]
+    if kind == "ctc":
+        from asr_b200.loss.ctc import CTCLossFn
+
+        x = t("logits", True)
+        loss = CTCLossFn.apply(x, t("targets"), t("in_lens"), t("tgt_lens"), False)
+        (loss * gl).sum().backward()
+        return {"loss": loss.detach().cpu().numpy(), "grad_logits": x.grad.cpu().numpy()}
+    e, d, w = t("enc", True), t("dec", True), t("W", True)
+    ints = (t("targets"), t("in_lens"), t("tgt_lens"))
+    if kind == "rnnt":
+        from asr_b200.loss.rnnt import rnnt_loss
+
+        loss = rnnt_loss(e, d, w, *ints, 0, tf32)
+        (loss * gl).sum().backward()
+        return {"loss": loss.detach().cpu().numpy(), "d_enc": e.grad.cpu().numpy(), "d_dec": d.grad.cpu().numpy(),
+                "dW": w.grad.cpu().numpy()}
+    from asr_b200.loss.tdt import tdt_loss
+
+    wd = t("W_dur", True)
+    loss = tdt_loss(e, d, w, wd, *ints, [int(x) for x in c["durations"]], 0, float(c["sigma"]), tf32)
+    (loss * gl).sum().backward()
+    return {"loss": loss.detach().cpu().numpy(), "d_enc": e.grad.cpu().numpy(), "d_dec": d.grad.cpu().numpy(),
+            "dW": w.grad.cpu().numpy(), "dW_dur": wd.grad.cpu().numpy()}
+
+
+@pytest.fixture(scope="module")
+def reference_fp32(tmp_path_factory):
+    return run_worker(REF_ROOT, {k: dict(v, tf32=0) for k, v in DRAWS.items()}, tmp_path_factory.mktemp("ref32"))
+
+
+@need_ref
+@pytest.mark.parametrize("name", sorted(DRAWS))
+def test_fp32_matches_reference_cuda_op(reference_fp32, name):
+    c = DRAWS[name]
+    want = reference_fp32[name]
+    got = ours(c)
+    rel = np.abs(got["loss"].astype(np.float64) - want["loss"]) / np.maximum(np.abs(want["loss"]), 1e-30)
+    msg = f"{name}: loss rel err {rel.max():.2e}"
+    for g in GRADS[c["kind"]]:
+        a, b = got[g].astype(np.float64), want[g].astype(np.float64)
+        msg += f"; {g} max-abs {np.abs(a - b).max(initial=0):.2e} (|max| {np.abs(b).max(initial=0):.2e})"
+    print("\n" + msg, end="")
+    assert rel.max() <= 1e-5, msg
+    for g in GRADS[c["kind"]]:
+        a, b = got[g].astype(np.float64), want[g].astype(np.float64)
+        err, scale = np.abs(a - b).max(initial=0), np.abs(b).max(initial=0)
+        assert err <= 1e-4 * max(1.0, scale), msg
