@@ -32,7 +32,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               "-Xptxas", "-warn-spills", f"-I{INCLUDE}", f"-I{CSRC}"]
-CU_SOURCES = ["lattice.cu", "ctc.cu", "dp_rnnt.cu", "dp_tdt.cu", "joint_simt.cu", "joint_tc.cu", "capi.cu",
+CU_SOURCES = ["lattice.cu", "ctc.cu", "dp_lattice.cu", "joint_simt.cu", "joint_tc.cu", "capi.cu",
               "profiler.cu", "noalloc.cu", "decode.cu", "ctc_head.cu", "ctc_beam.cu"]
 HEADERS = ["common.cuh", "dp.cuh", "joint.cuh", "profiler.cuh", "tc_common.cuh"]
 

@@ -29,7 +29,7 @@ struct TrWorkspace {
     float* cb = nullptr;    // backward: (cap,)
     float* ct = nullptr;    // backward: (cap,)
     float* gdur = nullptr;  // backward TDT: (cap, n_dur)
-    double* beta = nullptr;  // backward TDT: (B, T + 1, U), the alpha array's shape
+    double* beta = nullptr;  // backward: (B, T + 1, U), the TDT alpha array's shape
     void* joint = nullptr;  // joint-network scratch
     size_t joint_bytes = 0;
     // bf16 activations: fp32 copies for the SIMT path, fp32 gradient sums
@@ -66,10 +66,8 @@ size_t tr_workspace_bytes(const JointArgs& a, int64_t cap, bool tc, bool backwar
     if (sg.grads) n += align256(ne) + align256(nd);
     if (backward) {
         n += 2 * align256(sizeof(float) * cap);
-        if (a.n_dur > 0) {
-            n += align256(sizeof(float) * cap * a.n_dur);
-            n += align256(sizeof(double) * tdt_alpha_len(a));
-        }
+        n += align256(sizeof(double) * tdt_alpha_len(a));
+        if (a.n_dur > 0) n += align256(sizeof(float) * cap * a.n_dur);
     }
     n += align256(joint_scratch_bytes(a, cap, tc, backward));
     return n + 256;  // slack for aligning the base pointer
@@ -98,11 +96,11 @@ TrWorkspace carve(void* ws, const JointArgs& a, int64_t cap, bool tc, bool backw
         p += align256(sizeof(float) * cap);
         w.ct = reinterpret_cast<float*>(p);
         p += align256(sizeof(float) * cap);
+        w.beta = reinterpret_cast<double*>(p);
+        p += align256(sizeof(double) * tdt_alpha_len(a));
         if (a.n_dur > 0) {
             w.gdur = reinterpret_cast<float*>(p);
             p += align256(sizeof(float) * cap * a.n_dur);
-            w.beta = reinterpret_cast<double*>(p);
-            p += align256(sizeof(double) * tdt_alpha_len(a));
         }
     }
     w.joint = p;
@@ -278,7 +276,7 @@ int rnnt_backward_impl(const void* encoder, const void* decoder, int act_dtype, 
     if (rc) return rc;
     rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
     if (rc) return rc;
-    rc = launch_rnnt_beta(w.meta, B, U, log_P_blank, log_P_y, alpha, grad_loss, w.cb, w.ct, st);
+    rc = launch_rnnt_beta(w.meta, B, U, log_P_blank, log_P_y, alpha, grad_loss, w.cb, w.ct, w.beta, st);
     if (rc) return rc;
     float *ge, *gd;
     rc = zero_act_grads(a, w, grad_encoder, grad_decoder, &ge, &gd, st);

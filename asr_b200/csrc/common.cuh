@@ -67,6 +67,27 @@ __device__ __forceinline__ double lse_d(const double (&x)[N]) {
     return m + (double)__logf(e[0]);
 }
 
+// Diagonal-major order of a rows x cols lattice grid: anti-diagonals g = t + u
+// in order, u ascending within a diagonal. The recursions sweep anti-diagonals,
+// so storing the per-node lattice weights and the forward / backward variables
+// this way makes every diagonal one contiguous block (coalesced loads). Index
+// of node (t, u) within the grid:
+__host__ __device__ __forceinline__ int diag_index(int t, int u, int rows, int cols) {
+    const int g = t + u;
+    const int mn = rows < cols ? rows : cols, mx = rows < cols ? cols : rows;
+    int s;
+    if (g <= mn) {
+        s = g * (g + 1) / 2;
+    } else if (g <= mx) {
+        s = mn * (mn + 1) / 2 + (g - mn) * mn;
+    } else {
+        const int h = rows + cols - 1 - g;
+        s = rows * cols - h * (h + 1) / 2;
+    }
+    const int ulo = g - rows + 1 > 0 ? g - rows + 1 : 0;
+    return s + u - ulo;
+}
+
 // Per-batch lattice bookkeeping produced by lattice_prep_kernel.
 struct LatticeMeta {
     int32_t* Tb;    // (B,) clamped frames

@@ -291,7 +291,8 @@ int launch_ctc_grad(const double* alpha, const float* lp, const int32_t* tg, con
 }
 
 // (KS states per thread, NW warps per utterance) for L = 2S + 1 states: about two
-// states per thread, up to 8 warps, then more states per thread.
+// states per thread, up to 8 warps, then more states per thread; the longest
+// targets (L up to 8192, S up to 4095 labels) take 16 warps of 16 states.
 int ctc_shape(int S) {
     const int L = 2 * S + 1;
     if (L <= 32) return 11;
@@ -300,6 +301,9 @@ int ctc_shape(int S) {
     if (L <= 256) return 24;
     if (L <= 512) return 28;
     if (L <= 1024) return 48;
+    if (L <= 2048) return 88;
+    if (L <= 4096) return 168;
+    if (L <= 8192) return 1616;
     return 0;
 }
 
@@ -322,6 +326,10 @@ extern "C" int asr_ctc_alpha(const float* log_probs, const int32_t* targets, con
         case 24: return launch_ctc_alpha<2, 4>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
         case 28: return launch_ctc_alpha<2, 8>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
         case 48: return launch_ctc_alpha<4, 8>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 88: return launch_ctc_alpha<8, 8>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 168: return launch_ctc_alpha<16, 8>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
+        case 1616:
+            return launch_ctc_alpha<16, 16>(log_probs, targets, in_lens, tgt_lens, B, T, V, S, alpha, log_Z, st);
         default: return ASR_ERR_UNSUPPORTED;
     }
 }
@@ -340,6 +348,9 @@ int ctc_grad_dispatch(const double* alpha, const float* log_probs, const int32_t
         case 24: return launch_ctc_grad<2, 4>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
         case 28: return launch_ctc_grad<2, 8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
         case 48: return launch_ctc_grad<4, 8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 88: return launch_ctc_grad<8, 8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 168: return launch_ctc_grad<16, 8>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
+        case 1616: return launch_ctc_grad<16, 16>(alpha, log_probs, targets, in_lens, tgt_lens, grad_loss, z, p, B, T, V, S, grad, st);
         default: return ASR_ERR_UNSUPPORTED;
     }
 }

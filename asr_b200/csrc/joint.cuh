@@ -35,12 +35,15 @@ struct JointArgs {
     const float* bias;   // (V,) or nullptr
 };
 
-// Forward epilogue outputs (compact per-node arrays).
+// Forward epilogue outputs (compact per-node arrays). The lattice weights the
+// recursions read (lpb, lpy, lpd) are stored diagonal-major within each
+// utterance's block (diag_index over its T_b x U_b grid); lse, read back by the
+// backward joint, is node-major.
 struct JointFwdOut {
-    float* lpb;  // blank log-prob (minus sigma)
-    float* lse;  // token log-partition
-    float* lpy;  // label log-prob (minus sigma), kNeg without a label edge
-    float* lpd;  // (nodes, n_dur) duration log-probs, or nullptr
+    float* lpb;  // blank log-prob (minus sigma), diagonal-major
+    float* lse;  // token log-partition, node-major
+    float* lpy;  // label log-prob (minus sigma), kNeg without a label edge, diagonal-major
+    float* lpd;  // (nodes, n_dur) duration log-probs, diagonal-major, or nullptr
 };
 
 // Backward: per-node coefficients from the beta pass and the gradient outputs.

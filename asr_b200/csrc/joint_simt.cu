@@ -50,6 +50,7 @@ struct RowInfo {
     int64_t enc, dec;  // element offsets of the encoder / decoder rows
     int y;             // emitted label, -1 without a label edge
     int n;             // compact node id, -1 for an empty tile row
+    int dn;            // its place in the utterance's diagonal-major weight block
 };
 
 __device__ __forceinline__ RowInfo make_row(const JointArgs& a, int n, int N) {
@@ -58,6 +59,7 @@ __device__ __forceinline__ RowInfo make_row(const JointArgs& a, int n, int N) {
         r.enc = r.dec = 0;
         r.y = -1;
         r.n = -1;
+        r.dn = -1;
         return r;
     }
     const NodeCoord c = node_coord(a.m, a.B, n);
@@ -65,6 +67,7 @@ __device__ __forceinline__ RowInfo make_row(const JointArgs& a, int n, int N) {
     r.dec = ((int64_t)c.b * a.U + c.u) * a.d;
     r.y = (c.u < c.Ub - 1) ? __ldg(a.targets + (int64_t)c.b * a.S + c.u) : -1;
     r.n = n;
+    r.dn = __ldg(a.m.off + c.b) + diag_index(c.t, c.u, __ldg(a.m.Tb + c.b), c.Ub);
     return r;
 }
 
@@ -159,18 +162,18 @@ __global__ void __launch_bounds__(NT) simt_fwd_kernel(JointArgs a, JointFwdOut o
             __syncthreads();
         }
         if (tid < BM && rows[tid].n >= 0) {
-            const int n = rows[tid].n;
+            const int n = rows[tid].n, dn = rows[tid].dn;
             const float lse = r_m[tid] + __logf(r_s[tid]);
             o.lse[n] = lse;
-            o.lpb[n] = r_blank[tid] - lse - a.sigma;
-            o.lpy[n] = rows[tid].y >= 0 ? r_lab[tid] - lse - a.sigma : kNeg;
+            o.lpb[dn] = r_blank[tid] - lse - a.sigma;
+            o.lpy[dn] = rows[tid].y >= 0 ? r_lab[tid] - lse - a.sigma : kNeg;
             if (a.n_dur > 0) {
                 float md = -INFINITY;
                 for (int k = 0; k < a.n_dur; ++k) md = fmaxf(md, r_dur[tid][k]);
                 float sd = 0.f;
                 for (int k = 0; k < a.n_dur; ++k) sd += __expf(r_dur[tid][k] - md);
                 const float lz = md + __logf(sd);
-                for (int k = 0; k < a.n_dur; ++k) o.lpd[(int64_t)n * a.n_dur + k] = r_dur[tid][k] - lz;
+                for (int k = 0; k < a.n_dur; ++k) o.lpd[(int64_t)dn * a.n_dur + k] = r_dur[tid][k] - lz;
             }
         }
         __syncthreads();

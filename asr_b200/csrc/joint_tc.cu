@@ -401,9 +401,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n = begin + (unit * kCta + (int)rank) * kBM + row;
             const bool valid = n < end;
             int y = -1;
+            int dn = 0;  // forward: the node's place in its utterance's diagonal-major weight block
             if (valid) {
                 const NodeCoord c = node_coord(a.m, a.B, n);
                 y = (c.u < c.Ub - 1) ? __ldg(a.targets + (int64_t)c.b * a.S + c.u) : -1;
+                if (!kBwd) dn = __ldg(a.m.off + c.b) + diag_index(c.t, c.u, __ldg(a.m.Tb + c.b), c.Ub);
             }
             // forward state
             float m = -INFINITY, s = 0.f, lb = 0.f, ly = 0.f;
@@ -557,8 +559,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!kBwd && ok && valid) {
                 const float l = m + __logf(s);
                 P.fwd.lse[n] = l;
-                P.fwd.lpb[n] = lb - l - a.sigma;
-                P.fwd.lpy[n] = y >= 0 ? ly - l - a.sigma : kNeg;
+                P.fwd.lpb[dn] = lb - l - a.sigma;
+                P.fwd.lpy[dn] = y >= 0 ? ly - l - a.sigma : kNeg;
                 if (a.n_dur > 0) {
                     float md = -INFINITY;
 #pragma unroll
@@ -571,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float lz = md + __logf(sd);
 #pragma unroll
                     for (int k = 0; k < kMaxDurCols; ++k)
-                        if (k < a.n_dur) P.fwd.lpd[(int64_t)n * a.n_dur + k] = dur[k] - lz;
+                        if (k < a.n_dur) P.fwd.lpd[(int64_t)dn * a.n_dur + k] = dur[k] - lz;
                 }
             }
         }

@@ -168,8 +168,8 @@ def kernel_work(name, N, d, Vf, n_dur, frames=0, labels=0):
     Hidden rows (forward and backward): bf16 H written (2 * ceil64(d) bytes per
     node) plus the fp32 enc / dec rows read once (frames + labels rows of d floats).
     Recursions: per node, the 4-byte lattice weights read plus the float64 alpha
-    (or beta) written. TDT posteriors: the weights, alpha and beta read and the
-    4-byte posteriors / duration gradients written."""
+    written (forward); the backward reads the weights and alpha and writes beta
+    (TDT) and the 4-byte posteriors / duration gradients."""
     if name in GEMM_KERNELS:
         return "tensor", 2.0 * N * d * Vf
     if name == "joint_hidden":
@@ -177,10 +177,8 @@ def kernel_work(name, N, d, Vf, n_dur, frames=0, labels=0):
         return "hbm", 2.0 * (N * 2.0 * kpad + (frames + labels) * d * 4.0)
     if name == "tdt_alpha":
         return "hbm", N * (4.0 * (2 + n_dur) + 8.0)
-    if name == "tdt_beta":
-        return "hbm", N * (4.0 * (2 + n_dur) + 8.0)
-    if name == "tdt_posteriors":
-        return "hbm", N * (4.0 * (2 + n_dur) + 16.0 + 4.0 * (2 + n_dur))
+    if name == "tdt_beta_posteriors":  # weights and alpha read; beta, posteriors, duration grads written
+        return "hbm", N * (8.0 * (2 + n_dur) + 16.0)
     if name == "rnnt_alpha":
         return "hbm", N * (8.0 + 8.0)
     if name == "rnnt_beta_posteriors":

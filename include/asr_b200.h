@@ -38,7 +38,7 @@ typedef enum {
     ASR_OK = 0,
     ASR_ERR_INVALID_ARGUMENT = 1, /* a size/flag/pointer check failed on the host */
     ASR_ERR_WORKSPACE = 2,        /* workspace missing or smaller than *_workspace_bytes */
-    ASR_ERR_UNSUPPORTED = 3,      /* shape outside the compiled kernel range (e.g. U > 1024) */
+    ASR_ERR_UNSUPPORTED = 3,      /* shape outside the compiled kernel range (e.g. U > 8192) */
     ASR_ERR_CUDA = 4,             /* a CUDA launch or runtime call failed */
     ASR_ERR_SCRATCH_LIMIT = 5     /* problem needs more than the fixed scratch of a *_noalloc entry point */
 } asr_status_t;

@@ -4,10 +4,12 @@ path) against the float64 oracle at the BASELINE configurations' shapes.
 The joint's operands are rounded to bf16 (8 significant bits: hidden rows H =
 tanh(enc + dec) and the joint weights; G = d loss / d logits in the backward)
 and every sum is accumulated in fp32, so the results differ from the exact ones
-by that rounding. The bf16 bar documented for this path is
-(BF16_LOSS_RTOL, BF16_GRAD_RELNORM):
-  * loss: relative error per utterance;
-  * gradients: relative Frobenius-norm error of d_enc, d_dec, dW (and dW_dur).
+by that rounding. The bf16 bar documented for this path, about three times the
+largest error measured on B200 over the cases below (loss 3.9e-6, gradients
+2.5e-3), is (BF16_LOSS_RTOL, BF16_GRAD_RELNORM):
+  * loss: relative error per utterance <= 1.5e-5;
+  * gradients: relative Frobenius-norm error of d_enc, d_dec, dW (and dW_dur)
+    <= 7.5e-3.
 Cases:
   * configs 2-5 (tests.gpu_cases.config_draws): RNN-T char with T up to 400 and
     U up to 150, TDT BPE-1024, RNN-T BPE-1024 with d = 1024 (the streamed hidden
@@ -32,8 +34,8 @@ from tests.gpu_cases import config_draws
 
 pytestmark = pytest.mark.gpu
 
-BF16_LOSS_RTOL = 2e-3
-BF16_GRAD_RELNORM = 1e-2
+BF16_LOSS_RTOL = 1.5e-5
+BF16_GRAD_RELNORM = 7.5e-3
 
 DRAWS = config_draws()
 

@@ -5,7 +5,8 @@ own float64 oracles / torch CTC, and (b) the C oracle (oracle/) on seeded
 inputs larger than the fixtures. Tolerances (fp32 mode, tf32 = 0):
 loss relative error <= 1e-5 and gradient max-abs error <= 1e-4, the bar the
 reference's float32 kernels are held to; bf16 tensor-core mode (tf32 = 1) is
-held to the reference's own tf32 test bar (loss 5e-2, gradient rel-norm 5e-2).
+held to the bf16 bar measured for it (loss relative error 1.5e-5, gradient
+relative-norm error 7.5e-3; tests/test_bf16_parity_gpu.py).
 """
 
 import numpy as np
@@ -57,13 +58,24 @@ def assert_grad(got, want, name, atol=GRAD_ATOL, rtol=GRAD_RTOL):
     assert excess <= 0, f"{name}: max-abs error {err:.3e} exceeds {atol:.0e} + {rtol:.0e}*|ref|"
 
 
-def assert_bf16_close(got_loss, want_loss, grads):
-    """The reference's tf32 tolerance (tests/loss/test_tdt_loss.py:166-169)."""
-    np.testing.assert_allclose(got_loss.detach().double().cpu().numpy(), want_loss, rtol=5e-2, atol=5e-2)
+def assert_bf16_close(got_loss, want_loss, grads, loss_rtol=1.5e-5):
+    """The bf16 bar of the tensor-core path (tests/test_bf16_parity_gpu.py): loss
+    relative error <= 1.5e-5 per utterance, gradient relative-norm error <= 7.5e-3,
+    on the BASELINE activation distribution N(0, 1/d). Activations ~N(0, 1) (tanh
+    near saturation, logits about three times larger) measure up to 1.9e-4 on the
+    loss and are held to 6e-4."""
+    got = got_loss.detach().double().cpu().numpy()
+    rel = float((np.abs(got - want_loss) / np.maximum(np.abs(want_loss), 1e-30)).max())
+    msg = f"loss {rel:.2e}"
     for name, g, w in grads:
         g = g.detach().double().cpu().numpy()
-        rel = np.linalg.norm(g - w) / max(np.linalg.norm(w), 1e-30)
-        assert np.isfinite(g).all() and rel < 5e-2, f"{name}: bf16 grad rel-err {rel:.3e}"
+        msg += f", {name} {np.linalg.norm(g - w) / max(np.linalg.norm(w), 1e-30):.2e}"
+    print(" " + msg, end="")
+    assert rel <= loss_rtol, msg
+    for name, g, w in grads:
+        g = g.detach().double().cpu().numpy()
+        r = np.linalg.norm(g - w) / max(np.linalg.norm(w), 1e-30)
+        assert np.isfinite(g).all() and r <= 7.5e-3, f"{name}: {msg}"
 
 
 # ---------------------------------------------------------------- CTC
@@ -115,6 +127,24 @@ def test_ctc_long_targets():
     loss.sum().backward()
     lp = torch.log_softmax(torch.tensor(c["logits"]), -1).numpy()
     want, grad = oracle.ctc(lp, c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    assert_loss(loss, want)
+    assert_grad(x.grad, grad, "grad_logits")
+
+
+@pytest.mark.parametrize("S_rng,T_rng,B", [((1400, 1500), (1700, 1800), 2), ((3000, 3100), (3300, 3400), 1)])
+def test_ctc_very_long_targets(S_rng, T_rng, B):
+    """2S + 1 up to 3001 (8 warps of 16 states) and 6201 (16 warps of 16 states):
+    character-level targets of thousands of labels, which the reference's
+    state-looping kernels also take (ctc.cu:55-115)."""
+    from asr_b200.loss.ctc import CTCLossFn
+
+    c = ctc_case(13, B, T_rng, 40, S_rng)
+    x = leaf(c["logits"])
+    loss = CTCLossFn.apply(x, cuda(c["targets"]), cuda(c["in_lens"]), cuda(c["tgt_lens"]), False)
+    loss.sum().backward()
+    lp = torch.log_softmax(torch.tensor(c["logits"]), -1).numpy()
+    want, grad = oracle.ctc(lp, c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    assert np.isfinite(want).all()
     assert_loss(loss, want)
     assert_grad(x.grad, grad, "grad_logits")
 
@@ -189,7 +219,8 @@ def test_rnnt_bf16_mode_within_reference_tf32_bar():
     c = transducer_case(23, 4, (20, 30), (6, 10), 32, 64, act_std=1.0)
     loss, ge, gd, gw = run_rnnt(c, tf32=True)
     o = oracle.rnnt(c["enc"], c["dec"], c["W"], c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
-    assert_bf16_close(loss, o["loss"], [("d_enc", ge, o["d_enc"]), ("d_dec", gd, o["d_dec"]), ("dW", gw, o["dW"])])
+    assert_bf16_close(loss, o["loss"], [("d_enc", ge, o["d_enc"]), ("d_dec", gd, o["d_dec"]), ("dW", gw, o["dW"])],
+                      loss_rtol=6e-4)
 
 
 # ---------------------------------------------------------------- TDT
@@ -256,30 +287,63 @@ def test_tdt_widest_duration_ring():
         assert_grad(g, o[name], name)
 
 
-def test_tdt_long_label_axis_reads_weights_from_global_memory():
-    """900 label positions with durations 0..4: the alpha sweep's shared-memory
-    weight ring would not fit one SM, so it reads the edge weights at the source
-    nodes instead; results still match the oracle. With 900 label positions the
-    gradients reach magnitudes of 10^2..10^3 and sum ~22 K nodes in float32, so
-    they are held to 2e-5 of their largest magnitude (measured: 5e-6, smoothly
-    growing with U from 7e-7 at U = 60 through 3e-6 at U = 700 on the ring path)."""
-    c = transducer_case(47, 2, (10, 14), (880, 899), 16, 32, n_dur=5, act_std=0.7)
+def assert_grad_scaled(name, got, want, rel=2e-5):
+    """Long label axes: gradients reach 10^2..10^3 and are sums over thousands of
+    lattice nodes in float32 (d_enc over the label axis, dW over every node), so
+    they are held to 1e-4 plus `rel` of their largest magnitude (the float32
+    summation error grows with that magnitude)."""
+    g, w = got.detach().double().cpu().numpy(), np.asarray(want, np.float64)
+    err, scale = np.abs(g - w).max(initial=0), np.abs(w).max(initial=0)
+    print(f" {name} {err:.1e}/{scale:.1e}", end="")
+    assert err <= 1e-4 + rel * scale, f"{name}: max-abs error {err:.3e}, largest magnitude {scale:.3e}"
+
+
+@pytest.mark.parametrize(
+    "durations,U_rng,seed",
+    [
+        ([0, 1, 2, 3, 4], (880, 899), 47),  # 4 warps of 256 positions, weights staged in shared memory
+        ([0, 1, 1, 2, 4], (840, 860), 48),  # repeated duration class: the log-summed duration weights
+        ([0, 1, 2, 3, 4], (2000, 2047), 49),  # 8 warps; rings beyond shared memory: global-memory mode
+        (list(range(17)), (780, 799), 50),  # durations 0..16, 17 classes: global-memory mode
+    ],
+)
+def test_tdt_long_label_axis(durations, U_rng, seed):
+    """Label axes of hundreds to thousands of positions (the reference's TDT
+    recursion takes any length, tdt.cu:239-283): several warps per utterance,
+    the cross-warp scan of each frame, and, where the rings would not fit one SM,
+    the global-memory mode that reads the sources back from the alpha / beta
+    arrays."""
+    c = transducer_case(seed, 2, (10, 14), U_rng, 16, 32, n_dur=len(durations), act_std=0.7)
+    c["durations"] = np.array(durations, np.int32)
     loss, ge, gd, gw, gwd = run_tdt(c, sigma=0.05)
     o = _tdt_oracle(c, 0.05)
     assert_loss(loss, o["loss"])
     for name, g in (("d_enc", ge), ("d_dec", gd), ("dW", gw), ("dW_dur", gwd)):
-        got, want = g.detach().double().cpu().numpy(), o[name]
-        err, scale = np.abs(got - want).max(), np.abs(want).max()
-        assert err <= 1e-4 + 2e-5 * scale, f"{name}: max-abs error {err:.3e}, largest magnitude {scale:.3e}"
+        assert_grad_scaled(name, g, o[name])
 
 
-def test_tdt_wide_duration_ring_rejects_label_axis_beyond_one_cta():
-    """With durations up to 16 the recursions keep 18-20 diagonals of state per
-    label position, so one CTA per utterance (one thread per label position) fits
-    one SM's shared memory and registers only up to about a hundred label
-    positions: a longer label axis is reported as an unsupported shape before any
-    recursion is launched, never as a failed launch."""
-    c = transducer_case(46, 1, (20, 20), (600, 600), 16, 32, n_dur=17)
+@pytest.mark.parametrize("tf32", [False, True])
+def test_rnnt_long_label_axis(tf32):
+    """U = 2048 label positions (8 warps of 256): the reference's RNN-T recursion
+    strides over any label axis (rnnt.cu:227-229). Both joint paths; the bf16
+    path is held to its relative-norm bar (tests/test_bf16_parity_gpu.py)."""
+    c = transducer_case(51, 2, (10, 14), (2000, 2047), 16, 32, act_std=0.7)
+    loss, ge, gd, gw = run_rnnt(c, tf32=tf32)
+    o = oracle.rnnt(c["enc"], c["dec"], c["W"], c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    if tf32:
+        np.testing.assert_allclose(loss.detach().double().cpu().numpy(), o["loss"], rtol=1.5e-5)
+        for name, g in (("d_enc", ge), ("d_dec", gd), ("dW", gw)):
+            assert _rel(g.cpu(), torch.as_tensor(o[name])) <= 7.5e-3, name
+        return
+    assert_loss(loss, o["loss"])
+    for name, g in (("d_enc", ge), ("d_dec", gd), ("dW", gw)):
+        assert_grad_scaled(name, g, o[name])
+
+
+def test_label_axis_beyond_the_recursions_is_rejected_cleanly():
+    """Past 8192 label positions (32 warps of 256) the recursions report an
+    unsupported shape before anything is launched."""
+    c = transducer_case(52, 1, (4, 4), (8192, 8192), 8, 8, n_dur=5)
     with pytest.raises(RuntimeError, match="supported kernel range"):
         run_tdt(c, sigma=0.0)
 
@@ -312,7 +376,7 @@ def test_tdt_bf16_mode_within_reference_tf32_bar():
     loss, ge, gd, gw, gwd = run_tdt(c, tf32=True, sigma=0.0)
     o = _tdt_oracle(c, 0.0)
     assert_bf16_close(loss, o["loss"], [("d_enc", ge, o["d_enc"]), ("d_dec", gd, o["d_dec"]), ("dW", gw, o["dW"]),
-                                        ("dW_dur", gwd, o["dW_dur"])])
+                                        ("dW_dur", gwd, o["dW_dur"])], loss_rtol=6e-4)
 
 
 def test_tdt_bf16_bpe_config_matches_oracle():

@@ -12,10 +12,14 @@ always runs in a child process (baseline/ref_worker.py) that never loads ours.
    the fp32 bars of the other parity tests. This is the drop-in claim: the
    reference's Python code, unchanged, on our kernels.
 2. Our fp32 path (tf32 = 0) against the reference op's fp32 path on identical
-   seeded inputs drawn from the BASELINE configurations, at the tolerance the
-   build is held to: loss relative error <= 1e-5 and gradient max-abs error
-   <= 1e-4, relative to the gradient's largest magnitude where that exceeds 1
-   (both sides sum the gradients in float32).
+   seeded inputs drawn from the BASELINE configurations. Losses agree to 1e-5
+   (relative). The reference keeps its forward / backward variables in fp32
+   log space, so on these lattices its own gradients are off the float64
+   oracle by up to a few 1e-3 (dW, |dW| ~ 10); ours (float64 recursions) stay
+   within 1e-4 of the oracle, relative to the gradient's largest magnitude
+   where that exceeds 1. So the gradients are held to: ours - oracle within
+   that bar, and ours - reference within that bar plus the reference's own
+   distance from the oracle. Each case prints the three distances.
 
 Skipped when baseline/_ref holds no reference build.
 """
@@ -31,6 +35,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import oracle
 from tests.golden_io import load_cases
 from tests.gpu_cases import config_draws
 
@@ -129,20 +134,38 @@ def reference_fp32(tmp_path_factory):
     return run_worker(REF_ROOT, {k: dict(v, tf32=0) for k, v in DRAWS.items()}, tmp_path_factory.mktemp("ref32"))
 
 
+def exact(c: dict) -> dict:
+    """The float64 oracle's loss and gradients for a draw."""
+    kind = c["kind"]
+    if kind == "ctc":
+        lp = torch.log_softmax(torch.tensor(c["logits"], dtype=torch.float64), -1).numpy()
+        loss, grad = oracle.ctc(lp, c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+        return {"loss": loss, "grad_logits": grad}
+    if kind == "rnnt":
+        return oracle.rnnt(c["enc"], c["dec"], c["W"], c["targets"], c["in_lens"], c["tgt_lens"],
+                           grad_loss=c["grad_loss"])
+    return oracle.tdt(c["enc"], c["dec"], c["W"], c["W_dur"], c["targets"], c["in_lens"], c["tgt_lens"],
+                      c["durations"], sigma=float(c["sigma"]), grad_loss=c["grad_loss"])
+
+
 @need_ref
 @pytest.mark.parametrize("name", sorted(DRAWS))
 def test_fp32_matches_reference_cuda_op(reference_fp32, name):
     c = DRAWS[name]
-    want = reference_fp32[name]
+    ref = reference_fp32[name]
     got = ours(c)
-    rel = np.abs(got["loss"].astype(np.float64) - want["loss"]) / np.maximum(np.abs(want["loss"]), 1e-30)
-    msg = f"{name}: loss rel err {rel.max():.2e}"
+    ex = exact(c)
+    rel = np.abs(got["loss"].astype(np.float64) - ref["loss"]) / np.maximum(np.abs(ref["loss"]), 1e-30)
+    msg = f"{name}: loss rel err vs reference {rel.max():.2e}"
+    checks = []
     for g in GRADS[c["kind"]]:
-        a, b = got[g].astype(np.float64), want[g].astype(np.float64)
-        msg += f"; {g} max-abs {np.abs(a - b).max(initial=0):.2e} (|max| {np.abs(b).max(initial=0):.2e})"
+        a, r, x = (np.asarray(v[g], np.float64) for v in (got, ref, ex))
+        bar = 1e-4 * max(1.0, np.abs(x).max(initial=0))
+        d_ours, d_ref, d_pair = (np.abs(a - x).max(initial=0), np.abs(r - x).max(initial=0),
+                                 np.abs(a - r).max(initial=0))
+        msg += f"; {g}: ours-oracle {d_ours:.2e}, reference-oracle {d_ref:.2e}, ours-reference {d_pair:.2e}"
+        checks.append((g, d_ours <= bar, d_pair <= bar + d_ref))
     print("\n" + msg, end="")
     assert rel.max() <= 1e-5, msg
-    for g in GRADS[c["kind"]]:
-        a, b = got[g].astype(np.float64), want[g].astype(np.float64)
-        err, scale = np.abs(a - b).max(initial=0), np.abs(b).max(initial=0)
-        assert err <= 1e-4 * max(1.0, scale), msg
+    for g, ok_oracle, ok_ref in checks:
+        assert ok_oracle and ok_ref, f"{g}: {msg}"
