@@ -37,9 +37,10 @@ def capi_ops() -> ctypes.CDLL:
     return ctypes.CDLL(str(OPS_SO))
 
 
-def joint_uses_tensor_cores(V: int, n_dur: int, d: int) -> bool:
-    """True when tf32=True selects the bf16 tcgen05 joint for this shape."""
-    return bool(capi_ops().asr_joint_path(1, V, n_dur, d))
+def joint_uses_tensor_cores(V: int, n_dur: int, d: int, tf32: bool = True) -> bool:
+    """True when the tcgen05 joint runs for this shape: bf16 operands with
+    tf32=True, split fp32 operands (three bf16 products) with tf32=False."""
+    return bool(capi_ops().asr_joint_path(1 if tf32 else 0, V, n_dur, d))
 
 
 def capi() -> ctypes.CDLL:

@@ -8,6 +8,7 @@
 //   backward: lattice_prep -> beta recursion (posteriors, duration-logit grads)
 //             -> zero the gradients -> joint backward (dlogits, dH, dW)
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "dp.cuh"
@@ -160,8 +161,31 @@ int bind_activations(JointArgs& a, const void* enc, const void* dec, int act_dty
     return ASR_OK;
 }
 
-bool use_tc(int tf32, const JointArgs& a) { return tf32 != 0 && tc_supported(a); }
-bool use_tc_bwd(int tf32, const JointArgs& a) { return use_tc(tf32, a) && tc_backward_supported(a); }
+// Joint path. tf32 = 1: bf16 tensor cores. tf32 = 0 (the reference's fp32
+// semantics): the tensor cores on split operands (three bf16 products, fp32
+// accurate; JointArgs::split), or the fp32 SIMT joint where the tensor-core
+// kernels do not take the shape or ASR_B200_FP32_SIMT=1 asks for it. Sets
+// a.split to the path's value.
+bool fp32_simt_forced() {
+    static const bool forced = [] {
+        const char* e = std::getenv("ASR_B200_FP32_SIMT");
+        return e && e[0] == '1';
+    }();
+    return forced;
+}
+
+bool use_tc(int tf32, JointArgs& a) {
+    a.split = tf32 ? 0 : 1;
+    if ((tf32 || !fp32_simt_forced()) && tc_supported(a)) return true;
+    a.split = 0;
+    return false;
+}
+
+bool use_tc_bwd(int tf32, JointArgs& a) {
+    if (use_tc(tf32, a) && tc_backward_supported(a)) return true;
+    a.split = 0;
+    return false;
+}
 
 }  // namespace
 
@@ -214,8 +238,8 @@ int zero_act_grads(const JointArgs& a, const TrWorkspace& w, void* grad_encoder,
 size_t rnnt_workspace_impl(int B, int T, int U, int V, int d, int tf32, int backward, int act_dtype) {
     if (bad_dims(B, T, U, V, d) || check_act_dtype(act_dtype)) return 0;
     JointArgs a = make_args(nullptr, nullptr, nullptr, nullptr, nullptr, B, T, U, V, 0, d, U - 1, 0, 0.f);
-    return tr_workspace_bytes(a, node_capacity(B, T, U), backward ? use_tc_bwd(tf32, a) : use_tc(tf32, a),
-                              backward != 0, act_dtype);
+    const bool tc = backward ? use_tc_bwd(tf32, a) : use_tc(tf32, a);
+    return tr_workspace_bytes(a, node_capacity(B, T, U), tc, backward != 0, act_dtype);
 }
 
 int rnnt_forward_impl(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
@@ -358,8 +382,8 @@ namespace {
 size_t tdt_workspace_impl(int B, int T, int U, int V, int n_dur, int d, int tf32, int backward, int act_dtype) {
     if (bad_dims(B, T, U, V, d) || n_dur < 1 || check_act_dtype(act_dtype)) return 0;
     JointArgs a = make_args(nullptr, nullptr, nullptr, nullptr, nullptr, B, T, U, V, n_dur, d, U - 1, 0, 0.f);
-    return tr_workspace_bytes(a, node_capacity(B, T, U), backward ? use_tc_bwd(tf32, a) : use_tc(tf32, a),
-                              backward != 0, act_dtype);
+    const bool tc = backward ? use_tc_bwd(tf32, a) : use_tc(tf32, a);
+    return tr_workspace_bytes(a, node_capacity(B, T, U), tc, backward != 0, act_dtype);
 }
 
 int tdt_forward_impl(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,

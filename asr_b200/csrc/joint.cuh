@@ -33,6 +33,11 @@ struct JointArgs {
     const float* rms_g;  // (d,) RMSNorm weight
     float rms_eps;
     const float* bias;   // (V,) or nullptr
+    // Tensor-core path only. 0: bf16 operands (tf32 = 1). 1: fp32 accuracy from
+    // three bf16 products (tf32 = 0): each fp32 operand x = hi + lo with hi =
+    // bf16(x), lo = bf16(x - hi), and every GEMM sums hi*hi + lo*hi + hi*lo in
+    // fp32 (the dropped lo*lo and the rounding of lo are ~2^-16 of the product).
+    int split;
 };
 
 // Forward epilogue outputs (compact per-node arrays). The lattice weights the

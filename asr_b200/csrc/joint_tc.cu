@@ -58,9 +58,12 @@ constexpr int kSmemBudget = 227 * 1024;
 constexpr int kBarBytes = 8 * (2 * kMaxRing + 2 * kMaxKChunks + 5) + 16;
 
 struct Geom {
-    int kchunks;  // ceil(d / 64)
-    int kpad;     // kchunks * 64
+    int parts;    // operand parts along K: 1 (bf16) or 3 (split fp32: hi, lo, hi)
+    int kp;       // hidden columns of one part: ceil(d / 64) * 64
+    int kchunks;  // 64-column K chunks of the hidden rows over all parts
+    int kpad;     // parts * kp: width of the hidden rows H and of the weight rows Wf
     int vpad;     // ceil((V + n_dur) / 16) * 16
+    int gw;       // parts * vpad: width of the G rows and of the transposed weight
     int cw;       // vocabulary columns of a chunk (multiple of 16, <= 256)
     int lw;       // columns of the last chunk (multiple of 16, <= cw)
     int nchunks;  // chunks per tile
@@ -68,15 +71,25 @@ struct Geom {
     int nstream;  // streamed variant: ring stages
 };
 
+// Split fp32 mode (JointArgs::split): the operands are stored as K-blocks of
+// their bf16 parts, paired so that every GEMM is unchanged over a longer K:
+//   H  rows [H_hi | H_lo | H_hi]  with  Wf rows [W_hi | W_hi | W_lo]   (logits)
+//   G  rows [G_hi | G_hi | G_lo]  with  Wt rows [Wt_hi | Wt_lo | Wt_hi] (d hidden)
+//   dW = sum over blocks p of G_p^T H_p                                   (dW)
+// so each product is hi*hi + lo*hi + hi*lo.
+//
 // The vocabulary is cut into equal chunks (e.g. 1040 = 5 x 208): every chunk
 // runs the same number of full-width MMAs per weight stage, instead of a narrow
 // remainder chunk paying a full ring of weight stages for a few columns.
 Geom make_geom(const JointArgs& a) {
     Geom g;
     const int kd = a.d + (a.head && a.bias ? 1 : 0);  // CTC head: bias as a ones column
-    g.kchunks = (kd + kAK - 1) / kAK;
-    g.kpad = g.kchunks * kAK;
+    g.parts = a.split ? 3 : 1;
+    g.kp = (kd + kAK - 1) / kAK * kAK;
+    g.kchunks = g.parts * (g.kp / kAK);
+    g.kpad = g.parts * g.kp;
     g.vpad = (a.V + a.n_dur + 15) / 16 * 16;
+    g.gw = g.parts * g.vpad;
     g.nchunks = (g.vpad + kNC - 1) / kNC;
     g.cw = ((g.vpad + g.nchunks - 1) / g.nchunks + 15) / 16 * 16;
     g.nchunks = (g.vpad + g.cw - 1) / g.cw;
@@ -533,18 +546,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 gv[i] = x;
                             }
                         }
+                        auto pack16 = [](const float (&x)[16], uint4& u0, uint4& u1) {
+                            u0.x = pack_bf16(x[0], x[1]);
+                            u0.y = pack_bf16(x[2], x[3]);
+                            u0.z = pack_bf16(x[4], x[5]);
+                            u0.w = pack_bf16(x[6], x[7]);
+                            u1.x = pack_bf16(x[8], x[9]);
+                            u1.y = pack_bf16(x[10], x[11]);
+                            u1.z = pack_bf16(x[12], x[13]);
+                            u1.w = pack_bf16(x[14], x[15]);
+                        };
                         uint4 w0, w1;
-                        w0.x = pack_bf16(gv[0], gv[1]);
-                        w0.y = pack_bf16(gv[2], gv[3]);
-                        w0.z = pack_bf16(gv[4], gv[5]);
-                        w0.w = pack_bf16(gv[6], gv[7]);
-                        w1.x = pack_bf16(gv[8], gv[9]);
-                        w1.y = pack_bf16(gv[10], gv[11]);
-                        w1.z = pack_bf16(gv[12], gv[13]);
-                        w1.w = pack_bf16(gv[14], gv[15]);
-                        // one 32-byte store (a whole sector): rows are vpad * 2 bytes, a multiple
+                        // one 32-byte store (a whole sector): rows are gw * 2 bytes, a multiple
                         // of 32, and groups start on 16-column boundaries
-                        st_global_32B(P.G + (int64_t)(n - begin) * g.vpad + c0, w0, w1);
+                        __nv_bfloat16* grow = P.G + (int64_t)(n - begin) * g.gw + c0;
+                        if (g.parts == 1) {
+                            pack16(gv, w0, w1);
+                            st_global_32B(grow, w0, w1);
+                        } else {  // split fp32: G rows [hi | hi | lo]
+                            float gl[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float h = __bfloat162float(__float2bfloat16_rn(gv[i]));
+                                gl[i] = gv[i] - h;
+                                gv[i] = h;
+                            }
+                            pack16(gv, w0, w1);
+                            st_global_32B(grow, w0, w1);
+                            st_global_32B(grow + g.vpad, w0, w1);
+                            pack16(gl, w0, w1);
+                            st_global_32B(grow + 2 * g.vpad, w0, w1);
+                        }
                     }
                 }
                 tc_fence_before();
@@ -594,11 +626,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // [joint_W; joint_W_dur] -> bf16 (vpad, kpad), zero padded; optionally also the
 // transpose (kpad, vpad) used as the K-major B operand of dH.
 __global__ void prep_weights_kernel(const float* __restrict__ W, const float* __restrict__ Wd,
-                                    const float* __restrict__ bias, int V, int n_dur, int d, int vpad, int kpad,
-                                    __nv_bfloat16* __restrict__ Wf, __nv_bfloat16* __restrict__ Wt) {
-    const int64_t total = (int64_t)vpad * kpad;
+                                    const float* __restrict__ bias, int V, int n_dur, int d, int vpad, int kp,
+                                    int parts, __nv_bfloat16* __restrict__ Wf, __nv_bfloat16* __restrict__ Wt) {
+    const int64_t total = (int64_t)vpad * kp;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int r = (int)(i / kpad), k = (int)(i % kpad);
+        const int r = (int)(i / kp), k = (int)(i % kp);
         float x = 0.f;
         if (k < d) {
             if (r < V)
@@ -608,9 +640,23 @@ __global__ void prep_weights_kernel(const float* __restrict__ W, const float* __
         } else if (k == d && bias && r < V) {
             x = bias[r];  // CTC head: the weight of the ones column
         }
-        const __nv_bfloat16 b = __float2bfloat16_rn(x);
-        Wf[i] = b;
-        if (Wt) Wt[(int64_t)k * vpad + r] = b;
+        const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+        if (parts == 1) {
+            Wf[i] = hi;
+            if (Wt) Wt[(int64_t)k * vpad + r] = hi;
+        } else {  // split fp32: Wf rows [hi | hi | lo], Wt rows [hi | lo | hi]
+            const __nv_bfloat16 lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+            __nv_bfloat16* wf = Wf + (int64_t)r * 3 * kp + k;
+            wf[0] = hi;
+            wf[kp] = hi;
+            wf[2 * kp] = lo;
+            if (Wt) {
+                __nv_bfloat16* wt = Wt + (int64_t)k * 3 * vpad + r;
+                wt[0] = hi;
+                wt[vpad] = lo;
+                wt[2 * vpad] = hi;
+            }
+        }
     }
 }
 
@@ -721,16 +767,51 @@ constexpr int kHiddenRun = 64;
 __device__ __forceinline__ float load1(const float* p) { return __ldg(p); }
 __device__ __forceinline__ float load1(const __nv_bfloat16* p) { return __bfloat162float(p[0]); }
 
-template <typename TA>
+// H element: tanh.approx for the bf16 path (below bf16 resolution); the
+// accurate tanhf for the split fp32 path, whose parts resolve ~2^-16.
+template <int PARTS>
+__device__ __forceinline__ float hidden_tanh(float x) {
+    return PARTS == 1 ? tanh_fast(x) : tanhf(x);
+}
+
+__device__ __forceinline__ void store_h(__nv_bfloat16* p, const float (&h)[4]) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]));
+}
+__device__ __forceinline__ void store_h(__nv_bfloat16* p, const float (&h)[8]) {
+    *reinterpret_cast<uint4*>(p) =
+        make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]), pack_bf16(h[6], h[7]));
+}
+
+// Stores CE columns of an H row: bf16(h), or for the split path the parts
+// [hi | lo | hi] at column offsets 0, kp and 2 kp.
+template <int PARTS, int CE>
+__device__ __forceinline__ void store_parts(__nv_bfloat16* p, const float (&h)[CE], int kp) {
+    if (PARTS == 1) {
+        store_h(p, h);
+        return;
+    }
+    float hi[CE], lo[CE];
+#pragma unroll
+    for (int i = 0; i < CE; ++i) {
+        hi[i] = __bfloat162float(__float2bfloat16_rn(h[i]));
+        lo[i] = h[i] - hi[i];
+    }
+    store_h(p, hi);
+    store_h(p + kp, lo);
+    store_h(p + 2 * kp, hi);
+}
+
+template <typename TA, int PARTS>
 __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, const TA* __restrict__ enc,
-                                                        const TA* __restrict__ dec, int T, int U, int d, int kpad,
+                                                        const TA* __restrict__ dec, int T, int U, int d, int kp,
                                                         const int32_t* __restrict__ bounds, int pass,
                                                         __nv_bfloat16* __restrict__ H) {
     const int N = total_nodes(m, B);
     const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
     const int rows = e - s;
     const int rows_pad = (rows + kPassAlign - 1) / kPassAlign * kPassAlign;
-    const int c8n = kpad / 8;
+    const int c8n = kp / 8;
+    const int64_t stride = (int64_t)PARTS * kp;
     const int lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
     for (int r0 = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kHiddenRun; r0 < rows_pad;
@@ -743,9 +824,10 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
             Tb = __ldg(m.Tb + c.b);
         }
         for (int r = r0; r < r1; ++r) {
-            uint4* dst = reinterpret_cast<uint4*>(H + (int64_t)r * kpad);
+            __nv_bfloat16* dst = H + (int64_t)r * stride;
             if (r >= rows) {
-                for (int k8 = lane; k8 < c8n; k8 += 32) dst[k8] = make_uint4(0, 0, 0, 0);
+                const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                for (int k8 = lane; k8 < c8n; k8 += 32) store_parts<PARTS, 8>(dst + k8 * 8, z, kp);
                 continue;
             }
             const TA* er = enc + ((int64_t)c.b * T + c.t) * d;
@@ -754,13 +836,9 @@ __global__ void __launch_bounds__(256, 3) hidden_kernel(LatticeMeta m, int B, co
                 const int k = k8 * 8;
                 float h[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) h[i] = k + i < d ? tanh_fast(load1(er + k + i) + load1(dr + k + i)) : 0.f;
-                uint4 w;
-                w.x = pack_bf16(h[0], h[1]);
-                w.y = pack_bf16(h[2], h[3]);
-                w.z = pack_bf16(h[4], h[5]);
-                w.w = pack_bf16(h[6], h[7]);
-                dst[k8] = w;
+                for (int i = 0; i < 8; ++i)
+                    h[i] = k + i < d ? hidden_tanh<PARTS>(load1(er + k + i) + load1(dr + k + i)) : 0.f;
+                store_parts<PARTS, 8>(dst + k, h, kp);
             }
             // next node: next label position, next frame, or the next utterance
             if (++c.u == c.Ub) {
@@ -811,28 +889,21 @@ struct Chunk<__nv_bfloat16> {  // 8 columns; 16 bytes of H
     }
 };
 
-__device__ __forceinline__ void store_h(__nv_bfloat16* p, const float (&h)[4]) {
-    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]));
-}
-__device__ __forceinline__ void store_h(__nv_bfloat16* p, const float (&h)[8]) {
-    *reinterpret_cast<uint4*>(p) =
-        make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]), pack_bf16(h[6], h[7]));
-}
-
 template <int UNR>
 constexpr int kFlatMinBlocks = UNR <= 4 ? 3 : 2;
 
-template <typename TA, int UNR>
+template <typename TA, int UNR, int PARTS>
 __global__ void __launch_bounds__(kFlatWarps * 32, kFlatMinBlocks<UNR>)
     hidden_flat_kernel(LatticeMeta m, int B, const TA* __restrict__ enc, const TA* __restrict__ dec, int T, int U,
-                       int d, int kpad, const int32_t* __restrict__ bounds, int pass, __nv_bfloat16* __restrict__ H) {
+                       int d, int kp, const int32_t* __restrict__ bounds, int pass, __nv_bfloat16* __restrict__ H) {
     constexpr int CE = Chunk<TA>::kCols;
     __shared__ int2 rows_sm[kFlatWarps][kFlatRun];
     const int N = total_nodes(m, B);
     const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
     const int rows = e - s;
     const int rows_pad = (rows + kPassAlign - 1) / kPassAlign * kPassAlign;  // a multiple of kFlatRun
-    const int cn = kpad / CE, cd = d / CE;  // chunks per H row, chunks holding columns < d
+    const int cn = kp / CE, cd = d / CE;  // chunks per H row (one part), chunks holding columns < d
+    const int64_t stride = (int64_t)PARTS * kp;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int nwarps = gridDim.x * kFlatWarps;
     int2* rs = rows_sm[w];
@@ -848,7 +919,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, kFlatMinBlocks<UNR>)
             rs[lane] = v;
         }
         __syncwarp();
-        __nv_bfloat16* dst = H + (int64_t)r0 * kpad;
+        __nv_bfloat16* dst = H + (int64_t)r0 * stride;
         int rr = 0, kc = lane;  // chunk q = lane + 32 i lies in row rr, column chunk kc
         while (kc >= cn) kc -= cn, ++rr;
         for (int q0 = 0; q0 < total; q0 += 32 * UNR) {
@@ -877,13 +948,13 @@ __global__ void __launch_bounds__(kFlatWarps * 32, kFlatMinBlocks<UNR>)
                     ev[j].get(x);
                     dv[j].get(y);
 #pragma unroll
-                    for (int i = 0; i < CE; ++i) h[i] = tanh_fast(x[i] + y[i]);
+                    for (int i = 0; i < CE; ++i) h[i] = hidden_tanh<PARTS>(x[i] + y[i]);
                 } else {
                     k = -1 - k;
 #pragma unroll
                     for (int i = 0; i < CE; ++i) h[i] = 0.f;
                 }
-                store_h(dst + (int64_t)rj[j] * kpad + k * CE, h);
+                store_parts<PARTS, CE>(dst + (int64_t)rj[j] * stride + k * CE, h, kp);
             }
         }
         __syncwarp();  // rs is rewritten by the next run
@@ -902,17 +973,18 @@ __global__ void __launch_bounds__(kFlatWarps * 32, kFlatMinBlocks<UNR>)
 template <typename TA, int J, int R>
 constexpr int kRowsMinBlocks = (R + 1) * J * 4 <= 40 ? 3 : 2;
 
-template <typename TA, int J, int R>
+template <typename TA, int J, int R, int PARTS>
 __global__ void __launch_bounds__(kFlatWarps * 32, (kRowsMinBlocks<TA, J, R>))
     hidden_rows_kernel(LatticeMeta m, int B, const TA* __restrict__ enc, const TA* __restrict__ dec, int T, int U,
-                       int d, int kpad, const int32_t* __restrict__ bounds, int pass, __nv_bfloat16* __restrict__ H) {
+                       int d, int kp, const int32_t* __restrict__ bounds, int pass, __nv_bfloat16* __restrict__ H) {
     constexpr int CE = Chunk<TA>::kCols;
     __shared__ int2 rows_sm[kFlatWarps][kFlatRun + 1];
     const int N = total_nodes(m, B);
     const int s = min(bounds[pass], N), e = min(bounds[pass + 1], N);
     const int rows = e - s;
     const int rows_pad = (rows + kPassAlign - 1) / kPassAlign * kPassAlign;
-    const int cn = kpad / CE, cd = d / CE;
+    const int cn = kp / CE, cd = d / CE;
+    const int64_t stride = (int64_t)PARTS * kp;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int nwarps = gridDim.x * kFlatWarps;
     int2* rs = rows_sm[w];
@@ -964,7 +1036,7 @@ __global__ void __launch_bounds__(kFlatWarps * 32, (kRowsMinBlocks<TA, J, R>))
 #pragma unroll
             for (int i = 0; i < R; ++i) {
                 if (i >= n) break;
-                __nv_bfloat16* out = H + (int64_t)(r0 + rr + i) * kpad + lane * CE;
+                __nv_bfloat16* out = H + (int64_t)(r0 + rr + i) * stride + lane * CE;
 #pragma unroll
                 for (int j = 0; j < J; ++j) {
                     if (lane + 32 * j >= cn) break;
@@ -974,12 +1046,12 @@ __global__ void __launch_bounds__(kFlatWarps * 32, (kRowsMinBlocks<TA, J, R>))
                         ev[j].get(x);
                         dv[i][j].get(y);
 #pragma unroll
-                        for (int k = 0; k < CE; ++k) h[k] = tanh_fast(x[k] + y[k]);
+                        for (int k = 0; k < CE; ++k) h[k] = hidden_tanh<PARTS>(x[k] + y[k]);
                     } else {
 #pragma unroll
                         for (int k = 0; k < CE; ++k) h[k] = 0.f;
                     }
-                    store_h(out + 32 * CE * j, h);
+                    store_parts<PARTS, CE>(out + 32 * CE * j, h, kp);
                 }
             }
             rr += n;
@@ -988,37 +1060,37 @@ __global__ void __launch_bounds__(kFlatWarps * 32, (kRowsMinBlocks<TA, J, R>))
     }
 }
 
-template <typename TA, int J, int R>
-void launch_rows(const JointArgs& a, const TA* enc, const TA* dec, int kpad, const int32_t* bounds, int pass,
+template <typename TA, int J, int R, int PARTS>
+void launch_rows(const JointArgs& a, const TA* enc, const TA* dec, int kp, const int32_t* bounds, int pass,
                  __nv_bfloat16* H, cudaStream_t st) {
-    hidden_rows_kernel<TA, J, R><<<sm_count() * kRowsMinBlocks<TA, J, R>, kFlatWarps * 32, 0, st>>>(
-        a.m, a.B, enc, dec, a.T, a.U, a.d, kpad, bounds, pass, H);
+    hidden_rows_kernel<TA, J, R, PARTS><<<sm_count() * kRowsMinBlocks<TA, J, R>, kFlatWarps * 32, 0, st>>>(
+        a.m, a.B, enc, dec, a.T, a.U, a.d, kp, bounds, pass, H);
 }
 
 // J = chunks per lane per row (1..8). Three rows in flight per warp where the
 // registers allow it (measured best on B200 for d = 640 in both activation
 // types), two for the widest rows.
-template <typename TA>
-bool launch_rows_j(int J, const JointArgs& a, const TA* enc, const TA* dec, int kpad, const int32_t* bounds, int pass,
+template <typename TA, int PARTS>
+bool launch_rows_j(int J, const JointArgs& a, const TA* enc, const TA* dec, int kp, const int32_t* bounds, int pass,
                    __nv_bfloat16* H, cudaStream_t st) {
     switch (J) {
-        case 1: launch_rows<TA, 1, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
-        case 2: launch_rows<TA, 2, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
-        case 3: launch_rows<TA, 3, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
-        case 4: launch_rows<TA, 4, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
-        case 5: launch_rows<TA, 5, 3>(a, enc, dec, kpad, bounds, pass, H, st); return true;
-        case 6: launch_rows<TA, 6, 2>(a, enc, dec, kpad, bounds, pass, H, st); return true;
-        case 7: launch_rows<TA, 7, 2>(a, enc, dec, kpad, bounds, pass, H, st); return true;
-        case 8: launch_rows<TA, 8, 2>(a, enc, dec, kpad, bounds, pass, H, st); return true;
+        case 1: launch_rows<TA, 1, 3, PARTS>(a, enc, dec, kp, bounds, pass, H, st); return true;
+        case 2: launch_rows<TA, 2, 3, PARTS>(a, enc, dec, kp, bounds, pass, H, st); return true;
+        case 3: launch_rows<TA, 3, 3, PARTS>(a, enc, dec, kp, bounds, pass, H, st); return true;
+        case 4: launch_rows<TA, 4, 3, PARTS>(a, enc, dec, kp, bounds, pass, H, st); return true;
+        case 5: launch_rows<TA, 5, 3, PARTS>(a, enc, dec, kp, bounds, pass, H, st); return true;
+        case 6: launch_rows<TA, 6, 2, PARTS>(a, enc, dec, kp, bounds, pass, H, st); return true;
+        case 7: launch_rows<TA, 7, 2, PARTS>(a, enc, dec, kp, bounds, pass, H, st); return true;
+        case 8: launch_rows<TA, 8, 2, PARTS>(a, enc, dec, kp, bounds, pass, H, st); return true;
         default: return false;
     }
 }
 
-template <typename TA, int UNR>
-void launch_flat(const JointArgs& a, const TA* enc, const TA* dec, int kpad, const int32_t* bounds, int pass,
+template <typename TA, int UNR, int PARTS>
+void launch_flat(const JointArgs& a, const TA* enc, const TA* dec, int kp, const int32_t* bounds, int pass,
                  __nv_bfloat16* H, cudaStream_t st) {
-    hidden_flat_kernel<TA, UNR><<<sm_count() * kFlatMinBlocks<UNR>, kFlatWarps * 32, 0, st>>>(a.m, a.B, enc, dec, a.T, a.U, a.d, kpad,
-                                                                            bounds, pass, H);
+    hidden_flat_kernel<TA, UNR, PARTS><<<sm_count() * kFlatMinBlocks<UNR>, kFlatWarps * 32, 0, st>>>(
+        a.m, a.B, enc, dec, a.T, a.U, a.d, kp, bounds, pass, H);
 }
 
 // CTC head hidden rows: one warp per frame row, H = bf16(x * rsqrt(mean(x^2) + eps)
@@ -1063,35 +1135,47 @@ __global__ void __launch_bounds__(256) rms_hidden_kernel(LatticeMeta m, int B, c
     }
 }
 
-int launch_hidden(const JointArgs& a, int kpad, const int32_t* bounds, int pass, __nv_bfloat16* H, cudaStream_t st) {
+template <int PARTS>
+void launch_hidden_parts(const JointArgs& a, int kp, const int32_t* bounds, int pass, __nv_bfloat16* H,
+                         cudaStream_t st) {
+    if (a.vec) {
+        // row-stationary kernel up to 8 chunks per lane, the flat kernel for wider rows
+        const int J = (kp / (a.enc16 ? 8 : 4) + 31) / 32;
+        if (a.enc16) {
+            if (!launch_rows_j<__nv_bfloat16, PARTS>(J, a, a.enc16, a.dec16, kp, bounds, pass, H, st))
+                launch_flat<__nv_bfloat16, 4, PARTS>(a, a.enc16, a.dec16, kp, bounds, pass, H, st);
+        } else {
+            if (!launch_rows_j<float, PARTS>(J, a, a.enc, a.dec, kp, bounds, pass, H, st))
+                launch_flat<float, 4, PARTS>(a, a.enc, a.dec, kp, bounds, pass, H, st);
+        }
+    } else if (a.enc16) {
+        hidden_kernel<__nv_bfloat16, PARTS><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc16, a.dec16, a.T, a.U,
+                                                                            a.d, kp, bounds, pass, H);
+    } else {
+        hidden_kernel<float, PARTS><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.dec, a.T, a.U, a.d, kp, bounds,
+                                                                    pass, H);
+    }
+}
+
+// The hidden rows of one pass: H = bf16(tanh(enc + dec)) (g.kpad columns), or
+// its split parts, or the CTC head's RMSNorm rows.
+int launch_hidden(const JointArgs& a, const Geom& g, const int32_t* bounds, int pass, __nv_bfloat16* H,
+                  cudaStream_t st) {
     KernelTimer kt("joint_hidden", st);
     if (a.head) {
         if (a.enc16)
             rms_hidden_kernel<__nv_bfloat16><<<sm_count() * 8, 256, 0, st>>>(
-                a.m, a.B, a.enc16, a.rms_g, a.rms_eps, a.bias ? 1 : 0, a.T, a.d, kpad, bounds, pass, H);
+                a.m, a.B, a.enc16, a.rms_g, a.rms_eps, a.bias ? 1 : 0, a.T, a.d, g.kpad, bounds, pass, H);
         else
             rms_hidden_kernel<float><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.rms_g, a.rms_eps,
-                                                                     a.bias ? 1 : 0, a.T, a.d, kpad, bounds, pass, H);
+                                                                     a.bias ? 1 : 0, a.T, a.d, g.kpad, bounds, pass, H);
         ASR_LAUNCH_CHECK();
         return ASR_OK;
     }
-    if (a.vec) {
-        // row-stationary kernel up to 8 chunks per lane, the flat kernel for wider rows
-        const int J = (kpad / (a.enc16 ? 8 : 4) + 31) / 32;
-        if (a.enc16) {
-            if (!launch_rows_j<__nv_bfloat16>(J, a, a.enc16, a.dec16, kpad, bounds, pass, H, st))
-                launch_flat<__nv_bfloat16, 4>(a, a.enc16, a.dec16, kpad, bounds, pass, H, st);
-        } else {
-            if (!launch_rows_j<float>(J, a, a.enc, a.dec, kpad, bounds, pass, H, st))
-                launch_flat<float, 4>(a, a.enc, a.dec, kpad, bounds, pass, H, st);
-        }
-    } else if (a.enc16) {
-        hidden_kernel<__nv_bfloat16><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc16, a.dec16, a.T, a.U, a.d, kpad,
-                                                                     bounds, pass, H);
-    } else {
-        hidden_kernel<float><<<sm_count() * 8, 256, 0, st>>>(a.m, a.B, a.enc, a.dec, a.T, a.U, a.d, kpad, bounds, pass,
-                                                             H);
-    }
+    if (g.parts == 3)
+        launch_hidden_parts<3>(a, g.kp, bounds, pass, H, st);
+    else
+        launch_hidden_parts<1>(a, g.kp, bounds, pass, H, st);
     ASR_LAUNCH_CHECK();
     return ASR_OK;
 }
@@ -1225,7 +1309,7 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
     {
         KernelTimer kt("joint_prep_weights", st);
         prep_weights_kernel<<<sm_count() * 4, 256, 0, st>>>(a.W, a.Wd, a.head ? a.bias : nullptr, a.V, a.n_dur,
-                                                             a.d, g.vpad, g.kpad, Wf, nullptr);
+                                                             a.d, g.vpad, g.kp, g.parts, Wf, nullptr);
         ASR_LAUNCH_CHECK();
         plan_passes_kernel<<<(L.pp.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, L.pp.passes, L.pp.step, bounds);
         ASR_LAUNCH_CHECK();
@@ -1243,7 +1327,7 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
     P.err = err;
     for (int p = 0; p < L.pp.passes; ++p) {
         P.range.pass = p;
-        int rc = launch_hidden(a, g.kpad, bounds, p, H, st);
+        int rc = launch_hidden(a, g, bounds, p, H, st);
         if (rc != ASR_OK) return rc;
         KernelTimer kt("joint_fwd_tc", st);
         rc = launch_joint<false>(pairs, L.pp.step / kBM, smem_bytes_for(g.kchunks), mfull, mtail, mh, P, st);
@@ -1312,7 +1396,7 @@ struct DhWalk {
     bool dirty;          // d_dec rows of utterance b hold unflushed sums
 };
 
-template <bool kSmemDec>
+template <bool kSmemDec, bool kSplit>
 struct DhEpilogue {
     const DhParams& P;
     const int col;     // hidden column
@@ -1321,6 +1405,8 @@ struct DhEpilogue {
     float* sdin;       // [dec_rows][kDhM] dec copy
     float* sacc;       // [dec_rows][kDhM] d_dec sums
 
+    // h = tanh(enc + dec), recomputed as the hidden rows computed it
+    __device__ __forceinline__ float th(float x) const { return kSplit ? tanhf(x) : tanh_fast(x); }
     __device__ float enc_at(int b, int t) const {
         if (P.a.head) return 0.f;  // CTC head: d hidden itself, no tanh' to recompute
         return col_ok ? act(P.a.enc, P.a.enc16, ((int64_t)b * P.a.T + t) * P.a.d + col) : 0.f;
@@ -1383,7 +1469,7 @@ struct DhEpilogue {
             if (++w.u == w.Ub) end_frame(w);
             return;
         }
-        const float h = tanh_fast(w.e_cur + dec_at(w, w.u));
+        const float h = th(w.e_cur + dec_at(w, w.u));
         const float x = g * (1.f - h * h);
         w.acc_e += x;
         add_dec(w, w.u, x);
@@ -1414,7 +1500,7 @@ struct DhEpilogue {
         float lo[N], hi[N];
 #pragma unroll
         for (int i = 0; i < N; ++i) {
-            const float h = tanh_fast((i < k ? w.e_cur : w.e_nxt) + dv[i]);
+            const float h = th((i < k ? w.e_cur : w.e_nxt) + dv[i]);
             const float x = v[i] * (1.f - h * h);
             sacc[idx[i]] = sa[i] + x;
             lo[i] = i < k ? x : 0.f;
@@ -1444,7 +1530,7 @@ struct DhEpilogue {
     }
 };
 
-template <bool kSmemDec>
+template <bool kSmemDec, bool kSplit>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     tc_dh_kernel(const __grid_constant__ CUtensorMap map_wt, const __grid_constant__ CUtensorMap map_g, DhParams P) {
     extern __shared__ uint8_t smem_raw[];
@@ -1468,7 +1554,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int ntiles = e > s ? (e - s + kDhNodes - 1) / kDhNodes : 0;
     const int tile0 = (int)((int64_t)grp * ntiles / P.groups);
     const int tile1 = (int)((int64_t)(grp + 1) * ntiles / P.groups);
-    const int ksteps = (P.g.vpad + kDhK - 1) / kDhK;
+    const int ksteps = (P.g.gw + kDhK - 1) / kDhK;  // K: the vocabulary, over every part
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -1561,7 +1647,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int lane_base = 32 * (warp & 3);
         const int cl = lane_base + lane;
         const int col = dt * kDhM + cl;
-        const DhEpilogue<kSmemDec> ep{P, col, col < a.d, cl, sdin, sacc};
+        const DhEpilogue<kSmemDec, kSplit> ep{P, col, col < a.d, cl, sdin, sacc};
         DhWalk w;
         {
             const int n0 = s + tile0 * kDhNodes;
@@ -1648,7 +1734,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int* err = P.err;
 
     const int nvt = (P.g.vpad + kDwM - 1) / kDwM;
-    const int nkt = (P.g.kpad + kDwN - 1) / kDwN;
+    const int nkt = (P.g.kp + kDwN - 1) / kDwN;
     const int item = blockIdx.x;
     // split slowest: the CTAs of one row range run side by side and share its G / H rows in L2
     const int vt = item % nvt;
@@ -1658,7 +1744,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int rows = e > s ? (e - s + 63) / 64 * 64 : 0;  // zero rows pad the pass to 64
     const int per = ((rows / 64 + P.splits - 1) / P.splits) * 64;
     const int r0 = split * per, r1 = min(rows, r0 + per);
-    const int nsteps = (vt < nvt && r1 > r0) ? (r1 - r0) / 64 : 0;
+    // split fp32: one pass over the rows per part p, G block p against H block p
+    const int rsteps = (vt < nvt && r1 > r0) ? (r1 - r0) / 64 : 0;
+    const int nsteps = rsteps * P.g.parts;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kDwStages; ++i) {
@@ -1687,12 +1775,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int i = 0; i < nsteps; ++i) {
                 if (!mbar_wait(&b_empty[stage], phase ^ 1, err, 21)) break;
                 uint8_t* st = stages + (size_t)stage * kDwStageBytes;
-                const int r = r0 + i * 64;
+                const int part = i / rsteps;
+                const int r = r0 + (i - part * rsteps) * 64;
+                const int gc = part * P.g.vpad + vt * kDwM;  // G columns of this part
                 mbar_arrive_expect_tx(&b_full[stage], kDwStageBytes);
-                tma_load_2d(st, &map_g, vt * kDwM, r, &b_full[stage]);
-                tma_load_2d(st + kBox, &map_g, vt * kDwM + 64, r, &b_full[stage]);
+                tma_load_2d(st, &map_g, gc, r, &b_full[stage]);
+                tma_load_2d(st + kBox, &map_g, gc + 64, r, &b_full[stage]);
                 // H: kDwN / 64 column blocks of 64 in one box of the 3-D view
-                tma_load_3d(st + 2 * kBox, &map_h, 0, r, kt * (kDwN / 64), &b_full[stage]);
+                tma_load_3d(st + 2 * kBox, &map_h, 0, r, part * (P.g.kp / 64) + kt * (kDwN / 64), &b_full[stage]);
                 issued[stage] = true;
                 ipar[stage] = phase;
                 if (++stage == kDwStages) {
@@ -1797,8 +1887,8 @@ BwdLayout bwd_layout(const JointArgs& a, int64_t cap) {
         return o;
     };
     L.wf = take(sizeof(__nv_bfloat16) * (size_t)g.vpad * g.kpad);
-    L.wt = take(sizeof(__nv_bfloat16) * (size_t)g.kpad * g.vpad);
-    L.g = take(sizeof(__nv_bfloat16) * (size_t)L.step * g.vpad);
+    L.wt = take(sizeof(__nv_bfloat16) * (size_t)g.kp * g.gw);
+    L.g = take(sizeof(__nv_bfloat16) * (size_t)L.step * g.gw);
     L.h = take(sizeof(__nv_bfloat16) * (size_t)L.step * g.kpad);
     L.bounds = take(sizeof(int32_t) * (L.passes + 1));
     L.err = take(sizeof(int));
@@ -1841,7 +1931,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     {
         KernelTimer kt("joint_prep_weights", st);
         prep_weights_kernel<<<sms * 4, 256, 0, st>>>(a.W, a.Wd, a.head ? a.bias : nullptr, a.V, a.n_dur, a.d,
-                                                     g.vpad, g.kpad, Wf, Wt);
+                                                     g.vpad, g.kp, g.parts, Wf, Wt);
         ASR_LAUNCH_CHECK();
     }
     {
@@ -1855,9 +1945,9 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     CUtensorMap mfull, mtail, m_h, m_wt, m_g, m_gmn, m_hmn;
     if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
     if (!make_map(&m_h, H, rows, g.kpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
-    if (!make_map(&m_wt, Wt, g.kpad, g.vpad, kDhK, kDhM, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
-    if (!make_map(&m_g, G, rows, g.vpad, kDhK, kDhNodes, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
-    if (!make_map(&m_gmn, G, rows, g.vpad, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_wt, Wt, g.kp, g.gw, kDhK, kDhM, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_g, G, rows, g.gw, kDhK, kDhNodes, CU_TENSOR_MAP_SWIZZLE_64B)) return ASR_ERR_CUDA;
+    if (!make_map(&m_gmn, G, rows, g.gw, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
     if (!make_map_blocks(&m_hmn, H, rows, g.kpad, 64, kDwN / 64)) return ASR_ERR_CUDA;
 
     // dlogits kernel parameters
@@ -1881,14 +1971,15 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     DP.d_enc = o.d_enc;
     DP.d_dec = o.d_dec;
     DP.err = err;
-    DP.ndt = (g.kpad + kDhM - 1) / kDhM;
+    DP.ndt = (g.kp + kDhM - 1) / kDhM;
     DP.groups = std::max(1, sms / DP.ndt);
     const int limit = dyn_smem_limit();
     DP.dec_rows = !a.head && (int)dh_smem_bytes(2, a.U) <= limit ? a.U : 0;
     DP.stages = 2;
     while (DP.stages < 8 && (int)dh_smem_bytes(DP.stages + 1, DP.dec_rows) <= limit) ++DP.stages;
     const size_t smem_dh = dh_smem_bytes(DP.stages, DP.dec_rows);
-    auto dh_kernel = DP.dec_rows > 0 ? tc_dh_kernel<true> : tc_dh_kernel<false>;
+    auto dh_kernel = g.parts == 3 ? (DP.dec_rows > 0 ? tc_dh_kernel<true, true> : tc_dh_kernel<false, true>)
+                                  : (DP.dec_rows > 0 ? tc_dh_kernel<true, false> : tc_dh_kernel<false, false>);
     ASR_CUDA_TRY(cudaFuncSetAttribute(dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dh));
 
     DwParams WP;
@@ -1900,7 +1991,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     WP.dWd = o.dWd;
     WP.dbias = a.head ? o.dbias : nullptr;
     WP.err = err;
-    const int nvt = (g.vpad + kDwM - 1) / kDwM, nkt = (g.kpad + kDwN - 1) / kDwN;
+    const int nvt = (g.vpad + kDwM - 1) / kDwM, nkt = (g.kp + kDwN - 1) / kDwN;
     WP.splits = std::max(1, sms / (nvt * nkt));  // one wave: a CTA fills an SM's shared memory
     const size_t smem_dw = dw_smem_bytes();
     ASR_CUDA_TRY(cudaFuncSetAttribute(tc_dw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dw));
@@ -1911,7 +2002,7 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
         WP.pass = p;
         {
             KernelTimer kt("joint_dlogits_tc", st);
-            int rc = launch_hidden(a, g.kpad, bounds, p, H, st);
+            int rc = launch_hidden(a, g, bounds, p, H, st);
             if (rc != ASR_OK) return rc;
             rc = launch_joint<true>(pairs, L.step / kBM, smem_fw, mfull, mtail, m_h, TP, st);
             if (rc != ASR_OK) return rc;

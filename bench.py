@@ -186,6 +186,12 @@ def kernel_work(name, N, d, Vf, n_dur, frames=0, labels=0):
     return None, 0.0
 
 
+def joint_path_name(tc, tf32):
+    if not tc:
+        return "SIMT fp32"
+    return "tcgen05 bf16" if tf32 else "tcgen05 fp32 (three bf16 products of split operands)"
+
+
 def parse_profile(text):
     rows = {}
     for line in text.strip().splitlines():
@@ -491,16 +497,16 @@ def run_config(args):
         roof = {"kernel": top, "bound": k.get("bound"), "achieved": k.get("achieved"),
                 "peak": peaks["bf16_tflops_sustained"] if k.get("bound") == "tensor" else peaks["hbm_gbs"],
                 "unit": k.get("unit"), "frac": k.get("frac"), "traffic": None, "share": k["share"]}
-    tc = kind != "ctc" and tf32 and _lib.joint_uses_tensor_cores(cfg["V"], n_dur, d)
+    tc = kind != "ctc" and _lib.joint_uses_tensor_cores(cfg["V"], n_dur, d, tf32=tf32)
     line = {
         "metric": "fused joint+loss fwd+bwd utterances/s" if kind != "ctc" else "CTC loss fwd+bwd utterances/s",
         "value": round(B / (ms / 1000.0), 3), "unit": "utterances/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16" if tc else "f32", "data": "synthetic",
+        "vs_baseline": None, "dtype": "bf16" if tc and tf32 else "f32", "data": "synthetic",
         "config": {"workload": cfg["name"], "batch": B, "T": list(cfg["T"]), "U": list(cfg["U"]), "vocab": cfg["V"],
                    "d_model": d or None, "lattice_nodes": N if kind != "ctc" else None,
                    "l2": "flushed between timed steps (256 MB write)",
-                   "joint_path": None if kind == "ctc" else ("tcgen05 bf16" if tc else "SIMT fp32")},
+                   "joint_path": None if kind == "ctc" else joint_path_name(tc, tf32)},
         "roofline": roof, "cpu_baseline": None,
         "e2e": {"value": round(B / (e2e_ms / 1000.0), 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4)},
@@ -1322,19 +1328,19 @@ def main():
         ref_cuda = None
         if world == 1 and not args.no_reference_cuda and not args.batch:
             ref_cuda = reference_cuda_leg("c5", value)
-        tc = bool(args.tf32) and _lib.joint_uses_tensor_cores(VOCAB, len(DURATIONS), D_MODEL)
+        tc = _lib.joint_uses_tensor_cores(VOCAB, len(DURATIONS), D_MODEL, tf32=bool(args.tf32))
         line = {
             "metric": "fused joint+loss fwd+bwd utterances/s", "value": round(value, 3), "unit": "utterances/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16" if tc else "f32", "data": "synthetic",
+            "dtype": "bf16" if args.tf32 and tc else "f32", "data": "synthetic",
             "config": {"workload": "tdt_bpe1024_sharded", "global_batch": GLOBAL_B, "per_gpu_batch": len(mine),
                        "T": list(T_RANGE), "U": list(U_RANGE), "d_model": D_MODEL, "vocab": VOCAB,
                        "durations": DURATIONS, "sigma": SIGMA, "lattice_nodes_global": N_global,
                        "lattice_nodes_rank0": N_local, "shard_imbalance": round(shard_imbalance(
                            in_lens, tgt_lens, shards), 4), "parallelism": f"dp{world}",
                        "l2": "flushed between timed steps (256 MB write)",
-                       "joint_path": "tcgen05 bf16" if tc else "SIMT fp32", "activations": args.act_dtype},
+                       "joint_path": joint_path_name(tc, args.tf32), "activations": args.act_dtype},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4),

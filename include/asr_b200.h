@@ -319,8 +319,11 @@ int asr_greedy_scan(const float* encoder, const float* pred, const float* joint_
  * `stream`. Intended for debugging; the hot path never calls it. */
 int asr_workspace_status(const void* workspace, int B, int* clamped, asr_stream_t stream);
 
-/* Joint-network path a call takes: 1 = bf16 tcgen05 tensor cores, 0 = fp32 SIMT.
- * tf32 = 0 always selects the fp32 path. */
+/* Joint-network path a call takes: 1 = tcgen05 tensor cores, 0 = fp32 SIMT.
+ * With tf32 = 1 the tensor-core path uses bf16 operands; with tf32 = 0 it keeps
+ * fp32 accuracy by splitting every operand into two bf16 parts and summing three
+ * products (hi*hi + lo*hi + hi*lo) in fp32. ASR_B200_FP32_SIMT=1 in the
+ * environment sends tf32 = 0 calls to the SIMT path instead. */
 int asr_joint_path(int tf32, int V, int n_dur, int d);
 
 /* Per-kernel device timing of this library's own launches: while enabled, every

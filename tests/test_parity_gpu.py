@@ -668,3 +668,65 @@ def test_hidden_vector_paths_match_scalar_path(act, d):
     bar = 2e-4 if act == "bf16" else 1e-5
     for name, a, b in zip(("d_enc", "d_dec", "dW"), gv, gs):
         assert _rel(a, b) < bar, f"{name}: {_rel(a, b):.3e}"
+
+
+_SIMT_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from tests.gpu_cases import transducer_case
+from asr_b200 import _lib
+from asr_b200.loss.tdt import tdt_loss
+from asr_b200.loss.rnnt import rnnt_loss
+assert not _lib.joint_uses_tensor_cores(1024, 5, 640, tf32=False)
+out = {}
+c = transducer_case(71, 3, (60, 90), (10, 25), 1024, 640, n_dur=5)
+L = [torch.tensor(c[k], device="cuda", requires_grad=True) for k in ("enc", "dec", "W", "W_dur")]
+I = [torch.tensor(c[k], device="cuda") for k in ("targets", "in_lens", "tgt_lens")]
+loss = tdt_loss(*L, *I, list(range(5)), 0, 0.05, False)
+loss.sum().backward()
+out.update(tdt_loss=loss.detach().cpu().numpy(), **{f"tdt_{i}": t.grad.cpu().numpy() for i, t in enumerate(L)})
+c = transducer_case(72, 3, (60, 90), (10, 25), 30, 640)
+L = [torch.tensor(c[k], device="cuda", requires_grad=True) for k in ("enc", "dec", "W")]
+I = [torch.tensor(c[k], device="cuda") for k in ("targets", "in_lens", "tgt_lens")]
+loss = rnnt_loss(*L, *I, 0, False)
+loss.sum().backward()
+out.update(rnnt_loss=loss.detach().cpu().numpy(), **{f"rnnt_{i}": t.grad.cpu().numpy() for i, t in enumerate(L)})
+np.savez(sys.argv[2], **out)
+"""
+
+
+def test_fp32_simt_path_matches_oracle(tmp_path):
+    """tf32 = False runs the tensor cores on split operands by default; the fp32
+    SIMT joint (ASR_B200_FP32_SIMT=1, read once per process, and the path for
+    shapes the tensor-core kernels do not take) is checked against the oracle in
+    a process of its own at the fp32 bars."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = str(Path(__file__).resolve().parents[1])
+    f = tmp_path / "simt.npz"
+    env = dict(os.environ, ASR_B200_FP32_SIMT="1")
+    subprocess.run([sys.executable, "-c", _SIMT_SCRIPT, root, str(f)], check=True, env=env, timeout=600)
+    got = np.load(f)
+    c = transducer_case(71, 3, (60, 90), (10, 25), 1024, 640, n_dur=5)
+    o = _tdt_oracle(dict(c, sigma=0.05), 0.05)
+    np.testing.assert_allclose(got["tdt_loss"], o["loss"], rtol=LOSS_RTOL, atol=LOSS_ATOL)
+    for i, k in enumerate(("d_enc", "d_dec", "dW", "dW_dur")):
+        assert np.abs(got[f"tdt_{i}"] - o[k]).max() <= GRAD_ATOL, k
+    c = transducer_case(72, 3, (60, 90), (10, 25), 30, 640)
+    o = oracle.rnnt(c["enc"], c["dec"], c["W"], c["targets"], c["in_lens"], c["tgt_lens"], grad_loss=c["grad_loss"])
+    np.testing.assert_allclose(got["rnnt_loss"], o["loss"], rtol=LOSS_RTOL, atol=LOSS_ATOL)
+    for i, k in enumerate(("d_enc", "d_dec", "dW")):
+        assert np.abs(got[f"rnnt_{i}"] - o[k]).max() <= GRAD_ATOL, k
+
+
+def test_fp32_mode_runs_on_tensor_cores():
+    """The fp32 mode (tf32 = False) takes the tensor-core joint with split
+    operands at the BASELINE shapes (see test_fp32_simt_path_matches_oracle for
+    the SIMT path)."""
+    from asr_b200 import _lib
+
+    for V, nd, d in ((1024, 5, 640), (30, 0, 640), (1024, 0, 1024)):
+        assert _lib.joint_uses_tensor_cores(V, nd, d, tf32=False), (V, nd, d)
