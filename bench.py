@@ -100,11 +100,20 @@ class ClockSampler:
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,uuid")
 
-    def __init__(self, out_path=None):
+    def __init__(self, out_path=None, devices=1):
+        """Samples every GPU of the box; the summary covers the CUDA devices
+        0 .. devices - 1 of this process (matched by UUID), the GPUs the run uses."""
         self.proc = None
         self.out_path = out_path
+        self.uuids = None
+        try:
+            import torch
+
+            self.uuids = {str(torch.cuda.get_device_properties(i).uuid).lower() for i in range(devices)}
+        except Exception:  # noqa: BLE001 - no torch / CUDA: summarise every GPU
+            self.uuids = None
 
     def start(self):
         try:
@@ -132,6 +141,8 @@ class ClockSampler:
             if len(f) < 9:
                 continue
             if gpu_indices is not None and int(f[0]) not in gpu_indices:
+                continue
+            if self.uuids and len(f) >= 10 and f[9].lower().removeprefix("gpu-") not in self.uuids:
                 continue
             try:
                 sm.append(float(f[1]))
@@ -1185,7 +1196,7 @@ def main():
     torch.cuda.synchronize()
     lib = _lib.capi_ops()
     lib.asr_profiler_report(None, 0, 1)
-    clocks = ClockSampler(args.clocks_log) if rank == 0 else None
+    clocks = ClockSampler(args.clocks_log, devices=world) if rank == 0 else None
     if clocks:  # before the barrier: no rank may start timing while rank 0 waits for the sampler
         clocks.start()
         time.sleep(0.3)
