@@ -1166,6 +1166,8 @@ def main():
     tl = torch.tensor(host["tgt_lens"], device=dev)
     stream = torch.cuda.current_stream()
 
+    ar_events = []  # (start, end) of each all-reduce while timing it is on
+
     def step(e, d, tg, ilen, tlen):
         for p in (e, d, W, Wd):
             p.grad = None
@@ -1173,7 +1175,16 @@ def main():
         per = loss / tlen.clamp_min(1)
         total = per.sum() / GLOBAL_B  # global mean, as the systems' loss_per.mean()
         total.backward()
+        if world > 1 and timing_ar[0]:
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            out = allreduce_joint([W.grad, Wd.grad, total.detach().reshape(1)])
+            a1.record(stream)
+            ar_events.append((a0, a1))
+            return out
         return allreduce_joint([W.grad, Wd.grad, total.detach().reshape(1)])
+
+    timing_ar = [False]
 
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
 
@@ -1204,7 +1215,9 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     lib.asr_profiler_enable(1)
+    timing_ar[0] = True
     ms_total = timed_loop(lambda: step(enc, dec, targets, il, tl), args.steps)
+    timing_ar[0] = False
     lib.asr_profiler_enable(0)
     if world > 1:
         dist.barrier()
@@ -1279,6 +1292,15 @@ def main():
     e2e_total = p0.elapsed_time(p1)
 
     # ---- max over ranks
+    # per-rank device times of the timed steps (the imbalance the LPT split leaves)
+    # and of the all-reduce alone
+    ar_ms = sum(a.elapsed_time(b) for a, b in ar_events) / max(args.steps, 1) if ar_events else 0.0
+    mine = torch.tensor([ms_total / args.steps, ar_ms], device=dev, dtype=torch.float64)
+    per_rank = [mine.clone() for _ in range(world)]
+    if world > 1:
+        dist.all_gather(per_rank, mine)
+    rank_ms = [round(float(x[0]), 3) for x in per_rank]
+    allreduce_ms = round(max(float(x[1]) for x in per_rank), 4)
     t = torch.tensor([ms_total, e2e_total, e2e_serial_total], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1348,7 +1370,9 @@ def main():
             "config": {"workload": "tdt_bpe1024_sharded", "global_batch": GLOBAL_B, "per_gpu_batch": len(mine),
                        "T": list(T_RANGE), "U": list(U_RANGE), "d_model": D_MODEL, "vocab": VOCAB,
                        "durations": DURATIONS, "sigma": SIGMA, "lattice_nodes_global": N_global,
-                       "lattice_nodes_rank0": N_local, "shard_imbalance": round(shard_imbalance(
+                       "lattice_nodes_rank0": N_local, "rank_ms_per_step": rank_ms,
+                       "allreduce_ms_per_step": allreduce_ms if world > 1 else None,
+                       "shard_imbalance": round(shard_imbalance(
                            in_lens, tgt_lens, shards), 4), "parallelism": f"dp{world}",
                        "l2": "flushed between timed steps (256 MB write)",
                        "joint_path": joint_path_name(tc, args.tf32), "activations": args.act_dtype},
