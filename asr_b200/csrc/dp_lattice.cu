@@ -171,7 +171,7 @@ __device__ __forceinline__ float dur_lp(bool uniq, const int (&k)[MAXD + 1], con
 
 // ------------------------------------------------------------------ forward
 
-template <bool RNNT, int MAXD, int KS, bool GM>
+template <bool RNNT, int MAXD, bool GM>
 __global__ void __launch_bounds__(kMaxThreads) lattice_alpha_kernel(LatArgs a) {
     constexpr bool TDT = !RNNT;
     constexpr int RV = MAXD + 2;           // recursion variable of diagonals g - MAXD - 1 .. g
@@ -180,11 +180,11 @@ __global__ void __launch_bounds__(kMaxThreads) lattice_alpha_kernel(LatArgs a) {
     constexpr int NTK = RNNT ? 1 : MAXD + 1;  // token durations 0 .. NTK - 1
     constexpr int N = NB + NTK + 1;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int nt = blockDim.x, ks = KS > 0 ? KS : a.ks, upos = nt * ks;
+    const int nt = blockDim.x, ks = a.ks, upos = nt * ks;
     const int b = blockIdx.x;
     const int Tb = a.m.Tb[b], Ub = a.m.Ub[b], off = a.m.off[b];
     // one position per thread: only the warps holding positions < U_b take part
-    const int act = min(nt, (Ub + 31) & ~31);  // threads whose positions all lie past U_b leave
+    const int act = ks == 1 ? min(nt, (Ub + 31) & ~31) : nt;
     const int tid = threadIdx.x;
     if (tid >= act) return;
     const int arows = RNNT ? Tb : Tb + 1;  // rows of the stored alpha grid
@@ -251,15 +251,13 @@ __global__ void __launch_bounds__(kMaxThreads) lattice_alpha_kernel(LatArgs a) {
             rs[s2] = ring + r * upos;
         }
         const int alo = max(0, g - arows + 1);
-        // KS > 0: the positions of a thread are unrolled and computed branch-free
-        // (invalid ones on clamped, in-bounds addresses, then discarded), so their
-        // independent log-sum-exp chains interleave
-        auto node = [&](int j) {
+#pragma unroll 1
+        for (int j = 0; j < ks; ++j) {
             const int u = j * nt + tid;
             const int t = g - u;
             const bool in = u < Ub && t >= 0 && t <= Tb;
             Pair x = {kNeg, 0.f};
-            if (KS > 0 || in) {
+            if (in) {
                 const int ul = u >= 1 ? u - 1 : 0;
                 float hi[N], lo[N], wv[N];
                 bool ok[N];
@@ -306,22 +304,14 @@ __global__ void __launch_bounds__(kMaxThreads) lattice_alpha_kernel(LatArgs a) {
                 wv[N - 1] = 0.f;
                 ok[N - 1] = t == 0 && u == 0;
                 x = lse_pair(hi, lo, wv, ok);
-                if (!in) x = {kNeg, 0.f};
-                if (in && (RNNT ? t < Tb : true)) a.alpha[xoff + an + (u - alo)] = to_double(x);
-                if (in && t == Tb && u == Ub - 1) {  // terminal (rnnt.cu:242-248, tdt.cu:291-295)
+                if (RNNT ? t < Tb : true) a.alpha[xoff + an + (u - alo)] = to_double(x);
+                if (t == Tb && u == Ub - 1) {  // terminal (rnnt.cu:242-248, tdt.cu:291-295)
                     const double lp = to_double(x);
                     a.log_prob[b] = (float)lp;
                     a.loss[b] = (float)(-lp);
                 }
             }
             if (!GM) ring[rg * upos + u] = x;  // slot of diagonal g - MAXD - 2: unused now
-        };
-        if (KS > 0) {
-#pragma unroll
-            for (int j = 0; j < (KS > 0 ? KS : 1); ++j) node(j);
-        } else {
-#pragma unroll 1
-            for (int j = 0; j < ks; ++j) node(j);
         }
         an += diag_len(g, arows, Ub);
         sg = sg + 1 == S ? 0 : sg + 1;
@@ -340,16 +330,16 @@ __global__ void __launch_bounds__(kMaxThreads) lattice_alpha_kernel(LatArgs a) {
 // duration class, also zero-duration classes other than the d = 0 token
 // chain's. log Z is the forward's terminal, recomputed in float64.
 
-template <bool RNNT, int MAXD, int KS, bool GM>
+template <bool RNNT, int MAXD, bool GM>
 __global__ void __launch_bounds__(kMaxThreads) lattice_beta_kernel(LatArgs a) {
     constexpr bool TDT = !RNNT;
     constexpr int RV = MAXD + 2;    // beta of diagonals g .. g + MAXD + 1
     constexpr int S = kAhead + 1;   // weight diagonals g - P .. g
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int nt = blockDim.x, ks = KS > 0 ? KS : a.ks, upos = nt * ks;
+    const int nt = blockDim.x, ks = a.ks, upos = nt * ks;
     const int b = blockIdx.x;
     const int Tb = a.m.Tb[b], Ub = a.m.Ub[b], off = a.m.off[b], boff = a.m.aoff[b];
-    const int act = min(nt, (Ub + 31) & ~31);  // threads whose positions all lie past U_b leave
+    const int act = ks == 1 ? min(nt, (Ub + 31) & ~31) : nt;
     const int tid = threadIdx.x;
     if (tid >= act) return;
     const int arows = RNNT ? Tb : Tb + 1;
@@ -426,14 +416,15 @@ __global__ void __launch_bounds__(kMaxThreads) lattice_beta_kernel(LatArgs a) {
         const double* sa = astg + sg * upos;
         bn -= diag_len(g, Tb + 1, Ub);
         const int blo = max(0, g - Tb);
-        auto node = [&](int j) {  // see the forward: KS > 0 computes branch-free
+#pragma unroll 1
+        for (int j = 0; j < ks; ++j) {
             const int u = j * nt + tid;
             const int t = g - u;
             const bool in = u < Ub && t >= 0 && t <= Tb;
             Pair x = {kNeg, 0.f};
             if (in && t == Tb) {
                 x = {u == Ub - 1 ? 0.f : kNeg, 0.f};
-            } else if (KS > 0 || in) {
+            } else if (in) {
                 const bool can_tok = u < Ub - 1;
                 const int ur = can_tok ? u + 1 : u;
                 float lb, ly;
@@ -516,7 +507,7 @@ __global__ void __launch_bounds__(kMaxThreads) lattice_beta_kernel(LatArgs a) {
                     float* gd = a.gdur + (int64_t)nn * nd;
 #pragma unroll
                     for (int d = 0; d <= MAXD; ++d)
-                        if (in && dt.single[d] >= 0) gd[dt.single[d]] = gl * (gk[d] - ex2f(ldv[d] * kLog2e_f) * gsum);
+                        if (dt.single[d] >= 0) gd[dt.single[d]] = gl * (gk[d] - ex2f(ldv[d] * kLog2e_f) * gsum);
                 } else {
                     // several classes share a duration value: every class's edges,
                     // each with its own class log-prob
@@ -537,24 +528,13 @@ __global__ void __launch_bounds__(kMaxThreads) lattice_beta_kernel(LatArgs a) {
                         gsum += g2;
                     }
                     float* gd = a.gdur + (int64_t)nn * nd;
-                    if (in)
-                        for (int k = 0; k < nd; ++k) gd[k] = gl * (gi[k] - ex2f(ld[k] * kLog2e_f) * gsum);
+                    for (int k = 0; k < nd; ++k) gd[k] = gl * (gi[k] - ex2f(ld[k] * kLog2e_f) * gsum);
                 }
-                if (in) {
-                    a.cb[nn] = gl * bp;
-                    a.ct[nn] = gl * tp;
-                }
-                if (!in) x = {kNeg, 0.f};
+                a.cb[nn] = gl * bp;
+                a.ct[nn] = gl * tp;
             }
             if (in && (GM || TDT)) a.beta[boff + bn + (u - blo)] = to_double(x);
             if (!GM) ring[rg * upos + u] = x;  // slot of diagonal g + MAXD + 2: unused now
-        };
-        if (KS > 0) {
-#pragma unroll
-            for (int j = 0; j < (KS > 0 ? KS : 1); ++j) node(j);
-        } else {
-#pragma unroll 1
-            for (int j = 0; j < ks; ++j) node(j);
         }
     }
     if (!GM) cp_async_wait_n<0>();
@@ -586,31 +566,21 @@ int prepare(Kern k, size_t smem, int threads) {
     return ASR_OK;
 }
 
-// Two label positions per thread up to 1024 positions (their chains interleave,
-// see the kernels); past that, as many per thread as 512 threads need.
-constexpr int kPairKS = 2;
-
 template <bool FWD, bool RNNT, int MAXD>
 int launch_lattice(LatArgs a, int B, int U, const char* name, cudaStream_t st) {
     if (U < 1 || U > kMaxLabelPositions) return ASR_ERR_UNSUPPORTED;
+    const int nt = std::min(kMaxThreads, (U + 31) / 32 * 32);
+    a.ks = (U + nt - 1) / nt;
+    const int upos = nt * a.ks;
     const int nd = RNNT ? 0 : a.n_dur;
-    int nt = std::max(32, ((U + kPairKS - 1) / kPairKS + 31) / 32 * 32);
-    a.ks = kPairKS;
-    if (nt > kMaxThreads) {
-        nt = kMaxThreads;
-        a.ks = (U + nt - 1) / nt;
-    }
-    size_t smem = FWD ? alpha_smem(false, MAXD, nd, nt * a.ks) : beta_smem(false, MAXD, nd, nt * a.ks);
+    size_t smem = FWD ? alpha_smem(false, MAXD, nd, upos) : beta_smem(false, MAXD, nd, upos);
     const bool gm = smem > kSmemLimit;
     if (gm) {
         if (!FWD && !a.beta) return ASR_ERR_UNSUPPORTED;
         smem = 0;
     }
-    const bool fixed = a.ks == kPairKS && !gm;
-    auto k = FWD ? (gm ? lattice_alpha_kernel<RNNT, MAXD, 0, true>
-                       : fixed ? lattice_alpha_kernel<RNNT, MAXD, kPairKS, false> : lattice_alpha_kernel<RNNT, MAXD, 0, false>)
-                 : (gm ? lattice_beta_kernel<RNNT, MAXD, 0, true>
-                       : fixed ? lattice_beta_kernel<RNNT, MAXD, kPairKS, false> : lattice_beta_kernel<RNNT, MAXD, 0, false>);
+    auto k = FWD ? (gm ? lattice_alpha_kernel<RNNT, MAXD, true> : lattice_alpha_kernel<RNNT, MAXD, false>)
+                 : (gm ? lattice_beta_kernel<RNNT, MAXD, true> : lattice_beta_kernel<RNNT, MAXD, false>);
     if (int rc = prepare(k, smem, nt)) return rc;
     KernelTimer kt(name, st);
     k<<<B, nt, smem, st>>>(a);
