@@ -7,6 +7,7 @@ modules raises, so a run can never silently compute the loss elsewhere.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 import torch
@@ -51,3 +52,34 @@ def capi() -> ctypes.CDLL:
             raise RuntimeError(f"asr_b200 C-ABI library not built: {CAPI_SO} is missing")
         _capi = ctypes.CDLL(str(CAPI_SO))
     return _capi
+
+
+# Default device-memory budget of the logit stash (see logit_stash_budget).
+DEFAULT_STASH_GIB = 32.0
+
+
+def logit_stash_budget() -> int:
+    """Bytes the transducer losses may spend on the logit stash of one forward
+    (kept until its backward): ASR_B200_LOGIT_STASH_GB (GiB; 0 turns the stash
+    off, so the backward recomputes the logits GEMM), default 32 GiB. A stash
+    needs about 2 KB per lattice node at V = 1024 in the bf16 mode (4 KB in the
+    fp32 mode); nodes past the budget are recomputed."""
+    v = os.environ.get("ASR_B200_LOGIT_STASH_GB")
+    gib = DEFAULT_STASH_GIB if v is None or v == "" else float(v)
+    return max(0, int(gib * (1 << 30)))
+
+
+def logit_stash_layout(B: int, T: int, U: int, V: int, n_dur: int, d: int, tf32: bool) -> tuple[int, int]:
+    """(nodes, bytes per node) of the logit stash the transducer losses keep for
+    a (B, T, U) batch under logit_stash_budget(): the first `nodes` compact
+    lattice nodes are stashed (0 when the shape runs no tensor-core joint)."""
+    lib = capi_ops()
+    lib.asr_logit_stash_bytes.restype = ctypes.c_size_t
+    full = int(lib.asr_logit_stash_bytes(B, T, U, V, n_dur, d, 1 if tf32 else 0))
+    if full <= 512:
+        return 0, 0
+    per = (full - 512) // ((B * T * U + 255) // 256 * 256)
+    size = min(full, logit_stash_budget())
+    if size <= 512:
+        return 0, per
+    return (size - 512) // per // 256 * 256, per

@@ -187,6 +187,14 @@ bool use_tc_bwd(int tf32, JointArgs& a) {
     return false;
 }
 
+// The logit stash of a (forward, backward) pair: used when both directions run
+// the tensor-core joint (the stash layout follows its geometry); empty otherwise.
+LogitStash stash_view(int tf32, const JointArgs& a, const void* stash, size_t stash_bytes) {
+    JointArgs c = a;
+    if (!stash || !use_tc_bwd(tf32, c)) return LogitStash{nullptr, nullptr, 0};
+    return tc_stash_carve(c, const_cast<void*>(stash), stash_bytes);
+}
+
 }  // namespace
 
 extern "C" const char* asr_status_string(int status) {
@@ -245,7 +253,8 @@ size_t rnnt_workspace_impl(int B, int T, int U, int V, int d, int tf32, int back
 int rnnt_forward_impl(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
                       const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens, int B, int T, int U,
                       int V, int d, int S, int blank_idx, int tf32, float* loss, double* alpha, float* log_P_blank,
-                      float* log_P_y, float* log_prob, void* workspace, size_t workspace_bytes, asr_stream_t stream) {
+                      float* log_P_y, float* log_prob, void* workspace, size_t workspace_bytes, asr_stream_t stream,
+                      void* stash = nullptr, size_t stash_bytes = 0) {
     if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || check_act_dtype(act_dtype))
         return ASR_ERR_INVALID_ARGUMENT;
     if (B == 0) return ASR_OK;
@@ -266,7 +275,8 @@ int rnnt_forward_impl(const void* encoder, const void* decoder, int act_dtype, c
     rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
     if (rc) return rc;
     JointFwdOut o{log_P_blank, log_P_blank + cap, log_P_y, nullptr};
-    rc = tc ? tc_joint_forward(a, o, (int)cap, w.joint, w.joint_bytes, st) : simt_joint_forward(a, o, st);
+    rc = tc ? tc_joint_forward(a, o, (int)cap, w.joint, w.joint_bytes, st, stash_view(tf32, a, stash, stash_bytes))
+            : simt_joint_forward(a, o, st);
     if (rc) return rc;
     return launch_rnnt_alpha(w.meta, B, U, log_P_blank, log_P_y, alpha, log_prob, loss, st);
 }
@@ -276,7 +286,8 @@ int rnnt_backward_impl(const void* encoder, const void* decoder, int act_dtype, 
                        int V, int d, int S, int blank_idx, const double* alpha, const float* log_P_blank,
                        const float* log_P_y, const float* log_prob, const float* grad_loss, int tf32,
                        void* grad_encoder, void* grad_decoder, float* grad_joint_W, void* workspace,
-                       size_t workspace_bytes, asr_stream_t stream) {
+                       size_t workspace_bytes, asr_stream_t stream, const void* stash = nullptr,
+                       size_t stash_bytes = 0) {
     if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || check_act_dtype(act_dtype))
         return ASR_ERR_INVALID_ARGUMENT;
     if (!grad_joint_W) return ASR_ERR_INVALID_ARGUMENT;
@@ -308,7 +319,7 @@ int rnnt_backward_impl(const void* encoder, const void* decoder, int act_dtype, 
     ASR_CUDA_TRY(cudaMemsetAsync(grad_joint_W, 0, sizeof(float) * (size_t)V * d, st));
     JointBwdIn in{log_P_blank + cap, w.cb, w.ct, nullptr};
     JointBwdOut o{ge, gd, grad_joint_W, nullptr};
-    rc = tc ? tc_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st)
+    rc = tc ? tc_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st, stash_view(tf32, a, stash, stash_bytes))
             : simt_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st);
     if (rc) return rc;
     return finish_act_grads(a, w, grad_encoder, grad_decoder, st);
@@ -391,7 +402,7 @@ int tdt_forward_impl(const void* encoder, const void* decoder, int act_dtype, co
                      const int32_t* durations, int n_dur, int max_duration, int has_zero, int B, int T, int U, int V,
                      int d, int S, int blank_idx, float sigma, int tf32, float* loss, double* alpha,
                      float* log_P_blank, float* log_P_y, float* log_P_dur, float* log_prob, void* workspace,
-                     size_t workspace_bytes, asr_stream_t stream) {
+                     size_t workspace_bytes, asr_stream_t stream, void* stash = nullptr, size_t stash_bytes = 0) {
     if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || bad_tdt(n_dur, max_duration) ||
         check_act_dtype(act_dtype))
         return ASR_ERR_INVALID_ARGUMENT;
@@ -413,7 +424,8 @@ int tdt_forward_impl(const void* encoder, const void* decoder, int act_dtype, co
     rc = launch_lattice_prep(in_lens, tgt_lens, B, T, U, S, w.meta, st);
     if (rc) return rc;
     JointFwdOut o{log_P_blank, log_P_blank + cap, log_P_y, log_P_dur};
-    rc = tc ? tc_joint_forward(a, o, (int)cap, w.joint, w.joint_bytes, st) : simt_joint_forward(a, o, st);
+    rc = tc ? tc_joint_forward(a, o, (int)cap, w.joint, w.joint_bytes, st, stash_view(tf32, a, stash, stash_bytes))
+            : simt_joint_forward(a, o, st);
     if (rc) return rc;
     return launch_tdt_alpha(w.meta, B, U, max_duration, durations, n_dur, has_zero, log_P_blank, log_P_y, log_P_dur,
                             alpha, log_prob, loss, st);
@@ -425,7 +437,8 @@ int tdt_backward_impl(const void* encoder, const void* decoder, int act_dtype, c
                       int B, int T, int U, int V, int d, int S, int blank_idx, const double* alpha,
                       const float* log_P_blank, const float* log_P_y, const float* log_P_dur, const float* log_prob,
                       const float* grad_loss, int tf32, void* grad_encoder, void* grad_decoder, float* grad_joint_W,
-                      float* grad_joint_W_dur, void* workspace, size_t workspace_bytes, asr_stream_t stream) {
+                      float* grad_joint_W_dur, void* workspace, size_t workspace_bytes, asr_stream_t stream,
+                      const void* stash = nullptr, size_t stash_bytes = 0) {
     if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || bad_tdt(n_dur, max_duration) ||
         check_act_dtype(act_dtype))
         return ASR_ERR_INVALID_ARGUMENT;
@@ -462,7 +475,7 @@ int tdt_backward_impl(const void* encoder, const void* decoder, int act_dtype, c
     ASR_CUDA_TRY(cudaMemsetAsync(grad_joint_W_dur, 0, sizeof(float) * (size_t)n_dur * d, st));
     JointBwdIn in{log_P_blank + cap, w.cb, w.ct, w.gdur};
     JointBwdOut o{ge, gd, grad_joint_W, grad_joint_W_dur};
-    rc = tc ? tc_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st)
+    rc = tc ? tc_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st, stash_view(tf32, a, stash, stash_bytes))
             : simt_joint_backward(a, in, o, (int)cap, w.joint, w.joint_bytes, st);
     if (rc) return rc;
     return finish_act_grads(a, w, grad_encoder, grad_decoder, st);
@@ -546,4 +559,68 @@ extern "C" int asr_workspace_status(const void* workspace, int B, int* clamped, 
     ASR_CUDA_TRY(cudaStreamSynchronize(st));
     *clamped = v;
     return ASR_OK;
+}
+
+// ------------------------------------------------------------------ logit stash
+
+extern "C" size_t asr_logit_stash_bytes(int B, int T, int U, int V, int n_dur, int d, int tf32) {
+    if (bad_dims(B, T, U, V, d) || n_dur < 0 || B == 0) return 0;
+    JointArgs a = make_args(nullptr, nullptr, nullptr, nullptr, nullptr, B, T, U, V, n_dur, d, U - 1, 0, 0.f);
+    if (!use_tc_bwd(tf32, a)) return 0;
+    const int64_t nodes = (node_capacity(B, T, U) + 255) / 256 * 256;
+    return (size_t)nodes * tc_stash_bytes_per_node(a) + 512;
+}
+
+extern "C" int asr_rnnt_forward_stash(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                                      const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens, int B,
+                                      int T, int U, int V, int d, int S, int blank_idx, int tf32, float* loss,
+                                      double* alpha, float* log_P_blank, float* log_P_y, float* log_prob,
+                                      void* stash, size_t stash_bytes, void* workspace, size_t workspace_bytes,
+                                      asr_stream_t stream) {
+    return rnnt_forward_impl(encoder, decoder, act_dtype, joint_W, targets, in_lens, tgt_lens, B, T, U, V, d, S,
+                             blank_idx, tf32, loss, alpha, log_P_blank, log_P_y, log_prob, workspace,
+                             workspace_bytes, stream, stash, stash_bytes);
+}
+
+extern "C" int asr_rnnt_backward_stash(const void* encoder, const void* decoder, int act_dtype,
+                                       const float* joint_W, const int32_t* targets, const int32_t* in_lens,
+                                       const int32_t* tgt_lens, int B, int T, int U, int V, int d, int S,
+                                       int blank_idx, const double* alpha, const float* log_P_blank,
+                                       const float* log_P_y, const float* log_prob, const float* grad_loss, int tf32,
+                                       void* grad_encoder, void* grad_decoder, float* grad_joint_W,
+                                       const void* stash, size_t stash_bytes, void* workspace,
+                                       size_t workspace_bytes, asr_stream_t stream) {
+    return rnnt_backward_impl(encoder, decoder, act_dtype, joint_W, targets, in_lens, tgt_lens, B, T, U, V, d, S,
+                              blank_idx, alpha, log_P_blank, log_P_y, log_prob, grad_loss, tf32, grad_encoder,
+                              grad_decoder, grad_joint_W, workspace, workspace_bytes, stream, stash, stash_bytes);
+}
+
+extern "C" int asr_tdt_forward_stash(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                                     const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                                     const int32_t* tgt_lens, const int32_t* durations, int n_dur, int max_duration,
+                                     int has_zero, int B, int T, int U, int V, int d, int S, int blank_idx,
+                                     float sigma, int tf32, float* loss, double* alpha, float* log_P_blank,
+                                     float* log_P_y, float* log_P_dur, float* log_prob, void* stash,
+                                     size_t stash_bytes, void* workspace, size_t workspace_bytes,
+                                     asr_stream_t stream) {
+    return tdt_forward_impl(encoder, decoder, act_dtype, joint_W, joint_W_dur, targets, in_lens, tgt_lens, durations,
+                            n_dur, max_duration, has_zero, B, T, U, V, d, S, blank_idx, sigma, tf32, loss, alpha,
+                            log_P_blank, log_P_y, log_P_dur, log_prob, workspace, workspace_bytes, stream, stash,
+                            stash_bytes);
+}
+
+extern "C" int asr_tdt_backward_stash(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                                      const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                                      const int32_t* tgt_lens, const int32_t* durations, int n_dur,
+                                      int max_duration, int has_zero, int B, int T, int U, int V, int d, int S,
+                                      int blank_idx, const double* alpha, const float* log_P_blank,
+                                      const float* log_P_y, const float* log_P_dur, const float* log_prob,
+                                      const float* grad_loss, int tf32, void* grad_encoder, void* grad_decoder,
+                                      float* grad_joint_W, float* grad_joint_W_dur, const void* stash,
+                                      size_t stash_bytes, void* workspace, size_t workspace_bytes,
+                                      asr_stream_t stream) {
+    return tdt_backward_impl(encoder, decoder, act_dtype, joint_W, joint_W_dur, targets, in_lens, tgt_lens, durations,
+                             n_dur, max_duration, has_zero, B, T, U, V, d, S, blank_idx, alpha, log_P_blank, log_P_y,
+                             log_P_dur, log_prob, grad_loss, tf32, grad_encoder, grad_decoder, grad_joint_W,
+                             grad_joint_W_dur, workspace, workspace_bytes, stream, stash, stash_bytes);
 }

@@ -4,7 +4,8 @@
 // The joint output is  logits[n, c] = sum_k tanh(enc[b,t,k] + dec[b,u,k]) * Wf[c, k]
 // over the compact valid nodes n = (b, t, u) and the "full" column set
 // c in [0, Vf), Vf = V + n_dur: token columns first (joint_W), then the duration
-// head (joint_W_dur). No launcher ever writes the (nodes x Vf) logits to HBM.
+// head (joint_W_dur). The fp32 logits never reach HBM; the tensor-core forward
+// can keep a reduced-width copy for the backward (LogitStash).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -67,6 +68,26 @@ struct JointBwdOut {
     float* dbias;  // (V,), accumulated: CTC head mode with a bias, else nullptr
 };
 
+// Logit stash (tensor-core path): the forward keeps the logits of the first
+// `nodes` compact lattice nodes, and the backward forms their rows of
+// d loss / d logits in one streaming pass over the stash instead of recomputing
+// the logits GEMM; nodes past the stash are recomputed as before. Row n holds
+// x[n, c] = logit[n, c] - ref[n, j] for its vpad columns, ref[n, j] the row's
+// largest token logit within vocabulary chunk j (so the entries that carry the
+// softmax mass sit near 0): fp16 in the bf16 mode, fp32 in the split fp32 mode.
+// Its meta row holds ref[n, 0 .. nchunks), the log-partition lse[n] and the
+// label (int bits, -1 without a label edge): what the backward needs of the
+// node besides its edge posteriors, in one contiguous run.
+struct LogitStash {
+    void* data;   // (nodes, vpad) fp16 or fp32
+    float* meta;  // (nodes, nchunks + 2)
+    int nodes;    // a multiple of 256 (whole tiles of every kernel); 0 = no stash
+};
+// Bytes of one stashed node; the stash of `bytes` holds
+// floor((bytes - 512) / per node) nodes, rounded down to a multiple of 256.
+size_t tc_stash_bytes_per_node(const JointArgs& a);
+LogitStash tc_stash_carve(const JointArgs& a, void* stash, size_t bytes);
+
 // ---- fp32 SIMT path -----------------------------------------------------------
 int simt_joint_forward(const JointArgs& a, const JointFwdOut& o, cudaStream_t st);
 // Backward over node chunks [c0, c0 + chunk); G is a (chunk, Vf) fp32 scratch.
@@ -78,10 +99,10 @@ int simt_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwd
 bool tc_supported(const JointArgs& a);
 size_t tc_forward_scratch_bytes(const JointArgs& a, int node_capacity);
 int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity, void* scratch, size_t scratch_bytes,
-                     cudaStream_t st);
+                     cudaStream_t st, const LogitStash& stash = LogitStash{});
 bool tc_backward_supported(const JointArgs& a);
 size_t tc_backward_scratch_bytes(const JointArgs& a, int node_capacity);
 int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOut& o, int node_capacity,
-                      void* scratch, size_t scratch_bytes, cudaStream_t st);
+                      void* scratch, size_t scratch_bytes, cudaStream_t st, const LogitStash& stash = LogitStash{});
 
 }  // namespace asr

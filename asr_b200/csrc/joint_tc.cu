@@ -25,6 +25,7 @@
 // Every mbarrier wait is bounded; a timeout sets the kernel's error word and the
 // CTA drains its own TMA and MMA work, frees its TMEM and returns.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -173,13 +174,19 @@ struct TcParams {
     JointBwdIn bwd;   // backward inputs
     __nv_bfloat16* G;  // backward: (pass nodes, vpad) d loss / d logits
     PassRange range;   // node pass
+    LogitStash stash;  // forward: written for nodes below stash.nodes; backward: those nodes are skipped
     int* err;
 };
 
-__device__ __forceinline__ void node_range(const TcParams& P, bool, int& begin, int& end) {
+// Nodes [begin, end) of this launch within the pass that starts at `base` (the
+// row origin of the pass's H and G buffers). The backward leaves the stashed
+// nodes below stash.nodes to the stash kernel; base and stash.nodes are
+// multiples of 256, so its tiles start on whole tiles of the pass.
+__device__ __forceinline__ void node_range(const TcParams& P, bool bwd, int& base, int& begin, int& end) {
     const int N = total_nodes(P.a.m, P.a.B);
-    begin = min(P.range.bounds[P.range.pass], N);
+    base = min(P.range.bounds[P.range.pass], N);
     end = min(P.range.bounds[P.range.pass + 1], N);
+    begin = bwd ? min(end, max(base, P.stash.nodes)) : base;
 }
 
 // B ring geometry per CTA: a pair splits each 256-column chunk, so every CTA
@@ -189,11 +196,12 @@ __host__ __device__ constexpr int b_stage_bytes() { return kNC / kCta * kBK * 2;
 template <int kCta>
 __host__ __device__ constexpr int b_stages() { return kStages * kCta; }
 
-template <bool kBwd, int kCta, bool kStream>
+template <bool kBwd, int kCta, bool kStream, bool kStash = false>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_joint_kernel(const __grid_constant__ CUtensorMap map_full, const __grid_constant__ CUtensorMap map_tail,
                     const __grid_constant__ CUtensorMap map_h, TcParams P) {
     static_assert(!kStream || kCta == 1, "the streamed-A variant runs single CTAs");
+    static_assert(!kStash || (!kBwd && kCta == 1), "the forward of single CTAs writes the logit stash");
     extern __shared__ uint8_t smem_raw[];
     const Geom g = P.g;
     const int SB = kStream ? g.sstage : b_stage_bytes<kCta>();
@@ -207,8 +215,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tile 2p + rank in CTA `rank` (kCta = 2)
     const int unit0 = blockIdx.x / kCta, units_stride = gridDim.x / kCta;
 
-    int begin, end;
-    node_range(P, kBwd, begin, end);
+    int base, begin, end;
+    node_range(P, kBwd, base, begin, end);
+    const int row_off = begin - base;  // pass-relative H / G row of this launch's first node
     const int ntiles = end > begin ? (end - begin + kBM - 1) / kBM : 0;
     const int nunits = (ntiles + kCta - 1) / kCta;
 
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const CUtensorMap* map = width == g.cw ? &map_full : &map_tail;
                         if (kStream) {  // hidden chunk (tile rows x 64) then weight chunk
                             mbar_arrive_expect_tx(&sm.b_full[stage], kAChunkBytes + (uint32_t)width * kBK * 2);
-                            tma_load_2d(dst, &map_h, ks * kAK, unit * kBM, &sm.b_full[stage]);
+                            tma_load_2d(dst, &map_h, ks * kAK, row_off + unit * kBM, &sm.b_full[stage]);
                             tma_load_2d(dst + kAChunkBytes, map, ks * kBK, col, &sm.b_full[stage]);
                         } else if (kCta == 2) {
                             if (leader) mbar_arrive_expect_tx(&sm.b_full[stage], (uint32_t)width * kBK * 2);
@@ -378,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int k = 0; k < kMaxKChunks; ++k) issued[k] = false, ipar[k] = 0;
             for (int unit = unit0; ok && unit < nunits; unit += units_stride, ++it) {
-                const int row0 = (unit * kCta + (int)rank) * kBM;  // pass-relative H row
+                const int row0 = row_off + (unit * kCta + (int)rank) * kBM;  // pass-relative H row
                 for (int kc = 0; kc < g.kchunks; ++kc) {
                     if (it > 0 && !mbar_wait_cluster(&sm.a_empty[kc], (it - 1) & 1, err, 7)) {
                         ok = false;
@@ -447,6 +456,109 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + ((uint32_t)lane_base << 16) + buf * kNC;
+                if constexpr (kStash) {
+                    // Two sweeps of the chunk: its largest token logit mc, then the
+                    // exp-sum relative to mc, the blank / label / duration gathers and
+                    // the stash row x = logit - mc (nodes below stash.nodes).
+                    const bool keep = valid && n < P.stash.nodes;
+                    const int ng = width / 16;
+                    float mc = -INFINITY;
+                    for (int gi = 0; gi < ng; gi += 2) {
+                        const int c0 = col + gi * 16;
+                        if (gi + 1 < ng) {
+                            float v[32];
+                            tmem_ld32(taddr + gi * 16, v);
+                            if (c0 + 32 <= a.V) {
+#pragma unroll
+                                for (int s2 = 1; s2 < 32; s2 *= 2)
+#pragma unroll
+                                    for (int i = 0; i + s2 < 32; i += 2 * s2) v[i] = fmaxf(v[i], v[i + s2]);
+                                mc = fmaxf(mc, v[0]);
+                            } else {
+#pragma unroll
+                                for (int i = 0; i < 32; ++i)
+                                    if (c0 + i < a.V) mc = fmaxf(mc, v[i]);
+                            }
+                        } else {
+                            float v[16];
+                            tmem_ld16(taddr + gi * 16, v);
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                if (c0 + i < a.V) mc = fmaxf(mc, v[i]);
+                        }
+                    }
+                    float sc = 0.f;
+                    for (int gi = 0; gi < ng; ++gi) {
+                        const int c0 = col + gi * 16;
+                        float v[16], x[16];
+                        tmem_ld16(taddr + gi * 16, v);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) x[i] = v[i] - mc;
+                        if (c0 + 16 <= a.V) {
+                            float e[16];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) e[i] = ex2_fast(x[i] * kLog2e);
+#pragma unroll
+                            for (int s2 = 1; s2 < 16; s2 *= 2)
+#pragma unroll
+                                for (int i = 0; i + s2 < 16; i += 2 * s2) e[i] += e[i + s2];
+                            sc += e[0];
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                if (c0 + i == a.blank) lb = v[i];
+                                if (c0 + i == y) ly = v[i];
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const int c = c0 + i;
+                                if (c < a.V) {
+                                    sc += ex2_fast(x[i] * kLog2e);
+                                    if (c == a.blank) lb = v[i];
+                                    if (c == y) ly = v[i];
+                                } else if (c < Vf) {
+#pragma unroll
+                                    for (int k = 0; k < kMaxDurCols; ++k)
+                                        if (c - a.V == k) dur[k] = v[i];
+                                }
+                            }
+                        }
+                        if (keep) {
+                            const int64_t e0 = (int64_t)n * g.vpad + c0;
+                            if (g.parts == 1) {
+                                uint4 w0, w1;
+                                w0.x = pack_f16(x[0], x[1]);
+                                w0.y = pack_f16(x[2], x[3]);
+                                w0.z = pack_f16(x[4], x[5]);
+                                w0.w = pack_f16(x[6], x[7]);
+                                w1.x = pack_f16(x[8], x[9]);
+                                w1.y = pack_f16(x[10], x[11]);
+                                w1.z = pack_f16(x[12], x[13]);
+                                w1.w = pack_f16(x[14], x[15]);
+                                st_global_32B(static_cast<__half*>(P.stash.data) + e0, w0, w1);
+                            } else {
+                                float* dst = static_cast<float*>(P.stash.data) + e0;
+#pragma unroll
+                                for (int h = 0; h < 2; ++h) {
+                                    const uint4 lo = make_uint4(__float_as_uint(x[8 * h]), __float_as_uint(x[8 * h + 1]),
+                                                                __float_as_uint(x[8 * h + 2]),
+                                                                __float_as_uint(x[8 * h + 3]));
+                                    const uint4 hi = make_uint4(
+                                        __float_as_uint(x[8 * h + 4]), __float_as_uint(x[8 * h + 5]),
+                                        __float_as_uint(x[8 * h + 6]), __float_as_uint(x[8 * h + 7]));
+                                    st_global_32B(dst + 8 * h, lo, hi);
+                                }
+                            }
+                        }
+                    }
+                    if (mc > m) {
+                        s = s * __expf(m - mc) + sc;
+                        m = mc;
+                    } else if (mc > -INFINITY) {
+                        s += sc * __expf(mc - m);
+                    }
+                    if (keep) P.stash.meta[(int64_t)n * (g.nchunks + 2) + j] = mc;
+                } else
                 for (int gi = 0; gi < width / 16; ++gi) {
                     if (!kBwd && gi + 1 < width / 16 && col + gi * 16 + 32 <= a.V) {
                         // two token groups at once: one TMEM wait, and the max and the
@@ -559,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint4 w0, w1;
                         // one 32-byte store (a whole sector): rows are gw * 2 bytes, a multiple
                         // of 32, and groups start on 16-column boundaries
-                        __nv_bfloat16* grow = P.G + (int64_t)(n - begin) * g.gw + c0;
+                        __nv_bfloat16* grow = P.G + (int64_t)(n - base) * g.gw + c0;
                         if (g.parts == 1) {
                             pack16(gv, w0, w1);
                             st_global_32B(grow, w0, w1);
@@ -591,6 +703,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!kBwd && ok && valid) {
                 const float l = m + __logf(s);
                 P.fwd.lse[n] = l;
+                if (kStash && n < P.stash.nodes) {
+                    float* meta = P.stash.meta + (int64_t)n * (g.nchunks + 2) + g.nchunks;
+                    meta[0] = l;
+                    meta[1] = __int_as_float(y);
+                }
                 P.fwd.lpb[dn] = lb - l - a.sigma;
                 P.fwd.lpy[dn] = y >= 0 ? ly - l - a.sigma : kNeg;
                 if (a.n_dur > 0) {
@@ -1214,23 +1331,23 @@ bool joint_weight_maps(const Geom& g, const __nv_bfloat16* Wf, bool pairs, CUten
 }
 
 // Persistent launch over `tiles` 128-node tiles (at most one CTA per SM).
-template <bool kBwd>
+template <bool kBwd, bool kStash = false>
 int launch_joint(bool pairs, int64_t tiles, size_t smem, const CUtensorMap& mfull, const CUtensorMap& mtail,
                  const CUtensorMap& mh, const TcParams& P, cudaStream_t st) {
     const int sms = sm_count();
     const int grid1 = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sms));
     if (joint_stream(P.g)) {  // streamed hidden tiles
         const size_t smem_s = smem_bytes_for(P.g.kchunks, true, P.g.sstage, P.g.nstream);
-        ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem_s));
-        tc_joint_kernel<kBwd, 1, true><<<grid1, kThreads, smem_s, st>>>(mfull, mtail, mh, P);
+        auto kern = tc_joint_kernel<kBwd, 1, true, kStash>;
+        ASR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s));
+        kern<<<grid1, kThreads, smem_s, st>>>(mfull, mtail, mh, P);
         ASR_LAUNCH_CHECK();
         return ASR_OK;
     }
-    if (!pairs) {
-        ASR_CUDA_TRY(cudaFuncSetAttribute(tc_joint_kernel<kBwd, 1, false>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        tc_joint_kernel<kBwd, 1, false><<<grid1, kThreads, smem, st>>>(mfull, mtail, mh, P);
+    if (!pairs || kStash) {
+        auto kern = tc_joint_kernel<kBwd, 1, false, kStash>;
+        ASR_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        kern<<<grid1, kThreads, smem, st>>>(mfull, mtail, mh, P);
         ASR_LAUNCH_CHECK();
         return ASR_OK;
     }
@@ -1295,8 +1412,33 @@ size_t tc_forward_scratch_bytes(const JointArgs& a, int node_capacity) {
     return fwd_layout(a, node_capacity).total + 256;
 }
 
+// Stashed node counts are whole 256-node tiles of the d_hidden kernel, so the
+// recompute kernel's tiles after the stash start on a tile of the pass.
+constexpr int kStashAlign = 256;
+constexpr int kStashMaxChunks = 16;  // vocabulary chunks of a stashed row (vpad <= 16 x 256)
+
+size_t tc_stash_bytes_per_node(const JointArgs& a) {
+    const Geom g = make_geom(a);
+    return (size_t)g.vpad * (g.parts == 1 ? sizeof(__half) : sizeof(float)) + sizeof(float) * (g.nchunks + 2);
+}
+
+LogitStash tc_stash_carve(const JointArgs& a, void* stash, size_t bytes) {
+    LogitStash s{nullptr, nullptr, 0};
+    const size_t per = tc_stash_bytes_per_node(a);
+    if (!stash || bytes <= 512 || make_geom(a).nchunks > kStashMaxChunks) return s;
+    const int64_t nodes = std::min<int64_t>((int64_t)((bytes - 512) / per) / kStashAlign * kStashAlign, INT32_MAX / 2);
+    if (nodes <= 0) return s;
+    const Geom g = make_geom(a);
+    char* p = reinterpret_cast<char*>(al256(reinterpret_cast<uintptr_t>(stash)));
+    s.data = p;
+    p += al256((size_t)nodes * g.vpad * (g.parts == 1 ? sizeof(__half) : sizeof(float)));
+    s.meta = reinterpret_cast<float*>(p);
+    s.nodes = (int)nodes;
+    return s;
+}
+
 int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity, void* scratch, size_t scratch_bytes,
-                     cudaStream_t st) {
+                     cudaStream_t st, const LogitStash& stash) {
     const Geom g = make_geom(a);
     const FwdLayout L = fwd_layout(a, node_capacity);
     if (scratch_bytes < L.total) return ASR_ERR_WORKSPACE;
@@ -1314,7 +1456,9 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
         plan_passes_kernel<<<(L.pp.passes + 1 + 127) / 128, 128, 0, st>>>(a.m, a.B, L.pp.passes, L.pp.step, bounds);
         ASR_LAUNCH_CHECK();
     }
-    const bool pairs = joint_pairs() && !joint_stream(g);  // pairs use the resident hidden tile
+    const bool use_stash = stash.nodes > 0 && !a.head;
+    // pairs use the resident hidden tile; the stash-writing forward runs single CTAs
+    const bool pairs = joint_pairs() && !joint_stream(g) && !use_stash;
     CUtensorMap mfull, mtail, mh;
     if (!joint_weight_maps(g, Wf, pairs, &mfull, &mtail)) return ASR_ERR_CUDA;
     if (!make_map(&mh, H, (int)L.pp.step, g.kpad, kAK, kBM, CU_TENSOR_MAP_SWIZZLE_128B)) return ASR_ERR_CUDA;
@@ -1324,17 +1468,186 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
     P.g = g;
     P.fwd = o;
     P.range.bounds = bounds;
+    if (use_stash) P.stash = stash;
     P.err = err;
     for (int p = 0; p < L.pp.passes; ++p) {
         P.range.pass = p;
         int rc = launch_hidden(a, g, bounds, p, H, st);
         if (rc != ASR_OK) return rc;
         KernelTimer kt("joint_fwd_tc", st);
-        rc = launch_joint<false>(pairs, L.pp.step / kBM, smem_bytes_for(g.kchunks), mfull, mtail, mh, P, st);
+        rc = use_stash
+                 ? launch_joint<false, true>(pairs, L.pp.step / kBM, smem_bytes_for(g.kchunks), mfull, mtail, mh, P, st)
+                 : launch_joint<false>(pairs, L.pp.step / kBM, smem_bytes_for(g.kchunks), mfull, mtail, mh, P, st);
         if (rc != ASR_OK) return rc;
     }
     return ASR_OK;
 }
+
+// ------------------------------------------------------ dlogits from the stash
+//
+// G rows of the stashed nodes of a pass, [base, min(end, stash.nodes)):
+//   G[n, c] = exp(x[n, c] + ref[n, j] - lse[n]) * (cb + ct) - cb [c = blank] - ct [c = label]
+// for token columns (x the stashed logit - ref, j = c / cw), the duration-logit
+// gradients for the duration columns, zero for the padding; the split fp32 mode
+// stores the parts [hi | hi | lo]. A CTA takes tiles of kStashRows consecutive
+// rows: their meta rows, posteriors and duration gradients (contiguous runs)
+// go to shared memory first, then the tile's (row, 8-column group) items are
+// walked flat with kBatch stash loads in flight per thread before the first G
+// store, so every warp access covers 512 contiguous bytes and any vocabulary
+// size keeps all lanes busy. Bound by HBM: the stash row read (2 B per column,
+// 4 in the split mode) and the G row written. When the stash covers the rest of
+// the pass, rows up to the next 128-row boundary are zeroed, as the recompute
+// kernel's last tile does: the dW kernel reads whole 64-row blocks.
+
+namespace {
+
+struct StashParams {
+    JointArgs a;
+    Geom g;
+    const int32_t* bounds;
+    int pass;
+    LogitStash stash;
+    JointBwdIn in;
+    __nv_bfloat16* G;
+    uint32_t groups;       // 8-column groups of a row (vpad / 8)
+    uint32_t magic_row;    // ceil(2^32 / groups): item / groups = umulhi(item, magic_row)
+    uint32_t magic_chunk;  // ceil(2^32 / (cw / 8)): group -> vocabulary chunk
+};
+
+constexpr int kStashRows = 128;  // rows per CTA tile
+constexpr int kStashThreads = 256;
+
+template <int PARTS>
+__global__ void __launch_bounds__(kStashThreads, 4) stash_dlogits_kernel(StashParams P) {
+    constexpr int kBatch = PARTS == 1 ? 8 : 4;  // items whose stash loads are in flight together
+    __shared__ float s_e[kStashRows * kStashMaxChunks];  // ref * log2(e) - lse * log2(e) per (row, chunk)
+    __shared__ float s_cb[kStashRows], s_ct[kStashRows], s_pn[kStashRows];
+    __shared__ int s_y[kStashRows];
+    __shared__ float s_gd[kStashRows * kMaxDurCols];
+    const JointArgs& a = P.a;
+    const Geom& g = P.g;
+    const int N = total_nodes(a.m, a.B);
+    const int base = min(P.bounds[P.pass], N), end = min(P.bounds[P.pass + 1], N);
+    const int split = min(end, max(base, P.stash.nodes));
+    const int rows = split - base;
+    const int zrows = (split == end ? (end - base + 127) / 128 * 128 : rows) - rows;
+    const int nch = g.nchunks, mw = nch + 2, Vf = a.V + a.n_dur;
+    const int ntiles = (rows + kStashRows - 1) / kStashRows;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int r0 = tile * kStashRows;
+        const int R = min(kStashRows, rows - r0);
+        const int64_t row0 = (int64_t)(base + r0);  // global node of the tile's first row
+        __syncthreads();  // the previous tile's coefficients are no longer read
+        if (threadIdx.x < R) {
+            const int64_t n = row0 + threadIdx.x;
+            const float* meta = P.stash.meta + n * mw;
+            const float l2 = __ldg(meta + nch) * kLog2e;
+            for (int j = 0; j < nch; ++j) s_e[threadIdx.x * kStashMaxChunks + j] = fmaf(__ldg(meta + j), kLog2e, -l2);
+            s_y[threadIdx.x] = __float_as_int(__ldg(meta + nch + 1));
+            const float cb = __ldg(P.in.cb + n), ct = __ldg(P.in.ct + n);
+            s_cb[threadIdx.x] = cb;
+            s_ct[threadIdx.x] = ct;
+            s_pn[threadIdx.x] = cb + ct;
+        }
+        for (int i = threadIdx.x; i < R * a.n_dur; i += kStashThreads)
+            s_gd[(i / a.n_dur) * kMaxDurCols + i % a.n_dur] = __ldg(P.in.gdur + row0 * a.n_dur + i);
+        __syncthreads();
+        const uint32_t items = (uint32_t)R * P.groups;
+        for (uint32_t f0 = threadIdx.x; f0 < items; f0 += kStashThreads * kBatch) {
+            uint4 raw[kBatch][PARTS == 1 ? 1 : 2];
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const uint32_t f = f0 + (uint32_t)(k * kStashThreads);
+                if (f < items) {
+                    const uint32_t r = __umulhi(f, P.magic_row), q = f - r * P.groups;
+                    const int64_t e0 = (row0 + r) * g.vpad + q * 8;
+                    if (PARTS == 1) {
+                        raw[k][0] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __half*>(P.stash.data) + e0));
+                    } else {
+                        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const float*>(P.stash.data) + e0);
+                        raw[k][0] = __ldcs(src);
+                        raw[k][1] = __ldcs(src + 1);
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const uint32_t f = f0 + (uint32_t)(k * kStashThreads);
+                if (f >= items) break;
+                const uint32_t r = __umulhi(f, P.magic_row), q = f - r * P.groups;
+                const int c0 = (int)q * 8;
+                float x[8];
+                if (PARTS == 1) {
+                    const uint32_t ws[4] = {raw[k][0].x, raw[k][0].y, raw[k][0].z, raw[k][0].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 h2 = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
+                        x[2 * i] = h2.x;
+                        x[2 * i + 1] = h2.y;
+                    }
+                } else {
+                    x[0] = __uint_as_float(raw[k][0].x), x[1] = __uint_as_float(raw[k][0].y);
+                    x[2] = __uint_as_float(raw[k][0].z), x[3] = __uint_as_float(raw[k][0].w);
+                    x[4] = __uint_as_float(raw[k][1].x), x[5] = __uint_as_float(raw[k][1].y);
+                    x[6] = __uint_as_float(raw[k][1].z), x[7] = __uint_as_float(raw[k][1].w);
+                }
+                const float e = s_e[r * kStashMaxChunks + __umulhi(q, P.magic_chunk)];
+                const float pn = s_pn[r], cb = s_cb[r], ct = s_ct[r];
+                const int y = s_y[r];
+                float gv[8];
+                if (c0 + 8 <= a.V) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        float v = ex2_fast(fmaf(x[i], kLog2e, e)) * pn;
+                        v = (c0 + i == a.blank) ? v - cb : v;
+                        gv[i] = (c0 + i == y) ? v - ct : v;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int cc = c0 + i;
+                        float v = 0.f;
+                        if (cc < a.V) {
+                            v = ex2_fast(fmaf(x[i], kLog2e, e)) * pn;
+                            if (cc == a.blank) v -= cb;
+                            if (cc == y) v -= ct;
+                        } else if (cc < Vf) {
+                            v = s_gd[r * kMaxDurCols + (cc - a.V)];
+                        }
+                        gv[i] = v;
+                    }
+                }
+                __nv_bfloat16* grow = P.G + (int64_t)(r0 + r) * g.gw + c0;
+                if (PARTS == 1) {
+                    *reinterpret_cast<uint4*>(grow) = make_uint4(pack_bf16(gv[0], gv[1]), pack_bf16(gv[2], gv[3]),
+                                                                 pack_bf16(gv[4], gv[5]), pack_bf16(gv[6], gv[7]));
+                } else {  // split fp32: [hi | hi | lo]
+                    float lo[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float h = __bfloat162float(__float2bfloat16_rn(gv[i]));
+                        lo[i] = gv[i] - h;
+                        gv[i] = h;
+                    }
+                    const uint4 wh = make_uint4(pack_bf16(gv[0], gv[1]), pack_bf16(gv[2], gv[3]),
+                                                pack_bf16(gv[4], gv[5]), pack_bf16(gv[6], gv[7]));
+                    *reinterpret_cast<uint4*>(grow) = wh;
+                    *reinterpret_cast<uint4*>(grow + g.vpad) = wh;
+                    *reinterpret_cast<uint4*>(grow + 2 * g.vpad) =
+                        make_uint4(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]), pack_bf16(lo[4], lo[5]),
+                                   pack_bf16(lo[6], lo[7]));
+                }
+            }
+        }
+    }
+    // zero rows that pad the pass to whole 128-row tiles
+    const int zgroups = g.gw / 8;
+    for (int64_t i = (int64_t)blockIdx.x * kStashThreads + threadIdx.x; i < (int64_t)zrows * zgroups;
+         i += (int64_t)gridDim.x * kStashThreads)
+        *reinterpret_cast<uint4*>(P.G + (int64_t)(rows + i / zgroups) * g.gw + (i % zgroups) * 8) = make_uint4(0, 0, 0, 0);
+}
+
+}  // namespace
 
 // =================================================================== backward
 //
@@ -1915,7 +2228,7 @@ size_t tc_backward_scratch_bytes(const JointArgs& a, int node_capacity) {
 }
 
 int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOut& o, int node_capacity, void* scratch,
-                      size_t scratch_bytes, cudaStream_t st) {
+                      size_t scratch_bytes, cudaStream_t st, const LogitStash& stash) {
     const Geom g = make_geom(a);
     const BwdLayout L = bwd_layout(a, node_capacity);
     if (scratch_bytes < L.total) return ASR_ERR_WORKSPACE;
@@ -1960,6 +2273,21 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     TP.range.bounds = bounds;
     TP.err = err;
     const size_t smem_fw = smem_bytes_for(g.kchunks);
+    const bool use_stash = stash.nodes > 0 && !a.head;
+    if (use_stash) TP.stash = stash;
+    StashParams SP;
+    std::memset(&SP, 0, sizeof(SP));
+    SP.a = a;
+    SP.g = g;
+    SP.bounds = bounds;
+    SP.stash = TP.stash;
+    SP.in = in;
+    SP.G = G;
+    SP.groups = (uint32_t)(g.vpad / 8);
+    SP.magic_row = (uint32_t)(((1ull << 32) + SP.groups - 1) / SP.groups);
+    SP.magic_chunk = (uint32_t)(((1ull << 32) + g.cw / 8 - 1) / (g.cw / 8));
+    // every node below the capacity stashed: the recompute kernel has no work
+    const bool recompute = !use_stash || (int64_t)stash.nodes < (int64_t)node_capacity;
 
     // dH parameters: shared dec rows for the whole label range when they fit,
     // then the deepest pipeline that still fits
@@ -1998,13 +2326,24 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
 
     for (int p = 0; p < L.passes; ++p) {
         TP.range.pass = p;
+        SP.pass = p;
         DP.pass = p;
         WP.pass = p;
         {
-            KernelTimer kt("joint_dlogits_tc", st);
             int rc = launch_hidden(a, g, bounds, p, H, st);
             if (rc != ASR_OK) return rc;
-            rc = launch_joint<true>(pairs, L.step / kBM, smem_fw, mfull, mtail, m_h, TP, st);
+        }
+        if (use_stash) {
+            KernelTimer kt("joint_dlogits_stash", st);
+            if (g.parts == 1)
+                stash_dlogits_kernel<1><<<sms * 4, kStashThreads, 0, st>>>(SP);
+            else
+                stash_dlogits_kernel<3><<<sms * 4, kStashThreads, 0, st>>>(SP);
+            ASR_LAUNCH_CHECK();
+        }
+        if (recompute) {
+            KernelTimer kt("joint_dlogits_tc", st);
+            int rc = launch_joint<true>(pairs, L.step / kBM, smem_fw, mfull, mtail, m_h, TP, st);
             if (rc != ASR_OK) return rc;
         }
         {

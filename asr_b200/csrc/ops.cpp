@@ -13,6 +13,7 @@
 #include <torch/csrc/stable/ops.h>
 #include <torch/csrc/stable/tensor.h>
 
+#include <algorithm>
 #include <tuple>
 
 #include "asr_b200.h"
@@ -62,6 +63,14 @@ Tensor workspace(const Tensor& like, size_t bytes) {
 
 int dim(const Tensor& t, int i) { return (int)t.sizes()[i]; }
 
+// Logit stash of the *_stash ops: the bytes that hold every node of the
+// capacity, at most `budget`; a 1-byte placeholder (no stash) when the budget is
+// 0 or the shape does not run the tensor-core joint.
+Tensor stash_tensor(const Tensor& like, size_t full_bytes, int64_t budget) {
+    const size_t bytes = budget > 0 ? std::min(full_bytes, (size_t)budget) : 0;
+    return workspace(like, bytes > 512 ? bytes : 0);
+}
+
 int target_cols(const Tensor& targets) { return targets.dim() >= 2 ? dim(targets, 1) : 0; }
 
 // --------------------------------------------------------------------- CTC
@@ -107,10 +116,9 @@ Tensor ctc_grad(const Tensor& alpha, const Tensor& log_Z, const Tensor& log_prob
 
 // -------------------------------------------------------------------- RNN-T
 
-std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> rnnt_forward(const Tensor& encoder, const Tensor& decoder,
-                                                                const Tensor& joint_W, const Tensor& targets,
-                                                                const Tensor& in_lens, const Tensor& tgt_lens,
-                                                                int64_t blank_idx, int64_t tf32) {
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> rnnt_forward_impl(
+    const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& targets, const Tensor& in_lens,
+    const Tensor& tgt_lens, int64_t blank_idx, int64_t tf32, int64_t stash_budget) {
     const int act = act_dtype(encoder, decoder);
     ASR_CHECK_F32(joint_W);
     ASR_CHECK_I32(targets);
@@ -125,24 +133,44 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> rnnt_forward(const Tensor& en
     Tensor alpha = torch::stable::new_empty(encoder, {B, T, U}, ScalarType::Double);
     Tensor log_P_blank = torch::stable::new_empty(encoder, {2, B, T, U}, ScalarType::Float);
     Tensor log_P_y = torch::stable::new_empty(encoder, {B, T, U}, ScalarType::Float);
+    Tensor stash = stash_tensor(encoder, asr_logit_stash_bytes(B, T, U, V, 0, d, (int)tf32), stash_budget);
     const size_t wsb = asr_rnnt_workspace_bytes_ex(B, T, U, V, d, (int)tf32, 0, act);
     Tensor ws = workspace(encoder, wsb);
-    check_rc(asr_rnnt_forward_ex(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
-                              joint_W.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
-                              in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, U, V, d, S,
-                              (int)blank_idx, (int)tf32, loss.mutable_data_ptr<float>(),
-                              alpha.mutable_data_ptr<double>(), log_P_blank.mutable_data_ptr<float>(),
-                              log_P_y.mutable_data_ptr<float>(), log_prob.mutable_data_ptr<float>(),
-                              ws.mutable_data_ptr(), wsb, current_stream(encoder)),
+    check_rc(asr_rnnt_forward_stash(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
+                                    joint_W.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
+                                    in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, U, V,
+                                    d, S, (int)blank_idx, (int)tf32, loss.mutable_data_ptr<float>(),
+                                    alpha.mutable_data_ptr<double>(), log_P_blank.mutable_data_ptr<float>(),
+                                    log_P_y.mutable_data_ptr<float>(), log_prob.mutable_data_ptr<float>(),
+                                    stash.mutable_data_ptr(), (size_t)stash.numel(), ws.mutable_data_ptr(), wsb,
+                                    current_stream(encoder)),
              "asr::rnnt_forward");
+    return {loss, alpha, log_P_blank, log_P_y, log_prob, stash};
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> rnnt_forward(const Tensor& encoder, const Tensor& decoder,
+                                                                const Tensor& joint_W, const Tensor& targets,
+                                                                const Tensor& in_lens, const Tensor& tgt_lens,
+                                                                int64_t blank_idx, int64_t tf32) {
+    auto [loss, alpha, log_P_blank, log_P_y, log_prob, stash] =
+        rnnt_forward_impl(encoder, decoder, joint_W, targets, in_lens, tgt_lens, blank_idx, tf32, 0);
     return {loss, alpha, log_P_blank, log_P_y, log_prob};
 }
 
-std::tuple<Tensor, Tensor, Tensor> rnnt_backward(const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W,
-                                                 const Tensor& targets, const Tensor& in_lens,
-                                                 const Tensor& tgt_lens, int64_t blank_idx, const Tensor& alpha,
-                                                 const Tensor& log_P_blank, const Tensor& log_P_y,
-                                                 const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32) {
+// rnnt_forward that also returns the logit stash (at most stash_budget bytes)
+// for rnnt_backward_stash.
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> rnnt_forward_stash(
+    const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& targets, const Tensor& in_lens,
+    const Tensor& tgt_lens, int64_t blank_idx, int64_t tf32, int64_t stash_budget) {
+    return rnnt_forward_impl(encoder, decoder, joint_W, targets, in_lens, tgt_lens, blank_idx, tf32, stash_budget);
+}
+
+std::tuple<Tensor, Tensor, Tensor> rnnt_backward_impl(const Tensor& encoder, const Tensor& decoder,
+                                                      const Tensor& joint_W, const Tensor& targets,
+                                                      const Tensor& in_lens, const Tensor& tgt_lens, int64_t blank_idx,
+                                                      const Tensor& alpha, const Tensor& log_P_blank,
+                                                      const Tensor& log_P_y, const Tensor& log_prob,
+                                                      const Tensor& grad_loss, int64_t tf32, const Tensor* stash) {
     const int act = act_dtype(encoder, decoder);
     ASR_CHECK_F32(joint_W);
     ASR_CHECK_I32(targets);
@@ -162,24 +190,48 @@ std::tuple<Tensor, Tensor, Tensor> rnnt_backward(const Tensor& encoder, const Te
     Tensor g_W = torch::stable::new_empty(joint_W, {V, d});
     const size_t wsb = asr_rnnt_workspace_bytes_ex(B, T, U, V, d, (int)tf32, 1, act);
     Tensor ws = workspace(encoder, wsb);
-    check_rc(asr_rnnt_backward_ex(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
-                               joint_W.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
-                               in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, U, V, d,
-                               S, (int)blank_idx, alpha.const_data_ptr<double>(), log_P_blank.const_data_ptr<float>(),
-                               log_P_y.const_data_ptr<float>(), log_prob.const_data_ptr<float>(),
-                               grad_loss.const_data_ptr<float>(), (int)tf32, g_enc.mutable_data_ptr(),
-                               g_dec.mutable_data_ptr(), g_W.mutable_data_ptr<float>(), ws.mutable_data_ptr(),
-                               wsb, current_stream(encoder)),
+    check_rc(asr_rnnt_backward_stash(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
+                                     joint_W.const_data_ptr<float>(), targets.const_data_ptr<int32_t>(),
+                                     in_lens.const_data_ptr<int32_t>(), tgt_lens.const_data_ptr<int32_t>(), B, T, U, V,
+                                     d, S, (int)blank_idx, alpha.const_data_ptr<double>(),
+                                     log_P_blank.const_data_ptr<float>(), log_P_y.const_data_ptr<float>(),
+                                     log_prob.const_data_ptr<float>(), grad_loss.const_data_ptr<float>(), (int)tf32,
+                                     g_enc.mutable_data_ptr(), g_dec.mutable_data_ptr(), g_W.mutable_data_ptr<float>(),
+                                     stash ? stash->const_data_ptr() : nullptr, stash ? (size_t)stash->numel() : 0,
+                                     ws.mutable_data_ptr(), wsb, current_stream(encoder)),
              "asr::rnnt_backward");
     return {g_enc, g_dec, g_W};
 }
 
+std::tuple<Tensor, Tensor, Tensor> rnnt_backward(const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W,
+                                                 const Tensor& targets, const Tensor& in_lens,
+                                                 const Tensor& tgt_lens, int64_t blank_idx, const Tensor& alpha,
+                                                 const Tensor& log_P_blank, const Tensor& log_P_y,
+                                                 const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32) {
+    return rnnt_backward_impl(encoder, decoder, joint_W, targets, in_lens, tgt_lens, blank_idx, alpha, log_P_blank,
+                              log_P_y, log_prob, grad_loss, tf32, nullptr);
+}
+
+// rnnt_backward over the logit stash of rnnt_forward_stash (same tf32).
+std::tuple<Tensor, Tensor, Tensor> rnnt_backward_stash(const Tensor& encoder, const Tensor& decoder,
+                                                       const Tensor& joint_W, const Tensor& targets,
+                                                       const Tensor& in_lens, const Tensor& tgt_lens,
+                                                       int64_t blank_idx, const Tensor& alpha,
+                                                       const Tensor& log_P_blank, const Tensor& log_P_y,
+                                                       const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32,
+                                                       const Tensor& stash) {
+    STD_TORCH_CHECK(stash.is_cuda() && stash.is_contiguous() && stash.scalar_type() == ScalarType::Byte,
+                    "rnnt_backward_stash: stash is not a stash of rnnt_forward_stash");
+    return rnnt_backward_impl(encoder, decoder, joint_W, targets, in_lens, tgt_lens, blank_idx, alpha, log_P_blank,
+                              log_P_y, log_prob, grad_loss, tf32, &stash);
+}
+
 // ---------------------------------------------------------------------- TDT
 
-std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> tdt_forward(
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> tdt_forward_impl(
     const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
     const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
-    int64_t max_duration, int64_t has_zero, int64_t blank_idx, double sigma, int64_t tf32) {
+    int64_t max_duration, int64_t has_zero, int64_t blank_idx, double sigma, int64_t tf32, int64_t stash_budget) {
     const int act = act_dtype(encoder, decoder);
     ASR_CHECK_F32(joint_W);
     ASR_CHECK_F32(joint_W_dur);
@@ -197,26 +249,49 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> tdt_forward(
     Tensor log_P_blank = torch::stable::new_empty(encoder, {2, B, T, U}, ScalarType::Float);
     Tensor log_P_y = torch::stable::new_empty(encoder, {B, T, U}, ScalarType::Float);
     Tensor log_P_dur = torch::stable::new_empty(encoder, {B, T, U, Dn}, ScalarType::Float);
+    Tensor stash = stash_tensor(encoder, asr_logit_stash_bytes(B, T, U, V, Dn, d, (int)tf32), stash_budget);
     const size_t wsb = asr_tdt_workspace_bytes_ex(B, T, U, V, Dn, d, (int)tf32, 0, act);
     Tensor ws = workspace(encoder, wsb);
-    check_rc(asr_tdt_forward_ex(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
-                             joint_W.const_data_ptr<float>(), joint_W_dur.const_data_ptr<float>(),
-                             targets.const_data_ptr<int32_t>(), in_lens.const_data_ptr<int32_t>(),
-                             tgt_lens.const_data_ptr<int32_t>(), durations.const_data_ptr<int32_t>(), Dn,
-                             (int)max_duration, (int)has_zero, B, T, U, V, d, S, (int)blank_idx, (float)sigma,
-                             (int)tf32, loss.mutable_data_ptr<float>(), alpha.mutable_data_ptr<double>(),
-                             log_P_blank.mutable_data_ptr<float>(), log_P_y.mutable_data_ptr<float>(),
-                             log_P_dur.mutable_data_ptr<float>(), log_prob.mutable_data_ptr<float>(),
-                             ws.mutable_data_ptr(), wsb, current_stream(encoder)),
+    check_rc(asr_tdt_forward_stash(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
+                                   joint_W.const_data_ptr<float>(), joint_W_dur.const_data_ptr<float>(),
+                                   targets.const_data_ptr<int32_t>(), in_lens.const_data_ptr<int32_t>(),
+                                   tgt_lens.const_data_ptr<int32_t>(), durations.const_data_ptr<int32_t>(), Dn,
+                                   (int)max_duration, (int)has_zero, B, T, U, V, d, S, (int)blank_idx, (float)sigma,
+                                   (int)tf32, loss.mutable_data_ptr<float>(), alpha.mutable_data_ptr<double>(),
+                                   log_P_blank.mutable_data_ptr<float>(), log_P_y.mutable_data_ptr<float>(),
+                                   log_P_dur.mutable_data_ptr<float>(), log_prob.mutable_data_ptr<float>(),
+                                   stash.mutable_data_ptr(), (size_t)stash.numel(), ws.mutable_data_ptr(), wsb,
+                                   current_stream(encoder)),
              "asr::tdt_forward");
+    return {loss, alpha, log_P_blank, log_P_y, log_P_dur, log_prob, stash};
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> tdt_forward(
+    const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
+    const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
+    int64_t max_duration, int64_t has_zero, int64_t blank_idx, double sigma, int64_t tf32) {
+    auto [loss, alpha, log_P_blank, log_P_y, log_P_dur, log_prob, stash] =
+        tdt_forward_impl(encoder, decoder, joint_W, joint_W_dur, targets, in_lens, tgt_lens, durations, max_duration,
+                         has_zero, blank_idx, sigma, tf32, 0);
     return {loss, alpha, log_P_blank, log_P_y, log_P_dur, log_prob};
 }
 
-std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward(
+// tdt_forward that also returns the logit stash (at most stash_budget bytes)
+// for tdt_backward_stash.
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor> tdt_forward_stash(
+    const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
+    const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
+    int64_t max_duration, int64_t has_zero, int64_t blank_idx, double sigma, int64_t tf32, int64_t stash_budget) {
+    return tdt_forward_impl(encoder, decoder, joint_W, joint_W_dur, targets, in_lens, tgt_lens, durations,
+                            max_duration, has_zero, blank_idx, sigma, tf32, stash_budget);
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward_impl(
     const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
     const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
     int64_t max_duration, int64_t has_zero, int64_t blank_idx, const Tensor& alpha, const Tensor& log_P_blank,
-    const Tensor& log_P_y, const Tensor& log_P_dur, const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32) {
+    const Tensor& log_P_y, const Tensor& log_P_dur, const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32,
+    const Tensor* stash) {
     const int act = act_dtype(encoder, decoder);
     ASR_CHECK_F32(joint_W);
     ASR_CHECK_F32(joint_W_dur);
@@ -240,19 +315,44 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward(
     Tensor g_Wd = torch::stable::new_empty(joint_W_dur, {Dn, d});
     const size_t wsb = asr_tdt_workspace_bytes_ex(B, T, U, V, Dn, d, (int)tf32, 1, act);
     Tensor ws = workspace(encoder, wsb);
-    check_rc(asr_tdt_backward_ex(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
-                              joint_W.const_data_ptr<float>(), joint_W_dur.const_data_ptr<float>(),
-                              targets.const_data_ptr<int32_t>(), in_lens.const_data_ptr<int32_t>(),
-                              tgt_lens.const_data_ptr<int32_t>(), durations.const_data_ptr<int32_t>(), Dn,
-                              (int)max_duration, (int)has_zero, B, T, U, V, d, S, (int)blank_idx,
-                              alpha.const_data_ptr<double>(), log_P_blank.const_data_ptr<float>(),
-                              log_P_y.const_data_ptr<float>(), log_P_dur.const_data_ptr<float>(),
-                              log_prob.const_data_ptr<float>(), grad_loss.const_data_ptr<float>(), (int)tf32,
-                              g_enc.mutable_data_ptr(), g_dec.mutable_data_ptr(),
-                              g_W.mutable_data_ptr<float>(), g_Wd.mutable_data_ptr<float>(), ws.mutable_data_ptr(),
-                              wsb, current_stream(encoder)),
+    check_rc(asr_tdt_backward_stash(encoder.const_data_ptr(), decoder.const_data_ptr(), act,
+                                    joint_W.const_data_ptr<float>(), joint_W_dur.const_data_ptr<float>(),
+                                    targets.const_data_ptr<int32_t>(), in_lens.const_data_ptr<int32_t>(),
+                                    tgt_lens.const_data_ptr<int32_t>(), durations.const_data_ptr<int32_t>(), Dn,
+                                    (int)max_duration, (int)has_zero, B, T, U, V, d, S, (int)blank_idx,
+                                    alpha.const_data_ptr<double>(), log_P_blank.const_data_ptr<float>(),
+                                    log_P_y.const_data_ptr<float>(), log_P_dur.const_data_ptr<float>(),
+                                    log_prob.const_data_ptr<float>(), grad_loss.const_data_ptr<float>(), (int)tf32,
+                                    g_enc.mutable_data_ptr(), g_dec.mutable_data_ptr(), g_W.mutable_data_ptr<float>(),
+                                    g_Wd.mutable_data_ptr<float>(), stash ? stash->const_data_ptr() : nullptr,
+                                    stash ? (size_t)stash->numel() : 0, ws.mutable_data_ptr(), wsb,
+                                    current_stream(encoder)),
              "asr::tdt_backward");
     return {g_enc, g_dec, g_W, g_Wd};
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward(
+    const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
+    const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
+    int64_t max_duration, int64_t has_zero, int64_t blank_idx, const Tensor& alpha, const Tensor& log_P_blank,
+    const Tensor& log_P_y, const Tensor& log_P_dur, const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32) {
+    return tdt_backward_impl(encoder, decoder, joint_W, joint_W_dur, targets, in_lens, tgt_lens, durations,
+                             max_duration, has_zero, blank_idx, alpha, log_P_blank, log_P_y, log_P_dur, log_prob,
+                             grad_loss, tf32, nullptr);
+}
+
+// tdt_backward over the logit stash of tdt_forward_stash (same tf32).
+std::tuple<Tensor, Tensor, Tensor, Tensor> tdt_backward_stash(
+    const Tensor& encoder, const Tensor& decoder, const Tensor& joint_W, const Tensor& joint_W_dur,
+    const Tensor& targets, const Tensor& in_lens, const Tensor& tgt_lens, const Tensor& durations,
+    int64_t max_duration, int64_t has_zero, int64_t blank_idx, const Tensor& alpha, const Tensor& log_P_blank,
+    const Tensor& log_P_y, const Tensor& log_P_dur, const Tensor& log_prob, const Tensor& grad_loss, int64_t tf32,
+    const Tensor& stash) {
+    STD_TORCH_CHECK(stash.is_cuda() && stash.is_contiguous() && stash.scalar_type() == ScalarType::Byte,
+                    "tdt_backward_stash: stash is not a stash of tdt_forward_stash");
+    return tdt_backward_impl(encoder, decoder, joint_W, joint_W_dur, targets, in_lens, tgt_lens, durations,
+                             max_duration, has_zero, blank_idx, alpha, log_P_blank, log_P_y, log_P_dur, log_prob,
+                             grad_loss, tf32, &stash);
 }
 
 }  // namespace
@@ -280,7 +380,33 @@ STABLE_TORCH_LIBRARY(asr, m) {
         "int tf32) -> (Tensor, Tensor, Tensor, Tensor)");
 }
 
+// Ops of this library beside the reference's: the transducer ops with a logit
+// stash (asr_b200.loss uses them; the reference-schema ops above recompute).
+STABLE_TORCH_LIBRARY_FRAGMENT(asr, m) {
+    m.def(
+        "rnnt_forward_stash(Tensor encoder, Tensor decoder, Tensor joint_W, Tensor targets, Tensor in_lens, "
+        "Tensor tgt_lens, int blank_idx, int tf32, int stash_budget) -> (Tensor, Tensor, Tensor, Tensor, Tensor, "
+        "Tensor)");
+    m.def(
+        "rnnt_backward_stash(Tensor encoder, Tensor decoder, Tensor joint_W, Tensor targets, Tensor in_lens, "
+        "Tensor tgt_lens, int blank_idx, Tensor alpha, Tensor log_P_blank, Tensor log_P_y, Tensor log_prob, "
+        "Tensor grad_loss, int tf32, Tensor stash) -> (Tensor, Tensor, Tensor)");
+    m.def(
+        "tdt_forward_stash(Tensor encoder, Tensor decoder, Tensor joint_W, Tensor joint_W_dur, Tensor targets, "
+        "Tensor in_lens, Tensor tgt_lens, Tensor durations, int max_duration, int has_zero, int blank_idx, "
+        "float sigma, int tf32, int stash_budget) -> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)");
+    m.def(
+        "tdt_backward_stash(Tensor encoder, Tensor decoder, Tensor joint_W, Tensor joint_W_dur, Tensor targets, "
+        "Tensor in_lens, Tensor tgt_lens, Tensor durations, int max_duration, int has_zero, int blank_idx, "
+        "Tensor alpha, Tensor log_P_blank, Tensor log_P_y, Tensor log_P_dur, Tensor log_prob, Tensor grad_loss, "
+        "int tf32, Tensor stash) -> (Tensor, Tensor, Tensor, Tensor)");
+}
+
 STABLE_TORCH_LIBRARY_IMPL(asr, CUDA, m) {
+    m.impl("rnnt_forward_stash", TORCH_BOX(&rnnt_forward_stash));
+    m.impl("rnnt_backward_stash", TORCH_BOX(&rnnt_backward_stash));
+    m.impl("tdt_forward_stash", TORCH_BOX(&tdt_forward_stash));
+    m.impl("tdt_backward_stash", TORCH_BOX(&tdt_backward_stash));
     m.impl("ctc_alpha", TORCH_BOX(&ctc_alpha));
     m.impl("ctc_grad", TORCH_BOX(&ctc_grad));
     m.impl("rnnt_forward", TORCH_BOX(&rnnt_forward));

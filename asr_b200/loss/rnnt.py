@@ -13,8 +13,11 @@ class RNNTLossFn(torch.autograd.Function):
     """Fused joint network + RNN-T loss with an exact analytic backward.
 
     The joint ``tanh(enc + dec) @ joint_W.T`` and its log-softmax run inside the
-    kernels, so the (B, T, U, V) logits never exist in memory. ``tf32`` selects
-    the bf16 tensor-core joint (fp32 accumulation); the default is fp32-exact.
+    kernels, so the (B, T, U, V) logits are never materialised in fp32; the
+    forward keeps them (fp16, or fp32 in the fp32 mode) in a stash of at most
+    ``asr_b200._lib.logit_stash_budget()`` bytes for the backward, which
+    recomputes the logits of nodes past it. ``tf32`` selects the bf16
+    tensor-core joint (fp32 accumulation); the default is fp32-exact.
     """
 
     @staticmethod
@@ -22,11 +25,12 @@ class RNNTLossFn(torch.autograd.Function):
         targets = targets.int()
         in_lens = in_lens.int()
         tgt_lens = tgt_lens.int()
-        loss, alpha, log_P_blank, log_P_y, log_prob = torch.ops.asr.rnnt_forward(
-            encoder.contiguous(), decoder.contiguous(), joint_W.contiguous(), targets, in_lens, tgt_lens, blank_idx, tf32
+        loss, alpha, log_P_blank, log_P_y, log_prob, stash = torch.ops.asr.rnnt_forward_stash(
+            encoder.contiguous(), decoder.contiguous(), joint_W.contiguous(), targets, in_lens, tgt_lens, blank_idx,
+            tf32, _lib.logit_stash_budget(),
         )
         ctx.save_for_backward(encoder, decoder, joint_W, targets, in_lens, tgt_lens, alpha, log_P_blank, log_P_y,
-                              log_prob)
+                              log_prob, stash)
         ctx.blank_idx = blank_idx
         ctx.tf32 = tf32
         return loss
@@ -34,10 +38,10 @@ class RNNTLossFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, *grad_outputs):
         (grad_loss,) = grad_outputs
-        enc, dec, W, targets, in_lens, tgt_lens, alpha, log_P_blank, log_P_y, log_prob = ctx.saved_tensors
-        grad_encoder, grad_decoder, grad_joint_W = torch.ops.asr.rnnt_backward(
+        enc, dec, W, targets, in_lens, tgt_lens, alpha, log_P_blank, log_P_y, log_prob, stash = ctx.saved_tensors
+        grad_encoder, grad_decoder, grad_joint_W = torch.ops.asr.rnnt_backward_stash(
             enc.contiguous(), dec.contiguous(), W.contiguous(), targets, in_lens, tgt_lens, ctx.blank_idx, alpha,
-            log_P_blank, log_P_y, log_prob, grad_loss.contiguous(), ctx.tf32,
+            log_P_blank, log_P_y, log_prob, grad_loss.contiguous(), ctx.tf32, stash,
         )
         return grad_encoder, grad_decoder, grad_joint_W, None, None, None, None, None
 

@@ -23,7 +23,12 @@ def _durations_tensor(durations: list[int], device) -> torch.Tensor:
 
 
 class TDTLossFn(torch.autograd.Function):
-    """Fused two-head joint network + Token-and-Duration Transducer loss."""
+    """Fused two-head joint network + Token-and-Duration Transducer loss.
+
+    The forward keeps the joint's logits in a stash of at most
+    ``asr_b200._lib.logit_stash_budget()`` bytes until the backward, which then
+    forms d loss / d logits from it instead of recomputing the logits GEMM.
+    """
 
     @staticmethod
     def forward(ctx, encoder, decoder, joint_W, joint_W_dur, in_lens, tgt_lens, targets, durations, max_duration,
@@ -32,12 +37,12 @@ class TDTLossFn(torch.autograd.Function):
         in_lens = in_lens.int()
         tgt_lens = tgt_lens.int()
         durations = durations.int()
-        loss, alpha, log_P_blank, log_P_y, log_P_dur, log_prob = torch.ops.asr.tdt_forward(
+        loss, alpha, log_P_blank, log_P_y, log_P_dur, log_prob, stash = torch.ops.asr.tdt_forward_stash(
             encoder.contiguous(), decoder.contiguous(), joint_W.contiguous(), joint_W_dur.contiguous(), targets,
-            in_lens, tgt_lens, durations, max_duration, has_zero, blank_idx, sigma, tf32,
+            in_lens, tgt_lens, durations, max_duration, has_zero, blank_idx, sigma, tf32, _lib.logit_stash_budget(),
         )
         ctx.save_for_backward(encoder, decoder, joint_W, joint_W_dur, targets, in_lens, tgt_lens, durations, alpha,
-                              log_P_blank, log_P_y, log_P_dur, log_prob)
+                              log_P_blank, log_P_y, log_P_dur, log_prob, stash)
         ctx.max_duration = max_duration
         ctx.has_zero = has_zero
         ctx.blank_idx = blank_idx
@@ -48,11 +53,11 @@ class TDTLossFn(torch.autograd.Function):
     def backward(ctx, *grad_outputs):
         (grad_loss,) = grad_outputs
         (enc, dec, W, W_dur, targets, in_lens, tgt_lens, durations, alpha, log_P_blank, log_P_y, log_P_dur,
-         log_prob) = ctx.saved_tensors
-        grad_encoder, grad_decoder, grad_joint_W, grad_joint_W_dur = torch.ops.asr.tdt_backward(
+         log_prob, stash) = ctx.saved_tensors
+        grad_encoder, grad_decoder, grad_joint_W, grad_joint_W_dur = torch.ops.asr.tdt_backward_stash(
             enc.contiguous(), dec.contiguous(), W.contiguous(), W_dur.contiguous(), targets, in_lens, tgt_lens,
             durations, ctx.max_duration, ctx.has_zero, ctx.blank_idx, alpha, log_P_blank, log_P_y, log_P_dur,
-            log_prob, grad_loss.contiguous(), ctx.tf32,
+            log_prob, grad_loss.contiguous(), ctx.tf32, stash,
         )
         return (grad_encoder, grad_decoder, grad_joint_W, grad_joint_W_dur) + (None,) * 9
 

@@ -173,16 +173,23 @@ GEMM_KERNELS = ("joint_fwd_tc", "joint_dlogits_tc", "joint_dhidden_tc", "joint_d
                 "joint_fwd_simt", "joint_dlogits_simt", "joint_dhidden_simt", "joint_dweight_simt")
 
 
-def kernel_work(name, N, d, Vf, n_dur, frames=0, labels=0):
+def kernel_work(name, N, d, Vf, n_dur, frames=0, labels=0, stash_nodes=0, stash_per_node=0, g_width=0):
     """Algorithmic work of one step of kernel `name`: ('tensor', flops) or ('hbm', bytes).
-    Joint GEMMs: 2 * N * d * Vf each (forward, backward recompute, d_hidden, dW).
+    Joint GEMMs: 2 * N * d * Vf each (forward, backward recompute, d_hidden, dW);
+    the recompute covers only the nodes past the logit stash, whose G rows the
+    stash kernel forms from the stashed row (stash_per_node bytes) and the node's
+    lse, cb, ct and duration grads, writing the 2 * g_width-byte G row.
     Hidden rows (forward and backward): bf16 H written (2 * ceil64(d) bytes per
     node) plus the fp32 enc / dec rows read once (frames + labels rows of d floats).
     Recursions: per node, the 4-byte lattice weights read plus the float64 alpha
     written (forward); the backward reads the weights and alpha and writes beta
     (TDT) and the 4-byte posteriors / duration gradients."""
+    if name == "joint_dlogits_tc":
+        return "tensor", 2.0 * max(N - stash_nodes, 0) * d * Vf
     if name in GEMM_KERNELS:
         return "tensor", 2.0 * N * d * Vf
+    if name == "joint_dlogits_stash":
+        return "hbm", min(stash_nodes, N) * (stash_per_node + 12.0 + 4.0 * n_dur + 2.0 * g_width)
     if name == "joint_hidden":
         kpad = (d + 63) // 64 * 64
         return "hbm", 2.0 * (N * 2.0 * kpad + (frames + labels) * d * 4.0)
@@ -486,9 +493,15 @@ def run_config(args):
     peaks = measured_peaks()
     kernels, roof = {}, None
     total_ms = max(sum(v[1] for v in prof.values()), 1e-9)
+    stash_nodes, stash_per = (0, 0)
+    if kind != "ctc":
+        stash_nodes, stash_per = _lib.logit_stash_layout(B, host["enc"].shape[1], host["dec"].shape[1], cfg["V"],
+                                                         n_dur, d, tf32)
+    g_width = (Vf + 15) // 16 * 16 * (1 if tf32 else 3)
     for name, (launches, kms) in prof.items():
         bound, work = kernel_work(name, N, d, Vf, n_dur, frames=int(host["in_lens"].sum()),
-                                  labels=int((host["tgt_lens"] + 1).sum()))
+                                  labels=int((host["tgt_lens"] + 1).sum()), stash_nodes=stash_nodes,
+                                  stash_per_node=stash_per, g_width=g_width)
         if name.startswith("ctc_"):
             tv = int(host["in_lens"].sum()) * cfg["V"] * 4.0
             states = int((host["in_lens"].astype(np.int64) * (2 * host["tgt_lens"] + 1)).sum()) * 8.0
@@ -517,7 +530,8 @@ def run_config(args):
         "config": {"workload": cfg["name"], "batch": B, "T": list(cfg["T"]), "U": list(cfg["U"]), "vocab": cfg["V"],
                    "d_model": d or None, "lattice_nodes": N if kind != "ctc" else None,
                    "l2": "flushed between timed steps (256 MB write)",
-                   "joint_path": None if kind == "ctc" else joint_path_name(tc, tf32)},
+                   "joint_path": None if kind == "ctc" else joint_path_name(tc, tf32),
+                   "logit_stash_nodes": min(stash_nodes, N)},
         "roofline": roof, "cpu_baseline": None,
         "e2e": {"value": round(B / (e2e_ms / 1000.0), 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4)},
@@ -1316,9 +1330,14 @@ def main():
     roof = None
     per_kernel = {}
     total_ms = max(sum(v[1] for v in prof.values()), 1e-9)
+    stash_nodes, stash_per = _lib.logit_stash_layout(len(host["in_lens"]), host["enc"].shape[1],
+                                                     host["dec"].shape[1], VOCAB, len(DURATIONS), D_MODEL,
+                                                     bool(args.tf32))
+    g_width = (Vf + 15) // 16 * 16 * (1 if args.tf32 else 3)
     for name, (launches, kms) in prof.items():
         bound, work = kernel_work(name, N_local, D_MODEL, Vf, len(DURATIONS), frames=int(host["in_lens"].sum()),
-                                  labels=int((host["tgt_lens"] + 1).sum()))
+                                  labels=int((host["tgt_lens"] + 1).sum()), stash_nodes=stash_nodes,
+                                  stash_per_node=stash_per, g_width=g_width)
         per_launch_ms = kms / max(launches, 1)
         steps_launches = launches / args.steps
         work_per_launch = work / max(steps_launches, 1)
@@ -1375,7 +1394,9 @@ def main():
                        "shard_imbalance": round(shard_imbalance(
                            in_lens, tgt_lens, shards), 4), "parallelism": f"dp{world}",
                        "l2": "flushed between timed steps (256 MB write)",
-                       "joint_path": joint_path_name(tc, args.tf32), "activations": args.act_dtype},
+                       "joint_path": joint_path_name(tc, args.tf32), "activations": args.act_dtype,
+                       "logit_stash": {"nodes_rank0": min(stash_nodes, N_local), "bytes_per_node": stash_per,
+                                       "budget_bytes": _lib.logit_stash_budget()}},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "utterances/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4),

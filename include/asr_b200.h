@@ -174,6 +174,59 @@ int asr_tdt_backward_ex(const void* encoder, const void* decoder, int act_dtype,
                         void* grad_decoder, float* grad_joint_W, float* grad_joint_W_dur, void* workspace,
                         size_t workspace_bytes, asr_stream_t stream);
 
+/* ---------------------------------------------------- logit stash (*_stash variants)
+ *
+ * The *_ex entry points with a caller-owned logit stash: the forward keeps the
+ * joint's logits of the first lattice nodes that fit in `stash` (compact node
+ * order: utterance, frame, label position), and the backward forms d loss /
+ * d logits of those nodes in one streaming pass over the stash (about 4 KB of
+ * HBM traffic per node at V = 1024) instead of recomputing the logits GEMM
+ * (2 * d * (V + n_dur) FLOPs per node). Nodes past the stash are recomputed as
+ * in the *_ex backward. A stash row holds each logit minus the row's largest
+ * token logit of its vocabulary chunk: fp16 with the bf16 tensor-core joint
+ * (tf32 != 0; at most 2^-12 of that difference added to a logit, below the
+ * bf16 rounding of the joint's operands for the entries that carry the softmax
+ * mass), fp32 in the fp32 mode. The backward must get the same stash (contents
+ * untouched), stash_bytes and tf32 as its forward. stash = NULL (or a stash too
+ * small for 256 nodes) makes each identical to its *_ex entry point. The stash
+ * is used only where both directions run the tensor-core joint. No counterpart
+ * in the reference, whose backward always recomputes the logits
+ * (src/asr/loss/csrc/rnnt.cu:382-458, tdt.cu:602-704). */
+
+/* Bytes of a stash that holds every node of the capacity B*T*U (n_dur = 0 for
+ * RNN-T): ceil256(B*T*U) * (2 or 4 bytes * ceil16(V + n_dur) + 4 bytes per
+ * vocabulary chunk) + 512. 0 when the shape does not run the tensor-core joint
+ * in both directions (or without a CUDA device). A smaller stash holds the
+ * first floor((stash_bytes - 512) / bytes per node) nodes, in whole 256s. */
+size_t asr_logit_stash_bytes(int B, int T, int U, int V, int n_dur, int d, int tf32);
+int asr_rnnt_forward_stash(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                           const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens, int B, int T,
+                           int U, int V, int d, int S, int blank_idx, int tf32, float* loss, double* alpha,
+                           float* log_P_blank, float* log_P_y, float* log_prob, void* stash, size_t stash_bytes,
+                           void* workspace, size_t workspace_bytes, asr_stream_t stream);
+int asr_rnnt_backward_stash(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                            const int32_t* targets, const int32_t* in_lens, const int32_t* tgt_lens, int B, int T,
+                            int U, int V, int d, int S, int blank_idx, const double* alpha, const float* log_P_blank,
+                            const float* log_P_y, const float* log_prob, const float* grad_loss, int tf32,
+                            void* grad_encoder, void* grad_decoder, float* grad_joint_W, const void* stash,
+                            size_t stash_bytes, void* workspace, size_t workspace_bytes, asr_stream_t stream);
+int asr_tdt_forward_stash(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                          const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                          const int32_t* tgt_lens, const int32_t* durations, int n_dur, int max_duration,
+                          int has_zero, int B, int T, int U, int V, int d, int S, int blank_idx, float sigma,
+                          int tf32, float* loss, double* alpha, float* log_P_blank, float* log_P_y,
+                          float* log_P_dur, float* log_prob, void* stash, size_t stash_bytes, void* workspace,
+                          size_t workspace_bytes, asr_stream_t stream);
+int asr_tdt_backward_stash(const void* encoder, const void* decoder, int act_dtype, const float* joint_W,
+                           const float* joint_W_dur, const int32_t* targets, const int32_t* in_lens,
+                           const int32_t* tgt_lens, const int32_t* durations, int n_dur, int max_duration,
+                           int has_zero, int B, int T, int U, int V, int d, int S, int blank_idx,
+                           const double* alpha, const float* log_P_blank, const float* log_P_y,
+                           const float* log_P_dur, const float* log_prob, const float* grad_loss, int tf32,
+                           void* grad_encoder, void* grad_decoder, float* grad_joint_W, float* grad_joint_W_dur,
+                           const void* stash, size_t stash_bytes, void* workspace, size_t workspace_bytes,
+                           asr_stream_t stream);
+
 /* Bytes of the scratch array compiled into the library for asr_tdt_forward_noalloc. */
 #define ASR_TDT_FORWARD_NOALLOC_SCRATCH_BYTES (4u << 20)
 
