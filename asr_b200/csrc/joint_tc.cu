@@ -1491,10 +1491,11 @@ int tc_joint_forward(const JointArgs& a, const JointFwdOut& o, int node_capacity
 // gradients for the duration columns, zero for the padding; the split fp32 mode
 // stores the parts [hi | hi | lo]. A CTA takes tiles of kStashRows consecutive
 // rows: their meta rows, posteriors and duration gradients (contiguous runs)
-// go to shared memory first, then the tile's (row, 8-column group) items are
-// walked flat with kBatch stash loads in flight per thread before the first G
-// store, so every warp access covers 512 contiguous bytes and any vocabulary
-// size keeps all lanes busy. Bound by HBM: the stash row read (2 B per column,
+// go to shared memory first, then the tile's (row, 16-column group) items are
+// walked flat with kBatch items' stash loads in flight per thread before the
+// first G store (32-byte accesses, 1 KB contiguous per warp), so any vocabulary
+// size keeps all lanes busy. The blank and label corrections are applied only
+// to the items that hold those columns. Bound by HBM: the stash row read (2 B per column,
 // 4 in the split mode) and the G row written. When the stash covers the rest of
 // the pass, rows up to the next 128-row boundary are zeroed, as the recompute
 // kernel's last tile does: the dW kernel reads whole 64-row blocks.
@@ -1509,17 +1510,20 @@ struct StashParams {
     LogitStash stash;
     JointBwdIn in;
     __nv_bfloat16* G;
-    uint32_t groups;       // 8-column groups of a row (vpad / 8)
+    uint32_t groups;       // 16-column groups of a row (vpad / 16)
     uint32_t magic_row;    // ceil(2^32 / groups): item / groups = umulhi(item, magic_row)
-    uint32_t magic_chunk;  // ceil(2^32 / (cw / 8)): group -> vocabulary chunk
+    uint32_t magic_chunk;  // ceil(2^32 / (cw / 16)): group -> vocabulary chunk
 };
 
 constexpr int kStashRows = 128;  // rows per CTA tile
 constexpr int kStashThreads = 256;
 
 template <int PARTS>
-__global__ void __launch_bounds__(kStashThreads, 4) stash_dlogits_kernel(StashParams P) {
-    constexpr int kBatch = PARTS == 1 ? 8 : 4;  // items whose stash loads are in flight together
+__global__ void __launch_bounds__(kStashThreads, 3) stash_dlogits_kernel(StashParams P) {
+    // an item is 16 columns of a row: one or two 32-byte stash loads (fp16 / fp32)
+    constexpr int kES = PARTS == 1 ? 2 : 4;      // bytes per stashed value
+    constexpr int kLoads = PARTS == 1 ? 2 : 4;   // 16-byte loads per item
+    constexpr int kBatch = PARTS == 1 ? 4 : 2;   // items whose stash loads are in flight together
     __shared__ float s_e[kStashRows * kStashMaxChunks];  // ref * log2(e) - lse * log2(e) per (row, chunk)
     __shared__ float s_cb[kStashRows], s_ct[kStashRows], s_pn[kStashRows];
     __shared__ int s_y[kStashRows];
@@ -1553,21 +1557,19 @@ __global__ void __launch_bounds__(kStashThreads, 4) stash_dlogits_kernel(StashPa
             s_gd[(i / a.n_dur) * kMaxDurCols + i % a.n_dur] = __ldg(P.in.gdur + row0 * a.n_dur + i);
         __syncthreads();
         const uint32_t items = (uint32_t)R * P.groups;
+        // the tile's stash and G rows, addressed with 32-bit offsets from here
+        const char* sbase = static_cast<const char*>(P.stash.data) + row0 * g.vpad * kES;
+        __nv_bfloat16* gbase = P.G + (int64_t)r0 * g.gw;
         for (uint32_t f0 = threadIdx.x; f0 < items; f0 += kStashThreads * kBatch) {
-            uint4 raw[kBatch][PARTS == 1 ? 1 : 2];
+            uint4 raw[kBatch][kLoads];
 #pragma unroll
             for (int k = 0; k < kBatch; ++k) {
                 const uint32_t f = f0 + (uint32_t)(k * kStashThreads);
                 if (f < items) {
                     const uint32_t r = __umulhi(f, P.magic_row), q = f - r * P.groups;
-                    const int64_t e0 = (row0 + r) * g.vpad + q * 8;
-                    if (PARTS == 1) {
-                        raw[k][0] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __half*>(P.stash.data) + e0));
-                    } else {
-                        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const float*>(P.stash.data) + e0);
-                        raw[k][0] = __ldcs(src);
-                        raw[k][1] = __ldcs(src + 1);
-                    }
+                    const uint4* src = reinterpret_cast<const uint4*>(sbase + (r * g.vpad + q * 16) * kES);
+#pragma unroll
+                    for (int l = 0; l < kLoads; ++l) raw[k][l] = __ldcs(src + l);
                 }
             }
 #pragma unroll
@@ -1575,36 +1577,42 @@ __global__ void __launch_bounds__(kStashThreads, 4) stash_dlogits_kernel(StashPa
                 const uint32_t f = f0 + (uint32_t)(k * kStashThreads);
                 if (f >= items) break;
                 const uint32_t r = __umulhi(f, P.magic_row), q = f - r * P.groups;
-                const int c0 = (int)q * 8;
-                float x[8];
-                if (PARTS == 1) {
-                    const uint32_t ws[4] = {raw[k][0].x, raw[k][0].y, raw[k][0].z, raw[k][0].w};
+                const int c0 = (int)q * 16;
+                float x[16];  // the stashed values
+#pragma unroll
+                for (int l = 0; l < kLoads; ++l) {
+                    const uint32_t w[4] = {raw[k][l].x, raw[k][l].y, raw[k][l].z, raw[k][l].w};
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const float2 h2 = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
-                        x[2 * i] = h2.x;
-                        x[2 * i + 1] = h2.y;
+                        if (PARTS == 1) {
+                            const float2 h2 = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                            x[8 * l + 2 * i] = h2.x;
+                            x[8 * l + 2 * i + 1] = h2.y;
+                        } else {
+                            x[4 * l + i] = __uint_as_float(w[i]);
+                        }
                     }
-                } else {
-                    x[0] = __uint_as_float(raw[k][0].x), x[1] = __uint_as_float(raw[k][0].y);
-                    x[2] = __uint_as_float(raw[k][0].z), x[3] = __uint_as_float(raw[k][0].w);
-                    x[4] = __uint_as_float(raw[k][1].x), x[5] = __uint_as_float(raw[k][1].y);
-                    x[6] = __uint_as_float(raw[k][1].z), x[7] = __uint_as_float(raw[k][1].w);
                 }
                 const float e = s_e[r * kStashMaxChunks + __umulhi(q, P.magic_chunk)];
-                const float pn = s_pn[r], cb = s_cb[r], ct = s_ct[r];
-                const int y = s_y[r];
-                float gv[8];
-                if (c0 + 8 <= a.V) {
+                const float pn = s_pn[r];
+                float gv[16];
+                if (c0 + 16 <= a.V) {  // token columns: softmax * (cb + ct), then the two edges
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        float v = ex2_fast(fmaf(x[i], kLog2e, e)) * pn;
-                        v = (c0 + i == a.blank) ? v - cb : v;
-                        gv[i] = (c0 + i == y) ? v - ct : v;
+                    for (int i = 0; i < 16; ++i) gv[i] = ex2_fast(fmaf(x[i], kLog2e, e)) * pn;
+                    const int y = s_y[r];
+                    if ((unsigned)(a.blank - c0) < 16u || (unsigned)(y - c0) < 16u) {  // few items
+                        const float cb = s_cb[r], ct = s_ct[r];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            if (c0 + i == a.blank) gv[i] -= cb;
+                            if (c0 + i == y) gv[i] -= ct;
+                        }
                     }
-                } else {
+                } else {  // the row's last columns: tokens, duration-logit gradients, padding
+                    const int y = s_y[r];
+                    const float cb = s_cb[r], ct = s_ct[r];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < 16; ++i) {
                         const int cc = c0 + i;
                         float v = 0.f;
                         if (cc < a.V) {
@@ -1617,25 +1625,31 @@ __global__ void __launch_bounds__(kStashThreads, 4) stash_dlogits_kernel(StashPa
                         gv[i] = v;
                     }
                 }
-                __nv_bfloat16* grow = P.G + (int64_t)(r0 + r) * g.gw + c0;
+                __nv_bfloat16* grow = gbase + r * g.gw + c0;
                 if (PARTS == 1) {
-                    *reinterpret_cast<uint4*>(grow) = make_uint4(pack_bf16(gv[0], gv[1]), pack_bf16(gv[2], gv[3]),
-                                                                 pack_bf16(gv[4], gv[5]), pack_bf16(gv[6], gv[7]));
+                    st_global_32B(grow, make_uint4(pack_bf16(gv[0], gv[1]), pack_bf16(gv[2], gv[3]),
+                                                   pack_bf16(gv[4], gv[5]), pack_bf16(gv[6], gv[7])),
+                                  make_uint4(pack_bf16(gv[8], gv[9]), pack_bf16(gv[10], gv[11]),
+                                             pack_bf16(gv[12], gv[13]), pack_bf16(gv[14], gv[15])));
                 } else {  // split fp32: [hi | hi | lo]
-                    float lo[8];
+                    float lo[16];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < 16; ++i) {
                         const float h = __bfloat162float(__float2bfloat16_rn(gv[i]));
                         lo[i] = gv[i] - h;
                         gv[i] = h;
                     }
-                    const uint4 wh = make_uint4(pack_bf16(gv[0], gv[1]), pack_bf16(gv[2], gv[3]),
+                    const uint4 h0 = make_uint4(pack_bf16(gv[0], gv[1]), pack_bf16(gv[2], gv[3]),
                                                 pack_bf16(gv[4], gv[5]), pack_bf16(gv[6], gv[7]));
-                    *reinterpret_cast<uint4*>(grow) = wh;
-                    *reinterpret_cast<uint4*>(grow + g.vpad) = wh;
-                    *reinterpret_cast<uint4*>(grow + 2 * g.vpad) =
-                        make_uint4(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]), pack_bf16(lo[4], lo[5]),
-                                   pack_bf16(lo[6], lo[7]));
+                    const uint4 h1 = make_uint4(pack_bf16(gv[8], gv[9]), pack_bf16(gv[10], gv[11]),
+                                                pack_bf16(gv[12], gv[13]), pack_bf16(gv[14], gv[15]));
+                    st_global_32B(grow, h0, h1);
+                    st_global_32B(grow + g.vpad, h0, h1);
+                    st_global_32B(grow + 2 * g.vpad,
+                                  make_uint4(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]),
+                                             pack_bf16(lo[4], lo[5]), pack_bf16(lo[6], lo[7])),
+                                  make_uint4(pack_bf16(lo[8], lo[9]), pack_bf16(lo[10], lo[11]),
+                                             pack_bf16(lo[12], lo[13]), pack_bf16(lo[14], lo[15])));
                 }
             }
         }
@@ -2283,9 +2297,9 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     SP.stash = TP.stash;
     SP.in = in;
     SP.G = G;
-    SP.groups = (uint32_t)(g.vpad / 8);
+    SP.groups = (uint32_t)(g.vpad / 16);
     SP.magic_row = (uint32_t)(((1ull << 32) + SP.groups - 1) / SP.groups);
-    SP.magic_chunk = (uint32_t)(((1ull << 32) + g.cw / 8 - 1) / (g.cw / 8));
+    SP.magic_chunk = (uint32_t)(((1ull << 32) + g.cw / 16 - 1) / (g.cw / 16));
     // every node below the capacity stashed: the recompute kernel has no work
     const bool recompute = !use_stash || (int64_t)stash.nodes < (int64_t)node_capacity;
 
@@ -2335,10 +2349,11 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
         }
         if (use_stash) {
             KernelTimer kt("joint_dlogits_stash", st);
-            if (g.parts == 1)
-                stash_dlogits_kernel<1><<<sms * 4, kStashThreads, 0, st>>>(SP);
-            else
-                stash_dlogits_kernel<3><<<sms * 4, kStashThreads, 0, st>>>(SP);
+            // one resident wave: the CTAs stride over the pass's tiles
+            auto kern = g.parts == 1 ? stash_dlogits_kernel<1> : stash_dlogits_kernel<3>;
+            int per_sm = 1;
+            ASR_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kStashThreads, 0));
+            kern<<<sms * std::max(per_sm, 1), kStashThreads, 0, st>>>(SP);
             ASR_LAUNCH_CHECK();
         }
         if (recompute) {
