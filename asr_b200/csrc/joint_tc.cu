@@ -1511,11 +1511,16 @@ struct StashParams {
     JointBwdIn in;
     __nv_bfloat16* G;
     uint32_t groups;       // 16-column groups of a row (vpad / 16)
-    uint32_t magic_row;    // ceil(2^32 / groups): item / groups = umulhi(item, magic_row)
-    uint32_t magic_chunk;  // ceil(2^32 / (cw / 16)): group -> vocabulary chunk
+    uint32_t magic_row;    // ceil(2^32 / groups): item / groups = umulhi(item, magic_row); 0: groups = 1
+    uint32_t magic_chunk;  // ceil(2^32 / (cw / 16)): group -> vocabulary chunk; 0: cw = 16
 };
 
 constexpr int kStashRows = 128;  // rows per CTA tile
+
+// item / groups (0 = divide by one: ceil(2^32 / 1) does not fit the multiplier)
+__device__ __forceinline__ uint32_t row_of(uint32_t item, const StashParams& P) {
+    return P.magic_row ? __umulhi(item, P.magic_row) : item;
+}
 constexpr int kStashThreads = 256;
 
 template <int PARTS>
@@ -1566,7 +1571,7 @@ __global__ void __launch_bounds__(kStashThreads, 3) stash_dlogits_kernel(StashPa
             for (int k = 0; k < kBatch; ++k) {
                 const uint32_t f = f0 + (uint32_t)(k * kStashThreads);
                 if (f < items) {
-                    const uint32_t r = __umulhi(f, P.magic_row), q = f - r * P.groups;
+                    const uint32_t r = row_of(f, P), q = f - r * P.groups;
                     const uint4* src = reinterpret_cast<const uint4*>(sbase + (r * g.vpad + q * 16) * kES);
 #pragma unroll
                     for (int l = 0; l < kLoads; ++l) raw[k][l] = __ldcs(src + l);
@@ -1576,7 +1581,7 @@ __global__ void __launch_bounds__(kStashThreads, 3) stash_dlogits_kernel(StashPa
             for (int k = 0; k < kBatch; ++k) {
                 const uint32_t f = f0 + (uint32_t)(k * kStashThreads);
                 if (f >= items) break;
-                const uint32_t r = __umulhi(f, P.magic_row), q = f - r * P.groups;
+                const uint32_t r = row_of(f, P), q = f - r * P.groups;
                 const int c0 = (int)q * 16;
                 float x[16];  // the stashed values
 #pragma unroll
@@ -1593,7 +1598,7 @@ __global__ void __launch_bounds__(kStashThreads, 3) stash_dlogits_kernel(StashPa
                         }
                     }
                 }
-                const float e = s_e[r * kStashMaxChunks + __umulhi(q, P.magic_chunk)];
+                const float e = s_e[r * kStashMaxChunks + (P.magic_chunk ? __umulhi(q, P.magic_chunk) : q)];
                 const float pn = s_pn[r];
                 float gv[16];
                 if (c0 + 16 <= a.V) {  // token columns: softmax * (cb + ct), then the two edges
@@ -1812,6 +1817,32 @@ struct DhEpilogue {
     template <int N>
     __device__ void group(DhWalk& w, const float (&v)[N]) const {
         const int k = w.Ub - w.u;  // nodes left in frame t (at most one frame boundary here)
+        if (k >= N) {
+            // the whole group inside frame t (most groups): label positions u .. u + N - 1,
+            // one base address with constant offsets, no per-node frame selects
+            const float* din = sdin + w.u * kDhM + cl;
+            float* acc = sacc + w.u * kDhM + cl;
+            float dv[N], sa[N], xs[N];
+#pragma unroll
+            for (int i = 0; i < N; ++i) dv[i] = din[i * kDhM];
+#pragma unroll
+            for (int i = 0; i < N; ++i) sa[i] = acc[i * kDhM];
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                const float h = th(w.e_cur + dv[i]);
+                xs[i] = v[i] * (1.f - h * h);
+                acc[i * kDhM] = sa[i] + xs[i];
+            }
+#pragma unroll
+            for (int s2 = 1; s2 < N; s2 *= 2)
+#pragma unroll
+                for (int i = 0; i + s2 < N; i += 2 * s2) xs[i] += xs[i + s2];
+            w.acc_e += xs[0];
+            w.dirty = true;
+            w.u += N;
+            if (w.u == w.Ub) end_frame(w);
+            return;
+        }
         int idx[N];
 #pragma unroll
         for (int i = 0; i < N; ++i) {
@@ -2298,8 +2329,10 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     SP.in = in;
     SP.G = G;
     SP.groups = (uint32_t)(g.vpad / 16);
-    SP.magic_row = (uint32_t)(((1ull << 32) + SP.groups - 1) / SP.groups);
-    SP.magic_chunk = (uint32_t)(((1ull << 32) + g.cw / 16 - 1) / (g.cw / 16));
+    // ceil(2^32 / D), exact for every item index below 2^32 / D; 0 stands for D = 1
+    auto magic = [](uint32_t D) { return D == 1 ? 0u : (uint32_t)(((1ull << 32) + D - 1) / D); };
+    SP.magic_row = magic(SP.groups);
+    SP.magic_chunk = magic((uint32_t)(g.cw / 16));
     // every node below the capacity stashed: the recompute kernel has no work
     const bool recompute = !use_stash || (int64_t)stash.nodes < (int64_t)node_capacity;
 
