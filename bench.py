@@ -1305,16 +1305,35 @@ def main():
     torch.cuda.synchronize()
     e2e_total = p0.elapsed_time(p1)
 
+    # the gradient all-reduce on its own, every rank already there (after a
+    # barrier and a device sync): its transfer time, against the in-step window
+    # above, which also holds the wait for the slowest rank
+    ar_alone_ms = 0.0
+    if world > 1:
+        reps = 5
+        for _ in range(2):
+            allreduce_joint([W.grad, Wd.grad, torch.zeros(1, device=dev)])
+        torch.cuda.synchronize()
+        dist.barrier()
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        q0.record(stream)
+        for _ in range(reps):
+            allreduce_joint([W.grad, Wd.grad, torch.zeros(1, device=dev)])
+        q1.record(stream)
+        torch.cuda.synchronize()
+        ar_alone_ms = q0.elapsed_time(q1) / reps
+
     # ---- max over ranks
     # per-rank device times of the timed steps (the imbalance the LPT split leaves)
     # and of the all-reduce alone
     ar_ms = sum(a.elapsed_time(b) for a, b in ar_events) / max(args.steps, 1) if ar_events else 0.0
-    mine = torch.tensor([ms_total / args.steps, ar_ms], device=dev, dtype=torch.float64)
+    mine = torch.tensor([ms_total / args.steps, ar_ms, ar_alone_ms], device=dev, dtype=torch.float64)
     per_rank = [mine.clone() for _ in range(world)]
     if world > 1:
         dist.all_gather(per_rank, mine)
     rank_ms = [round(float(x[0]), 3) for x in per_rank]
     allreduce_ms = round(max(float(x[1]) for x in per_rank), 4)
+    allreduce_alone_ms = round(max(float(x[2]) for x in per_rank), 4)
     t = torch.tensor([ms_total, e2e_total, e2e_serial_total], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1391,6 +1410,7 @@ def main():
                        "durations": DURATIONS, "sigma": SIGMA, "lattice_nodes_global": N_global,
                        "lattice_nodes_rank0": N_local, "rank_ms_per_step": rank_ms,
                        "allreduce_ms_per_step": allreduce_ms if world > 1 else None,
+                       "allreduce_alone_ms": allreduce_alone_ms if world > 1 else None,
                        "shard_imbalance": round(shard_imbalance(
                            in_lens, tgt_lens, shards), 4), "parallelism": f"dp{world}",
                        "l2": "flushed between timed steps (256 MB write)",
