@@ -1694,8 +1694,8 @@ namespace {
 constexpr int kDhM = 128;                          // hidden columns per work item (UMMA M)
 constexpr int kDhNodes = 256;                      // nodes per tile (UMMA N)
 constexpr int kDhK = 32;                           // vocabulary per stage (64 B rows)
-constexpr int kDhABytes = kDhM * kDhK * 2;         // 8 KB
-constexpr int kDhStageBytes = kDhABytes + kDhNodes * kDhK * 2;  // 24 KB (4 stages beat 2 of 48 KB here)
+constexpr int kDhABytes = kDhM * kDhK * 2;         // 8 KB; a stage adds the G rows (16 KB, 8 KB per CTA of a pair):
+                                                   // 4 stages of 24 KB beat 2 of 48 KB here
 constexpr int kDwM = 128;         // vocabulary rows per dW work item (UMMA M)
 constexpr int kDwN = 320;         // hidden columns per dW work item (UMMA N = 192 + 128)
 constexpr int kBwdThreads = 192;  // TMA, MMA, 4 epilogue warps
@@ -1888,15 +1888,23 @@ struct DhEpilogue {
     }
 };
 
-template <bool kSmemDec, bool kSplit>
+// kCta = 2: a CTA pair (cluster of two, cta_group::2) runs one M = 256 MMA over
+// two hidden slices: each CTA streams its own slice of the transposed weight
+// (A) and half of the node tile's G rows (B), and keeps its slice's 128 x 256
+// accumulator in its own TMEM, so the epilogue is the single-CTA one. Per SM a
+// stage carries a third fewer bytes for the same MMA time. With an odd slice
+// count the last pair's second CTA has no slice: its weight rows are past the
+// hidden width (the loads fill zeros) and its epilogue only releases buffers.
+template <bool kSmemDec, bool kSplit, int kCta = 1>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     tc_dh_kernel(const __grid_constant__ CUtensorMap map_wt, const __grid_constant__ CUtensorMap map_g, DhParams P) {
+    constexpr int SB = kDhABytes + (kDhNodes / kCta) * kDhK * 2;  // stage: A slice + this CTA's G rows
     extern __shared__ uint8_t smem_raw[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const JointArgs& a = P.a;
     const int S = P.stages;
     uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* sdin = reinterpret_cast<float*>(stages + (size_t)S * kDhStageBytes);  // [dec_rows][kDhM]
+    float* sdin = reinterpret_cast<float*>(stages + (size_t)S * SB);  // [dec_rows][kDhM]
     float* sacc = sdin + (size_t)P.dec_rows * kDhM;                               // [dec_rows][kDhM]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sacc + (size_t)P.dec_rows * kDhM);  // 512 B multiples: aligned
     uint64_t* b_full = bars;
@@ -1908,7 +1916,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int* err = P.err;
 
     const int s = P.bounds[P.pass], e = P.bounds[P.pass + 1];
-    const int dt = blockIdx.x % P.ndt, grp = blockIdx.x / P.ndt;
+    const uint32_t rank = kCta == 2 ? cluster_ctarank() : 0;
+    const bool leader = rank == 0;
+    // work item: hidden slice dt of node-range group grp (a pair: slices 2 j and 2 j + 1)
+    const int nslot = kCta == 2 ? (P.ndt + 1) / 2 : P.ndt;
+    const int unit = (int)blockIdx.x / kCta;
+    const int dt = kCta == 2 ? 2 * (unit % nslot) + (int)rank : unit % nslot;
+    const int grp = unit / nslot;
+    const bool slice_ok = dt < P.ndt;
+    auto in_leader = [&](uint64_t* bar) { return kCta == 2 ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar); };
+    auto in_peer = [&](uint64_t* bar) { return mapa_shared(smem_u32(bar), 1); };
     const int ntiles = e > s ? (e - s + kDhNodes - 1) / kDhNodes : 0;
     const int tile0 = (int)((int64_t)grp * ntiles / P.groups);
     const int tile1 = (int)((int64_t)(grp + 1) * ntiles / P.groups);
@@ -1921,14 +1938,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&t_full[i], 1);
-            mbar_init(&t_empty[i], 4);
+            mbar_init(&t_empty[i], 4 * kCta);  // every epilogue warp of the pair releases the buffer
         }
         mbar_init(done, 1);
         fence_barrier_init();
         prefetch_tensormap(&map_wt);
         prefetch_tensormap(&map_g);
     }
-    if (warp == 1) tmem_alloc(tmem_slot, 2 * kDhNodes);
+    if (kCta == 2) {
+        cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
+        if (warp == 1) tmem_alloc_pair(tmem_slot, 2 * kDhNodes);
+    } else if (warp == 1) {
+        tmem_alloc(tmem_slot, 2 * kDhNodes);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -1944,14 +1966,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             bool ok = true;
             for (int tile = tile0; ok && tile < tile1; ++tile) {
                 for (int k = 0; k < ksteps; ++k) {
-                    if (!mbar_wait(&b_empty[stage], phase ^ 1, err, 11)) {
+                    if (!mbar_wait_cluster(&b_empty[stage], phase ^ 1, err, 11)) {
                         ok = false;
                         break;
                     }
-                    uint8_t* st = stages + (size_t)stage * kDhStageBytes;
-                    mbar_arrive_expect_tx(&b_full[stage], kDhStageBytes);
-                    tma_load_2d(st, &map_wt, k * kDhK, dt * kDhM, &b_full[stage]);
-                    tma_load_2d(st + kDhABytes, &map_g, k * kDhK, tile * kDhNodes, &b_full[stage]);
+                    uint8_t* st = stages + (size_t)stage * SB;
+                    if (kCta == 2) {  // both CTAs' bytes land on the even CTA's barrier
+                        if (leader) mbar_arrive_expect_tx(&b_full[stage], 2 * SB);
+                        tma_load_2d_pair(st, &map_wt, k * kDhK, dt * kDhM, in_leader(&b_full[stage]));
+                        tma_load_2d_pair(st + kDhABytes, &map_g, k * kDhK, tile * kDhNodes + (int)rank * (kDhNodes / 2),
+                                         in_leader(&b_full[stage]));
+                    } else {
+                        mbar_arrive_expect_tx(&b_full[stage], SB);
+                        tma_load_2d(st, &map_wt, k * kDhK, dt * kDhM, &b_full[stage]);
+                        tma_load_2d(st + kDhABytes, &map_g, k * kDhK, tile * kDhNodes, &b_full[stage]);
+                    }
                     issued[stage] = true;
                     ipar[stage] = phase;
                     if (++stage == S) {
@@ -1960,45 +1989,70 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     }
                 }
             }
-            for (int i = 0; i < S; ++i)
-                if (issued[i]) mbar_wait(&b_full[i], ipar[i], err, 12);
+            if (leader)  // the even CTA's full barriers count both CTAs' copies
+                for (int i = 0; i < S; ++i)
+                    if (issued[i]) mbar_wait_cluster(&b_full[i], ipar[i], err, 12);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = idesc_bf16(kDhM, kDhNodes, false, false);
+        auto commit_both = [&](uint64_t* bar) {
+            if (kCta == 2) {
+                mma_commit_pair(smem_u32(bar));
+                mma_commit_pair(in_peer(bar));
+            } else {
+                mma_commit(bar);
+            }
+        };
+        if (lane == 0 && leader) {
+            const uint32_t idesc = idesc_bf16(kDhM * kCta, kDhNodes, false, false);
             const uint32_t sbase = smem_u32(stages);
             int stage = 0;
             uint32_t phase = 0, q = 0;
             bool ok = true;
             for (int tile = tile0; ok && tile < tile1; ++tile, ++q) {
                 const uint32_t buf = q & 1;
-                if (!mbar_wait(&t_empty[buf], ((q >> 1) & 1) ^ 1, err, 13)) {
+                if (!mbar_wait_cluster(&t_empty[buf], ((q >> 1) & 1) ^ 1, err, 13)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 for (int k = 0; k < ksteps; ++k) {
-                    if (!mbar_wait(&b_full[stage], phase, err, 14)) {
+                    if (!mbar_wait_cluster(&b_full[stage], phase, err, 14)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st = sbase + stage * kDhStageBytes;
+                    const uint32_t st = sbase + stage * SB;
 #pragma unroll
-                    for (int kk = 0; kk < kDhK / 16; ++kk)
-                        mma_bf16(tmem_base + buf * kDhNodes, desc_k64(st + kk * 32),
-                                 desc_k64(st + kDhABytes + kk * 32), idesc, (k | kk) != 0 ? 1u : 0u);
-                    mma_commit(&b_empty[stage]);
+                    for (int kk = 0; kk < kDhK / 16; ++kk) {
+                        const uint64_t ad = desc_k64(st + kk * 32), bd = desc_k64(st + kDhABytes + kk * 32);
+                        if (kCta == 2)
+                            mma_bf16_pair(tmem_base + buf * kDhNodes, ad, bd, idesc, (k | kk) != 0 ? 1u : 0u);
+                        else
+                            mma_bf16(tmem_base + buf * kDhNodes, ad, bd, idesc, (k | kk) != 0 ? 1u : 0u);
+                    }
+                    commit_both(&b_empty[stage]);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
-                if (ok) mma_commit(&t_full[buf]);
+                if (ok) commit_both(&t_full[buf]);
             }
-            mma_commit(done);
+            commit_both(done);
             mbar_wait(done, 0, err, 15);
+        } else if (kCta == 2 && lane == 0) {
+            mbar_wait_cluster(done, 0, err, 15);  // odd CTA: the even CTA's MMAs write this TMEM
+        }
+    } else if (tile1 > tile0 && !slice_ok) {
+        // a pair's CTA without a hidden slice: release each accumulator buffer
+        uint32_t q = 0;
+        for (int tile = tile0; tile < tile1; ++tile, ++q) {
+            const uint32_t buf = q & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster(&t_full[buf], (q >> 1) & 1, err, 16))) break;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(in_leader(&t_empty[buf]));
         }
     } else if (tile1 > tile0) {
         // ------------------------------------------------------------------- epilogue
@@ -2018,7 +2072,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         bool ok = true;
         for (int tile = tile0; tile < tile1; ++tile, ++q) {
             const uint32_t buf = q & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&t_full[buf], (q >> 1) & 1, err, 16))) {
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster(&t_full[buf], (q >> 1) & 1, err, 16))) {
                 ok = false;
                 break;
             }
@@ -2049,7 +2103,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&t_empty[buf]);
+            if (lane == 0) {
+                if (kCta == 2)
+                    mbar_arrive_cluster(in_leader(&t_empty[buf]));
+                else
+                    mbar_arrive(&t_empty[buf]);
+            }
         }
         // the range may end inside a frame / an utterance: add the partial sums
         if (ok && w.b < a.B) {
@@ -2060,8 +2119,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
     tc_fence_before();
     __syncthreads();
-    tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, 2 * kDhNodes);
+    if (kCta == 2) {
+        cluster_sync();  // no CTA leaves while its pair may still read its smem or signal it
+        tc_fence_after();
+        if (warp == 1) tmem_dealloc_pair(tmem_base, 2 * kDhNodes);
+    } else {
+        tc_fence_after();
+        if (warp == 1) tmem_dealloc(tmem_base, 2 * kDhNodes);
+    }
 }
 
 struct DwParams {
@@ -2254,9 +2319,20 @@ BwdLayout bwd_layout(const JointArgs& a, int64_t cap) {
     return L;
 }
 
-size_t dh_smem_bytes(int stages, int dec_rows) {
-    return 1024 + (size_t)stages * kDhStageBytes + 2 * sizeof(float) * (size_t)dec_rows * kDhM + 8 * (2 * stages + 5) +
-           16;
+size_t dh_smem_bytes(int stages, int dec_rows, int cta = 1) {
+    const size_t sb = kDhABytes + (size_t)(kDhNodes / cta) * kDhK * 2;
+    return 1024 + (size_t)stages * sb + 2 * sizeof(float) * (size_t)dec_rows * kDhM + 8 * (2 * stages + 5) + 16;
+}
+
+// CTA pairs for the d_hidden kernel when ASR_B200_DH_PAIRS=1. Off by default:
+// on B200 the pairs measured slower at config 5 (26.9 vs 22.5 ms, one CTA in
+// six without a slice at d = 640) and at config 4 (9.6 vs 8.9 ms, none idle).
+bool dh_pairs() {
+    static const bool pairs = [] {
+        const char* e = std::getenv("ASR_B200_DH_PAIRS");
+        return e && e[0] == '1';
+    }();
+    return pairs;
 }
 
 size_t dw_smem_bytes() { return 1024 + (size_t)kDwStages * kDwStageBytes + 8 * (2 * kDwStages + 2) + 16; }
@@ -2347,15 +2423,24 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     DP.d_dec = o.d_dec;
     DP.err = err;
     DP.ndt = (g.kp + kDhM - 1) / kDhM;
-    DP.groups = std::max(1, sms / DP.ndt);
+    // CTA pairs take two hidden slices per node tile (the CTC head keeps single CTAs)
+    const int dh_cta = dh_pairs() && !a.head && DP.ndt > 1 ? 2 : 1;
+    const int dh_units = dh_cta == 2 ? (DP.ndt + 1) / 2 : DP.ndt;  // work items per node range
+    DP.groups = std::max(1, sms / (dh_units * dh_cta));
     const int limit = dyn_smem_limit();
-    DP.dec_rows = !a.head && (int)dh_smem_bytes(2, a.U) <= limit ? a.U : 0;
+    DP.dec_rows = !a.head && (int)dh_smem_bytes(2, a.U, dh_cta) <= limit ? a.U : 0;
     DP.stages = 2;
-    while (DP.stages < 8 && (int)dh_smem_bytes(DP.stages + 1, DP.dec_rows) <= limit) ++DP.stages;
-    const size_t smem_dh = dh_smem_bytes(DP.stages, DP.dec_rows);
-    auto dh_kernel = g.parts == 3 ? (DP.dec_rows > 0 ? tc_dh_kernel<true, true> : tc_dh_kernel<false, true>)
-                                  : (DP.dec_rows > 0 ? tc_dh_kernel<true, false> : tc_dh_kernel<false, false>);
+    while (DP.stages < 8 && (int)dh_smem_bytes(DP.stages + 1, DP.dec_rows, dh_cta) <= limit) ++DP.stages;
+    const size_t smem_dh = dh_smem_bytes(DP.stages, DP.dec_rows, dh_cta);
+    auto dh_kernel = dh_cta == 2
+                         ? (g.parts == 3 ? (DP.dec_rows > 0 ? tc_dh_kernel<true, true, 2> : tc_dh_kernel<false, true, 2>)
+                                         : (DP.dec_rows > 0 ? tc_dh_kernel<true, false, 2> : tc_dh_kernel<false, false, 2>))
+                         : (g.parts == 3 ? (DP.dec_rows > 0 ? tc_dh_kernel<true, true> : tc_dh_kernel<false, true>)
+                                         : (DP.dec_rows > 0 ? tc_dh_kernel<true, false> : tc_dh_kernel<false, false>));
     ASR_CUDA_TRY(cudaFuncSetAttribute(dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dh));
+    CUtensorMap m_g2;  // the pair's half tiles of G rows
+    if (dh_cta == 2 && !make_map(&m_g2, G, rows, g.gw, kDhK, kDhNodes / 2, CU_TENSOR_MAP_SWIZZLE_64B))
+        return ASR_ERR_CUDA;
 
     DwParams WP;
     std::memset(&WP, 0, sizeof(WP));
@@ -2396,8 +2481,24 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
         }
         {
             KernelTimer kt("joint_dhidden_tc", st);
-            dh_kernel<<<DP.groups * DP.ndt, kBwdThreads, smem_dh, st>>>(m_wt, m_g, DP);
-            ASR_LAUNCH_CHECK();
+            if (dh_cta == 2) {
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3(DP.groups * dh_units * 2);
+                cfg.blockDim = dim3(kBwdThreads);
+                cfg.dynamicSmemBytes = smem_dh;
+                cfg.stream = st;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = 2;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                ASR_CUDA_TRY(cudaLaunchKernelEx(&cfg, dh_kernel, m_wt, m_g2, DP));
+            } else {
+                dh_kernel<<<DP.groups * DP.ndt, kBwdThreads, smem_dh, st>>>(m_wt, m_g, DP);
+                ASR_LAUNCH_CHECK();
+            }
         }
         {
             KernelTimer kt("joint_dweight_tc", st);

@@ -538,28 +538,37 @@ np.savez(sys.argv[2], loss=loss.detach().cpu().numpy(), *[t.grad.cpu().numpy() f
 
 
 def test_tdt_bf16_joint_variants_agree(tmp_path):
-    """The joint kernel's variants compute the same sums: streamed hidden tiles
-    (the default), the resident hidden tile (ASR_B200_JOINT_STREAM=0) and the
-    opt-in CTA pairs (ASR_B200_JOINT_PAIRS=1, one M = 256 MMA per pair of SMs).
-    Each runs in its own process: the switches are read once per process."""
+    """The joint kernels' variants compute the same sums: streamed hidden tiles
+    (the default), the resident hidden tile (ASR_B200_JOINT_STREAM=0), the
+    opt-in CTA pairs of the logits kernel (ASR_B200_JOINT_PAIRS=1, one M = 256
+    MMA per pair of SMs) and of the d_hidden kernel (ASR_B200_DH_PAIRS=1: two
+    hidden slices per pair, d = 640 leaving one CTA of the last pair without a
+    slice). Each runs in its own process: the switches are read once per process."""
     import os
     import subprocess
     import sys
     from pathlib import Path
 
     root = str(Path(__file__).resolve().parents[1])
-    variants = {"stream": {}, "resident": {"ASR_B200_JOINT_STREAM": "0"}, "pairs": {"ASR_B200_JOINT_PAIRS": "1"}}
+    # the logits-kernel variants run the backward's recompute, so they run with the
+    # logit stash off and are compared with the streamed kernel without it
+    off = {"ASR_B200_LOGIT_STASH_GB": "0"}
+    variants = {"stream": {}, "dh_pairs": {"ASR_B200_DH_PAIRS": "1"}, "resident_stash": {"ASR_B200_JOINT_STREAM": "0"},
+                "stream_nostash": off,
+                "resident": dict(off, ASR_B200_JOINT_STREAM="0"), "pairs": dict(off, ASR_B200_JOINT_PAIRS="1")}
     out = {}
     for name, extra in variants.items():
         f = tmp_path / f"{name}.npz"
-        env = {k: v for k, v in os.environ.items() if not k.startswith("ASR_B200_JOINT_")}
+        env = {k: v for k, v in os.environ.items()
+               if not k.startswith(("ASR_B200_JOINT_", "ASR_B200_DH_", "ASR_B200_LOGIT_"))}
         env.update(extra)
         subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, root, str(f)], check=True, env=env, timeout=300)
         out[name] = np.load(f)
-    for name in ("resident", "pairs"):
-        np.testing.assert_allclose(out[name]["loss"], out["stream"]["loss"], rtol=1e-6)
+    for name, base in (("dh_pairs", "stream"), ("resident_stash", "stream"), ("resident", "stream_nostash"),
+                       ("pairs", "stream_nostash")):
+        np.testing.assert_allclose(out[name]["loss"], out[base]["loss"], rtol=1e-6)
         for k in ("arr_0", "arr_1", "arr_2", "arr_3"):
-            a, b = out[name][k].astype(np.float64), out["stream"][k].astype(np.float64)
+            a, b = out[name][k].astype(np.float64), out[base][k].astype(np.float64)
             assert np.linalg.norm(a - b) <= 1e-5 * np.linalg.norm(b), (name, k)
 
 
