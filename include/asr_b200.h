@@ -81,8 +81,10 @@ size_t asr_rnnt_workspace_bytes(int B, int T, int U, int V, int d, int tf32, int
 
 /* Replaces rnnt_forward_cuda (rnnt.cu:320-380; asr::rnnt_forward, rnnt_bindings.cpp:24-26).
  * encoder (B,T,d), decoder (B,U,d), joint_W (V,d), targets (B,S) with S >= U-1.
- * tf32 = 0: fp32-accurate joint GEMMs (SIMT FMA). tf32 != 0: bf16 tcgen05 tensor-core
- * joint with fp32 accumulation (the reference's opt-in fast mode).
+ * tf32 = 0: fp32-accurate joint GEMMs (tcgen05 tensor cores on split bf16 operands,
+ * three products per fp32 product; fp32 FMA for shapes outside them, see
+ * asr_joint_path). tf32 != 0: bf16 tcgen05 tensor-core joint with fp32
+ * accumulation (the reference's opt-in fast mode).
  * Outputs: loss (B,) = -log P(y|x); log_prob (B,) = log P(y|x);
  *   alpha        capacity B*T*U      float64 forward variable per valid node;
  *   log_P_blank  capacity 2*B*T*U    plane 0: blank log-prob, plane 1: token log-partition;
@@ -187,7 +189,8 @@ int asr_tdt_backward_ex(const void* encoder, const void* decoder, int act_dtype,
  * (tf32 != 0; at most 2^-12 of that difference added to a logit, below the
  * bf16 rounding of the joint's operands for the entries that carry the softmax
  * mass), fp32 in the fp32 mode. The backward must get the same stash (contents
- * untouched), stash_bytes and tf32 as its forward. stash = NULL (or a stash too
+ * untouched), stash_bytes and tf32 as its forward; the backward only reads it,
+ * so several backwards over one forward may share it. stash = NULL (or a stash too
  * small for 256 nodes) makes each identical to its *_ex entry point. The stash
  * is used only where both directions run the tensor-core joint. No counterpart
  * in the reference, whose backward always recomputes the logits

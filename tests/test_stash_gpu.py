@@ -124,3 +124,32 @@ def test_stash_one_column_group(tf32, monkeypatch):
     without = run_ours(c, tf32)
     for k in GRADS:
         assert relnorm(with_stash[k], without[k]) <= (2e-3 if tf32 else 1e-5), k
+
+
+@pytest.mark.parametrize("tf32", [True, False])
+def test_second_backward_over_one_forward(tf32):
+    """retain_graph: two backwards over one forward read the same stash (the
+    backward leaves it untouched); both match the oracle's gradients at the
+    path's bar, and each other."""
+    import torch
+
+    from asr_b200.loss.tdt import tdt_loss
+
+    c = DRAWS["c3_tdt_bpe"]
+    dev = torch.device("cuda")
+    leaves = [torch.tensor(c[k], device=dev, requires_grad=True) for k in ("enc", "dec", "W", "W_dur")]
+    ints = [torch.tensor(c[k], device=dev) for k in ("targets", "in_lens", "tgt_lens")]
+    loss = tdt_loss(*leaves, *ints, [int(x) for x in c["durations"]], 0, float(c["sigma"]), tf32)
+    grads = []
+    for _ in range(2):
+        g = torch.autograd.grad(loss.sum(), leaves, retain_graph=True)
+        grads.append([x.double().cpu().numpy() for x in g])
+    want = oracle_of(c)
+    for name, a, b in zip(GRADS, grads[0], grads[1]):
+        assert relnorm(b, a) <= (2e-3 if tf32 else 1e-5), name
+        for got in (a, b):
+            if tf32:
+                assert relnorm(got, want[name]) <= BF16_GRAD_RELNORM, name
+            else:  # the fp32 bar of the other parity tests
+                err, scale = np.abs(got - want[name]).max(), np.abs(want[name]).max()
+                assert err <= 1e-4 * max(1.0, scale), f"{name}: max-abs {err:.3e}"
