@@ -255,6 +255,7 @@ int rnnt_forward_impl(const void* encoder, const void* decoder, int act_dtype, c
                       int V, int d, int S, int blank_idx, int tf32, float* loss, double* alpha, float* log_P_blank,
                       float* log_P_y, float* log_prob, void* workspace, size_t workspace_bytes, asr_stream_t stream,
                       void* stash = nullptr, size_t stash_bytes = 0) {
+    NvtxRange range("asr::rnnt_forward");
     if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || check_act_dtype(act_dtype))
         return ASR_ERR_INVALID_ARGUMENT;
     if (B == 0) return ASR_OK;
@@ -288,6 +289,7 @@ int rnnt_backward_impl(const void* encoder, const void* decoder, int act_dtype, 
                        void* grad_encoder, void* grad_decoder, float* grad_joint_W, void* workspace,
                        size_t workspace_bytes, asr_stream_t stream, const void* stash = nullptr,
                        size_t stash_bytes = 0) {
+    NvtxRange range("asr::rnnt_backward");
     if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || check_act_dtype(act_dtype))
         return ASR_ERR_INVALID_ARGUMENT;
     if (!grad_joint_W) return ASR_ERR_INVALID_ARGUMENT;
@@ -403,6 +405,7 @@ int tdt_forward_impl(const void* encoder, const void* decoder, int act_dtype, co
                      int d, int S, int blank_idx, float sigma, int tf32, float* loss, double* alpha,
                      float* log_P_blank, float* log_P_y, float* log_P_dur, float* log_prob, void* workspace,
                      size_t workspace_bytes, asr_stream_t stream, void* stash = nullptr, size_t stash_bytes = 0) {
+    NvtxRange range("asr::tdt_forward");
     if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || bad_tdt(n_dur, max_duration) ||
         check_act_dtype(act_dtype))
         return ASR_ERR_INVALID_ARGUMENT;
@@ -439,6 +442,7 @@ int tdt_backward_impl(const void* encoder, const void* decoder, int act_dtype, c
                       const float* grad_loss, int tf32, void* grad_encoder, void* grad_decoder, float* grad_joint_W,
                       float* grad_joint_W_dur, void* workspace, size_t workspace_bytes, asr_stream_t stream,
                       const void* stash = nullptr, size_t stash_bytes = 0) {
+    NvtxRange range("asr::tdt_backward");
     if (bad_dims(B, T, U, V, d) || S < 0 || blank_idx < 0 || blank_idx >= V || bad_tdt(n_dur, max_duration) ||
         check_act_dtype(act_dtype))
         return ASR_ERR_INVALID_ARGUMENT;

@@ -315,6 +315,7 @@ using namespace asr;
 extern "C" int asr_ctc_alpha(const float* log_probs, const int32_t* targets, const int32_t* in_lens,
                              const int32_t* tgt_lens, int B, int T, int V, int S, double* alpha, float* log_Z,
                              asr_stream_t stream) {
+    NvtxRange range("asr::ctc_alpha");
     if (B < 0 || T < 1 || V < 1 || S < 0) return ASR_ERR_INVALID_ARGUMENT;
     if (B == 0) return ASR_OK;
     if (!log_probs || !in_lens || !tgt_lens || !alpha || !log_Z || (S > 0 && !targets)) return ASR_ERR_INVALID_ARGUMENT;
@@ -360,6 +361,7 @@ int ctc_grad_dispatch(const double* alpha, const float* log_probs, const int32_t
 extern "C" int asr_ctc_grad(const double* alpha, const float* log_Z, const float* log_probs, const int32_t* targets,
                             const int32_t* in_lens, const int32_t* tgt_lens, const float* grad_loss,
                             int zero_infinity, int B, int T, int V, int S, float* grad_logits, asr_stream_t stream) {
+    NvtxRange range("asr::ctc_grad");
     if (B < 0 || T < 1 || V < 1 || S < 0) return ASR_ERR_INVALID_ARGUMENT;
     if (B == 0) return ASR_OK;
     if (!alpha || !log_Z || !log_probs || !in_lens || !tgt_lens || !grad_loss || !grad_logits ||

@@ -36,6 +36,7 @@ cudaEvent_t take_event() {
 }  // namespace
 
 KernelTimer::KernelTimer(const char* name, cudaStream_t stream) : name_(name), stream_(stream) {
+    nvtxRangePushA(name);
     std::lock_guard<std::mutex> lock(g_mu);
     if (!g_on) return;
     start_ = take_event();
@@ -43,6 +44,7 @@ KernelTimer::KernelTimer(const char* name, cudaStream_t stream) : name_(name), s
 }
 
 KernelTimer::~KernelTimer() {
+    nvtxRangePop();
     if (!start_) return;
     std::lock_guard<std::mutex> lock(g_mu);
     cudaEvent_t stop = take_event();
