@@ -1762,9 +1762,21 @@ struct DhEpilogue {
         w.e_cur = enc_at(b, t);
         w.e_nxt = t + 1 < w.Tb ? enc_at(b, t + 1) : 0.f;
         if (kSmemDec) {
-            for (int u = 0; u < w.Ub; ++u) {
-                sdin[u * kDhM + cl] = col_ok ? act(P.a.dec, P.a.dec16, ((int64_t)b * P.a.U + u) * P.a.d + col) : 0.f;
-                sacc[u * kDhM + cl] = 0.f;
+            // 16 label positions' loads in flight before their shared-memory stores
+            // (a load behind each store would pay one memory latency per position)
+            for (int u0 = 0; u0 < w.Ub; u0 += 16) {
+                float v[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    v[i] = (col_ok && u0 + i < w.Ub)
+                               ? act(P.a.dec, P.a.dec16, ((int64_t)b * P.a.U + u0 + i) * P.a.d + col)
+                               : 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    if (u0 + i < w.Ub) {
+                        sdin[(u0 + i) * kDhM + cl] = v[i];
+                        sacc[(u0 + i) * kDhM + cl] = 0.f;
+                    }
             }
         }
         w.dirty = false;
