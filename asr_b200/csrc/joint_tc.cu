@@ -1547,19 +1547,31 @@ __global__ void __launch_bounds__(kStashThreads, 3) stash_dlogits_kernel(StashPa
         const int R = min(kStashRows, rows - r0);
         const int64_t row0 = (int64_t)(base + r0);  // global node of the tile's first row
         __syncthreads();  // the previous tile's coefficients are no longer read
+        // every coefficient load of the row issued before the first shared store
+        // (a load behind each store would pay one memory latency per value)
         if (threadIdx.x < R) {
             const int64_t n = row0 + threadIdx.x;
             const float* meta = P.stash.meta + n * mw;
-            const float l2 = __ldg(meta + nch) * kLog2e;
-            for (int j = 0; j < nch; ++j) s_e[threadIdx.x * kStashMaxChunks + j] = fmaf(__ldg(meta + j), kLog2e, -l2);
-            s_y[threadIdx.x] = __float_as_int(__ldg(meta + nch + 1));
+            float ref[kStashMaxChunks];
+#pragma unroll
+            for (int j = 0; j < kStashMaxChunks; ++j) ref[j] = j < nch ? __ldg(meta + j) : 0.f;
+            const float lse = __ldg(meta + nch), yv = __ldg(meta + nch + 1);
             const float cb = __ldg(P.in.cb + n), ct = __ldg(P.in.ct + n);
+            float gd[kMaxDurCols];
+#pragma unroll
+            for (int k = 0; k < kMaxDurCols; ++k) gd[k] = k < a.n_dur ? __ldg(P.in.gdur + n * a.n_dur + k) : 0.f;
+            const float l2 = lse * kLog2e;
+#pragma unroll
+            for (int j = 0; j < kStashMaxChunks; ++j)
+                if (j < nch) s_e[threadIdx.x * kStashMaxChunks + j] = fmaf(ref[j], kLog2e, -l2);
+            s_y[threadIdx.x] = __float_as_int(yv);
             s_cb[threadIdx.x] = cb;
             s_ct[threadIdx.x] = ct;
             s_pn[threadIdx.x] = cb + ct;
+#pragma unroll
+            for (int k = 0; k < kMaxDurCols; ++k)
+                if (k < a.n_dur) s_gd[threadIdx.x * kMaxDurCols + k] = gd[k];
         }
-        for (int i = threadIdx.x; i < R * a.n_dur; i += kStashThreads)
-            s_gd[(i / a.n_dur) * kMaxDurCols + i % a.n_dur] = __ldg(P.in.gdur + row0 * a.n_dur + i);
         __syncthreads();
         const uint32_t items = (uint32_t)R * P.groups;
         // the tile's stash and G rows, addressed with 32-bit offsets from here
