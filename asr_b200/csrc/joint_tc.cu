@@ -32,6 +32,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "joint.cuh"
 #include "tc_common.cuh"
@@ -1733,6 +1734,9 @@ __device__ __forceinline__ float act(const float* f32, const __nv_bfloat16* b16,
 
 // Walk state of one epilogue thread over consecutive nodes (warp-uniform except
 // the per-column values).
+__device__ __forceinline__ float dec_value(float x) { return x; }
+__device__ __forceinline__ float dec_value(__nv_bfloat16 x) { return __bfloat162float(x); }
+
 struct DhWalk {
     int b, t, u, Tb, Ub;
     float e_cur, e_nxt;  // enc[b, t, col], enc[b, t + 1, col]
@@ -1746,7 +1750,10 @@ struct DhEpilogue {
     const int col;     // hidden column
     const bool col_ok;
     const int cl;      // column within the slice (shared-memory column)
-    float* sdin;       // [dec_rows][kDhM] dec copy
+    // [dec_rows][kDhM] dec copy: bf16 on the bf16 path (it only enters tanh(enc + dec),
+    // far below the path's rounding), which leaves shared memory for another ring stage
+    using DecT = typename std::conditional<kSplit, float, __nv_bfloat16>::type;
+    DecT* sdin;
     float* sacc;       // [dec_rows][kDhM] d_dec sums
 
     // h = tanh(enc + dec), recomputed as the hidden rows computed it
@@ -1756,7 +1763,7 @@ struct DhEpilogue {
         return col_ok ? act(P.a.enc, P.a.enc16, ((int64_t)b * P.a.T + t) * P.a.d + col) : 0.f;
     }
     __device__ float dec_at(const DhWalk& w, int u) const {
-        if (kSmemDec) return sdin[u * kDhM + cl];
+        if (kSmemDec) return dec_value(sdin[u * kDhM + cl]);
         return col_ok ? act(P.a.dec, P.a.dec16, ((int64_t)w.b * P.a.U + u) * P.a.d + col) : 0.f;
     }
     __device__ void add_dec(const DhWalk& w, int u, float x) const {
@@ -1786,7 +1793,7 @@ struct DhEpilogue {
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
                     if (u0 + i < w.Ub) {
-                        sdin[(u0 + i) * kDhM + cl] = v[i];
+                        sdin[(u0 + i) * kDhM + cl] = DecT(v[i]);
                         sacc[(u0 + i) * kDhM + cl] = 0.f;
                     }
             }
@@ -1844,11 +1851,11 @@ struct DhEpilogue {
         if (k >= N) {
             // the whole group inside frame t (most groups): label positions u .. u + N - 1,
             // one base address with constant offsets, no per-node frame selects
-            const float* din = sdin + w.u * kDhM + cl;
+            const DecT* din = sdin + w.u * kDhM + cl;
             float* acc = sacc + w.u * kDhM + cl;
             float dv[N], sa[N], xs[N];
 #pragma unroll
-            for (int i = 0; i < N; ++i) dv[i] = din[i * kDhM];
+            for (int i = 0; i < N; ++i) dv[i] = dec_value(din[i * kDhM]);
 #pragma unroll
             for (int i = 0; i < N; ++i) sa[i] = acc[i * kDhM];
 #pragma unroll
@@ -1876,7 +1883,7 @@ struct DhEpilogue {
         }
         float dv[N], sa[N];
 #pragma unroll
-        for (int i = 0; i < N; ++i) dv[i] = sdin[idx[i]];
+        for (int i = 0; i < N; ++i) dv[i] = dec_value(sdin[idx[i]]);
 #pragma unroll
         for (int i = 0; i < N; ++i) sa[i] = sacc[idx[i]];
         float lo[N], hi[N];
@@ -1928,8 +1935,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const JointArgs& a = P.a;
     const int S = P.stages;
     uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* sdin = reinterpret_cast<float*>(stages + (size_t)S * SB);  // [dec_rows][kDhM]
-    float* sacc = sdin + (size_t)P.dec_rows * kDhM;                               // [dec_rows][kDhM]
+    using DecT = typename DhEpilogue<kSmemDec, kSplit>::DecT;
+    DecT* sdin = reinterpret_cast<DecT*>(stages + (size_t)S * SB);  // [dec_rows][kDhM]
+    float* sacc = reinterpret_cast<float*>(sdin + (size_t)P.dec_rows * kDhM);  // [dec_rows][kDhM]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sacc + (size_t)P.dec_rows * kDhM);  // 512 B multiples: aligned
     uint64_t* b_full = bars;
     uint64_t* b_empty = bars + S;
@@ -2343,9 +2351,9 @@ BwdLayout bwd_layout(const JointArgs& a, int64_t cap) {
     return L;
 }
 
-size_t dh_smem_bytes(int stages, int dec_rows, int cta = 1) {
+size_t dh_smem_bytes(int stages, int dec_rows, int cta = 1, int dec_bytes = 4) {
     const size_t sb = kDhABytes + (size_t)(kDhNodes / cta) * kDhK * 2;
-    return 1024 + (size_t)stages * sb + 2 * sizeof(float) * (size_t)dec_rows * kDhM + 8 * (2 * stages + 5) + 16;
+    return 1024 + (size_t)stages * sb + (size_t)(dec_bytes + 4) * dec_rows * kDhM + 8 * (2 * stages + 5) + 16;
 }
 
 // CTA pairs for the d_hidden kernel when ASR_B200_DH_PAIRS=1. Off by default:
@@ -2452,10 +2460,11 @@ int tc_joint_backward(const JointArgs& a, const JointBwdIn& in, const JointBwdOu
     const int dh_units = dh_cta == 2 ? (DP.ndt + 1) / 2 : DP.ndt;  // work items per node range
     DP.groups = std::max(1, sms / (dh_units * dh_cta));
     const int limit = dyn_smem_limit();
-    DP.dec_rows = !a.head && (int)dh_smem_bytes(2, a.U, dh_cta) <= limit ? a.U : 0;
+    const int dec_bytes = g.parts == 3 ? 4 : 2;  // the shared dec copy: fp32 on the split path, bf16 otherwise
+    DP.dec_rows = !a.head && (int)dh_smem_bytes(2, a.U, dh_cta, dec_bytes) <= limit ? a.U : 0;
     DP.stages = 2;
-    while (DP.stages < 8 && (int)dh_smem_bytes(DP.stages + 1, DP.dec_rows, dh_cta) <= limit) ++DP.stages;
-    const size_t smem_dh = dh_smem_bytes(DP.stages, DP.dec_rows, dh_cta);
+    while (DP.stages < 8 && (int)dh_smem_bytes(DP.stages + 1, DP.dec_rows, dh_cta, dec_bytes) <= limit) ++DP.stages;
+    const size_t smem_dh = dh_smem_bytes(DP.stages, DP.dec_rows, dh_cta, dec_bytes);
     auto dh_kernel = dh_cta == 2
                          ? (g.parts == 3 ? (DP.dec_rows > 0 ? tc_dh_kernel<true, true, 2> : tc_dh_kernel<false, true, 2>)
                                          : (DP.dec_rows > 0 ? tc_dh_kernel<true, false, 2> : tc_dh_kernel<false, false, 2>))
