@@ -2173,7 +2173,7 @@ struct DwParams {
     int* err;
 };
 
-constexpr int kDwStages = 3;
+constexpr int kDwStages = 4;
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     tc_dw_kernel(const __grid_constant__ CUtensorMap map_g, const __grid_constant__ CUtensorMap map_h, DwParams P) {
